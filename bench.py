@@ -1,0 +1,484 @@
+#!/usr/bin/env python
+"""Filtered-QKV hot-path benchmark: one layer's forward + backward, tokens/s.
+
+`python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config config2]`
+Under torchrun each rank drives one GPU on its own batch shard (weak scaling) and the step
+ends with the all-reduce of the filter gradients (the path's one exchange step).
+
+A step is the reference's layer composition: projection (x[B,T,C] x W^T -> [B,F,T]), scan,
+scan backward, projection backward (dx and dW), [all-reduce of dW, d logit_bias, d init].
+`value`: device-resident inputs, timed with CUDA events, max over ranks.
+`e2e`: the same step through the public module API (filter forward + autograd backward),
+with the step's inputs (x and the upstream q/k/v gradients) copied from pinned host memory
+and the step's result (the logit-bias gradient) read back, inside the timed region.
+Prints one JSON line (rank 0).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "filtered-QKV fwd+bwd tokens/s"
+UNIT = "tokens/s"
+
+CONFIGS = {
+    # BASELINE configs 1-3 mapped onto the reference parameterisation (head_dim 128, r = 128 ->
+    # one decay logit per head per token; F = (NH + 2 NKVH) * 129).
+    "config2": dict(B=32, T=1024, C=768, NH=6, NKVH=6, D=128, r=128, dtype="bf16", bias=0.0,
+                    desc="d=12 training shape: B=32/rank, T=1024, C=768, 6+6+6 heads x 128, r=128, bf16"),
+    "config3": dict(B=4, T=16384, C=1024, NH=8, NKVH=8, D=128, r=128, dtype="bf16", bias=-3.0,
+                    desc="long sequence: B=4/rank, T=16384, C=1024, 8+8+8 heads x 128, r=128, bf16, a~0.95"),
+    "config1": dict(B=2, T=256, C=768, NH=6, NKVH=6, D=128, r=128, dtype="f32", bias=0.0,
+                    desc="CPU-runnable shape in fp32: B=2/rank, T=256, C=768, 6+6+6 heads x 128"),
+}
+
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return {k: float(d[k]) for k in FALLBACK_PEAKS}, "measured"
+    except (OSError, KeyError, ValueError):
+        return dict(FALLBACK_PEAKS), "fallback"
+
+
+def profile_traffic(kernel: str, config: str):
+    """DRAM bytes per launch recorded from an ncu capture in profiles/<kernel>_<config>.md
+    (line `dram_bytes_per_launch: N`), or None."""
+    p = os.path.join(ROOT, "profiles", f"{kernel}_{config}.md")
+    try:
+        with open(p) as f:
+            for line in f:
+                if line.strip().startswith("dram_bytes_per_launch:"):
+                    return float(line.split(":", 1)[1].strip().split()[0])
+    except OSError:
+        pass
+    return None
+
+
+# ------------------------------------------------------------------------------------------
+# Clock sampling during the timed region
+# ------------------------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str):
+        self.gpu_id = gpu_id
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", self.gpu_id, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx.append(float(parts[1]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[3:7]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def gpu_id_for(dev_index: int) -> str:
+    import torch
+
+    try:
+        props = torch.cuda.get_device_properties(dev_index)
+        bus = getattr(props, "pci_bus_id", None)
+        dom = getattr(props, "pci_domain_id", None)
+        devid = getattr(props, "pci_device_id", None)
+        if bus is not None and dom is not None and devid is not None:
+            return f"{dom:08X}:{bus:02X}:{devid:02X}.0"
+    except Exception:
+        pass
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        return vis.split(",")[dev_index]
+    return str(dev_index)
+
+
+# ------------------------------------------------------------------------------------------
+# Workload
+# ------------------------------------------------------------------------------------------
+def make_inputs(cfg, device, seed):
+    import torch
+
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    B, T, C, NH, NKVH, D, r = (cfg[k] for k in ("B", "T", "C", "NH", "NKVH", "D", "r"))
+    H, Da = NH + 2 * NKVH, D // r
+    F = H * (D + Da)
+    dt = torch.bfloat16 if cfg["dtype"] == "bf16" else torch.float32
+    x = torch.randn(B, T, C, generator=g).to(dt)
+    wv = torch.randn(H, D, C, generator=g) / math.sqrt(C)      # value rows ~ N(0, 1/sqrt(C))
+    wl = torch.randn(H, Da, C, generator=g) * 0.02            # decay-logit rows ~ N(0, 0.02)
+    W = torch.cat([wv, wl], dim=1).reshape(F, C)              # head-major interleaved, fp32 master
+    bias = torch.full((H, Da), float(cfg["bias"]))
+    init = torch.zeros(H, D)
+    gq = torch.randn(B, NH, T, D, generator=g).to(dt)
+    gk = torch.randn(B, NKVH, T, D, generator=g).to(dt)
+    gv = torch.randn(B, NKVH, T, D, generator=g).to(dt)
+    host = dict(x=x, W=W, bias=bias, init=init, gq=gq, gk=gk, gv=gv)
+    dev = {k: v.to(device) for k, v in host.items()}
+    return host, dev, dict(B=B, T=T, C=C, NH=NH, NKVH=NKVH, D=D, r=r, H=H, Da=Da, F=F, dt=dt)
+
+
+def run_ours(args, cfg):
+    import torch
+    import torch.distributed as dist
+
+    import nanochat_filter_b200 as nf
+    from nanochat_filter_b200 import _lib
+    from nanochat_filter_b200.dist import GradBucket
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        from datetime import timedelta
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    _lib.load()
+
+    host, d, s = make_inputs(cfg, device, seed=1234 + rank)
+    B, T, C, NH, NKVH, D, r, H, Da, F, dt = (s[k] for k in ("B", "T", "C", "NH", "NKVH", "D", "r", "H", "Da", "F",
+                                                           "dt"))
+    ops = torch.ops.nanochat_cuda
+    scan_args = (NH, NKVH, Da, r)
+    W = d["W"]
+    Wg = torch.zeros_like(W)
+    bias = d["bias"]
+    init = d["init"]
+    bucket_params = [torch.nn.Parameter(W), torch.nn.Parameter(bias), torch.nn.Parameter(init)]
+    bucket = GradBucket(bucket_params) if world > 1 else None
+
+    ev = None
+
+    def step(record):
+        # one layer fwd + bwd with the same operators the filter's autograd graph runs
+        w_c = W.to(dt)                                              # weight cast (autocast's job)
+        inits = init.to(dt).unsqueeze(0).expand(B, -1, -1).contiguous()
+        if record is not None:
+            record[0].record()
+        comb = ops.fused_linear_transpose_cuda_op(d["x"], w_c)       # [B, F, T]
+        if record is not None:
+            record[1].record()
+        combined = comb.transpose(1, 2)
+        q, k, v = ops.ltv_fused_concat_head_major_register_cast_blelloch_scan_cuda_op(
+            combined, inits, bias, *scan_args, 8, 8, 4, 32, 2, 8, True)
+        if record is not None:
+            record[2].record()
+        gc = torch.empty_like(combined)
+        gi = torch.empty_like(inits)
+        gb = torch.zeros_like(bias)
+        if record is not None:
+            record[3].record()
+        ops.ltv_fused_concat_head_major_register_cast_blelloch_scan_cuda_backward_kernel(
+            combined, inits, bias, q, k, v, d["gq"], d["gk"], d["gv"], gc, gi, gb, *scan_args, 32, 2, 8, True)
+        if record is not None:
+            record[4].record()
+        gx = torch.empty_like(d["x"])
+        if record is not None:
+            record[5].record()
+        ops.fused_linear_transpose_backward_kernel(d["x"], w_c, gc.transpose(1, 2), gx, Wg)
+        if record is not None:
+            record[6].record()
+        if bucket is not None:
+            bucket_params[0].grad = Wg
+            bucket_params[1].grad = gb
+            bucket_params[2].grad = gi.float().sum(0)
+            bucket.reduce()
+        return gx
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    for _ in range(max(args.warmup, 3)):
+        step(None)
+    torch.cuda.synchronize()
+    assert _lib.all_workspace_errors() == 0, "a device-side wait timed out during warm-up"
+
+    # ---------------- timed region (device-resident inputs) ----------------
+    K = args.steps
+    events = [[torch.cuda.Event(enable_timing=True) for _ in range(7)] for _ in range(K)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(gpu_id_for(local))
+    barrier()
+    torch.cuda.synchronize()
+    sampler.start()
+    time.sleep(0.3)
+    wall0 = time.time()
+    start.record()
+    for i in range(K):
+        step(events[i])
+    end.record()
+    torch.cuda.synchronize()
+    wall = time.time() - wall0
+    barrier()
+    clocks = sampler.stop()
+    elapsed_ms = start.elapsed_time(end)
+    phases = {"gemm_fwd": (0, 1), "scan_fwd": (1, 2), "scan_bwd": (3, 4), "gemm_bwd": (5, 6)}
+    phase_ms = {n: statistics.mean(events[i][a].elapsed_time(events[i][b]) for i in range(K))
+                for n, (a, b) in phases.items()}
+    if world > 1:
+        t = torch.tensor([elapsed_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed_ms = float(t.item())
+    ms_per_step = elapsed_ms / K
+    value = world * B * T / (ms_per_step / 1e3)
+    assert _lib.all_workspace_errors() == 0, "a device-side wait timed out during the timed region"
+
+    # ---------------- e2e through the public module API ----------------
+    filt = nf.LtvCudaFusedConcatHeadMajorRegisterCastBlellochScanQkvFilter(NH, NKVH, D, r).to(device)
+    with torch.no_grad():
+        filt.c.weight.copy_(W)
+        filt.logit_bias.copy_(bias)
+        filt.init_param.copy_(init)
+    e2e_bucket = GradBucket([filt.c.weight, filt.logit_bias, filt.init_param]) if world > 1 else None
+    pin = {k: host[k].pin_memory() for k in ("x", "gq", "gk", "gv")}
+    xd = torch.empty_like(d["x"])
+    gds = {k: torch.empty_like(d[k]) for k in ("gq", "gk", "gv")}
+    out_host = torch.empty((H, Da), dtype=torch.float32).pin_memory()
+    h2d_bytes = sum(t.numel() * t.element_size() for t in pin.values())
+    d2h_bytes = out_host.numel() * out_host.element_size()
+
+    def e2e_step():
+        xd.copy_(pin["x"], non_blocking=True)
+        for k2 in ("gq", "gk", "gv"):
+            gds[k2].copy_(pin[k2], non_blocking=True)
+        filt.zero_grad(set_to_none=True)
+        xin = xd.detach().requires_grad_(True)
+        q, k, v = filt(xin, nf.LtvInitValues())
+        torch.autograd.backward([q, k, v], [gds["gq"].transpose(1, 2), gds["gk"].transpose(1, 2),
+                                            gds["gv"].transpose(1, 2)])
+        if e2e_bucket is not None:
+            e2e_bucket.reduce()
+        out_host.copy_(filt.logit_bias.grad, non_blocking=True)
+
+    for _ in range(max(args.warmup, 3)):
+        e2e_step()
+    torch.cuda.synchronize()
+    K2 = max(3, min(K, 20))
+    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    s2.record()
+    for _ in range(K2):
+        e2e_step()
+    e2.record()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = s2.elapsed_time(e2)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_value = world * B * T / (e2e_ms / K2 / 1e3)
+
+    # ---------------- roofline of the dominant kernel and of the step ----------------
+    peaks, peaks_src = load_peaks()
+    sustained = elapsed_ms >= 1000.0
+    tc_peak = peaks["bf16_tflops_sustained"] if sustained else peaks["bf16_tflops"]
+    gemm_bwd_flops = 4.0 * B * T * C * F
+    achieved = gemm_bwd_flops / (phase_ms["gemm_bwd"] / 1e3) / 1e12
+    traffic = profile_traffic("gemm_bwd", args.config)
+    step_flops = 6.0 * B * T * C * F
+    esz = 2 if dt == torch.bfloat16 else 4
+    step_bytes = float(B * T * (6 * C + 6 * H * D) * esz + F * C * esz)
+    t_tc = step_flops / (tc_peak * 1e12)
+    t_hbm = step_bytes / (peaks["hbm_gbs"] * 1e9)
+    step_frac = max(t_tc, t_hbm) / (ms_per_step / 1e3) if world == 1 else None
+
+    result = {
+        "metric": METRIC,
+        "value": round(value, 1),
+        "unit": UNIT,
+        "n_gpus": world,
+        "steps": K,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_per_step, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": cfg["dtype"],
+        "data": "synthetic (seeded N(0,1) activations and upstream grads; value rows N(0,1/sqrt(C)), "
+                "decay rows N(0,0.02); random-init weights)",
+        "config": {
+            "workload": f"{args.config}: {cfg['desc']}",
+            "tokens_per_rank_per_step": B * T,
+            "parallelism": f"dp{world} (batch-sharded; all_reduce of filter grads)" if world > 1 else "single GPU",
+            "l2": "working set per step > 126 MB L2 (inputs larger than L2; no flush)",
+        },
+        "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": h2d_bytes,
+                "d2h_bytes_per_step": d2h_bytes, "steps": K2,
+                "path": "LtvCudaFusedConcatHeadMajorRegisterCastBlellochScanQkvFilter forward + autograd backward"},
+        "gpu_launches": 5 * K,
+        "roofline": {"bound": "tensor", "kernel": "gemm_tc_kernel (projection backward: dx + dW)",
+                     "achieved": round(achieved, 1), "peak": tc_peak, "unit": "TFLOP/s",
+                     "frac": round(achieved / tc_peak, 4),
+                     "traffic": traffic,
+                     "peak_source": f"{peaks_src} ({'sustained' if sustained else 'burst'})",
+                     "algorithmic_flops_per_launch": gemm_bwd_flops},
+        "step_roofline": {"frac": None if step_frac is None else round(step_frac, 4),
+                          "bound": "tensor" if t_tc >= t_hbm else "hbm",
+                          "t_tensor_us": round(t_tc * 1e6, 1), "t_hbm_us": round(t_hbm * 1e6, 1),
+                          "flops_per_step": step_flops, "bytes_per_step": step_bytes},
+        "phases_ms": {k: round(v, 4) for k, v in phase_ms.items()},
+        "clocks": clocks,
+        "wall_s_timed": round(wall, 3),
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline(cfg, args.cpu_seconds)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+
+
+# ------------------------------------------------------------------------------------------
+# CPU baseline / reference arm: the oracle port of the reference's CPU algorithm
+# ------------------------------------------------------------------------------------------
+def _oracle_sample(cfg, seqs, seed=7):
+    import numpy as np
+
+    rng = np.random.default_rng(seed)
+    T, C, NH, NKVH, D, r = (cfg[k] for k in ("T", "C", "NH", "NKVH", "D", "r"))
+    H, Da = NH + 2 * NKVH, D // r
+    F = H * (D + Da)
+    x = rng.standard_normal((seqs, T, C)).astype(np.float32)
+    w = np.concatenate([rng.standard_normal((H, D, C)) / np.sqrt(C), rng.standard_normal((H, Da, C)) * 0.02],
+                       axis=1).reshape(F, C).astype(np.float32)
+    init = np.zeros((seqs, H, D), np.float32)
+    bias = np.full((H, Da), float(cfg["bias"]), np.float32)
+    gq = rng.standard_normal((seqs, NH, T, D)).astype(np.float32)
+    gk = rng.standard_normal((seqs, NKVH, T, D)).astype(np.float32)
+    gv = rng.standard_normal((seqs, NKVH, T, D)).astype(np.float32)
+    return x, w, init, bias, gq, gk, gv, NH, NKVH, Da, r
+
+
+def cpu_baseline(cfg, seconds=10.0, seqs=1):
+    """Times the oracle port (C, OpenMP over all host cores) on `seqs` sequences of the workload,
+    repeating until `seconds` of work (at most 8 repeats)."""
+    from oracle import oracle as O
+
+    O.build()
+    sample = _oracle_sample(cfg, seqs)
+    bf16 = cfg["dtype"] == "bf16"
+    O.layer_fwd_bwd(*sample, bf16=bf16)  # warm-up (thread pool, page faults)
+    times = []
+    t_all = time.perf_counter()
+    while len(times) < 8 and (time.perf_counter() - t_all < seconds or len(times) < 1):
+        t0 = time.perf_counter()
+        O.layer_fwd_bwd(*sample, bf16=bf16)
+        times.append(time.perf_counter() - t0)
+    med = statistics.median(times)
+    cores = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+    return {"value": round(seqs * cfg["T"] / med, 2), "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": f"{seqs} sequence(s) x {cfg['T']} tokens of {cfg['desc']}; oracle/ltv_oracle.c "
+                      f"(C restatement of the reference's CPU oracle, double-accumulated GEMMs), "
+                      f"median of {len(times)} runs"}
+
+
+def run_reference(args, cfg):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import oracle as O
+
+    O.build()
+    sample = _oracle_sample(cfg, 1)
+    bf16 = cfg["dtype"] == "bf16"
+    for _ in range(max(1, min(args.warmup, 2))):
+        O.layer_fwd_bwd(*sample, bf16=bf16)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        O.layer_fwd_bwd(*sample, bf16=bf16)
+        times.append(time.perf_counter() - t0)
+    total = sum(times)
+    value = args.steps * cfg["T"] / total
+    cores = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+    n = int(os.environ.get("WORLD_SIZE", "1"))
+    sample_desc = (f"1 sequence x {cfg['T']} tokens per step of {cfg['desc']}; oracle port "
+                   "(the reference's CPU path is a torch Python oracle that cannot run on the GPU box)")
+    print(json.dumps({
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": n, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(1e3 * total / args.steps, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": cfg["dtype"], "data": "synthetic",
+        "config": {"workload": f"{args.config}: {cfg['desc']}", "tokens_per_step": cfg["T"]},
+        "impl": "reference",
+        "cpu_baseline": {"value": round(value, 2), "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": sample_desc},
+        "e2e": {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="config2")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    cfg = CONFIGS[args.config]
+    if args.impl == "reference":
+        run_reference(args, cfg)
+    else:
+        run_ours(args, cfg)
+
+
+if __name__ == "__main__":
+    main()

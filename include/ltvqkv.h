@@ -1,0 +1,188 @@
+/*
+ * ltvqkv.h — C ABI of the B200 filtered-QKV hot path (libltvqkv.so).
+ *
+ * The filtered-QKV layer of nanochat-filter computes, per attention layer,
+ *   combined[b, f, t] = sum_c W[f, c] * x[b, t, c]                      (projection)
+ *   alpha[b, t, h, g] = sigmoid(combined[b, h*(D+Da)+D+g, t] + logit_bias[h, g])
+ *   h[t] = (1 - alpha[t]) * h[t-1] + alpha[t] * u[t]                     (EWMA scan)
+ * with u = the D value rows of head h, alpha shared by groups of r channels
+ * (Da = D / r logit rows per head, head-major rows: [h0 values | h0 logits | h1 ...],
+ * Q heads, then K heads, then V heads), h[-1] = inits[b, h, :].
+ *
+ * Every entry point:
+ *   - takes device pointers, element strides (int64, in elements) and sizes;
+ *   - enqueues work on `stream` (a cudaStream_t, NULL = legacy default stream)
+ *     and returns without synchronising;
+ *   - never allocates device memory: the caller passes outputs and, where a kernel
+ *     needs scratch, a workspace of at least the size the matching *_workspace_bytes
+ *     query returns. A workspace must be zero-filled once before its first use; each
+ *     call leaves it ready for the next call on the same stream. Calls that may run
+ *     concurrently on the GPU must use different workspaces.
+ *   - returns LTVQKV_OK or an error status (never aborts the process).
+ *
+ * dtype codes: LTVQKV_DTYPE_F32 (float) or LTVQKV_DTYPE_BF16 (bfloat16 storage,
+ * fp32 arithmetic). logit_bias and its gradient are always fp32.
+ */
+#ifndef LTVQKV_H_
+#define LTVQKV_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LTVQKV_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define LTVQKV_API __attribute__((visibility("default")))
+#else
+#define LTVQKV_API
+#endif
+
+enum ltvqkv_dtype {
+  LTVQKV_DTYPE_F32 = 0,
+  LTVQKV_DTYPE_BF16 = 1,
+};
+
+enum ltvqkv_status {
+  LTVQKV_OK = 0,
+  LTVQKV_ERR_INVALID_ARG = 1, /* null pointer where data is required, negative size */
+  LTVQKV_ERR_SHAPE = 2,       /* sizes inconsistent or beyond what the kernels support */
+  LTVQKV_ERR_STRIDE = 3,      /* a layout the kernel does not accept */
+  LTVQKV_ERR_DTYPE = 4,       /* unknown dtype code */
+  LTVQKV_ERR_ALIGN = 5,       /* pointer alignment a kernel needs is not met */
+  LTVQKV_ERR_LAUNCH = 6,      /* CUDA launch or runtime error */
+  LTVQKV_ERR_TIMEOUT = 7,     /* a bounded device-side wait gave up (read by ltvqkv_workspace_error) */
+  LTVQKV_ERR_WORKSPACE = 8,   /* workspace missing or smaller than required */
+  LTVQKV_ERR_UNSUPPORTED = 9, /* valid request this build does not implement */
+};
+
+/* Library ABI version (LTVQKV_ABI_VERSION). */
+LTVQKV_API int ltvqkv_abi_version(void);
+
+/* Static, human-readable text for a status code. */
+LTVQKV_API const char* ltvqkv_status_string(int status);
+
+/* Text of the last CUDA error seen by this library on the calling thread ("" if none). */
+LTVQKV_API const char* ltvqkv_last_cuda_error(void);
+
+/* ------------------------------------------------------------------------------------------
+ * Scan: replaces cpp_ewma_cuda.ltv_fused_concat_head_major_register_cast_blelloch_scan_cuda_forward
+ * (reference cpp_ewma/src/ltv_fused_concat_head_major_register_cast_blelloch_scan_cuda_forward.cu:532-552,
+ * bound in cpp_ewma/src/bindings.cpp; called from
+ * nanochat/ops/ltv_cuda_fused_concat_head_major_register_cast_blelloch_scan.py:35-71).
+ *
+ * combined: [B, T, F] with element strides (sc_b, sc_t, sc_e), F = H*(D+Da), H = NH+2*NKVH,
+ *           D = Da*r. Any strides are accepted; (F*T, 1, T) (the transposed projection output)
+ *           and (T*F, F, 1) take vectorised paths.
+ * inits:    [B, H, D] contiguous, same dtype as combined.
+ * out_q/k/v:[B, NH, T, D] / [B, NKVH, T, D] / [B, NKVH, T, D] contiguous, same dtype.
+ * use_sigmoid: 1 -> alpha = sigmoid(logit + bias); 0 -> alpha = logit + bias.
+ * ------------------------------------------------------------------------------------------ */
+LTVQKV_API size_t ltvqkv_scan_workspace_bytes(int B, int T, int NH, int NKVH, int Da, int r);
+
+LTVQKV_API int ltvqkv_scan_fwd(int dtype,
+                    const void* combined, int64_t sc_b, int64_t sc_t, int64_t sc_e,
+                    const void* inits, const float* logit_bias,
+                    void* out_q, void* out_k, void* out_v,
+                    int B, int T, int NH, int NKVH, int Da, int r, int use_sigmoid,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
+/* Scan backward: replaces cpp_ewma_cuda.ltv_fused_concat_head_major_register_cast_blelloch_scan_cuda_backward
+ * (reference cpp_ewma/src/ltv_fused_concat_head_major_register_cast_blelloch_scan_cuda_backward.cu:882-976;
+ * called from nanochat/ops/ltv_cuda_fused_concat_head_major_register_cast_blelloch_scan.py:145-193).
+ *
+ * h_strides / g_strides: 4 element strides (b, h, t, d) for each of hq, hk, hv (saved forward
+ * outputs) and grad_hq, grad_hk, grad_hv (upstream gradients); any strides are accepted.
+ * grad_combined: [B, T, F] with strides (gc_b, gc_t, gc_e) — written for every element
+ *                (value channels: du = alpha*g_hat; logit channels: sum over the r channels
+ *                of the group of d_alpha * alpha*(1-alpha)).
+ * grad_inits:    [B, H, D] contiguous, written.
+ * grad_logit_bias: [H, Da] fp32, ACCUMULATED into (+=), as the reference's atomicAdd is.
+ * Deterministic: no floating-point atomics.
+ */
+LTVQKV_API int ltvqkv_scan_bwd(int dtype,
+                    const void* combined, int64_t sc_b, int64_t sc_t, int64_t sc_e,
+                    const void* inits, const float* logit_bias,
+                    const void* hq, const int64_t* hq_strides,
+                    const void* hk, const int64_t* hk_strides,
+                    const void* hv, const int64_t* hv_strides,
+                    const void* grad_hq, const int64_t* gq_strides,
+                    const void* grad_hk, const int64_t* gk_strides,
+                    const void* grad_hv, const int64_t* gv_strides,
+                    void* grad_combined, int64_t gc_b, int64_t gc_t, int64_t gc_e,
+                    void* grad_inits, float* grad_logit_bias,
+                    int B, int T, int NH, int NKVH, int Da, int r, int use_sigmoid,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------------------------
+ * Projection ("fused linear transpose"): replaces cpp_ewma_cuda.fused_linear_transpose
+ * (reference cpp_ewma/src/fused_linear_transpose_forward.cu:23-58; called from
+ * nanochat/ops/fused_linear_transpose.py:20-41).
+ *   out[b, f, t] = sum_k weight[f, k] * x[b, t, k]
+ * x [B, T, K], weight [F, K], out [B, F, T], all contiguous and of `dtype`; fp32 accumulation.
+ * bf16 with K % 8 == 0 and T % 8 == 0 runs on tcgen05 tensor cores (TMA-fed, TMEM
+ * accumulators); other shapes and fp32 run a CUDA-core kernel with fp32 products.
+ * ------------------------------------------------------------------------------------------ */
+LTVQKV_API size_t ltvqkv_gemm_workspace_bytes(void);
+
+LTVQKV_API int ltvqkv_gemm_fwd(int dtype, const void* x, const void* weight, void* out,
+                    int B, int T, int K, int F,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
+/* Projection backward: replaces cpp_ewma_cuda.fused_linear_transpose_backward
+ * (reference cpp_ewma/src/fused_linear_transpose_backward.cu:22-132; called from
+ * nanochat/ops/fused_linear_transpose.py:84-101).
+ *   grad_x[b, t, k]   = sum_f grad_out[b, f, t] * weight[f, k]      (overwritten)
+ *   grad_weight[f, k] = sum_b sum_t grad_out[b, f, t] * x[b, t, k]  (overwritten)
+ * grad_out [B, F, T] with strides (go_b, go_f, go_t): contiguous (F*T, T, 1) or the
+ * transposed view (F*T, 1, F). x, weight, grad_x use `dtype`; grad_weight uses
+ * grad_weight_dtype (fp32 master weights under autocast). One launch computes both.
+ */
+LTVQKV_API int ltvqkv_gemm_bwd(int dtype, const void* x, const void* weight,
+                    const void* grad_out, int64_t go_b, int64_t go_f, int64_t go_t,
+                    void* grad_x, void* grad_weight, int grad_weight_dtype,
+                    int B, int T, int K, int F,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------------------------
+ * Decode: one incremental filter step per token, replacing the T == 1 pass of
+ * LtvCudaFusedConcatHeadMajorRegisterCastBlellochScanQkvFilter.forward with cached state
+ * (reference nanochat/ltv_cuda_fused_concat_head_major_register_cast_blelloch_scan_qkv_filter.py:24-73
+ * with previous_values from nanochat/kv_cache.py:212-257): projection of x[b, :],
+ * rounding of the projected values to `dtype` (as the reference's [B,F,1] buffer does), gate,
+ * and one recurrence step, in one launch.
+ *   x:       [B, C] contiguous.    weight: [F, C] contiguous.
+ *   prev_q/k/v: [B, NH|NKVH, D] with element strides (b, h, d) each given as 3 int64; NULL
+ *            prev_q means "no cached state": init_param [H, D] (contiguous) is used for every b.
+ *   out_q/k/v: [B, NH|NKVH, D] with element strides (3 int64 each); may alias prev_* exactly
+ *            (in-place state update) but must not partially overlap them.
+ * ------------------------------------------------------------------------------------------ */
+LTVQKV_API int ltvqkv_decode_step(int dtype, const void* x, const void* weight, const float* logit_bias,
+                       const void* prev_q, const int64_t* pq_strides,
+                       const void* prev_k, const int64_t* pk_strides,
+                       const void* prev_v, const int64_t* pv_strides,
+                       const void* init_param,
+                       void* out_q, const int64_t* oq_strides,
+                       void* out_k, const int64_t* ok_strides,
+                       void* out_v, const int64_t* ov_strides,
+                       int B, int C, int NH, int NKVH, int Da, int r, int use_sigmoid,
+                       void* stream);
+
+/* Reads and clears the device-side error word of a workspace (synchronises `stream`).
+ * *err_out receives LTVQKV_OK or LTVQKV_ERR_TIMEOUT. */
+LTVQKV_API int ltvqkv_workspace_error(void* workspace, void* stream, uint32_t* err_out);
+
+/* Failure-path check (no reference counterpart): launches one thread that waits on a
+ * workspace word nothing sets, gives up after limit_ns (at most 5 s), records
+ * LTVQKV_ERR_TIMEOUT in the workspace and returns; read it with ltvqkv_workspace_error.
+ * This is the bounded-wait path of every inter-CTA wait in the library. */
+LTVQKV_API int ltvqkv_debug_wait_timeout(void* workspace, uint64_t limit_ns, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LTVQKV_H_ */

@@ -1,0 +1,94 @@
+// Library-level entry points of libltvqkv: version, status text, CUDA error capture and the
+// workspace error query.
+#include <stdio.h>
+#include <string.h>
+
+#include "ltvqkv_common.cuh"
+
+namespace {
+thread_local char g_last_cuda_error[256] = {0};
+}
+
+namespace ltvqkv_host {
+void set_last_cuda_error(cudaError_t e) {
+  if (e == cudaSuccess) return;
+  const char* name = cudaGetErrorName(e);
+  const char* text = cudaGetErrorString(e);
+  snprintf(g_last_cuda_error, sizeof(g_last_cuda_error), "%s: %s", name ? name : "?", text ? text : "?");
+}
+int check_launch() {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e);
+    return LTVQKV_ERR_LAUNCH;
+  }
+  return LTVQKV_OK;
+}
+}  // namespace ltvqkv_host
+
+extern "C" int ltvqkv_abi_version(void) { return LTVQKV_ABI_VERSION; }
+
+extern "C" const char* ltvqkv_status_string(int status) {
+  switch (status) {
+    case LTVQKV_OK: return "ok";
+    case LTVQKV_ERR_INVALID_ARG: return "invalid argument";
+    case LTVQKV_ERR_SHAPE: return "unsupported or inconsistent shape";
+    case LTVQKV_ERR_STRIDE: return "unsupported stride layout";
+    case LTVQKV_ERR_DTYPE: return "unsupported dtype";
+    case LTVQKV_ERR_ALIGN: return "misaligned pointer";
+    case LTVQKV_ERR_LAUNCH: return "CUDA launch/runtime error";
+    case LTVQKV_ERR_TIMEOUT: return "device-side wait timed out";
+    case LTVQKV_ERR_WORKSPACE: return "workspace missing or too small";
+    case LTVQKV_ERR_UNSUPPORTED: return "unsupported request";
+    default: return "unknown status";
+  }
+}
+
+extern "C" const char* ltvqkv_last_cuda_error(void) { return g_last_cuda_error; }
+
+extern "C" int ltvqkv_workspace_error(void* workspace, void* stream, uint32_t* err_out) {
+  if (!workspace || !err_out) return LTVQKV_ERR_INVALID_ARG;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  ltvqkv::WorkspaceHeader* ws = reinterpret_cast<ltvqkv::WorkspaceHeader*>(workspace);
+  uint32_t v = 0;
+  cudaError_t e = cudaMemcpyAsync(&v, &ws->error, sizeof(v), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e == cudaSuccess && v != 0) {
+    uint32_t zero = 0;
+    e = cudaMemcpyAsync(&ws->error, &zero, sizeof(zero), cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  }
+  if (e != cudaSuccess) {
+    ltvqkv_host::set_last_cuda_error(e);
+    return LTVQKV_ERR_LAUNCH;
+  }
+  *err_out = v;
+  return LTVQKV_OK;
+}
+
+// ------------------------------------------------------------------------------------------
+// Failure-path self test: one thread waits on a workspace word that nothing ever sets, with a
+// caller-given wall-clock limit, records LTVQKV_ERR_TIMEOUT in the workspace error word and
+// returns — the same bounded-wait path every inter-CTA wait of the library takes.
+// ------------------------------------------------------------------------------------------
+namespace {
+__global__ void wait_never_set_kernel(ltvqkv::WorkspaceHeader* ws, unsigned long long limit_ns) {
+  const unsigned int* flag = &ws->pad[0];
+  unsigned long long t0 = ltvqkv::global_timer_ns();
+  while (ltvqkv::ld_acquire_u32(flag) != 0xFFFFFFFFu) {
+    __nanosleep(1000);
+    if (ltvqkv::global_timer_ns() - t0 > limit_ns) {
+      ltvqkv::record_timeout(ws, 0xD00Du);
+      return;
+    }
+  }
+}
+}  // namespace
+
+extern "C" int ltvqkv_debug_wait_timeout(void* workspace, uint64_t limit_ns, void* stream) {
+  if (!workspace) return LTVQKV_ERR_WORKSPACE;
+  if (limit_ns > 5000000000ull) return LTVQKV_ERR_INVALID_ARG;
+  wait_never_set_kernel<<<1, 1, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<ltvqkv::WorkspaceHeader*>(workspace), (unsigned long long)limit_ns);
+  return ltvqkv_host::check_launch();
+}

@@ -1,0 +1,260 @@
+// Shared device/host helpers for libltvqkv (sm_100a only).
+//
+// Contents: bf16/fp32 load-store helpers, the workspace header used by every kernel that
+// needs scratch, bounded spin-waits (every wait gives up after a wall-clock limit, records
+// LTVQKV_ERR_TIMEOUT in the workspace and lets the kernel return), and thin inline-PTX
+// wrappers for mbarriers, TMA (cp.async.bulk.tensor, no cluster multicast anywhere) and
+// tcgen05 (TMEM alloc, MMA, commit, ld).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/ltvqkv.h"
+
+#define LTVQKV_DEVICE __device__ __forceinline__
+
+namespace ltvqkv {
+
+// ------------------------------------------------------------------------------------------
+// Workspace header. Lives at the start of every workspace; zero-filled once by the caller.
+// tile_counter / exit_counter drive dynamic tile scheduling and are reset by the last CTA of
+// each launch, so the next launch on the same stream starts from zero again. `epoch` tags
+// the look-back flags of the scan kernels: the last CTA bumps it, so flags written by older
+// launches never match the current one and the flag array needs no clearing between calls.
+// ------------------------------------------------------------------------------------------
+struct WorkspaceHeader {
+  unsigned int tile_counter;
+  unsigned int exit_counter;
+  unsigned int epoch;
+  unsigned int error;
+  unsigned int error_where;
+  unsigned int pad[59];  // header is 256 bytes
+};
+static_assert(sizeof(WorkspaceHeader) == 256, "workspace header must be 256 bytes");
+
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s per wait
+
+LTVQKV_DEVICE unsigned long long global_timer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+LTVQKV_DEVICE void record_timeout(WorkspaceHeader* ws, unsigned int where) {
+  if (ws != nullptr) {
+    atomicExch(&ws->error, (unsigned int)LTVQKV_ERR_TIMEOUT);
+    atomicExch(&ws->error_where, where);
+  }
+}
+
+// Dynamic tile ticket: each CTA draws tiles in order; the draw that exceeds `total` returns
+// total (callers stop). Launch finalisation resets the counters (see finish_launch).
+LTVQKV_DEVICE unsigned int draw_ticket(WorkspaceHeader* ws) { return atomicAdd(&ws->tile_counter, 1u); }
+
+// Called once per CTA by one thread after the CTA has drawn its last ticket and finished
+// every global write whose ordering matters. The last CTA resets the counters and bumps the
+// epoch for the next launch on this workspace.
+LTVQKV_DEVICE void finish_launch(WorkspaceHeader* ws, unsigned int num_ctas) {
+  __threadfence();
+  unsigned int done = atomicAdd(&ws->exit_counter, 1u);
+  if (done == num_ctas - 1) {
+    atomicExch(&ws->tile_counter, 0u);
+    atomicExch(&ws->exit_counter, 0u);
+    atomicAdd(&ws->epoch, 1u);
+    __threadfence();
+  }
+}
+
+// ------------------------------------------------------------------------------------------
+// Element conversion
+// ------------------------------------------------------------------------------------------
+template <typename T> struct Elem;
+template <> struct Elem<float> {
+  static LTVQKV_DEVICE float load(const float* p) { return *p; }
+  static LTVQKV_DEVICE void store(float* p, float v) { *p = v; }
+  static LTVQKV_DEVICE float to_f(float v) { return v; }
+  static LTVQKV_DEVICE float from_f(float v) { return v; }
+};
+template <> struct Elem<__nv_bfloat16> {
+  static LTVQKV_DEVICE float load(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+  static LTVQKV_DEVICE void store(__nv_bfloat16* p, float v) { *p = __float2bfloat16_rn(v); }
+  static LTVQKV_DEVICE float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+  static LTVQKV_DEVICE __nv_bfloat16 from_f(float v) { return __float2bfloat16_rn(v); }
+};
+
+// Logistic function evaluated with the CUDA math library's expf (the reference evaluates
+// 1 / (1 + expf(-x)) in fp32, cpp_ewma/src/ltv_fused_concat_head_major_register_cast_scan_cuda_common.cuh:114-117).
+LTVQKV_DEVICE float sigmoid_f32(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+// ------------------------------------------------------------------------------------------
+// Release/acquire flag helpers (gpu scope)
+// ------------------------------------------------------------------------------------------
+LTVQKV_DEVICE void st_release_u32(unsigned int* p, unsigned int v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+LTVQKV_DEVICE unsigned int ld_acquire_u32(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+LTVQKV_DEVICE float ld_cg_f32(const float* p) { return __ldcg(p); }
+
+// ------------------------------------------------------------------------------------------
+// Shared-memory address helpers
+// ------------------------------------------------------------------------------------------
+LTVQKV_DEVICE uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+// ------------------------------------------------------------------------------------------
+// mbarrier
+// ------------------------------------------------------------------------------------------
+LTVQKV_DEVICE void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+LTVQKV_DEVICE void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+LTVQKV_DEVICE void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+LTVQKV_DEVICE void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+LTVQKV_DEVICE bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait on an mbarrier phase. Returns false (after recording a timeout) when the
+// phase did not complete within kWaitLimitNs or another role already gave up (*abort != 0).
+LTVQKV_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, WorkspaceHeader* ws,
+                             unsigned int where) {
+  if (mbar_try_wait(bar, parity)) return true;
+  unsigned long long t0 = global_timer_ns();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort) return false;
+    if (global_timer_ns() - t0 > kWaitLimitNs) {
+      *abort = 1;
+      record_timeout(ws, where);
+      return false;
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------
+// TMA (tiled bulk tensor copies; plain CTA-local destinations)
+// ------------------------------------------------------------------------------------------
+LTVQKV_DEVICE void tma_prefetch_desc(const CUtensorMap* m) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(m) : "memory");
+}
+LTVQKV_DEVICE void tma_load_3d(void* smem_dst, const CUtensorMap* m, uint64_t* bar, int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(m), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+LTVQKV_DEVICE void tma_store_3d(const CUtensorMap* m, const void* smem_src, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(m),
+               "r"(smem_u32(smem_src)), "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
+}
+LTVQKV_DEVICE void tma_store_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+LTVQKV_DEVICE void tma_store_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+LTVQKV_DEVICE void tma_store_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+LTVQKV_DEVICE void tma_store_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+LTVQKV_DEVICE void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// ------------------------------------------------------------------------------------------
+// tcgen05
+// ------------------------------------------------------------------------------------------
+LTVQKV_DEVICE void tmem_alloc(uint32_t* smem_slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_slot)),
+               "r"(ncols)
+               : "memory");
+}
+LTVQKV_DEVICE void tmem_relinquish() { asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory"); }
+LTVQKV_DEVICE void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+LTVQKV_DEVICE void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+LTVQKV_DEVICE void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// D[tmem] (+)= A[smem] * B[smem]^T, bf16 inputs, fp32 accumulation (kind::f16).
+LTVQKV_DEVICE void umma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrive on an mbarrier once all previously issued tcgen05.mma of this thread complete.
+LTVQKV_DEVICE void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+LTVQKV_DEVICE void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// 32 lanes x 32 columns of 32-bit values: thread i of the warp receives row (lane base + i),
+// columns [col, col+32).
+LTVQKV_DEVICE void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+        "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
+        "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
+        "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+}
+
+// UMMA shared-memory matrix descriptor for a 128-byte-swizzled operand tile
+// (sm_100 descriptor: start>>4 in [0,14), LBO>>4 in [16,30), SBO>>4 in [32,46), version 1 at
+// bit 46, base offset 0, layout type SWIZZLE_128B (2) in [61,64)).
+//   K-major tile:  rows of 128 B (64 bf16 along K), 8-row atoms 1024 B apart  -> SBO = 1024.
+//   MN-major tile: rows of 128 B (64 bf16 along M/N) per k, 8-k atoms 1024 B apart -> SBO = 1024,
+//                  successive 64-wide M/N blocks LBO bytes apart.
+LTVQKV_DEVICE uint64_t umma_desc_sw128(uint32_t smem_addr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1u << 46;
+  d |= (uint64_t)2u << 61;
+  return d;
+}
+
+// Instruction descriptor for kind::f16 with bf16 A/B and fp32 D.
+__host__ __device__ constexpr uint32_t umma_idesc_bf16(int M, int N, int a_mn_major, int b_mn_major) {
+  return (1u << 4)                          // D format: f32
+         | (1u << 7)                        // A format: bf16
+         | (1u << 10)                       // B format: bf16
+         | ((uint32_t)(a_mn_major & 1) << 15)
+         | ((uint32_t)(b_mn_major & 1) << 16)
+         | ((uint32_t)(N >> 3) << 17)
+         | ((uint32_t)(M >> 4) << 24);
+}
+
+}  // namespace ltvqkv
+
+// ------------------------------------------------------------------------------------------
+// Host-side helpers shared by the .cu files
+// ------------------------------------------------------------------------------------------
+namespace ltvqkv_host {
+void set_last_cuda_error(cudaError_t e);
+int check_launch();  // returns LTVQKV_OK or LTVQKV_ERR_LAUNCH (and records the CUDA error text)
+inline bool valid_dtype(int dtype) { return dtype == LTVQKV_DTYPE_F32 || dtype == LTVQKV_DTYPE_BF16; }
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+}  // namespace ltvqkv_host

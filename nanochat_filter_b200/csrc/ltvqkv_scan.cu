@@ -1,0 +1,650 @@
+// Filter scan (EWMA with time-varying gain), forward and backward, for sm_100a.
+//
+// Semantics follow the reference's sequential oracle
+// (nanochat/ops/ltv_reference_ops.py:7-34 QuantizedStateUpdate, :37-124 the scan loop):
+//   alpha_t = sigmoid(logit_t + bias)            (or logit_t + bias without sigmoid)
+//   h_t     = (1 - alpha_t) * h_{t-1} + alpha_t * u_t     fp32 carry, output rounded to dtype
+// backward:
+//   g^_t    = g_t + (1 - alpha_{t+1}) * g^_{t+1}
+//   du_t    = alpha_t * g^_t
+//   dalpha  = g^_t * (u_t - h_{t-1})  with h_{t-1} the SAVED (dtype-rounded) output, inits at t=0
+//   dlogit  = sum over the r channels of the group of dalpha * alpha*(1-alpha)
+//   dinits  = g^_0 * (1 - alpha_0);  dbias = sum over b, t of dlogit.
+//
+// Design (B200): one CTA per (batch, head, T-chunk) tile holding all D channels of the head, so
+// the per-group dlogit reduction stays inside the CTA (no atomics). Inside a tile, each channel
+// is split into P segments of L steps; a thread scans its segment sequentially in registers,
+// segments are composed as affine maps (a, x): carry_out = a * carry_in + x. Across T-chunks,
+// carries propagate by decoupled look-back over a flag/payload array in the workspace: a tile
+// publishes its aggregate, walks back over predecessors until an inclusive prefix, then
+// publishes its own inclusive carry. Tiles are drawn from a ticket counter in chunk-major
+// order, so every predecessor was scheduled earlier (no deadlock); each spin is bounded.
+#include <algorithm>
+
+#include "ltvqkv_common.cuh"
+
+namespace ltvqkv {
+
+enum : unsigned int { kFlagNone = 0, kFlagAgg = 1, kFlagIncl = 2 };
+
+struct ScanGeometry {
+  int B, T, NH, NKVH, Da, r, D, H, F;
+  int TT;        // tokens per tile
+  int nchunks;   // ceil(T / TT)
+  int P;         // threads per channel
+  int L;         // tokens per thread segment (TT = P * L)
+  int nthreads;  // D * P
+};
+
+__host__ __device__ inline int pow2_floor(int v) {
+  int p = 1;
+  while (p * 2 <= v) p *= 2;
+  return p;
+}
+
+// Tile geometry shared by host sizing and kernels. `budget` = target channel*token elements.
+inline ScanGeometry make_geometry(int B, int T, int NH, int NKVH, int Da, int r, int budget) {
+  ScanGeometry g;
+  g.B = B; g.T = T; g.NH = NH; g.NKVH = NKVH; g.Da = Da; g.r = r;
+  g.D = Da * r; g.H = NH + 2 * NKVH; g.F = g.H * (g.D + Da);
+  int P = pow2_floor(std::max(1, 256 / std::max(1, g.D)));
+  P = std::min(P, 32);
+  g.P = P;
+  g.nthreads = g.D * P;
+  int L = budget / std::max(1, g.D * P);
+  L = std::max(1, std::min(L, 64));
+  g.L = L;
+  g.TT = P * L;
+  g.nchunks = T > 0 ? (T + g.TT - 1) / g.TT : 0;
+  return g;
+}
+
+constexpr int kFwdBudget = 8192;
+constexpr int kBwdBudget = 4096;
+
+struct ScanWorkspaceLayout {
+  size_t flags, aggA, aggX, inclX, bias_part, total;
+};
+
+inline ScanWorkspaceLayout scan_ws_layout(const ScanGeometry& g) {
+  using ltvqkv_host::align_up;
+  ScanWorkspaceLayout L;
+  size_t tiles = (size_t)g.B * g.H * g.nchunks;
+  size_t off = sizeof(WorkspaceHeader);
+  L.flags = off; off = align_up(off + tiles * 4, 256);
+  L.aggA = off;  off = align_up(off + tiles * g.Da * 4, 256);
+  L.aggX = off;  off = align_up(off + tiles * g.D * 4, 256);
+  L.inclX = off; off = align_up(off + tiles * g.D * 4, 256);
+  L.bias_part = off; off = align_up(off + (size_t)g.B * g.nchunks * g.H * g.Da * 4, 256);
+  L.total = off;
+  return L;
+}
+
+struct ScanFwdArgs {
+  const void* combined;
+  long long sc_b, sc_t, sc_e;
+  const void* inits;
+  const float* logit_bias;
+  void* out[3];
+  ScanGeometry g;
+  int use_sigmoid;
+  WorkspaceHeader* ws;
+  unsigned int* flags;
+  float* aggA;
+  float* aggX;
+  float* inclX;
+};
+
+struct ScanBwdArgs {
+  const void* combined;
+  long long sc_b, sc_t, sc_e;
+  const void* inits;
+  const float* logit_bias;
+  const void* h[3];
+  long long hs[3][4];
+  const void* gh[3];
+  long long gs[3][4];
+  void* grad_combined;
+  long long gc_b, gc_t, gc_e;
+  void* grad_inits;
+  ScanGeometry g;
+  int use_sigmoid;
+  WorkspaceHeader* ws;
+  unsigned int* flags;
+  float* aggA;
+  float* aggX;
+  float* inclX;
+  float* bias_part;
+};
+
+// Which output tensor and local head a global head index maps to (Q heads, K heads, V heads).
+LTVQKV_DEVICE void split_head(int h, int NH, int NKVH, int& which, int& hloc, int& nheads) {
+  if (h < NH) { which = 0; hloc = h; nheads = NH; }
+  else if (h < NH + NKVH) { which = 1; hloc = h - NH; nheads = NKVH; }
+  else { which = 2; hloc = h - NH - NKVH; nheads = NKVH; }
+}
+
+// Spin (one thread) until the flag of a predecessor tile carries the current epoch and a
+// state; returns the state, or kFlagIncl with *timed_out set when the wait gave up.
+LTVQKV_DEVICE unsigned int wait_flag(const unsigned int* flag, unsigned int epoch_tag, WorkspaceHeader* ws,
+                                     bool* timed_out) {
+  unsigned long long t0 = 0;
+  for (unsigned int it = 0;; ++it) {
+    unsigned int f = ld_acquire_u32(flag);
+    if ((f >> 2) == epoch_tag && (f & 3u) != kFlagNone) return f & 3u;
+    if (it == 64) t0 = global_timer_ns();
+    if (it > 64) {
+      __nanosleep(64);
+      if (global_timer_ns() - t0 > kWaitLimitNs) {
+        record_timeout(ws, 0x5CA0u);
+        *timed_out = true;
+        return kFlagIncl;
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------
+// Forward
+// ------------------------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(1024) scan_fwd_kernel(ScanFwdArgs args) {
+  extern __shared__ float smem[];
+  const ScanGeometry& g = args.g;
+  const int D = g.D, TT = g.TT, P = g.P, L = g.L, Da = g.Da, r = g.r;
+  const int ldu = TT + 1;
+  float* U = smem;                       // [D][TT+1]
+  float* alpha = U + D * ldu;            // [Da][TT]
+  float* segA = alpha + Da * TT;         // [D*P]
+  float* segX = segA + D * P;            // [D*P]
+  float* shE = segX + D * P;             // [D]
+  __shared__ unsigned int sh_tile, sh_state, sh_epoch;
+
+  const int tid = threadIdx.x;
+  if (tid == 0) {
+    sh_tile = draw_ticket(args.ws);
+    sh_epoch = *((volatile unsigned int*)&args.ws->epoch) & 0x3FFFFFFFu;
+  }
+  __syncthreads();
+  const unsigned int tile = sh_tile;
+  const unsigned int epoch = sh_epoch;
+  const int BH = g.B * g.H;
+  const int j = (int)(tile / BH);  // chunk index (chunk-major ticket order)
+  const int bh = (int)(tile % BH);
+  const int b = bh / g.H, h = bh % g.H;
+  const int t0 = j * TT;
+  const int tlen = min(TT, g.T - t0);
+
+  const T* cb = reinterpret_cast<const T*>(args.combined) + (long long)b * args.sc_b;
+  const int head_col = h * (D + Da);
+
+  // Gate values for this tile.
+  for (int i = tid; i < Da * TT; i += blockDim.x) {
+    int gi = i / TT, t = i - gi * TT;
+    if (t < tlen) {
+      float l = Elem<T>::load(cb + (long long)(t0 + t) * args.sc_t + (long long)(head_col + D + gi) * args.sc_e) +
+                args.logit_bias[h * Da + gi];
+      alpha[gi * TT + t] = args.use_sigmoid ? sigmoid_f32(l) : l;
+    }
+  }
+  // Value tile, coalesced along whichever of (t, channel) is unit-stride.
+  if (args.sc_t == 1) {
+    for (int i = tid; i < D * TT; i += blockDim.x) {
+      int c = i / TT, t = i - c * TT;
+      if (t < tlen) U[c * ldu + t] = Elem<T>::load(cb + (long long)(t0 + t) + (long long)(head_col + c) * args.sc_e);
+    }
+  } else {
+    for (int i = tid; i < D * TT; i += blockDim.x) {
+      int t = i / D, c = i - t * D;
+      if (t < tlen)
+        U[c * ldu + t] = Elem<T>::load(cb + (long long)(t0 + t) * args.sc_t + (long long)(head_col + c) * args.sc_e);
+    }
+  }
+  __syncthreads();
+
+  const int c = tid / P, s = tid - (tid / P) * P;
+  const int gi = c / r;
+  const int seg0 = s * L, seg1 = min(seg0 + L, tlen);
+  {
+    float a = 1.f, x = 0.f;
+    for (int t = seg0; t < seg1; ++t) {
+      float al = alpha[gi * TT + t];
+      x = (1.0f - al) * x + al * U[c * ldu + t];
+      a *= (1.0f - al);
+    }
+    segA[c * P + s] = a;
+    segX[c * P + s] = x;
+  }
+  __syncthreads();
+  float ea = 1.f, ex = 0.f;  // composition of segments 0..s-1 of this channel
+  for (int sp = 0; sp < s; ++sp) {
+    ex = segA[c * P + sp] * ex + segX[c * P + sp];
+    ea *= segA[c * P + sp];
+  }
+  const bool is_last_seg = (s == P - 1);
+  float tileA = 0.f, tileX = 0.f;
+  if (is_last_seg) {
+    float a = segA[c * P + s], x = segX[c * P + s];
+    tileA = ea * a;
+    tileX = a * ex + x;
+  }
+
+  const long long tile_idx = (long long)j * BH + bh;  // payload slot of this tile
+  if (j == 0) {
+    if (is_last_seg) {
+      float E = Elem<T>::load(reinterpret_cast<const T*>(args.inits) + ((long long)b * g.H + h) * D + c);
+      shE[c] = E;
+      args.inclX[tile_idx * D + c] = tileA * E + tileX;
+      __threadfence();
+    }
+    __syncthreads();
+    if (tid == 0) st_release_u32(&args.flags[tile_idx], (epoch << 2) | kFlagIncl);
+  } else {
+    if (is_last_seg) {
+      args.aggX[tile_idx * D + c] = tileX;
+      if (c % r == 0) args.aggA[tile_idx * Da + gi] = tileA;
+      __threadfence();
+    }
+    __syncthreads();
+    if (tid == 0) st_release_u32(&args.flags[tile_idx], (epoch << 2) | kFlagAgg);
+    // Look back over predecessor chunks of the same (b, h).
+    float accA = 1.f, accX = 0.f;
+    bool timed_out = false;
+    for (int k = j - 1; k >= 0; --k) {
+      const long long pidx = (long long)k * BH + bh;
+      if (tid == 0) sh_state = wait_flag(&args.flags[pidx], epoch, args.ws, &timed_out);
+      __syncthreads();
+      const unsigned int st = sh_state;
+      if (is_last_seg) {
+        if (st == kFlagIncl) {
+          float prev = timed_out ? 0.f : ld_cg_f32(&args.inclX[pidx * D + c]);
+          shE[c] = accA * prev + accX;
+        } else {
+          float Ak = ld_cg_f32(&args.aggA[pidx * Da + gi]);
+          float Xk = ld_cg_f32(&args.aggX[pidx * D + c]);
+          accX = accA * Xk + accX;
+          accA *= Ak;
+        }
+      }
+      __syncthreads();
+      if (st == kFlagIncl) break;
+    }
+    if (is_last_seg) {
+      args.inclX[tile_idx * D + c] = tileA * shE[c] + tileX;
+      __threadfence();
+    }
+    __syncthreads();
+    if (tid == 0) st_release_u32(&args.flags[tile_idx], (epoch << 2) | kFlagIncl);
+  }
+
+  // Final pass: walk the segment from its exact carry, overwriting U with h.
+  {
+    float carry = ea * shE[c] + ex;
+    for (int t = seg0; t < seg1; ++t) {
+      float al = alpha[gi * TT + t];
+      carry = (1.0f - al) * carry + al * U[c * ldu + t];
+      U[c * ldu + t] = carry;
+    }
+  }
+  __syncthreads();
+
+  int which, hloc, nheads;
+  split_head(h, g.NH, g.NKVH, which, hloc, nheads);
+  T* out = reinterpret_cast<T*>(args.out[which]) + (((long long)b * nheads + hloc) * g.T + t0) * D;
+  for (int i = tid; i < D * tlen; i += blockDim.x) {
+    int t = i / D, cc = i - t * D;
+    Elem<T>::store(out + (long long)t * D + cc, U[cc * ldu + t]);
+  }
+
+  if (tid == 0) finish_launch(args.ws, gridDim.x);
+}
+
+// ------------------------------------------------------------------------------------------
+// Backward
+// ------------------------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(1024) scan_bwd_kernel(ScanBwdArgs args) {
+  extern __shared__ float smem[];
+  const ScanGeometry& g = args.g;
+  const int D = g.D, TT = g.TT, P = g.P, L = g.L, Da = g.Da, r = g.r;
+  const int ld = TT + 1;
+  float* G = smem;                 // [D][TT+1]: upstream grad, then g^
+  float* Hs = G + D * ld;          // [D][TT+1]: h_{t-1}, then dlogit contributions
+  float* alpha = Hs + D * ld;      // [Da][TT+1]: alpha_{t0+t}, t = 0..tlen (alpha_T := 0)
+  float* segA = alpha + Da * ld;   // [D*P]
+  float* segX = segA + D * P;      // [D*P]
+  float* shE = segX + D * P;       // [D]
+  float* red = shE + D;            // [Da][TT]
+  __shared__ unsigned int sh_tile, sh_state, sh_epoch;
+
+  const int tid = threadIdx.x;
+  if (tid == 0) {
+    sh_tile = draw_ticket(args.ws);
+    sh_epoch = *((volatile unsigned int*)&args.ws->epoch) & 0x3FFFFFFFu;
+  }
+  __syncthreads();
+  const unsigned int tile = sh_tile;
+  const unsigned int epoch = sh_epoch;
+  const int BH = g.B * g.H;
+  const int j = g.nchunks - 1 - (int)(tile / BH);  // reverse chunk order
+  const int bh = (int)(tile % BH);
+  const int b = bh / g.H, h = bh % g.H;
+  const int t0 = j * TT;
+  const int tlen = min(TT, g.T - t0);
+  int which, hloc, nheads;
+  split_head(h, g.NH, g.NKVH, which, hloc, nheads);
+
+  const T* cb = reinterpret_cast<const T*>(args.combined) + (long long)b * args.sc_b;
+  const int head_col = h * (D + Da);
+
+  for (int i = tid; i < Da * ld; i += blockDim.x) {
+    int gi = i / ld, t = i - gi * ld;
+    if (t <= tlen) {
+      float al = 0.f;
+      if (t0 + t < g.T) {
+        float l = Elem<T>::load(cb + (long long)(t0 + t) * args.sc_t + (long long)(head_col + D + gi) * args.sc_e) +
+                  args.logit_bias[h * Da + gi];
+        al = args.use_sigmoid ? sigmoid_f32(l) : l;
+      }
+      alpha[gi * ld + t] = al;
+    }
+  }
+  {
+    const T* gp = reinterpret_cast<const T*>(args.gh[which]);
+    const long long* st = args.gs[which];
+    const T* base = gp + (long long)b * st[0] + (long long)hloc * st[1];
+    if (st[3] == 1 || st[2] != 1) {
+      for (int i = tid; i < D * TT; i += blockDim.x) {
+        int t = i / D, c = i - t * D;
+        if (t < tlen) G[c * ld + t] = Elem<T>::load(base + (long long)(t0 + t) * st[2] + (long long)c * st[3]);
+      }
+    } else {
+      for (int i = tid; i < D * TT; i += blockDim.x) {
+        int c = i / TT, t = i - c * TT;
+        if (t < tlen) G[c * ld + t] = Elem<T>::load(base + (long long)(t0 + t) + (long long)c * st[3]);
+      }
+    }
+  }
+  __syncthreads();
+
+  const int c = tid / P, s = tid - (tid / P) * P;
+  const int gi = c / r;
+  const int seg0 = min(s * L, tlen), seg1 = min(s * L + L, tlen);
+  {
+    float a = 1.f, x = 0.f;
+    for (int t = seg1 - 1; t >= seg0; --t) {
+      float an = 1.0f - alpha[gi * ld + t + 1];
+      x = an * x + G[c * ld + t];
+      a *= an;
+    }
+    segA[c * P + s] = a;
+    segX[c * P + s] = x;
+  }
+  __syncthreads();
+  float ea = 1.f, ex = 0.f;  // composition of segments s+1..P-1 (to the right)
+  for (int sp = P - 1; sp > s; --sp) {
+    ex = segA[c * P + sp] * ex + segX[c * P + sp];
+    ea *= segA[c * P + sp];
+  }
+  const bool is_first_seg = (s == 0);
+  float tileA = 0.f, tileX = 0.f;
+  if (is_first_seg) {
+    float a = segA[c * P], x = segX[c * P];
+    tileA = ea * a;
+    tileX = a * ex + x;
+  }
+
+  const long long tile_idx = (long long)j * BH + bh;
+  if (j == g.nchunks - 1) {
+    if (is_first_seg) {
+      shE[c] = 0.f;
+      args.inclX[tile_idx * D + c] = tileX;
+      __threadfence();
+    }
+    __syncthreads();
+    if (tid == 0) st_release_u32(&args.flags[tile_idx], (epoch << 2) | kFlagIncl);
+  } else {
+    if (is_first_seg) {
+      args.aggX[tile_idx * D + c] = tileX;
+      if (c % r == 0) args.aggA[tile_idx * Da + gi] = tileA;
+      __threadfence();
+    }
+    __syncthreads();
+    if (tid == 0) st_release_u32(&args.flags[tile_idx], (epoch << 2) | kFlagAgg);
+    float accA = 1.f, accX = 0.f;
+    bool timed_out = false;
+    for (int k = j + 1; k < g.nchunks; ++k) {
+      const long long pidx = (long long)k * BH + bh;
+      if (tid == 0) sh_state = wait_flag(&args.flags[pidx], epoch, args.ws, &timed_out);
+      __syncthreads();
+      const unsigned int st = sh_state;
+      if (is_first_seg) {
+        if (st == kFlagIncl) {
+          float prev = timed_out ? 0.f : ld_cg_f32(&args.inclX[pidx * D + c]);
+          shE[c] = accA * prev + accX;
+        } else {
+          float Ak = ld_cg_f32(&args.aggA[pidx * Da + gi]);
+          float Xk = ld_cg_f32(&args.aggX[pidx * D + c]);
+          accX = accA * Xk + accX;
+          accA *= Ak;
+        }
+      }
+      __syncthreads();
+      if (st == kFlagIncl) break;
+    }
+    if (is_first_seg) {
+      args.inclX[tile_idx * D + c] = tileA * shE[c] + tileX;
+      __threadfence();
+    }
+    __syncthreads();
+    if (tid == 0) st_release_u32(&args.flags[tile_idx], (epoch << 2) | kFlagIncl);
+  }
+
+  {
+    float carry = ea * shE[c] + ex;  // g^ at the token right after this segment
+    for (int t = seg1 - 1; t >= seg0; --t) {
+      carry = (1.0f - alpha[gi * ld + t + 1]) * carry + G[c * ld + t];
+      G[c * ld + t] = carry;
+    }
+  }
+  // h_{t-1} for the tile (saved forward output, or inits at t = 0).
+  {
+    const T* hp = reinterpret_cast<const T*>(args.h[which]);
+    const long long* st = args.hs[which];
+    const T* base = hp + (long long)b * st[0] + (long long)hloc * st[1];
+    const T* ini = reinterpret_cast<const T*>(args.inits) + ((long long)b * g.H + h) * D;
+    for (int i = tid; i < D * TT; i += blockDim.x) {
+      int t = i / D, cc = i - t * D;
+      if (t < tlen) {
+        int tt = t0 + t - 1;
+        Hs[cc * ld + t] = tt < 0 ? Elem<T>::load(ini + cc) : Elem<T>::load(base + (long long)tt * st[2] + (long long)cc * st[3]);
+      }
+    }
+  }
+  __syncthreads();
+
+  // Elementwise part: du, dalpha -> dlogit contributions, dinits.
+  T* gcb = reinterpret_cast<T*>(args.grad_combined) + (long long)b * args.gc_b;
+  const bool t_fast = (args.sc_t == 1 || args.gc_t == 1);
+  for (int i = tid; i < D * TT; i += blockDim.x) {
+    int cc, t;
+    if (t_fast) { cc = i / TT; t = i - cc * TT; }
+    else { t = i / D; cc = i - t * D; }
+    if (t >= tlen) continue;
+    const int gg = cc / r;
+    const float al = alpha[gg * ld + t];
+    const float ghat = G[cc * ld + t];
+    const float u = Elem<T>::load(cb + (long long)(t0 + t) * args.sc_t + (long long)(head_col + cc) * args.sc_e);
+    Elem<T>::store(gcb + (long long)(t0 + t) * args.gc_t + (long long)(head_col + cc) * args.gc_e, al * ghat);
+    const float dalpha = (u - Hs[cc * ld + t]) * ghat;
+    Hs[cc * ld + t] = args.use_sigmoid ? dalpha * (al * (1.0f - al)) : dalpha;
+    if (t0 + t == 0)
+      Elem<T>::store(reinterpret_cast<T*>(args.grad_inits) + ((long long)b * g.H + h) * D + cc, ghat * (1.0f - al));
+  }
+  __syncthreads();
+  for (int i = tid; i < Da * TT; i += blockDim.x) {
+    int gg = i / TT, t = i - gg * TT;
+    if (t < tlen) {
+      float sum = 0.f;
+      for (int k = 0; k < r; ++k) sum += Hs[(gg * r + k) * ld + t];
+      Elem<T>::store(gcb + (long long)(t0 + t) * args.gc_t + (long long)(head_col + D + gg) * args.gc_e, sum);
+      red[gg * TT + t] = sum;
+    }
+  }
+  __syncthreads();
+  for (int gg = tid; gg < Da; gg += blockDim.x) {
+    float sum = 0.f;
+    for (int t = 0; t < tlen; ++t) sum += red[gg * TT + t];
+    args.bias_part[(((long long)b * g.nchunks + j) * g.H + h) * Da + gg] = sum;
+  }
+
+  if (tid == 0) finish_launch(args.ws, gridDim.x);
+}
+
+// grad_logit_bias[h, g] += sum over (b, chunk) of the per-tile partials, in a fixed order.
+__global__ void bias_reduce_kernel(const float* part, float* grad_bias, int B, int nchunks, int H, int Da) {
+  int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= H * Da) return;
+  float sum = 0.f;
+  for (int bj = 0; bj < B * nchunks; ++bj) sum += part[(long long)bj * H * Da + idx];
+  grad_bias[idx] += sum;
+}
+
+__global__ void zero_grad_inits_kernel(void* p, long long n, int bf16) {
+  long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  if (bf16) reinterpret_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(0.f);
+  else reinterpret_cast<float*>(p)[i] = 0.f;
+}
+
+inline size_t fwd_smem_bytes(const ScanGeometry& g) {
+  return sizeof(float) * ((size_t)g.D * (g.TT + 1) + (size_t)g.Da * g.TT + 2 * (size_t)g.D * g.P + g.D);
+}
+inline size_t bwd_smem_bytes(const ScanGeometry& g) {
+  return sizeof(float) * (2 * (size_t)g.D * (g.TT + 1) + (size_t)g.Da * (g.TT + 1) + 2 * (size_t)g.D * g.P + g.D +
+                          (size_t)g.Da * g.TT);
+}
+
+}  // namespace ltvqkv
+
+using namespace ltvqkv;
+
+static int validate_scan_shape(int B, int T, int NH, int NKVH, int Da, int r) {
+  if (B < 0 || T < 0 || NH < 0 || NKVH < 0 || Da <= 0 || r <= 0) return LTVQKV_ERR_SHAPE;
+  if (NH + 2 * NKVH <= 0) return LTVQKV_ERR_SHAPE;
+  long long D = (long long)Da * r;
+  if (D > 1024) return LTVQKV_ERR_SHAPE;
+  return LTVQKV_OK;
+}
+
+extern "C" size_t ltvqkv_scan_workspace_bytes(int B, int T, int NH, int NKVH, int Da, int r) {
+  if (validate_scan_shape(B, T, NH, NKVH, Da, r) != LTVQKV_OK) return 0;
+  ScanGeometry gf = make_geometry(B, T, NH, NKVH, Da, r, kFwdBudget);
+  ScanGeometry gb = make_geometry(B, T, NH, NKVH, Da, r, kBwdBudget);
+  return std::max(scan_ws_layout(gf).total, scan_ws_layout(gb).total);
+}
+
+extern "C" int ltvqkv_scan_fwd(int dtype, const void* combined, int64_t sc_b, int64_t sc_t, int64_t sc_e,
+                               const void* inits, const float* logit_bias, void* out_q, void* out_k, void* out_v,
+                               int B, int T, int NH, int NKVH, int Da, int r, int use_sigmoid, void* workspace,
+                               size_t workspace_bytes, void* stream) {
+  if (!ltvqkv_host::valid_dtype(dtype)) return LTVQKV_ERR_DTYPE;
+  int st = validate_scan_shape(B, T, NH, NKVH, Da, r);
+  if (st != LTVQKV_OK) return st;
+  if (B == 0 || T == 0) return LTVQKV_OK;
+  if (!combined || !inits || !logit_bias || (NH > 0 && !out_q) || (NKVH > 0 && (!out_k || !out_v)))
+    return LTVQKV_ERR_INVALID_ARG;
+  ScanGeometry g = make_geometry(B, T, NH, NKVH, Da, r, kFwdBudget);
+  ScanWorkspaceLayout wl = scan_ws_layout(g);
+  if (!workspace || workspace_bytes < wl.total) return LTVQKV_ERR_WORKSPACE;
+  char* ws = reinterpret_cast<char*>(workspace);
+  ScanFwdArgs a;
+  a.combined = combined; a.sc_b = sc_b; a.sc_t = sc_t; a.sc_e = sc_e;
+  a.inits = inits; a.logit_bias = logit_bias;
+  a.out[0] = out_q; a.out[1] = out_k; a.out[2] = out_v;
+  a.g = g; a.use_sigmoid = use_sigmoid;
+  a.ws = reinterpret_cast<WorkspaceHeader*>(ws);
+  a.flags = reinterpret_cast<unsigned int*>(ws + wl.flags);
+  a.aggA = reinterpret_cast<float*>(ws + wl.aggA);
+  a.aggX = reinterpret_cast<float*>(ws + wl.aggX);
+  a.inclX = reinterpret_cast<float*>(ws + wl.inclX);
+  size_t smem = fwd_smem_bytes(g);
+  unsigned int grid = (unsigned int)((long long)B * g.H * g.nchunks);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (dtype == LTVQKV_DTYPE_BF16) {
+    cudaFuncSetAttribute(scan_fwd_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    scan_fwd_kernel<__nv_bfloat16><<<grid, g.nthreads, smem, s>>>(a);
+  } else {
+    cudaFuncSetAttribute(scan_fwd_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    scan_fwd_kernel<float><<<grid, g.nthreads, smem, s>>>(a);
+  }
+  return ltvqkv_host::check_launch();
+}
+
+extern "C" int ltvqkv_scan_bwd(int dtype, const void* combined, int64_t sc_b, int64_t sc_t, int64_t sc_e,
+                               const void* inits, const float* logit_bias, const void* hq, const int64_t* hq_strides,
+                               const void* hk, const int64_t* hk_strides, const void* hv, const int64_t* hv_strides,
+                               const void* grad_hq, const int64_t* gq_strides, const void* grad_hk,
+                               const int64_t* gk_strides, const void* grad_hv, const int64_t* gv_strides,
+                               void* grad_combined, int64_t gc_b, int64_t gc_t, int64_t gc_e, void* grad_inits,
+                               float* grad_logit_bias, int B, int T, int NH, int NKVH, int Da, int r, int use_sigmoid,
+                               void* workspace, size_t workspace_bytes, void* stream) {
+  if (!ltvqkv_host::valid_dtype(dtype)) return LTVQKV_ERR_DTYPE;
+  int st = validate_scan_shape(B, T, NH, NKVH, Da, r);
+  if (st != LTVQKV_OK) return st;
+  if (B == 0) return LTVQKV_OK;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int H = NH + 2 * NKVH;
+  const int D = Da * r;
+  if (T == 0) {
+    // No outputs: d inits is zero, d bias unchanged.
+    if (!grad_inits) return LTVQKV_ERR_INVALID_ARG;
+    long long n = (long long)B * H * D;
+    zero_grad_inits_kernel<<<(unsigned int)((n + 255) / 256), 256, 0, s>>>(grad_inits, n, dtype == LTVQKV_DTYPE_BF16);
+    return ltvqkv_host::check_launch();
+  }
+  if (!combined || !inits || !logit_bias || !grad_combined || !grad_inits || !grad_logit_bias)
+    return LTVQKV_ERR_INVALID_ARG;
+  if ((NH > 0 && (!hq || !grad_hq || !hq_strides || !gq_strides)) ||
+      (NKVH > 0 && (!hk || !hv || !grad_hk || !grad_hv || !hk_strides || !hv_strides || !gk_strides || !gv_strides)))
+    return LTVQKV_ERR_INVALID_ARG;
+  ScanGeometry g = make_geometry(B, T, NH, NKVH, Da, r, kBwdBudget);
+  ScanWorkspaceLayout wl = scan_ws_layout(g);
+  if (!workspace || workspace_bytes < wl.total) return LTVQKV_ERR_WORKSPACE;
+  char* ws = reinterpret_cast<char*>(workspace);
+  ScanBwdArgs a;
+  a.combined = combined; a.sc_b = sc_b; a.sc_t = sc_t; a.sc_e = sc_e;
+  a.inits = inits; a.logit_bias = logit_bias;
+  a.h[0] = hq; a.h[1] = hk; a.h[2] = hv;
+  a.gh[0] = grad_hq; a.gh[1] = grad_hk; a.gh[2] = grad_hv;
+  const int64_t* hs[3] = {hq_strides, hk_strides, hv_strides};
+  const int64_t* gs[3] = {gq_strides, gk_strides, gv_strides};
+  for (int i = 0; i < 3; ++i)
+    for (int k = 0; k < 4; ++k) {
+      a.hs[i][k] = hs[i] ? hs[i][k] : 0;
+      a.gs[i][k] = gs[i] ? gs[i][k] : 0;
+    }
+  a.grad_combined = grad_combined; a.gc_b = gc_b; a.gc_t = gc_t; a.gc_e = gc_e;
+  a.grad_inits = grad_inits;
+  a.g = g; a.use_sigmoid = use_sigmoid;
+  a.ws = reinterpret_cast<WorkspaceHeader*>(ws);
+  a.flags = reinterpret_cast<unsigned int*>(ws + wl.flags);
+  a.aggA = reinterpret_cast<float*>(ws + wl.aggA);
+  a.aggX = reinterpret_cast<float*>(ws + wl.aggX);
+  a.inclX = reinterpret_cast<float*>(ws + wl.inclX);
+  a.bias_part = reinterpret_cast<float*>(ws + wl.bias_part);
+  size_t smem = bwd_smem_bytes(g);
+  unsigned int grid = (unsigned int)((long long)B * g.H * g.nchunks);
+  if (dtype == LTVQKV_DTYPE_BF16) {
+    cudaFuncSetAttribute(scan_bwd_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    scan_bwd_kernel<__nv_bfloat16><<<grid, g.nthreads, smem, s>>>(a);
+  } else {
+    cudaFuncSetAttribute(scan_bwd_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    scan_bwd_kernel<float><<<grid, g.nthreads, smem, s>>>(a);
+  }
+  int rc = ltvqkv_host::check_launch();
+  if (rc != LTVQKV_OK) return rc;
+  int hd = H * Da;
+  bias_reduce_kernel<<<(hd + 127) / 128, 128, 0, s>>>(a.bias_part, grad_logit_bias, B, g.nchunks, H, Da);
+  return ltvqkv_host::check_launch();
+}

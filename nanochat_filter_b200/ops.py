@@ -1,0 +1,383 @@
+"""torch.library operators of the filtered-QKV hot path (namespace `nanochat_cuda`).
+
+Same op names, schemas, ownership and error behaviour as the reference's registry
+(nanochat/ops/ltv_cuda_ops.py:3, 115-145, 242-250; implementations in
+nanochat/ops/ltv_cuda_fused_concat_head_major_register_cast_blelloch_scan.py:31-289 and
+nanochat/ops/fused_linear_transpose.py:20-134; fake kernels in nanochat/ops/ltv_cuda_meta.py),
+so code written against the reference's `torch.ops.nanochat_cuda.*` runs unchanged:
+
+  ltv_fused_concat_head_major_register_cast_blelloch_scan_cuda_op      (autograd)
+  ltv_fused_concat_head_major_register_cast_blelloch_scan_cuda_forward_kernel
+  ltv_fused_concat_head_major_register_cast_blelloch_scan_cuda_backward_kernel
+  fused_linear_transpose_cuda_op                                       (autograd)
+  fused_linear_transpose
+  fused_linear_transpose_backward_kernel
+
+plus one op the reference does not have, `ltv_decode_step` (one-launch decode update).
+
+The CUDA implementations call libltvqkv.so through its C ABI; only "CUDA" and "Meta"
+dispatch keys are registered, so CPU tensors raise NotImplementedError from the dispatcher —
+there is no CPU fallback. The scan's tuning integers are accepted and ignored (the B200
+kernels pick their own tiling).
+"""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from . import _lib
+
+_SCAN_OP = "ltv_fused_concat_head_major_register_cast_blelloch_scan_cuda_op"
+_SCAN_FWD = "ltv_fused_concat_head_major_register_cast_blelloch_scan_cuda_forward_kernel"
+_SCAN_BWD = "ltv_fused_concat_head_major_register_cast_blelloch_scan_cuda_backward_kernel"
+
+lib = torch.library.Library("nanochat_cuda", "DEF")
+
+lib.define(
+    f"{_SCAN_OP}("
+    "Tensor combined, Tensor inits, Tensor logit_bias, "
+    "int NH, int NKVH, int da, int r, "
+    "int scan_threads_forward, int r_threads_forward, int r_items_forward, "
+    "int scan_threads_backward, int r_threads_backward, int r_items_backward, "
+    "bool use_sigmoid"
+    ") -> (Tensor, Tensor, Tensor)"
+)
+lib.define(
+    f"{_SCAN_FWD}("
+    "Tensor combined, Tensor inits, Tensor logit_bias, "
+    "Tensor(a!) out_q, Tensor(b!) out_k, Tensor(c!) out_v, "
+    "int T, int NH, int NKVH, int da, int r, "
+    "int scan_threads_forward, int r_threads_forward, int r_items_forward, "
+    "bool use_sigmoid"
+    ") -> ()"
+)
+lib.define(
+    f"{_SCAN_BWD}("
+    "Tensor combined, Tensor inits, Tensor logit_bias, "
+    "Tensor hq, Tensor hk, Tensor hv, "
+    "Tensor grad_hq, Tensor grad_hk, Tensor grad_hv, "
+    "Tensor(a!) grad_combined, Tensor(b!) grad_inits, Tensor(c!) grad_logit_bias, "
+    "int NH, int NKVH, int da, int r, "
+    "int scan_threads_backward, int r_threads_backward, int r_items_backward, "
+    "bool use_sigmoid"
+    ") -> ()"
+)
+lib.define("fused_linear_transpose(Tensor x, Tensor weight, Tensor(a!) out) -> ()")
+lib.define("fused_linear_transpose_cuda_op(Tensor x, Tensor weight) -> Tensor")
+lib.define(
+    "fused_linear_transpose_backward_kernel("
+    "Tensor x, Tensor weight, Tensor grad_out, Tensor(a!) grad_x, Tensor(b!) grad_weight"
+    ") -> ()"
+)
+lib.define(
+    "ltv_decode_step("
+    "Tensor x, Tensor weight, Tensor logit_bias, Tensor? prev_q, Tensor? prev_k, Tensor? prev_v, "
+    "Tensor init_param, int NH, int NKVH, int da, int r, bool use_sigmoid"
+    ") -> (Tensor, Tensor, Tensor)"
+)
+
+
+# ------------------------------------------------------------------------------------------
+# Scan
+# ------------------------------------------------------------------------------------------
+def _check_scan_inputs(combined, inits, logit_bias, NH, NKVH, da, r):
+    if combined.dim() != 3:
+        raise RuntimeError(f"combined must be [B, T, F], got {tuple(combined.shape)}")
+    H = NH + 2 * NKVH
+    D = da * r
+    B, T, F = combined.shape
+    if F != H * (D + da):
+        raise RuntimeError(f"combined has F={F}, expected (NH+2*NKVH)*(D+da) = {H * (D + da)}")
+    if tuple(inits.shape) != (B, H, D):
+        raise RuntimeError(f"inits must be [B, H, D] = {(B, H, D)}, got {tuple(inits.shape)}")
+    if tuple(logit_bias.shape) != (H, da):
+        raise RuntimeError(f"logit_bias must be [H, da] = {(H, da)}, got {tuple(logit_bias.shape)}")
+    if combined.dtype != inits.dtype:
+        raise RuntimeError(f"combined ({combined.dtype}) and inits ({inits.dtype}) must share a dtype")
+    if logit_bias.dtype != torch.float32:
+        raise RuntimeError(f"logit_bias must be float32, got {logit_bias.dtype}")
+
+
+@torch.library.impl(f"nanochat_cuda::{_SCAN_FWD}", "CUDA")
+def _scan_forward_kernel(combined, inits, logit_bias, out_q, out_k, out_v, T, NH, NKVH, da, r,
+                         scan_threads_forward, r_threads_forward, r_items_forward, use_sigmoid):
+    _check_scan_inputs(combined, inits, logit_bias, NH, NKVH, da, r)
+    L = _lib.load()
+    B = combined.shape[0]
+    inits = inits.contiguous()
+    logit_bias = logit_bias.contiguous()
+    for o in (out_q, out_k, out_v):
+        if not o.is_contiguous() or o.dtype != combined.dtype:
+            raise RuntimeError("out_q/out_k/out_v must be contiguous and share combined's dtype")
+    nbytes = L.ltvqkv_scan_workspace_bytes(B, T, NH, NKVH, da, r)
+    ws = _lib.workspace(combined.device, nbytes)
+    sc = combined.stride()
+    rc = L.ltvqkv_scan_fwd(_lib.dtype_code(combined.dtype), combined.data_ptr(), sc[0], sc[1], sc[2],
+                           inits.data_ptr(), logit_bias.data_ptr(), out_q.data_ptr(), out_k.data_ptr(),
+                           out_v.data_ptr(), B, T, NH, NKVH, da, r, int(bool(use_sigmoid)),
+                           ws.data_ptr(), ws.numel(), _lib.stream_handle(combined.device))
+    _lib.check(rc, "ltvqkv_scan_fwd")
+
+
+@torch.library.impl(f"nanochat_cuda::{_SCAN_OP}", "CUDA")
+def _scan_op(combined, inits, logit_bias, NH, NKVH, da, r, scan_threads_forward, r_threads_forward,
+             r_items_forward, scan_threads_backward, r_threads_backward, r_items_backward, use_sigmoid):
+    B, T, _ = combined.shape
+    D = da * r
+    kw = dict(device=combined.device, dtype=combined.dtype, memory_format=torch.contiguous_format)
+    out_q = torch.empty((B, NH, T, D), **kw)
+    out_k = torch.empty((B, NKVH, T, D), **kw)
+    out_v = torch.empty((B, NKVH, T, D), **kw)
+    _scan_forward_kernel(combined, inits, logit_bias, out_q, out_k, out_v, T, NH, NKVH, da, r,
+                         scan_threads_forward, r_threads_forward, r_items_forward, use_sigmoid)
+    return out_q, out_k, out_v
+
+
+@torch.library.impl(f"nanochat_cuda::{_SCAN_BWD}", "CUDA")
+def _scan_backward_kernel(combined, inits, logit_bias, hq, hk, hv, grad_hq, grad_hk, grad_hv, grad_combined,
+                          grad_inits, grad_logit_bias, NH, NKVH, da, r, scan_threads_backward, r_threads_backward,
+                          r_items_backward, use_sigmoid):
+    _check_scan_inputs(combined, inits, logit_bias, NH, NKVH, da, r)
+    L = _lib.load()
+    B, T, _ = combined.shape
+    inits = inits.contiguous()
+    logit_bias = logit_bias.contiguous()
+    if not grad_inits.is_contiguous() or not grad_logit_bias.is_contiguous():
+        raise RuntimeError("grad_inits and grad_logit_bias must be contiguous")
+    if grad_combined.shape != combined.shape or grad_combined.dtype != combined.dtype:
+        raise RuntimeError("grad_combined must match combined's shape and dtype")
+    for t in (hq, hk, hv, grad_hq, grad_hk, grad_hv):
+        if t.dtype != combined.dtype:
+            raise RuntimeError("saved outputs and their gradients must share combined's dtype")
+    nbytes = L.ltvqkv_scan_workspace_bytes(B, T, NH, NKVH, da, r)
+    ws = _lib.workspace(combined.device, nbytes)
+    sc, gc = combined.stride(), grad_combined.stride()
+    S = _lib.strides
+    rc = L.ltvqkv_scan_bwd(
+        _lib.dtype_code(combined.dtype), combined.data_ptr(), sc[0], sc[1], sc[2], inits.data_ptr(),
+        logit_bias.data_ptr(),
+        hq.data_ptr(), S(hq.stride()), hk.data_ptr(), S(hk.stride()), hv.data_ptr(), S(hv.stride()),
+        grad_hq.data_ptr(), S(grad_hq.stride()), grad_hk.data_ptr(), S(grad_hk.stride()),
+        grad_hv.data_ptr(), S(grad_hv.stride()),
+        grad_combined.data_ptr(), gc[0], gc[1], gc[2], grad_inits.data_ptr(), grad_logit_bias.data_ptr(),
+        B, T, NH, NKVH, da, r, int(bool(use_sigmoid)), ws.data_ptr(), ws.numel(),
+        _lib.stream_handle(combined.device))
+    _lib.check(rc, "ltvqkv_scan_bwd")
+
+
+def _scan_setup(ctx, inputs, output):
+    (combined, inits, logit_bias, NH, NKVH, da, r, _sf, _rf, _if, sb, rb, ib, use_sigmoid) = inputs
+    hq, hk, hv = output
+    ctx.save_for_backward(combined, inits, logit_bias, hq, hk, hv)
+    ctx.NH, ctx.NKVH, ctx.da, ctx.r = NH, NKVH, da, r
+    ctx.tuning = (sb, rb, ib)
+    ctx.use_sigmoid = use_sigmoid
+
+
+def _scan_backward(ctx, grad_hq, grad_hk, grad_hv):
+    combined, inits, logit_bias, hq, hk, hv = ctx.saved_tensors
+    grad_hq = torch.zeros_like(hq) if grad_hq is None else grad_hq
+    grad_hk = torch.zeros_like(hk) if grad_hk is None else grad_hk
+    grad_hv = torch.zeros_like(hv) if grad_hv is None else grad_hv
+    grad_combined = torch.empty_like(combined)
+    grad_inits = torch.empty_like(inits, memory_format=torch.contiguous_format)
+    grad_logit_bias = torch.zeros_like(logit_bias, memory_format=torch.contiguous_format)
+    torch.ops.nanochat_cuda.ltv_fused_concat_head_major_register_cast_blelloch_scan_cuda_backward_kernel(
+        combined, inits, logit_bias, hq, hk, hv, grad_hq, grad_hk, grad_hv, grad_combined, grad_inits,
+        grad_logit_bias, ctx.NH, ctx.NKVH, ctx.da, ctx.r, *ctx.tuning, ctx.use_sigmoid)
+    return (grad_combined, grad_inits, grad_logit_bias) + (None,) * 11
+
+
+torch.library.register_autograd(f"nanochat_cuda::{_SCAN_OP}", _scan_backward, setup_context=_scan_setup)
+
+
+@torch.library.register_fake(f"nanochat_cuda::{_SCAN_OP}")
+def _scan_op_fake(combined, inits, logit_bias, NH, NKVH, da, r, *tuning_and_flag):
+    B, T, _ = combined.shape
+    D = da * r
+    return (combined.new_empty((B, NH, T, D)), combined.new_empty((B, NKVH, T, D)),
+            combined.new_empty((B, NKVH, T, D)))
+
+
+@torch.library.register_fake(f"nanochat_cuda::{_SCAN_FWD}")
+def _scan_fwd_fake(*args):
+    return None
+
+
+@torch.library.register_fake(f"nanochat_cuda::{_SCAN_BWD}")
+def _scan_bwd_fake(*args):
+    return None
+
+
+# ------------------------------------------------------------------------------------------
+# Projection ("fused linear transpose")
+# ------------------------------------------------------------------------------------------
+def _is_transposed_grad_out(g: torch.Tensor) -> bool:
+    return g.stride(1) == 1 and g.stride(2) == g.size(1) and g.stride(0) == g.size(1) * g.size(2)
+
+
+@torch.library.impl("nanochat_cuda::fused_linear_transpose", "CUDA")
+def _fused_linear_transpose(x, weight, out):
+    if not x.is_contiguous() or not weight.is_contiguous() or not out.is_contiguous():
+        raise RuntimeError("fused_linear_transpose requires contiguous x, weight, and out tensors")
+    L = _lib.load()
+    B, T, K = x.shape
+    F = weight.shape[0]
+    if weight.shape[1] != K or tuple(out.shape) != (B, F, T):
+        raise RuntimeError(f"shape mismatch: x {tuple(x.shape)}, weight {tuple(weight.shape)}, out {tuple(out.shape)}")
+    if out.dtype != x.dtype:
+        raise RuntimeError("out must have x's dtype")
+    w = weight if weight.dtype == x.dtype else weight.to(x.dtype)
+    ws = _lib.workspace(x.device, L.ltvqkv_gemm_workspace_bytes())
+    rc = L.ltvqkv_gemm_fwd(_lib.dtype_code(x.dtype), x.data_ptr(), w.data_ptr(), out.data_ptr(), B, T, K, F,
+                           ws.data_ptr(), ws.numel(), _lib.stream_handle(x.device))
+    _lib.check(rc, "ltvqkv_gemm_fwd")
+
+
+@torch.library.impl("nanochat_cuda::fused_linear_transpose_cuda_op", "CUDA")
+def _fused_linear_transpose_op(x, weight):
+    B, T, _ = x.shape
+    F = weight.size(0)
+    # Every element is written by the kernel, so no zero fill is needed.
+    out = torch.empty((B, F, T), dtype=x.dtype, device=x.device)
+    _fused_linear_transpose(x, weight, out)
+    return out
+
+
+@torch.library.impl("nanochat_cuda::fused_linear_transpose_backward_kernel", "CUDA")
+def _fused_linear_transpose_backward_kernel(x, weight, grad_out, grad_x, grad_weight):
+    if not x.is_contiguous() or not weight.is_contiguous() or not (
+            grad_out.is_contiguous() or _is_transposed_grad_out(grad_out)):
+        raise RuntimeError(
+            "fused_linear_transpose_backward_kernel requires contiguous x and weight, and either contiguous or "
+            f"transposed grad_out. Found strides: x={x.stride()}, weight={weight.stride()}, "
+            f"grad_out={grad_out.stride()}")
+    L = _lib.load()
+    B, T, K = x.shape
+    F = weight.shape[0]
+    w = weight if weight.dtype == grad_out.dtype else weight.to(grad_out.dtype)
+    xx = x if x.dtype == grad_out.dtype else x.to(grad_out.dtype)
+    gx = grad_x if (grad_x.is_contiguous() and grad_x.dtype == grad_out.dtype) else torch.empty(
+        (B, T, K), dtype=grad_out.dtype, device=x.device)
+    if not grad_weight.is_contiguous():
+        raise RuntimeError("grad_weight must be contiguous")
+    ws = _lib.workspace(x.device, L.ltvqkv_gemm_workspace_bytes())
+    gs = grad_out.stride()
+    rc = L.ltvqkv_gemm_bwd(_lib.dtype_code(grad_out.dtype), xx.data_ptr(), w.data_ptr(), grad_out.data_ptr(),
+                           gs[0], gs[1], gs[2], gx.data_ptr(), grad_weight.data_ptr(),
+                           _lib.dtype_code(grad_weight.dtype), B, T, K, F, ws.data_ptr(), ws.numel(),
+                           _lib.stream_handle(x.device))
+    _lib.check(rc, "ltvqkv_gemm_bwd")
+    if gx is not grad_x:
+        grad_x.copy_(gx)
+
+
+def _flt_setup(ctx, inputs, output):
+    x, weight = inputs
+    ctx.save_for_backward(x, weight)
+
+
+def _flt_backward(ctx, grad_out):
+    x, weight = ctx.saved_tensors
+    if not x.is_contiguous() or not weight.is_contiguous() or not (
+            grad_out.is_contiguous() or _is_transposed_grad_out(grad_out)):
+        raise RuntimeError(
+            "fused_linear_transpose backward requires contiguous x and weight, and either contiguous or transposed "
+            f"grad_out. Found strides: x={x.stride()}, weight={weight.stride()}, grad_out={grad_out.stride()}")
+    # Every element of both gradients is written by the kernel.
+    grad_x = torch.empty_like(x, memory_format=torch.contiguous_format)
+    grad_weight = torch.empty_like(weight, memory_format=torch.contiguous_format)
+    torch.ops.nanochat_cuda.fused_linear_transpose_backward_kernel(x, weight, grad_out, grad_x, grad_weight)
+    return grad_x, grad_weight
+
+
+torch.library.register_autograd("nanochat_cuda::fused_linear_transpose_cuda_op", _flt_backward,
+                                setup_context=_flt_setup)
+
+
+@torch.library.register_fake("nanochat_cuda::fused_linear_transpose_cuda_op")
+def _flt_fake(x, weight):
+    B, T, _ = x.shape
+    return x.new_empty((B, weight.shape[0], T))
+
+
+@torch.library.register_fake("nanochat_cuda::fused_linear_transpose")
+def _flt_kernel_fake(x, weight, out):
+    return None
+
+
+@torch.library.register_fake("nanochat_cuda::fused_linear_transpose_backward_kernel")
+def _flt_bwd_fake(x, weight, grad_out, grad_x, grad_weight):
+    return None
+
+
+# ------------------------------------------------------------------------------------------
+# Decode step
+# ------------------------------------------------------------------------------------------
+@torch.library.impl("nanochat_cuda::ltv_decode_step", "CUDA")
+def _decode_step(x, weight, logit_bias, prev_q, prev_k, prev_v, init_param, NH, NKVH, da, r, use_sigmoid):
+    L = _lib.load()
+    if x.dim() == 3:
+        if x.shape[1] != 1:
+            raise RuntimeError("ltv_decode_step takes one token per sequence")
+        x = x.reshape(x.shape[0], x.shape[2])
+    x = x.contiguous()
+    B, C = x.shape
+    D = da * r
+    H = NH + 2 * NKVH
+    w = (weight if weight.dtype == x.dtype else weight.to(x.dtype)).contiguous()
+    if tuple(w.shape) != (H * (D + da), C):
+        raise RuntimeError(f"weight must be [{H * (D + da)}, {C}], got {tuple(w.shape)}")
+    logit_bias = logit_bias.contiguous()
+    init = (init_param if init_param.dtype == x.dtype else init_param.to(x.dtype)).contiguous()
+    kw = dict(device=x.device, dtype=x.dtype)
+    oq, ok, ov = torch.empty((B, NH, D), **kw), torch.empty((B, NKVH, D), **kw), torch.empty((B, NKVH, D), **kw)
+    S = _lib.strides
+    if prev_q is not None:
+        for p, n in ((prev_q, NH), (prev_k, NKVH), (prev_v, NKVH)):
+            if p is None or tuple(p.shape) != (B, n, D) or p.dtype != x.dtype:
+                raise RuntimeError("previous states must be [B, heads, D] in x's dtype")
+        pargs = [prev_q.data_ptr(), S(prev_q.stride()), prev_k.data_ptr(), S(prev_k.stride()),
+                 prev_v.data_ptr(), S(prev_v.stride())]
+    else:
+        pargs = [None, None, None, None, None, None]
+    rc = L.ltvqkv_decode_step(_lib.dtype_code(x.dtype), x.data_ptr(), w.data_ptr(), logit_bias.data_ptr(), *pargs,
+                              init.data_ptr(), oq.data_ptr(), S(oq.stride()), ok.data_ptr(), S(ok.stride()),
+                              ov.data_ptr(), S(ov.stride()), B, C, NH, NKVH, da, r, int(bool(use_sigmoid)),
+                              _lib.stream_handle(x.device))
+    _lib.check(rc, "ltvqkv_decode_step")
+    return oq, ok, ov
+
+
+@torch.library.register_fake("nanochat_cuda::ltv_decode_step")
+def _decode_step_fake(x, weight, logit_bias, prev_q, prev_k, prev_v, init_param, NH, NKVH, da, r, use_sigmoid):
+    B = x.shape[0]
+    D = da * r
+    return x.new_empty((B, NH, D)), x.new_empty((B, NKVH, D)), x.new_empty((B, NKVH, D))
+
+
+# ------------------------------------------------------------------------------------------
+# Functional wrappers (reference nanochat/ops/ltv_cuda_ops.py:256-299)
+# ------------------------------------------------------------------------------------------
+def fused_linear_transpose(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
+    """Returns weight @ x^T per batch, shaped (B, F, T), contiguous."""
+    return torch.ops.nanochat_cuda.fused_linear_transpose_cuda_op(x, weight)
+
+
+def ltv_cuda_fused_concat_head_major_register_cast_blelloch_scan(
+        combined: torch.Tensor, inits: torch.Tensor, logit_bias: torch.Tensor, NH: int, NKVH: int, da: int, r: int,
+        scan_threads_forward: int, r_threads_forward: int, r_items_forward: int, scan_threads_backward: int,
+        r_threads_backward: int, r_items_backward: int, use_sigmoid: bool):
+    return torch.ops.nanochat_cuda.ltv_fused_concat_head_major_register_cast_blelloch_scan_cuda_op(
+        combined, inits, logit_bias, NH, NKVH, da, r, scan_threads_forward, r_threads_forward, r_items_forward,
+        scan_threads_backward, r_threads_backward, r_items_backward, use_sigmoid)
+
+
+def ltv_decode_step(x: torch.Tensor, weight: torch.Tensor, logit_bias: torch.Tensor,
+                    prev_q: Optional[torch.Tensor], prev_k: Optional[torch.Tensor], prev_v: Optional[torch.Tensor],
+                    init_param: torch.Tensor, NH: int, NKVH: int, da: int, r: int, use_sigmoid: bool = True):
+    """One incremental filter step for x [B, C] (or [B, 1, C]); returns the new states."""
+    return torch.ops.nanochat_cuda.ltv_decode_step(x, weight, logit_bias, prev_q, prev_k, prev_v, init_param, NH,
+                                                    NKVH, da, r, use_sigmoid)

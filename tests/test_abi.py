@@ -1,0 +1,87 @@
+"""C-ABI checks that need no GPU: the library loads, exports every entry point include/ltvqkv.h
+declares, and validates arguments before touching the device."""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from conftest import ROOT
+from nanochat_filter_b200 import _lib
+
+HEADER = os.path.join(ROOT, "include", "ltvqkv.h")
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    return re.findall(r"LTVQKV_API\s+[\w\s\*]+?\b(ltvqkv_\w+)\s*\(", text)
+
+
+def test_header_declares_all_bound_symbols():
+    syms = declared_symbols()
+    assert len(syms) == len(set(syms))
+    assert set(syms) == set(_lib.EXPORTED_SYMBOLS)
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    for s in declared_symbols():
+        assert hasattr(lib, s), s
+        assert ctypes.cast(getattr(lib, s), ctypes.c_void_p).value
+
+
+def test_version_and_status_strings():
+    lib = _lib.load()
+    assert lib.ltvqkv_abi_version() == 1
+    for code, text in ((0, "ok"), (2, "shape"), (7, "timed out"), (8, "workspace")):
+        assert text in lib.ltvqkv_status_string(code).decode()
+    assert lib.ltvqkv_status_string(999).decode() == "unknown status"
+
+
+def test_workspace_sizes():
+    lib = _lib.load()
+    small = lib.ltvqkv_scan_workspace_bytes(1, 16, 1, 1, 1, 2)
+    big = lib.ltvqkv_scan_workspace_bytes(32, 1024, 6, 6, 1, 128)
+    assert 256 < small < big
+    assert lib.ltvqkv_scan_workspace_bytes(1, 16, 1, 1, 0, 2) == 0  # invalid shape
+    assert lib.ltvqkv_scan_workspace_bytes(1, 16, 1, 1, 1, 2048) == 0  # head dim beyond 1024
+    assert lib.ltvqkv_gemm_workspace_bytes() >= 256
+
+
+def test_argument_validation_without_device():
+    lib = _lib.load()
+    # bad dtype code
+    assert lib.ltvqkv_scan_fwd(7, None, 0, 0, 0, None, None, None, None, None, 1, 1, 1, 1, 1, 1, 1, None, 0,
+                               None) == 4
+    # empty batch / sequence: nothing to do
+    assert lib.ltvqkv_scan_fwd(1, None, 0, 0, 0, None, None, None, None, None, 0, 5, 1, 1, 1, 1, 1, None, 0,
+                               None) == 0
+    assert lib.ltvqkv_scan_fwd(1, None, 0, 0, 0, None, None, None, None, None, 3, 0, 1, 1, 1, 1, 1, None, 0,
+                               None) == 0
+    # missing data pointers
+    assert lib.ltvqkv_scan_fwd(1, None, 0, 0, 0, None, None, None, None, None, 1, 4, 1, 1, 1, 1, 1, None, 0,
+                               None) == 1
+    # workspace too small (checked before any launch)
+    fake = ctypes.c_void_p(0x10000)
+    assert lib.ltvqkv_scan_fwd(1, fake, 12, 1, 4, fake, fake, fake, fake, fake, 1, 4, 1, 1, 1, 1, 1, fake, 16,
+                               None) == 8
+    # negative / inconsistent shapes
+    assert lib.ltvqkv_gemm_fwd(1, None, None, None, -1, 4, 4, 4, None, 0, None) == 2
+    assert lib.ltvqkv_gemm_fwd(1, None, None, None, 0, 4, 4, 4, None, 0, None) == 0
+    assert lib.ltvqkv_gemm_bwd(1, None, None, None, 12, 1, 4, None, None, 0, 1, 4, 4, 3, None, 0, None) == 3
+    assert lib.ltvqkv_decode_step(1, None, None, None, None, None, None, None, None, None, None, None, None,
+                                  None, None, None, None, 0, 8, 1, 1, 1, 1, 1, None) == 0
+    assert lib.ltvqkv_decode_step(1, None, None, None, None, None, None, None, None, None, None, None, None,
+                                  None, None, None, None, 2, 8, 1, 1, 1, 1, 1, None) == 1
+
+
+def test_check_raises_runtime_error():
+    with pytest.raises(RuntimeError, match="ltvqkv_scan_fwd failed: invalid argument"):
+        _lib.check(1, "ltvqkv_scan_fwd")
+    with pytest.raises(TypeError):
+        import torch
+
+        _lib.dtype_code(torch.float16)

@@ -1,0 +1,97 @@
+"""Multi-rank gradient exchange on CPU (gloo, world size 2).
+
+Each rank holds one batch shard, computes the filtered-QKV gradients of its shard with the CPU
+oracle (standing in for the GPU kernels, which these CPU ranks cannot run), stores them as the
+parameters' .grad and calls the package's bucketed all_reduce. After the exchange every rank
+must hold the full-batch gradient average — the data-parallel contract of the training configs.
+"""
+
+from __future__ import annotations
+
+import os
+import socket
+
+import numpy as np
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from conftest import ROOT
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _problem(seed=0, B=4, T=16, NH=1, NKVH=1, D=8, r=4):
+    rng = np.random.default_rng(seed)
+    H, Da = NH + 2 * NKVH, D // r
+    C = NH * D
+    F = H * (D + Da)
+    x = rng.standard_normal((B, T, C)).astype(np.float32)
+    w = (rng.standard_normal((F, C)) / np.sqrt(C)).astype(np.float32)
+    init = (0.5 * rng.standard_normal((H, D))).astype(np.float32)
+    bias = rng.standard_normal((H, Da)).astype(np.float32)
+    gq = rng.standard_normal((B, NH, T, D)).astype(np.float32)
+    gk = rng.standard_normal((B, NKVH, T, D)).astype(np.float32)
+    gv = rng.standard_normal((B, NKVH, T, D)).astype(np.float32)
+    return dict(x=x, w=w, init=init, bias=bias, gq=gq, gk=gk, gv=gv, NH=NH, NKVH=NKVH, Da=Da, r=r)
+
+
+def _grads(p, sl):
+    import sys
+    sys.path.insert(0, ROOT)
+    from oracle import oracle as O
+
+    B = p["x"][sl].shape[0]
+    res = O.layer_fwd_bwd(p["x"][sl], p["w"], np.repeat(p["init"][None], B, 0), p["bias"], p["gq"][sl], p["gk"][sl],
+                          p["gv"][sl], p["NH"], p["NKVH"], p["Da"], p["r"], bf16=False)
+    # parameter gradients of the shard's mean loss contribution (scaled by the shard size)
+    return res["grad_w"], res["grad_logit_bias"], res["grad_inits"].sum(0)
+
+
+def _worker(rank, world, port, out_q):
+    import sys
+    sys.path.insert(0, ROOT)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from nanochat_filter_b200 import LtvCombinedHeadMajorQkvFilter
+        from nanochat_filter_b200.dist import sync_filter_grads
+
+        p = _problem()
+        B = p["x"].shape[0]
+        shard = slice(rank * B // world, (rank + 1) * B // world)
+        f = LtvCombinedHeadMajorQkvFilter(p["NH"], p["NKVH"], p["Da"] * p["r"], p["r"])
+        gw, gb, gi = _grads(p, shard)
+        f.c.weight.grad = torch.from_numpy(gw)
+        f.logit_bias.grad = torch.from_numpy(gb)
+        f.init_param.grad = torch.from_numpy(gi)
+        sync_filter_grads([f])
+        out_q.put((rank, f.c.weight.grad.numpy().copy(), f.logit_bias.grad.numpy().copy(),
+                   f.init_param.grad.numpy().copy()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_gradient_average_matches_full_batch():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for pr in procs:
+        pr.start()
+    results = [q.get(timeout=240) for _ in range(2)]
+    for pr in procs:
+        pr.join(timeout=60)
+        assert pr.exitcode == 0
+    p = _problem()
+    gw, gb, gi = _grads(p, slice(None))
+    for _, rw, rb, ri in results:
+        # the average over 2 equal shards is half the full-batch sum
+        np.testing.assert_allclose(rw, gw / 2, rtol=1e-5, atol=1e-6)
+        np.testing.assert_allclose(rb, gb / 2, rtol=1e-5, atol=1e-6)
+        np.testing.assert_allclose(ri, gi / 2, rtol=1e-5, atol=1e-6)

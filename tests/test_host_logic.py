@@ -1,0 +1,163 @@
+"""Host-side behaviour that needs no GPU: operator schemas and fake kernels (torch.compile
+tracing), module API and parameter layout, dtype policy, KV-cache state handling, and the
+absence of any CPU fallback."""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+import nanochat_filter_b200 as nf
+from nanochat_filter_b200 import filters, util
+
+OPS = torch.ops.nanochat_cuda
+
+
+def test_operator_schemas_match_reference_names():
+    names = {
+        "ltv_fused_concat_head_major_register_cast_blelloch_scan_cuda_op",
+        "ltv_fused_concat_head_major_register_cast_blelloch_scan_cuda_forward_kernel",
+        "ltv_fused_concat_head_major_register_cast_blelloch_scan_cuda_backward_kernel",
+        "fused_linear_transpose",
+        "fused_linear_transpose_cuda_op",
+        "fused_linear_transpose_backward_kernel",
+        "ltv_decode_step",
+    }
+    for n in names:
+        assert hasattr(OPS, n), n
+    schema = str(OPS.ltv_fused_concat_head_major_register_cast_blelloch_scan_cuda_op.default._schema)
+    assert "int scan_threads_forward" in schema and "bool use_sigmoid" in schema
+    schema = str(OPS.ltv_fused_concat_head_major_register_cast_blelloch_scan_cuda_backward_kernel.default._schema)
+    assert "Tensor(a!) grad_combined" in schema and "Tensor(c!) grad_logit_bias" in schema
+
+
+def test_fake_kernels_give_reference_shapes():
+    B, T, C, NH, NKVH, D, r = 3, 17, 256, 2, 1, 128, 64
+    Da = D // r
+    H = NH + 2 * NKVH
+    F = H * (D + Da)
+    x = torch.empty(B, T, C, device="meta")
+    w = torch.empty(F, C, device="meta")
+    out = OPS.fused_linear_transpose_cuda_op(x, w)
+    assert out.shape == (B, F, T)
+    comb = out.transpose(1, 2)
+    q, k, v = OPS.ltv_fused_concat_head_major_register_cast_blelloch_scan_cuda_op(
+        comb, torch.empty(B, H, D, device="meta"), torch.empty(H, Da, device="meta"), NH, NKVH, Da, r, 8, 8, 4,
+        32, 2, 8, True)
+    assert q.shape == (B, NH, T, D) and k.shape == (B, NKVH, T, D) and v.shape == (B, NKVH, T, D)
+    sq, sk, sv = OPS.ltv_decode_step(torch.empty(B, C, device="meta"), w, torch.empty(H, Da, device="meta"), None,
+                                     None, None, torch.empty(H, D, device="meta"), NH, NKVH, Da, r, True)
+    assert sq.shape == (B, NH, D) and sk.shape == (B, NKVH, D)
+
+
+def test_filter_on_meta_device_traces_shapes():
+    f = nf.LtvCudaFusedConcatHeadMajorRegisterCastBlellochScanQkvFilter(6, 6, 128, 128).to("meta")
+    x = torch.empty(2, 64, 768, device="meta")
+    q, k, v = f(x, nf.LtvInitValues())
+    assert q.shape == (2, 64, 6, 128) and k.shape == (2, 64, 6, 128) and v.shape == (2, 64, 6, 128)
+
+
+def test_no_cpu_fallback():
+    x = torch.randn(1, 8, 16)
+    w = torch.randn(24, 16)
+    with pytest.raises(NotImplementedError):
+        OPS.fused_linear_transpose_cuda_op(x, w)
+    comb = torch.randn(1, 8, 3 * 3)
+    with pytest.raises(NotImplementedError):
+        OPS.ltv_fused_concat_head_major_register_cast_blelloch_scan_cuda_op(
+            comb, torch.randn(1, 3, 2), torch.randn(3, 1), 1, 1, 1, 2, 8, 8, 4, 32, 2, 8, True)
+
+
+def test_parameters_and_head_major_init_layout():
+    NH, NKVH, D, r = 2, 1, 8, 4
+    f = nf.LtvCudaFusedConcatHeadMajorRegisterCastBlellochScanQkvFilter(NH, NKVH, D, r)
+    H, Da, C = NH + 2 * NKVH, D // r, NH * D
+    assert f.c.weight.shape == (H * (D + Da), C)
+    assert f.logit_bias.shape == (H, Da) and f.init_param.shape == (H, D)
+    torch.manual_seed(0)
+    f.init_weights(alpha_mlp_bias_init=2.0, weight_s=0.1, bias_s=0.25, init_s=0.3)
+    assert f.logit_bias.min() >= 1.75 and f.logit_bias.max() <= 2.25
+    assert f.init_param.abs().max() <= 0.3
+    # rows: [head h values (D) | head h logits (Da)] for h = 0..H-1
+    torch.manual_seed(0)
+    vals = torch.empty(H * D, C).uniform_(-0.1, 0.1)
+    logits = torch.empty(H * Da, C).uniform_(-0.1, 0.1)
+    w = f.c.weight.detach().view(H, D + Da, C)
+    torch.testing.assert_close(w[:, :D].reshape(H * D, C), vals)
+    torch.testing.assert_close(w[:, D:].reshape(H * Da, C), logits)
+    mats, lins = f.get_matrix_linear_params()
+    assert mats == [f.c.weight] and lins == [f.logit_bias, f.init_param]
+    assert f.ltv_parameter_count() == H * Da * C + H * Da + H * D
+    assert f.estimate_flops(1024) == 6 * H * Da * C + 7 * H * D
+
+
+def test_dtype_policy_and_inits_resolution():
+    assert util.should_run_ltv_in_fp32("cpu") is False
+    with torch.autocast("cpu", dtype=torch.bfloat16):
+        assert util.should_run_ltv_in_fp32("cpu") is False
+    p = torch.randn(3, 4)
+    e = util.resolve_inits_original_dtype(2, p, util.LtvInitValues())
+    assert e.shape == (2, 3, 4) and torch.equal(e[1], p)
+    q, k, v = torch.randn(2, 1, 4), torch.randn(2, 1, 4), torch.randn(2, 1, 4)
+    e = util.resolve_inits_original_dtype(2, p, util.LtvInitValues(q, k, v))
+    assert torch.equal(e, torch.cat([q, k, v], 1))
+    assert util.env_int("LTVQKV_SURELY_UNSET_VARIABLE", 5) == 5
+
+
+def test_kv_cache_last_qkv_semantics():
+    cache = nf.KVCache(batch_size=2, num_q_heads=2, num_kv_heads=1, seq_len=16, head_dim=4, num_layers=2)
+    assert not cache.has_last_qkv(0)
+    q, k, v = torch.randn(2, 2, 4), torch.randn(2, 1, 4), torch.randn(2, 1, 4)
+    cache.update_last_qkv(0, q, k, v)
+    assert cache.has_last_qkv(0) and not cache.has_last_qkv(1)
+    cache.update_last_qkv(1, q + 1, k + 1, v + 1)
+    assert cache.has_last_qkv(1)
+    assert torch.equal(cache.last_qkv.q.special[1], q + 1)
+    # a later step overwrites layer 0 again
+    cache.update_last_qkv(0, q * 2, k * 2, v * 2)
+    assert torch.equal(cache.last_qkv.k.special[0], k * 2)
+    # prefill broadcasts a batch-1 state over the batch
+    one = nf.KVCache(batch_size=1, num_q_heads=2, num_kv_heads=1, seq_len=16, head_dim=4, num_layers=2)
+    one.update_last_qkv(0, q[:1], k[:1], v[:1])
+    one.update_last_qkv(1, q[1:], k[1:], v[1:])
+    one.pos = 7
+    many = nf.KVCache(batch_size=3, num_q_heads=2, num_kv_heads=1, seq_len=16, head_dim=4, num_layers=2)
+    many.prefill(one)
+    assert many.pos == 7 and many.has_last_qkv(1)
+    assert torch.equal(many.last_qkv.q.special[0], q[:1].expand(3, 2, 4))
+
+
+class _FakeFilter(torch.nn.Module):
+    def __init__(self):
+        super().__init__()
+        self.calls = []
+
+    def forward(self, x, previous_values):
+        # previous_values are views of the cache state (as in the reference), so record copies
+        self.calls.append(nf.LtvInitValues(*(None if t is None else t.clone() for t in (
+            previous_values.q, previous_values.k, previous_values.v))))
+        B, T, _ = x.shape
+        return (torch.full((B, T, 2, 4), float(T)), torch.full((B, T, 1, 4), 1.0), torch.full((B, T, 1, 4), 2.0))
+
+
+def test_computer_module_threads_cache_state():
+    filt = _FakeFilter()
+    mod = nf.LtvCombinedQkvComputerModule(0, filt)
+    cache = nf.KVCache(batch_size=2, num_q_heads=2, num_kv_heads=1, seq_len=16, head_dim=4, num_layers=1)
+    mod(torch.zeros(2, 5, 8), cache)
+    assert filt.calls[-1].q is None
+    mod(torch.zeros(2, 1, 8), cache)
+    assert filt.calls[-1].q is not None and torch.equal(filt.calls[-1].q, torch.full((2, 2, 4), 5.0))
+    assert torch.equal(cache.last_qkv.q.special[0], torch.full((2, 2, 4), 1.0))
+    mod(torch.zeros(2, 3, 8), None)
+    assert filt.calls[-1].q is None
+
+
+def test_filter_parameter_discovery():
+    from nanochat_filter_b200.dist import filter_parameters
+
+    m = torch.nn.ModuleList([nf.LtvCombinedQkvComputerModule(i, filters.LtvCombinedHeadMajorQkvFilter(2, 1, 8, 4))
+                             for i in range(2)])
+    ps = filter_parameters([m])
+    assert len(ps) == 6
+    assert ps[0] is m[0].ltv_filter.c.weight
