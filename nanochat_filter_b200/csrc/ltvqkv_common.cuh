@@ -89,6 +89,14 @@ template <> struct Elem<__nv_bfloat16> {
 // 1 / (1 + expf(-x)) in fp32, cpp_ewma/src/ltv_fused_concat_head_major_register_cast_scan_cuda_common.cuh:114-117).
 LTVQKV_DEVICE float sigmoid_f32(float x) { return 1.0f / (1.0f + expf(-x)); }
 
+// Logistic function for the fp32 exact-order path: exp evaluated in double and rounded to float
+// (within half an ulp of the float result of the host's correctly-rounding expf in all but
+// rare boundary cases), then the add and the divide each rounded once.
+LTVQKV_DEVICE float sigmoid_f32_exact(float x) {
+  const float e = (float)exp(-(double)x);
+  return __fdiv_rn(1.0f, __fadd_rn(1.0f, e));
+}
+
 // ------------------------------------------------------------------------------------------
 // Release/acquire flag helpers (gpu scope)
 // ------------------------------------------------------------------------------------------

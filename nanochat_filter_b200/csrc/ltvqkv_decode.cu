@@ -35,13 +35,19 @@ LTVQKV_DEVICE void dec_split_head(int h, int NH, int NKVH, int& which, int& hloc
   else { which = 2; hloc = h - NH - NKVH; }
 }
 
+// Dot product of two rows, accumulated in fp32 for bf16 storage and in double for fp32 storage
+// (the oracle's definition of the fp32 projection).
+template <typename T> struct DecAcc { using type = float; };
+template <> struct DecAcc<float> { using type = double; };
+
 template <typename T>
 LTVQKV_DEVICE float dot_row(const T* __restrict__ a, const T* __restrict__ b, int C, int lane) {
-  float acc = 0.f;
-  for (int k = lane; k < C; k += 32) acc = fmaf(Elem<T>::load(a + k), Elem<T>::load(b + k), acc);
+  using Acc = typename DecAcc<T>::type;
+  Acc acc = 0;
+  for (int k = lane; k < C; k += 32) acc += (Acc)Elem<T>::load(a + k) * (Acc)Elem<T>::load(b + k);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-  return acc;
+  return (float)acc;
 }
 
 template <typename T>
@@ -74,8 +80,9 @@ __global__ void __launch_bounds__(kDecThreads) decode_step_kernel(DecodeArgs a) 
       const int cc = i / nb, bb = i - (i / nb) * nb;
       const int c = c0 + cc, b = b0 + bb;
       const int g = c / a.r;
-      float l = res[nv + (g - g0)][bb] + a.logit_bias[h * a.Da + g];
-      float al = a.use_sigmoid ? sigmoid_f32(l) : l;
+      float l = __fadd_rn(res[nv + (g - g0)][bb], a.logit_bias[h * a.Da + g]);
+      float al = l;
+      if (a.use_sigmoid) al = sizeof(T) == 4 ? sigmoid_f32_exact(l) : sigmoid_f32(l);
       float hp;
       if (a.prev[0] != nullptr) {
         const long long* ps = a.ps[which];
@@ -83,7 +90,8 @@ __global__ void __launch_bounds__(kDecThreads) decode_step_kernel(DecodeArgs a) 
       } else {
         hp = Elem<T>::load(reinterpret_cast<const T*>(a.init_param) + (long long)h * a.D + c);
       }
-      float hn = (1.0f - al) * hp + al * res[cc][bb];
+      // separately rounded products and sum, the reference's fp32 update order
+      float hn = __fadd_rn(__fmul_rn(__fsub_rn(1.0f, al), hp), __fmul_rn(al, res[cc][bb]));
       const long long* os = a.os[which];
       Elem<T>::store(reinterpret_cast<T*>(a.out[which]) + b * os[0] + hloc * os[1] + c * os[2], hn);
     }

@@ -329,10 +329,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 }
 
 // ------------------------------------------------------------------------------------------
-// CUDA-core GEMM for fp32 (true fp32 products, fp32 accumulation) and for bf16 shapes the
-// TMA path cannot address (row pitches not a multiple of 16 bytes).
+// CUDA-core GEMM for fp32 and for bf16 shapes the TMA path cannot address (row pitches not a
+// multiple of 16 bytes).
 //   C[ob][m][n] = sum_rb sum_k A[ob,rb][m][k] * B[ob,rb][n][k]
+// fp32 inputs accumulate in double (a product of two floats is exact in double), so the fp32
+// result is the correctly rounded sum up to double rounding — the oracle's definition; bf16
+// inputs accumulate in fp32 like the tensor-core path.
 // ------------------------------------------------------------------------------------------
+template <typename Tin> struct AccOf { using type = float; };
+template <> struct AccOf<float> { using type = double; };
+
 struct SimtArgs {
   const void* A;
   const void* B;
@@ -351,7 +357,8 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(SimtArgs a) {
   const int ob = blockIdx.z;
   const int m0 = blockIdx.y * TM, n0 = blockIdx.x * TN;
   const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
-  float acc[4][4] = {};
+  using Acc = typename AccOf<Tin>::type;
+  Acc acc[4][4] = {};
   const Tin* Ab = reinterpret_cast<const Tin*>(a.A) + ob * a.a_ob;
   const Tin* Bb = reinterpret_cast<const Tin*>(a.B) + ob * a.b_ob;
   for (int rb = 0; rb < a.red_batches; ++rb) {
@@ -381,7 +388,7 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(SimtArgs a) {
 #pragma unroll
         for (int i = 0; i < 4; ++i)
 #pragma unroll
-          for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+          for (int j = 0; j < 4; ++j) acc[i][j] = (Acc)av[i] * (Acc)bv[j] + acc[i][j];
       }
       __syncthreads();
     }
@@ -392,7 +399,7 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(SimtArgs a) {
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       int m = m0 + ty * 4 + i, n = n0 + tx * 4 + j;
-      if (m < a.M && n < a.N) Elem<Tout>::store(Cb + m * a.c_m + n * a.c_n, acc[i][j]);
+      if (m < a.M && n < a.N) Elem<Tout>::store(Cb + m * a.c_m + n * a.c_n, (float)acc[i][j]);
     }
 }
 

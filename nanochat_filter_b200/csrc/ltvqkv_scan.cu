@@ -501,6 +501,112 @@ __global__ void __launch_bounds__(1024) scan_bwd_kernel(ScanBwdArgs args) {
   if (tid == 0) finish_launch(args.ws, gridDim.x);
 }
 
+// ------------------------------------------------------------------------------------------
+// fp32 exact-order path. One CTA per (batch, head), one thread per channel, sequential in t,
+// with every multiply and add separately rounded (no FMA contraction): the operation order of
+// the reference's sequential oracle (ltv_reference_ops.py:103-122 and the autograd backward of
+// QuantizedStateUpdate, :20-34), so fp32 results match it to the last bit up to the library
+// expf. Used for dtype fp32, where the tolerance is 1e-5; bf16 takes the chunked kernels.
+// ------------------------------------------------------------------------------------------
+struct ExactArgs {
+  const float* combined;
+  long long sc_b, sc_t, sc_e;
+  const float* inits;
+  const float* logit_bias;
+  float* out[3];
+  const float* h[3];
+  long long hs[3][4];
+  const float* gh[3];
+  long long gs[3][4];
+  float* grad_combined;
+  long long gc_b, gc_t, gc_e;
+  float* grad_inits;
+  float* bias_part;  // [B][H][Da]
+  int B, T, NH, NKVH, Da, r, D, H, use_sigmoid;
+};
+
+LTVQKV_DEVICE float exact_alpha(const ExactArgs& a, const float* cb, int t, int head_col, int h, int g) {
+  float raw = __fadd_rn(cb[(long long)t * a.sc_t + (long long)(head_col + a.D + g) * a.sc_e], a.logit_bias[h * a.Da + g]);
+  return a.use_sigmoid ? sigmoid_f32_exact(raw) : raw;
+}
+
+__global__ void __launch_bounds__(1024) scan_fwd_exact_kernel(ExactArgs a) {
+  const int bh = blockIdx.x;
+  const int b = bh / a.H, h = bh % a.H;
+  const int c = threadIdx.x;
+  if (c >= a.D) return;
+  int which, hloc, nheads;
+  split_head(h, a.NH, a.NKVH, which, hloc, nheads);
+  const float* cb = a.combined + (long long)b * a.sc_b;
+  const int head_col = h * (a.D + a.Da);
+  const int g = c / a.r;
+  float st = a.inits[((long long)b * a.H + h) * a.D + c];
+  float* out = a.out[which] + ((long long)b * nheads + hloc) * (long long)a.T * a.D + c;
+  for (int t = 0; t < a.T; ++t) {
+    const float al = exact_alpha(a, cb, t, head_col, h, g);
+    const float u = cb[(long long)t * a.sc_t + (long long)(head_col + c) * a.sc_e];
+    const float t1 = __fmul_rn(__fsub_rn(1.0f, al), st);
+    const float t2 = __fmul_rn(al, u);
+    st = __fadd_rn(t1, t2);
+    out[(long long)t * a.D] = st;
+  }
+}
+
+__global__ void __launch_bounds__(1024) scan_bwd_exact_kernel(ExactArgs a) {
+  extern __shared__ float red[];  // [D] per-channel terms of the group sums
+  const int bh = blockIdx.x;
+  const int b = bh / a.H, h = bh % a.H;
+  const int c = threadIdx.x;
+  const bool active = c < a.D;
+  int which, hloc, nheads;
+  split_head(h, a.NH, a.NKVH, which, hloc, nheads);
+  const float* cb = a.combined + (long long)b * a.sc_b;
+  float* gcb = a.grad_combined + (long long)b * a.gc_b;
+  const int head_col = h * (a.D + a.Da);
+  const int g = active ? c / a.r : 0;
+  const long long* hs = a.hs[which];
+  const long long* gs = a.gs[which];
+  const float* hp = a.h[which] + (long long)b * hs[0] + (long long)hloc * hs[1] + (long long)c * hs[3];
+  const float* gp = a.gh[which] + (long long)b * gs[0] + (long long)hloc * gs[1] + (long long)c * gs[3];
+  const float init = active ? a.inits[((long long)b * a.H + h) * a.D + c] : 0.f;
+  float gacc = 0.f;
+  float bias_acc = 0.f;  // threads c < Da accumulate their group's bias gradient
+  for (int t = a.T - 1; t >= 0; --t) {
+    float al = 0.f, term = 0.f;
+    if (active) {
+      gacc = __fadd_rn(gacc, gp[(long long)t * gs[2]]);
+      al = exact_alpha(a, cb, t, head_col, h, g);
+      const float u = cb[(long long)t * a.sc_t + (long long)(head_col + c) * a.sc_e];
+      const float sprev = t > 0 ? hp[(long long)(t - 1) * hs[2]] : init;
+      gcb[(long long)t * a.gc_t + (long long)(head_col + c) * a.gc_e] = __fmul_rn(gacc, al);
+      term = __fmul_rn(gacc, __fsub_rn(u, sprev));
+      red[c] = term;
+    }
+    __syncthreads();
+    if (c < a.Da) {
+      float ga = 0.f;
+      for (int k = 0; k < a.r; ++k) ga = __fadd_rn(ga, red[c * a.r + k]);
+      const float ag = exact_alpha(a, cb, t, head_col, h, c);
+      const float graw = a.use_sigmoid ? __fmul_rn(__fmul_rn(ga, __fsub_rn(1.0f, ag)), ag) : ga;
+      gcb[(long long)t * a.gc_t + (long long)(head_col + a.D + c) * a.gc_e] = graw;
+      bias_acc = __fadd_rn(bias_acc, graw);
+    }
+    __syncthreads();
+    if (active) gacc = __fmul_rn(gacc, __fsub_rn(1.0f, al));
+  }
+  if (active) a.grad_inits[((long long)b * a.H + h) * a.D + c] = gacc;
+  if (c < a.Da) a.bias_part[((long long)b * a.H + h) * a.Da + c] = bias_acc;
+}
+
+// grad_logit_bias[h, g] += sum over b (descending, the oracle's order) of per-(b, h) partials.
+__global__ void bias_reduce_exact_kernel(const float* part, float* grad_bias, int B, int H, int Da) {
+  int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= H * Da) return;
+  float sum = 0.f;
+  for (int b = B - 1; b >= 0; --b) sum = __fadd_rn(sum, part[(long long)b * H * Da + idx]);
+  grad_bias[idx] = __fadd_rn(grad_bias[idx], sum);
+}
+
 // grad_logit_bias[h, g] += sum over (b, chunk) of the per-tile partials, in a fixed order.
 __global__ void bias_reduce_kernel(const float* part, float* grad_bias, int B, int nchunks, int H, int Da) {
   int idx = blockIdx.x * blockDim.x + threadIdx.x;
@@ -568,9 +674,20 @@ extern "C" int ltvqkv_scan_fwd(int dtype, const void* combined, int64_t sc_b, in
   a.aggA = reinterpret_cast<float*>(ws + wl.aggA);
   a.aggX = reinterpret_cast<float*>(ws + wl.aggX);
   a.inclX = reinterpret_cast<float*>(ws + wl.inclX);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (dtype == LTVQKV_DTYPE_F32) {
+    ExactArgs e = {};
+    e.combined = reinterpret_cast<const float*>(combined); e.sc_b = sc_b; e.sc_t = sc_t; e.sc_e = sc_e;
+    e.inits = reinterpret_cast<const float*>(inits); e.logit_bias = logit_bias;
+    e.out[0] = reinterpret_cast<float*>(out_q); e.out[1] = reinterpret_cast<float*>(out_k);
+    e.out[2] = reinterpret_cast<float*>(out_v);
+    e.B = B; e.T = T; e.NH = NH; e.NKVH = NKVH; e.Da = Da; e.r = r; e.D = g.D; e.H = g.H; e.use_sigmoid = use_sigmoid;
+    int threads = (g.D + 31) / 32 * 32;
+    scan_fwd_exact_kernel<<<(unsigned int)(B * g.H), threads, 0, s>>>(e);
+    return ltvqkv_host::check_launch();
+  }
   size_t smem = fwd_smem_bytes(g);
   unsigned int grid = (unsigned int)((long long)B * g.H * g.nchunks);
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (dtype == LTVQKV_DTYPE_BF16) {
     cudaFuncSetAttribute(scan_fwd_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     scan_fwd_kernel<__nv_bfloat16><<<grid, g.nthreads, smem, s>>>(a);
@@ -633,6 +750,28 @@ extern "C" int ltvqkv_scan_bwd(int dtype, const void* combined, int64_t sc_b, in
   a.aggX = reinterpret_cast<float*>(ws + wl.aggX);
   a.inclX = reinterpret_cast<float*>(ws + wl.inclX);
   a.bias_part = reinterpret_cast<float*>(ws + wl.bias_part);
+  if (dtype == LTVQKV_DTYPE_F32) {
+    ExactArgs e = {};
+    e.combined = reinterpret_cast<const float*>(combined); e.sc_b = sc_b; e.sc_t = sc_t; e.sc_e = sc_e;
+    e.inits = reinterpret_cast<const float*>(inits); e.logit_bias = logit_bias;
+    const void* hh[3] = {hq, hk, hv};
+    const void* gg[3] = {grad_hq, grad_hk, grad_hv};
+    for (int i = 0; i < 3; ++i) {
+      e.h[i] = reinterpret_cast<const float*>(hh[i]);
+      e.gh[i] = reinterpret_cast<const float*>(gg[i]);
+      for (int k = 0; k < 4; ++k) { e.hs[i][k] = a.hs[i][k]; e.gs[i][k] = a.gs[i][k]; }
+    }
+    e.grad_combined = reinterpret_cast<float*>(grad_combined); e.gc_b = gc_b; e.gc_t = gc_t; e.gc_e = gc_e;
+    e.grad_inits = reinterpret_cast<float*>(grad_inits);
+    e.bias_part = a.bias_part;
+    e.B = B; e.T = T; e.NH = NH; e.NKVH = NKVH; e.Da = Da; e.r = r; e.D = D; e.H = H; e.use_sigmoid = use_sigmoid;
+    int threads = (D + 31) / 32 * 32;
+    scan_bwd_exact_kernel<<<(unsigned int)(B * H), threads, sizeof(float) * threads, s>>>(e);
+    int rc = ltvqkv_host::check_launch();
+    if (rc != LTVQKV_OK) return rc;
+    bias_reduce_exact_kernel<<<(H * Da + 127) / 128, 128, 0, s>>>(a.bias_part, grad_logit_bias, B, H, Da);
+    return ltvqkv_host::check_launch();
+  }
   size_t smem = bwd_smem_bytes(g);
   unsigned int grid = (unsigned int)((long long)B * g.H * g.nchunks);
   if (dtype == LTVQKV_DTYPE_BF16) {

@@ -100,7 +100,6 @@ def _check_scan_inputs(combined, inits, logit_bias, NH, NKVH, da, r):
         raise RuntimeError(f"logit_bias must be float32, got {logit_bias.dtype}")
 
 
-@torch.library.impl(f"nanochat_cuda::{_SCAN_FWD}", "CUDA")
 def _scan_forward_kernel(combined, inits, logit_bias, out_q, out_k, out_v, T, NH, NKVH, da, r,
                          scan_threads_forward, r_threads_forward, r_items_forward, use_sigmoid):
     _check_scan_inputs(combined, inits, logit_bias, NH, NKVH, da, r)
@@ -121,7 +120,6 @@ def _scan_forward_kernel(combined, inits, logit_bias, out_q, out_k, out_v, T, NH
     _lib.check(rc, "ltvqkv_scan_fwd")
 
 
-@torch.library.impl(f"nanochat_cuda::{_SCAN_OP}", "CUDA")
 def _scan_op(combined, inits, logit_bias, NH, NKVH, da, r, scan_threads_forward, r_threads_forward,
              r_items_forward, scan_threads_backward, r_threads_backward, r_items_backward, use_sigmoid):
     B, T, _ = combined.shape
@@ -135,7 +133,6 @@ def _scan_op(combined, inits, logit_bias, NH, NKVH, da, r, scan_threads_forward,
     return out_q, out_k, out_v
 
 
-@torch.library.impl(f"nanochat_cuda::{_SCAN_BWD}", "CUDA")
 def _scan_backward_kernel(combined, inits, logit_bias, hq, hk, hv, grad_hq, grad_hk, grad_hv, grad_combined,
                           grad_inits, grad_logit_bias, NH, NKVH, da, r, scan_threads_backward, r_threads_backward,
                           r_items_backward, use_sigmoid):
@@ -218,7 +215,6 @@ def _is_transposed_grad_out(g: torch.Tensor) -> bool:
     return g.stride(1) == 1 and g.stride(2) == g.size(1) and g.stride(0) == g.size(1) * g.size(2)
 
 
-@torch.library.impl("nanochat_cuda::fused_linear_transpose", "CUDA")
 def _fused_linear_transpose(x, weight, out):
     if not x.is_contiguous() or not weight.is_contiguous() or not out.is_contiguous():
         raise RuntimeError("fused_linear_transpose requires contiguous x, weight, and out tensors")
@@ -236,7 +232,6 @@ def _fused_linear_transpose(x, weight, out):
     _lib.check(rc, "ltvqkv_gemm_fwd")
 
 
-@torch.library.impl("nanochat_cuda::fused_linear_transpose_cuda_op", "CUDA")
 def _fused_linear_transpose_op(x, weight):
     B, T, _ = x.shape
     F = weight.size(0)
@@ -246,7 +241,6 @@ def _fused_linear_transpose_op(x, weight):
     return out
 
 
-@torch.library.impl("nanochat_cuda::fused_linear_transpose_backward_kernel", "CUDA")
 def _fused_linear_transpose_backward_kernel(x, weight, grad_out, grad_x, grad_weight):
     if not x.is_contiguous() or not weight.is_contiguous() or not (
             grad_out.is_contiguous() or _is_transposed_grad_out(grad_out)):
@@ -316,7 +310,6 @@ def _flt_bwd_fake(x, weight, grad_out, grad_x, grad_weight):
 # ------------------------------------------------------------------------------------------
 # Decode step
 # ------------------------------------------------------------------------------------------
-@torch.library.impl("nanochat_cuda::ltv_decode_step", "CUDA")
 def _decode_step(x, weight, logit_bias, prev_q, prev_k, prev_v, init_param, NH, NKVH, da, r, use_sigmoid):
     L = _lib.load()
     if x.dim() == 3:
@@ -356,6 +349,18 @@ def _decode_step_fake(x, weight, logit_bias, prev_q, prev_k, prev_v, init_param,
     B = x.shape[0]
     D = da * r
     return x.new_empty((B, NH, D)), x.new_empty((B, NKVH, D)), x.new_empty((B, NKVH, D))
+
+
+# ------------------------------------------------------------------------------------------
+# Registration (explicit calls: the decorator form does not hand the function back)
+# ------------------------------------------------------------------------------------------
+torch.library.impl(f"nanochat_cuda::{_SCAN_FWD}", "CUDA", _scan_forward_kernel)
+torch.library.impl(f"nanochat_cuda::{_SCAN_OP}", "CUDA", _scan_op)
+torch.library.impl(f"nanochat_cuda::{_SCAN_BWD}", "CUDA", _scan_backward_kernel)
+torch.library.impl("nanochat_cuda::fused_linear_transpose", "CUDA", _fused_linear_transpose)
+torch.library.impl("nanochat_cuda::fused_linear_transpose_cuda_op", "CUDA", _fused_linear_transpose_op)
+torch.library.impl("nanochat_cuda::fused_linear_transpose_backward_kernel", "CUDA", _fused_linear_transpose_backward_kernel)
+torch.library.impl("nanochat_cuda::ltv_decode_step", "CUDA", _decode_step)
 
 
 # ------------------------------------------------------------------------------------------

@@ -65,15 +65,21 @@ def test_filter_forward_backward_vs_oracle(cuda_device, dtype):
     ref = O.layer_fwd_bwd(_np(x), _np(f.c.weight), inits, _np(f.logit_bias),
                           _np(gq.transpose(1, 2)), _np(gk.transpose(1, 2)), _np(gv.transpose(1, 2)),
                           NH, NKVH, D // r, r, bf16=bf16)
+    # fp32: elementwise relative error (floor 1% of the tensor's max) <= 1e-5.
+    # bf16: the layer rounds three times in sequence (projection buffer, scan output, gradient
+    # buffer) and a one-ulp flip at any of them moves its dependents, so the composed layer is
+    # compared norm-wise: max|a - e| <= 2e-2 * max|e|. Each stage alone is held to the
+    # elementwise bound in test_gpu_scan.py / test_gpu_gemm.py.
     tol = 2e-2 if bf16 else 1e-5
+    floor = 1.0 if bf16 else FLOOR
     errs = {
-        "q": max_rel_err(_np(q.transpose(1, 2)), ref["hq"], FLOOR),
-        "k": max_rel_err(_np(k.transpose(1, 2)), ref["hk"], FLOOR),
-        "v": max_rel_err(_np(v.transpose(1, 2)), ref["hv"], FLOOR),
-        "dx": max_rel_err(_np(x.grad), ref["grad_x"], FLOOR),
-        "dW": max_rel_err(_np(f.c.weight.grad), ref["grad_w"], FLOOR),
-        "dbias": max_rel_err(_np(f.logit_bias.grad), ref["grad_logit_bias"], FLOOR),
-        "dinit": max_rel_err(_np(f.init_param.grad), ref["grad_inits"].sum(0), FLOOR),
+        "q": max_rel_err(_np(q.transpose(1, 2)), ref["hq"], floor),
+        "k": max_rel_err(_np(k.transpose(1, 2)), ref["hk"], floor),
+        "v": max_rel_err(_np(v.transpose(1, 2)), ref["hv"], floor),
+        "dx": max_rel_err(_np(x.grad), ref["grad_x"], floor),
+        "dW": max_rel_err(_np(f.c.weight.grad), ref["grad_w"], floor),
+        "dbias": max_rel_err(_np(f.logit_bias.grad), ref["grad_logit_bias"], floor),
+        "dinit": max_rel_err(_np(f.init_param.grad), ref["grad_inits"].sum(0), floor),
     }
     bad = {k2: e for k2, e in errs.items() if e > tol}
     assert not bad, f"above {tol}: {bad} (all {errs})"
@@ -101,17 +107,18 @@ def test_decode_token_by_token_equals_batch_forward(cuda_device, dtype):
         qf, kf, vf = mod(x, None)
         cache = KVCache(B, NH, NKVH, T, D, num_layers=1)
         qs, ks, vs = [], [], []
-        q0, k0, v0 = mod(x[:, :prompt], cache)
+        q0, k0, v0 = mod(x[:, :prompt].contiguous(), cache)
         qs.append(q0); ks.append(k0); vs.append(v0)
         for t in range(prompt, T):
-            q1, k1, v1 = mod(x[:, t:t + 1], cache)
+            q1, k1, v1 = mod(x[:, t:t + 1].contiguous(), cache)
             qs.append(q1); ks.append(k1); vs.append(v1)
     qd, kd, vd = torch.cat(qs, 1), torch.cat(ks, 1), torch.cat(vs, 1)
-    # fp32: identical arithmetic up to GEMM summation order. bf16: the cache holds the rounded
-    # state (as the reference's does), the batch scan carries fp32 — a few bf16 ulps over 7 steps.
-    tol = 1e-5 if dtype == torch.float32 else 3e-2
+    # fp32: the same arithmetic (elementwise, floor 1% of max). bf16: the cache holds the rounded
+    # state (as the reference's does) while the batch scan carries fp32, so each decode step
+    # restarts from a value one rounding away; compared norm-wise.
+    tol, floor = (1e-5, FLOOR) if dtype == torch.float32 else (3e-2, 1.0)
     for a, e in ((qd, qf), (kd, kf), (vd, vf)):
-        assert max_rel_err(_np(a), _np(e), FLOOR) <= tol
+        assert max_rel_err(_np(a), _np(e), floor) <= tol
     # the cache holds the last step
     torch.testing.assert_close(cache.last_qkv.q.special[0], qd[:, -1], rtol=0, atol=0)
 

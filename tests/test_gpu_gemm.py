@@ -47,7 +47,7 @@ def test_gemm_golden(cuda_device, key):
 
 
 def _reference(x, w, g):
-    xf, wf, gf = x.float(), w.float(), g.float()
+    xf, wf, gf = x.detach().float(), w.detach().float(), g.detach().float()
     out = torch.matmul(wf, xf.transpose(1, 2))                 # [B, F, T]
     gx = torch.matmul(gf.transpose(1, 2), wf)                  # [B, T, K]
     gw = torch.einsum("bft,btk->fk", gf, xf)                   # [F, K]
@@ -86,10 +86,11 @@ def test_gemm_fp32_master_weight_grad(cuda_device):
     out.backward(g)
     assert w.grad.dtype == torch.float32
     eo, egx, egw = _reference(x, w.detach().to(torch.bfloat16), g)
-    assert max_rel_err(out.float().cpu().numpy(), eo.cpu().numpy()) <= 2e-2
+    assert max_rel_err(out.detach().float().cpu().numpy(), eo.cpu().numpy()) <= 2e-2
     assert max_rel_err(x.grad.float().cpu().numpy(), egx.cpu().numpy()) <= 2e-2
-    # fp32 accumulation over 4096 tokens, written in fp32
-    assert max_rel_err(w.grad.cpu().numpy(), egw.cpu().numpy()) <= 1e-4
+    # fp32 (tensor-core) accumulation over 4096 tokens, written in fp32: norm-wise bound, since
+    # entries that cancel to near zero carry the accumulation noise of the whole sum
+    assert max_rel_err(w.grad.cpu().numpy(), egw.cpu().numpy(), 1.0) <= 1e-5
 
 
 def test_gemm_fp32_config1(cuda_device):
