@@ -15,10 +15,11 @@
 // the per-group dlogit reduction stays inside the CTA (no atomics). Inside a tile, each channel
 // is split into P segments of L steps; a thread scans its segment sequentially in registers,
 // segments are composed as affine maps (a, x): carry_out = a * carry_in + x. Across T-chunks,
-// carries propagate by decoupled look-back over a flag/payload array in the workspace: a tile
-// publishes its aggregate, walks back over predecessors until an inclusive prefix, then
-// publishes its own inclusive carry. Tiles are drawn from a ticket counter in chunk-major
-// order, so every predecessor was scheduled earlier (no deadlock); each spin is bounded.
+// carries propagate by look-back over a flag/payload array in the workspace: every 8th chunk is
+// an anchor publishing its inclusive carry, the others publish aggregates; a tile composes its
+// anchor's carry with the aggregates in between in chunk order (a fixed association, so results
+// do not depend on timing). Tiles are drawn from a ticket counter in chunk-major order, so every
+// tile waited on was scheduled earlier (no deadlock); each spin is bounded.
 #include <algorithm>
 
 #include "ltvqkv_common.cuh"
@@ -26,6 +27,7 @@
 namespace ltvqkv {
 
 enum : unsigned int { kFlagNone = 0, kFlagAgg = 1, kFlagIncl = 2 };
+constexpr int kAnchorStride = 8;  // chunks between look-back anchors
 
 struct ScanGeometry {
   int B, T, NH, NKVH, Da, r, D, H, F;
@@ -230,45 +232,42 @@ __global__ void __launch_bounds__(1024) scan_fwd_kernel(ScanFwdArgs args) {
   }
 
   const long long tile_idx = (long long)j * BH + bh;  // payload slot of this tile
+  // Deterministic look-back: every kAnchorStride-th chunk is an anchor that publishes its
+  // inclusive carry; any other chunk publishes its aggregate and derives its carry-in from its
+  // anchor's inclusive carry composed with the aggregates in between, in chunk order — the
+  // same association whatever the timing, so results are identical run to run.
+  const bool is_anchor = (j % kAnchorStride) == 0;
   if (j == 0) {
-    if (is_last_seg) {
-      float E = Elem<T>::load(reinterpret_cast<const T*>(args.inits) + ((long long)b * g.H + h) * D + c);
-      shE[c] = E;
-      args.inclX[tile_idx * D + c] = tileA * E + tileX;
-      __threadfence();
-    }
-    __syncthreads();
-    if (tid == 0) st_release_u32(&args.flags[tile_idx], (epoch << 2) | kFlagIncl);
+    if (is_last_seg) shE[c] = Elem<T>::load(reinterpret_cast<const T*>(args.inits) + ((long long)b * g.H + h) * D + c);
   } else {
-    if (is_last_seg) {
-      args.aggX[tile_idx * D + c] = tileX;
-      if (c % r == 0) args.aggA[tile_idx * Da + gi] = tileA;
-      __threadfence();
+    if (!is_anchor) {
+      if (is_last_seg) {
+        args.aggX[tile_idx * D + c] = tileX;
+        if (c % r == 0) args.aggA[tile_idx * Da + gi] = tileA;
+        __threadfence();
+      }
+      __syncthreads();
+      if (tid == 0) st_release_u32(&args.flags[tile_idx], (epoch << 2) | kFlagAgg);
     }
-    __syncthreads();
-    if (tid == 0) st_release_u32(&args.flags[tile_idx], (epoch << 2) | kFlagAgg);
-    // Look back over predecessor chunks of the same (b, h).
-    float accA = 1.f, accX = 0.f;
+    const int m = (j - 1) / kAnchorStride * kAnchorStride;
     bool timed_out = false;
-    for (int k = j - 1; k >= 0; --k) {
+    float E = 0.f;
+    for (int k = m; k < j; ++k) {
       const long long pidx = (long long)k * BH + bh;
       if (tid == 0) sh_state = wait_flag(&args.flags[pidx], epoch, args.ws, &timed_out);
       __syncthreads();
-      const unsigned int st = sh_state;
-      if (is_last_seg) {
-        if (st == kFlagIncl) {
-          float prev = timed_out ? 0.f : ld_cg_f32(&args.inclX[pidx * D + c]);
-          shE[c] = accA * prev + accX;
+      if (is_last_seg && !timed_out) {
+        if (k == m) {
+          E = ld_cg_f32(&args.inclX[pidx * D + c]);
         } else {
-          float Ak = ld_cg_f32(&args.aggA[pidx * Da + gi]);
-          float Xk = ld_cg_f32(&args.aggX[pidx * D + c]);
-          accX = accA * Xk + accX;
-          accA *= Ak;
+          E = ld_cg_f32(&args.aggA[pidx * Da + gi]) * E + ld_cg_f32(&args.aggX[pidx * D + c]);
         }
       }
       __syncthreads();
-      if (st == kFlagIncl) break;
     }
+    if (is_last_seg) shE[c] = E;
+  }
+  if (is_anchor) {
     if (is_last_seg) {
       args.inclX[tile_idx * D + c] = tileA * shE[c] + tileX;
       __threadfence();
@@ -276,6 +275,7 @@ __global__ void __launch_bounds__(1024) scan_fwd_kernel(ScanFwdArgs args) {
     __syncthreads();
     if (tid == 0) st_release_u32(&args.flags[tile_idx], (epoch << 2) | kFlagIncl);
   }
+  __syncthreads();
 
   // Final pass: walk the segment from its exact carry, overwriting U with h.
   {
@@ -395,43 +395,41 @@ __global__ void __launch_bounds__(1024) scan_bwd_kernel(ScanBwdArgs args) {
   }
 
   const long long tile_idx = (long long)j * BH + bh;
-  if (j == g.nchunks - 1) {
-    if (is_first_seg) {
-      shE[c] = 0.f;
-      args.inclX[tile_idx * D + c] = tileX;
-      __threadfence();
-    }
-    __syncthreads();
-    if (tid == 0) st_release_u32(&args.flags[tile_idx], (epoch << 2) | kFlagIncl);
+  // Deterministic look-back in reverse chunk order (see the forward kernel): rj counts chunks
+  // from the end; anchors publish inclusive carries, the others aggregates.
+  const int rj = g.nchunks - 1 - j;
+  const bool is_anchor = (rj % kAnchorStride) == 0;
+  if (rj == 0) {
+    if (is_first_seg) shE[c] = 0.f;
   } else {
-    if (is_first_seg) {
-      args.aggX[tile_idx * D + c] = tileX;
-      if (c % r == 0) args.aggA[tile_idx * Da + gi] = tileA;
-      __threadfence();
+    if (!is_anchor) {
+      if (is_first_seg) {
+        args.aggX[tile_idx * D + c] = tileX;
+        if (c % r == 0) args.aggA[tile_idx * Da + gi] = tileA;
+        __threadfence();
+      }
+      __syncthreads();
+      if (tid == 0) st_release_u32(&args.flags[tile_idx], (epoch << 2) | kFlagAgg);
     }
-    __syncthreads();
-    if (tid == 0) st_release_u32(&args.flags[tile_idx], (epoch << 2) | kFlagAgg);
-    float accA = 1.f, accX = 0.f;
+    const int mr = (rj - 1) / kAnchorStride * kAnchorStride;
     bool timed_out = false;
-    for (int k = j + 1; k < g.nchunks; ++k) {
-      const long long pidx = (long long)k * BH + bh;
+    float E = 0.f;
+    for (int rk = mr; rk < rj; ++rk) {
+      const long long pidx = (long long)(g.nchunks - 1 - rk) * BH + bh;
       if (tid == 0) sh_state = wait_flag(&args.flags[pidx], epoch, args.ws, &timed_out);
       __syncthreads();
-      const unsigned int st = sh_state;
-      if (is_first_seg) {
-        if (st == kFlagIncl) {
-          float prev = timed_out ? 0.f : ld_cg_f32(&args.inclX[pidx * D + c]);
-          shE[c] = accA * prev + accX;
+      if (is_first_seg && !timed_out) {
+        if (rk == mr) {
+          E = ld_cg_f32(&args.inclX[pidx * D + c]);
         } else {
-          float Ak = ld_cg_f32(&args.aggA[pidx * Da + gi]);
-          float Xk = ld_cg_f32(&args.aggX[pidx * D + c]);
-          accX = accA * Xk + accX;
-          accA *= Ak;
+          E = ld_cg_f32(&args.aggA[pidx * Da + gi]) * E + ld_cg_f32(&args.aggX[pidx * D + c]);
         }
       }
       __syncthreads();
-      if (st == kFlagIncl) break;
     }
+    if (is_first_seg) shE[c] = E;
+  }
+  if (is_anchor) {
     if (is_first_seg) {
       args.inclX[tile_idx * D + c] = tileA * shE[c] + tileX;
       __threadfence();
@@ -439,6 +437,7 @@ __global__ void __launch_bounds__(1024) scan_bwd_kernel(ScanBwdArgs args) {
     __syncthreads();
     if (tid == 0) st_release_u32(&args.flags[tile_idx], (epoch << 2) | kFlagIncl);
   }
+  __syncthreads();
 
   {
     float carry = ea * shE[c] + ex;  // g^ at the token right after this segment
@@ -787,3 +786,4 @@ extern "C" int ltvqkv_scan_bwd(int dtype, const void* combined, int64_t sc_b, in
   bias_reduce_kernel<<<(hd + 127) / 128, 128, 0, s>>>(a.bias_part, grad_logit_bias, B, g.nchunks, H, Da);
   return ltvqkv_host::check_launch();
 }
+
