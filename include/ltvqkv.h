@@ -57,6 +57,7 @@ enum ltvqkv_status {
   LTVQKV_ERR_TIMEOUT = 7,     /* a bounded device-side wait gave up (read by ltvqkv_workspace_error) */
   LTVQKV_ERR_WORKSPACE = 8,   /* workspace missing or smaller than required */
   LTVQKV_ERR_UNSUPPORTED = 9, /* valid request this build does not implement */
+  LTVQKV_ERR_TOO_LARGE = 10,  /* problem needs more scratch than ltvqkv_scan_fwd_noalloc's fixed array */
 };
 
 /* Library ABI version (LTVQKV_ABI_VERSION). */
@@ -89,6 +90,24 @@ LTVQKV_API int ltvqkv_scan_fwd(int dtype,
                     void* out_q, void* out_k, void* out_v,
                     int B, int T, int NH, int NKVH, int Da, int r, int use_sigmoid,
                     void* workspace, size_t workspace_bytes, void* stream);
+
+/* Allocation-free variant of ltvqkv_scan_fwd (no counterpart in the reference). For callers
+ * that cannot allocate device memory or hand out a workspace on the call path — plugin hosts
+ * and serving runtimes that own all device memory under a fixed plan, or foreign-language
+ * callers without an allocator. Same arguments and results as ltvqkv_scan_fwd minus the
+ * workspace: the look-back scratch is a fixed 32 MiB file-scope device array in the library
+ * (held on every GPU that loads the library until exit). Shapes whose forward scratch exceeds
+ * it return LTVQKV_ERR_TOO_LARGE (D = 128, r = 128: about 1 KiB per (batch, head, 64-token
+ * chunk) tile, so up to about 32 k tiles; B=4, T=16384, 8+8+8 heads needs 24 576 and fits). Calls no cudaMalloc/cudaFree.
+ * The first call on a device looks up the array's address (may load the library's device code
+ * there) and should come before any stream capture. All calls share the array and each clears
+ * its counters and flags on `stream`: calls that overlap on the GPU race. */
+LTVQKV_API int ltvqkv_scan_fwd_noalloc(int dtype,
+                    const void* combined, int64_t sc_b, int64_t sc_t, int64_t sc_e,
+                    const void* inits, const float* logit_bias,
+                    void* out_q, void* out_k, void* out_v,
+                    int B, int T, int NH, int NKVH, int Da, int r, int use_sigmoid,
+                    void* stream);
 
 /* Scan backward: replaces cpp_ewma_cuda.ltv_fused_concat_head_major_register_cast_blelloch_scan_cuda_backward
  * (reference cpp_ewma/src/ltv_fused_concat_head_major_register_cast_blelloch_scan_cuda_backward.cu:882-976;

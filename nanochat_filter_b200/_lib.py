@@ -34,6 +34,7 @@ EXPORTED_SYMBOLS = (
     "ltvqkv_decode_step",
     "ltvqkv_workspace_error",
     "ltvqkv_debug_wait_timeout",
+    "ltvqkv_scan_fwd_noalloc",
 )
 
 _lib: Optional[ctypes.CDLL] = None
@@ -79,6 +80,9 @@ def _declare(lib: ctypes.CDLL) -> None:
                                        _i, _i, _i, _i, _i, _i, _i, _vp]
     lib.ltvqkv_workspace_error.restype = _i
     lib.ltvqkv_workspace_error.argtypes = [_vp, _vp, ctypes.POINTER(ctypes.c_uint32)]
+    lib.ltvqkv_scan_fwd_noalloc.restype = _i
+    lib.ltvqkv_scan_fwd_noalloc.argtypes = [_i, _vp, _i64, _i64, _i64, _vp, _pf, _vp, _vp, _vp,
+                                            _i, _i, _i, _i, _i, _i, _i, _vp]
     lib.ltvqkv_debug_wait_timeout.restype = _i
     lib.ltvqkv_debug_wait_timeout.argtypes = [_vp, ctypes.c_uint64, _vp]
 

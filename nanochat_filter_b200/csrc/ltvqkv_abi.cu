@@ -40,6 +40,7 @@ extern "C" const char* ltvqkv_status_string(int status) {
     case LTVQKV_ERR_TIMEOUT: return "device-side wait timed out";
     case LTVQKV_ERR_WORKSPACE: return "workspace missing or too small";
     case LTVQKV_ERR_UNSUPPORTED: return "unsupported request";
+    case LTVQKV_ERR_TOO_LARGE: return "problem exceeds the fixed 32 MiB scratch of the allocation-free entry point";
     default: return "unknown status";
   }
 }

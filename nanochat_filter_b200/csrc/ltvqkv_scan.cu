@@ -21,6 +21,7 @@
 // do not depend on timing). Tiles are drawn from a ticket counter in chunk-major order, so every
 // tile waited on was scheduled earlier (no deadlock); each spin is bounded.
 #include <algorithm>
+#include <mutex>
 
 #include "ltvqkv_common.cuh"
 
@@ -787,3 +788,71 @@ extern "C" int ltvqkv_scan_bwd(int dtype, const void* combined, int64_t sc_b, in
   return ltvqkv_host::check_launch();
 }
 
+// ------------------------------------------------------------------------------------------
+// Allocation-free forward scan.
+//
+// For callers that cannot allocate device memory on the call path: plugin hosts and serving
+// runtimes that own every byte of device memory under a fixed plan, or foreign-language callers
+// without access to an allocator. The look-back scratch of the forward scan lives in the
+// file-scope array below instead of a caller workspace. Its size is fixed at
+// kNoAllocScratchBytes (32 MiB); every GPU that loads this library holds it until the process
+// exits. Problems whose forward-scan scratch would exceed it are rejected with
+// LTVQKV_ERR_TOO_LARGE before anything is launched.
+//
+// Host code must not pass the array's name to a kernel (on the host it is only a stand-in for
+// the device symbol); the first call on each device looks up the array's device address with
+// cudaGetSymbolAddress while that device is current, checks the result and caches it. That
+// first call may cause the driver to load this library's device code on that device, so it
+// should come before any stream capture. Every call clears the part of the array that must
+// start at zero (header counters and epoch, look-back flags) with cudaMemsetAsync on the
+// caller's stream; all calls share the array, so calls that overlap on the GPU race with each
+// other and must be serialised by the caller (one stream, or events).
+// ------------------------------------------------------------------------------------------
+namespace {
+constexpr size_t kNoAllocScratchBytes = (size_t)32 << 20;
+__device__ __align__(256) unsigned char g_scan_noalloc_scratch[kNoAllocScratchBytes];
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+}  // namespace
+
+extern "C" int ltvqkv_scan_fwd_noalloc(int dtype, const void* combined, int64_t sc_b, int64_t sc_t, int64_t sc_e,
+                                       const void* inits, const float* logit_bias, void* out_q, void* out_k,
+                                       void* out_v, int B, int T, int NH, int NKVH, int Da, int r, int use_sigmoid,
+                                       void* stream) {
+  if (!ltvqkv_host::valid_dtype(dtype)) return LTVQKV_ERR_DTYPE;
+  int st = validate_scan_shape(B, T, NH, NKVH, Da, r);
+  if (st != LTVQKV_OK) return st;
+  if (B == 0 || T == 0) return LTVQKV_OK;
+  const ScanGeometry g = make_geometry(B, T, NH, NKVH, Da, r, kFwdBudget);
+  const ScanWorkspaceLayout wl = scan_ws_layout(g);
+  if (wl.total > kNoAllocScratchBytes) return LTVQKV_ERR_TOO_LARGE;
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    ltvqkv_host::set_last_cuda_error(e);
+    return LTVQKV_ERR_LAUNCH;
+  }
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return LTVQKV_ERR_UNSUPPORTED;
+  void* ptr = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    ptr = g_noalloc_ptr[dev];
+    if (ptr == nullptr) {
+      e = cudaGetSymbolAddress(&ptr, g_scan_noalloc_scratch);
+      if (e != cudaSuccess || ptr == nullptr) {
+        ltvqkv_host::set_last_cuda_error(e);
+        return LTVQKV_ERR_LAUNCH;
+      }
+      g_noalloc_ptr[dev] = ptr;
+    }
+  }
+  // Header (ticket/exit counters, epoch) and the look-back flags must start at zero.
+  e = cudaMemsetAsync(ptr, 0, wl.aggA, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) {
+    ltvqkv_host::set_last_cuda_error(e);
+    return LTVQKV_ERR_LAUNCH;
+  }
+  return ltvqkv_scan_fwd(dtype, combined, sc_b, sc_t, sc_e, inits, logit_bias, out_q, out_k, out_v, B, T, NH, NKVH,
+                         Da, r, use_sigmoid, ptr, kNoAllocScratchBytes, stream);
+}
