@@ -147,6 +147,12 @@ LTVQKV_DEVICE unsigned int wait_flag(const unsigned int* flag, unsigned int epoc
   }
 }
 
+}  // namespace ltvqkv
+
+#include "ltvqkv_scan_fast.cuh"
+
+namespace ltvqkv {
+
 // ------------------------------------------------------------------------------------------
 // Forward
 // ------------------------------------------------------------------------------------------
@@ -607,13 +613,23 @@ __global__ void bias_reduce_exact_kernel(const float* part, float* grad_bias, in
   grad_bias[idx] = __fadd_rn(grad_bias[idx], sum);
 }
 
-// grad_logit_bias[h, g] += sum over (b, chunk) of the per-tile partials, in a fixed order.
-__global__ void bias_reduce_kernel(const float* part, float* grad_bias, int B, int nchunks, int H, int Da) {
-  int idx = blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= H * Da) return;
+// grad_logit_bias[h, g] += sum over (b, chunk) of the per-tile partials: one CTA per (h, g),
+// each thread sums a fixed strided subset, then a fixed shared-memory tree (deterministic).
+constexpr int kBiasReduceThreads = 256;
+__global__ void __launch_bounds__(kBiasReduceThreads) bias_reduce_kernel(const float* part, float* grad_bias, int B,
+                                                                         int nchunks, int H, int Da) {
+  __shared__ float sm[kBiasReduceThreads];
+  const int idx = blockIdx.x;  // h * Da + g
+  const int n = B * nchunks;
   float sum = 0.f;
-  for (int bj = 0; bj < B * nchunks; ++bj) sum += part[(long long)bj * H * Da + idx];
-  grad_bias[idx] += sum;
+  for (int bj = threadIdx.x; bj < n; bj += kBiasReduceThreads) sum += part[(long long)bj * H * Da + idx];
+  sm[threadIdx.x] = sum;
+  __syncthreads();
+  for (int o = kBiasReduceThreads / 2; o > 0; o >>= 1) {
+    if (threadIdx.x < o) sm[threadIdx.x] += sm[threadIdx.x + o];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) grad_bias[idx] += sm[0];
 }
 
 __global__ void zero_grad_inits_kernel(void* p, long long n, int bf16) {
@@ -647,7 +663,8 @@ extern "C" size_t ltvqkv_scan_workspace_bytes(int B, int T, int NH, int NKVH, in
   if (validate_scan_shape(B, T, NH, NKVH, Da, r) != LTVQKV_OK) return 0;
   ScanGeometry gf = make_geometry(B, T, NH, NKVH, Da, r, kFwdBudget);
   ScanGeometry gb = make_geometry(B, T, NH, NKVH, Da, r, kBwdBudget);
-  return std::max(scan_ws_layout(gf).total, scan_ws_layout(gb).total);
+  ScanGeometry gx = fast_geometry(B, T, NH, NKVH, Da, r);
+  return std::max({scan_ws_layout(gf).total, scan_ws_layout(gb).total, scan_ws_layout(gx).total});
 }
 
 extern "C" int ltvqkv_scan_fwd(int dtype, const void* combined, int64_t sc_b, int64_t sc_t, int64_t sc_e,
@@ -684,6 +701,29 @@ extern "C" int ltvqkv_scan_fwd(int dtype, const void* combined, int64_t sc_b, in
     e.B = B; e.T = T; e.NH = NH; e.NKVH = NKVH; e.Da = Da; e.r = r; e.D = g.D; e.H = g.H; e.use_sigmoid = use_sigmoid;
     int threads = (g.D + 31) / 32 * 32;
     scan_fwd_exact_kernel<<<(unsigned int)(B * g.H), threads, 0, s>>>(e);
+    return ltvqkv_host::check_launch();
+  }
+  if (dtype == LTVQKV_DTYPE_BF16 && sc_t == 1 && sc_e % 8 == 0 && sc_b % 8 == 0 && fast_shape_ok(T, Da, r) &&
+      aligned16p(combined) && aligned16p(inits) && (NH == 0 || aligned16p(out_q)) &&
+      (NKVH == 0 || (aligned16p(out_k) && aligned16p(out_v)))) {
+    const ScanGeometry gx = fast_geometry(B, T, NH, NKVH, Da, r);
+    const ScanWorkspaceLayout wx = scan_ws_layout(gx);
+    if (workspace_bytes < wx.total) return LTVQKV_ERR_WORKSPACE;
+    FastFwdArgs f;
+    f.combined = reinterpret_cast<const __nv_bfloat16*>(combined); f.sc_b = sc_b; f.sc_e = sc_e;
+    f.inits = reinterpret_cast<const __nv_bfloat16*>(inits); f.logit_bias = logit_bias;
+    f.out[0] = reinterpret_cast<__nv_bfloat16*>(out_q); f.out[1] = reinterpret_cast<__nv_bfloat16*>(out_k);
+    f.out[2] = reinterpret_cast<__nv_bfloat16*>(out_v);
+    f.B = B; f.T = T; f.NH = NH; f.NKVH = NKVH; f.Da = Da; f.r = r; f.D = gx.D; f.H = gx.H;
+    f.nchunks = gx.nchunks; f.use_sigmoid = use_sigmoid;
+    f.ws = reinterpret_cast<WorkspaceHeader*>(ws);
+    f.flags = reinterpret_cast<unsigned int*>(ws + wx.flags);
+    f.aggA = reinterpret_cast<float*>(ws + wx.aggA);
+    f.aggX = reinterpret_cast<float*>(ws + wx.aggX);
+    f.inclX = reinterpret_cast<float*>(ws + wx.inclX);
+    const size_t fsm = fast_fwd_smem_bytes(gx.D, Da);
+    cudaFuncSetAttribute(scan_fwd_fast_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fsm);
+    scan_fwd_fast_kernel<<<(unsigned int)((long long)B * gx.H * gx.nchunks), 2 * gx.D, fsm, s>>>(f);
     return ltvqkv_host::check_launch();
   }
   size_t smem = fwd_smem_bytes(g);
@@ -772,6 +812,49 @@ extern "C" int ltvqkv_scan_bwd(int dtype, const void* combined, int64_t sc_b, in
     bias_reduce_exact_kernel<<<(H * Da + 127) / 128, 128, 0, s>>>(a.bias_part, grad_logit_bias, B, H, Da);
     return ltvqkv_host::check_launch();
   }
+  {
+    auto rows_ok = [&](const void* p, const int64_t* st) {
+      return p == nullptr || (aligned16p(p) && st[3] == 1 && st[0] % 8 == 0 && st[1] % 8 == 0 && st[2] % 8 == 0);
+    };
+    const int tpg = r / 32;
+    const bool r_ok = r % 32 == 0 && tpg >= 1 && (tpg & (tpg - 1)) == 0;
+    if (dtype == LTVQKV_DTYPE_BF16 && r_ok && fast_shape_ok(T, Da, r) && sc_t == 1 && sc_e % 8 == 0 &&
+        sc_b % 8 == 0 && gc_t == 1 && gc_e % 8 == 0 && gc_b % 8 == 0 && aligned16p(combined) &&
+        aligned16p(grad_combined) && aligned16p(inits) && rows_ok(hq, hq_strides) && rows_ok(grad_hq, gq_strides) &&
+        (NKVH == 0 || (rows_ok(hk, hk_strides) && rows_ok(hv, hv_strides) && rows_ok(grad_hk, gk_strides) &&
+                       rows_ok(grad_hv, gv_strides)))) {
+      const ScanGeometry gx = fast_geometry(B, T, NH, NKVH, Da, r);
+      const ScanWorkspaceLayout wx = scan_ws_layout(gx);
+      if (workspace_bytes < wx.total) return LTVQKV_ERR_WORKSPACE;
+      FastBwdArgs f;
+      f.combined = reinterpret_cast<const __nv_bfloat16*>(combined); f.sc_b = sc_b; f.sc_e = sc_e;
+      f.inits = reinterpret_cast<const __nv_bfloat16*>(inits); f.logit_bias = logit_bias;
+      const void* hh[3] = {hq, hk, hv};
+      const void* gg[3] = {grad_hq, grad_hk, grad_hv};
+      for (int i = 0; i < 3; ++i) {
+        f.h[i] = reinterpret_cast<const __nv_bfloat16*>(hh[i]);
+        f.gh[i] = reinterpret_cast<const __nv_bfloat16*>(gg[i]);
+        for (int k = 0; k < 3; ++k) { f.hs[i][k] = a.hs[i][k]; f.gs[i][k] = a.gs[i][k]; }
+      }
+      f.grad_combined = reinterpret_cast<__nv_bfloat16*>(grad_combined); f.gc_b = gc_b; f.gc_e = gc_e;
+      f.grad_inits = reinterpret_cast<__nv_bfloat16*>(grad_inits);
+      f.bias_part = reinterpret_cast<float*>(ws + wx.bias_part);
+      f.B = B; f.T = T; f.NH = NH; f.NKVH = NKVH; f.Da = Da; f.r = r; f.D = gx.D; f.H = gx.H;
+      f.nchunks = gx.nchunks; f.use_sigmoid = use_sigmoid;
+      f.ws = reinterpret_cast<WorkspaceHeader*>(ws);
+      f.flags = reinterpret_cast<unsigned int*>(ws + wx.flags);
+      f.aggA = reinterpret_cast<float*>(ws + wx.aggA);
+      f.aggX = reinterpret_cast<float*>(ws + wx.aggX);
+      f.inclX = reinterpret_cast<float*>(ws + wx.inclX);
+      const size_t fsm = fast_bwd_smem_bytes(gx.D, Da);
+      cudaFuncSetAttribute(scan_bwd_fast_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fsm);
+      scan_bwd_fast_kernel<<<(unsigned int)((long long)B * gx.H * gx.nchunks), 2 * gx.D, fsm, s>>>(f);
+      int rc = ltvqkv_host::check_launch();
+      if (rc != LTVQKV_OK) return rc;
+      bias_reduce_kernel<<<H * Da, kBiasReduceThreads, 0, s>>>(f.bias_part, grad_logit_bias, B, gx.nchunks, H, Da);
+      return ltvqkv_host::check_launch();
+    }
+  }
   size_t smem = bwd_smem_bytes(g);
   unsigned int grid = (unsigned int)((long long)B * g.H * g.nchunks);
   if (dtype == LTVQKV_DTYPE_BF16) {
@@ -783,8 +866,7 @@ extern "C" int ltvqkv_scan_bwd(int dtype, const void* combined, int64_t sc_b, in
   }
   int rc = ltvqkv_host::check_launch();
   if (rc != LTVQKV_OK) return rc;
-  int hd = H * Da;
-  bias_reduce_kernel<<<(hd + 127) / 128, 128, 0, s>>>(a.bias_part, grad_logit_bias, B, g.nchunks, H, Da);
+  bias_reduce_kernel<<<H * Da, kBiasReduceThreads, 0, s>>>(a.bias_part, grad_logit_bias, B, g.nchunks, H, Da);
   return ltvqkv_host::check_launch();
 }
 
@@ -824,9 +906,9 @@ extern "C" int ltvqkv_scan_fwd_noalloc(int dtype, const void* combined, int64_t 
   int st = validate_scan_shape(B, T, NH, NKVH, Da, r);
   if (st != LTVQKV_OK) return st;
   if (B == 0 || T == 0) return LTVQKV_OK;
-  const ScanGeometry g = make_geometry(B, T, NH, NKVH, Da, r, kFwdBudget);
-  const ScanWorkspaceLayout wl = scan_ws_layout(g);
-  if (wl.total > kNoAllocScratchBytes) return LTVQKV_ERR_TOO_LARGE;
+  const ScanWorkspaceLayout wl = scan_ws_layout(make_geometry(B, T, NH, NKVH, Da, r, kFwdBudget));
+  const ScanWorkspaceLayout wx = scan_ws_layout(fast_geometry(B, T, NH, NKVH, Da, r));
+  if (std::max(wl.total, wx.total) > kNoAllocScratchBytes) return LTVQKV_ERR_TOO_LARGE;
   int dev = -1;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) {
@@ -848,7 +930,7 @@ extern "C" int ltvqkv_scan_fwd_noalloc(int dtype, const void* combined, int64_t 
     }
   }
   // Header (ticket/exit counters, epoch) and the look-back flags must start at zero.
-  e = cudaMemsetAsync(ptr, 0, wl.aggA, reinterpret_cast<cudaStream_t>(stream));
+  e = cudaMemsetAsync(ptr, 0, std::max(wl.aggA, wx.aggA), reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) {
     ltvqkv_host::set_last_cuda_error(e);
     return LTVQKV_ERR_LAUNCH;

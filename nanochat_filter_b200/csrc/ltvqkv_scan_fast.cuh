@@ -1,0 +1,443 @@
+// Vectorised bf16 scan kernels for the production layouts (included by ltvqkv_scan.cu).
+//
+// Layouts: combined / grad_combined are the transposed view of a [B, F, T] buffer (t unit
+// stride), the saved outputs and their gradients are [B, heads, T, D] with d unit stride (any
+// b/h/t strides, so the attention layer's transposed q/k gradients qualify).
+//
+// A CTA owns one (b, head, 64-token chunk) tile with 2*D threads: thread (c, s) holds channel c
+// and tokens [32 s, 32 s + 32) of the chunk. t-contiguous rows are read and written straight
+// from/to registers with 16-byte vector accesses (4 per thread); d-contiguous tiles pass through
+// shared memory ([64][D] bf16, one contiguous 16 KB block per tile in global memory). The two
+// 32-token segments of a channel are adjacent lanes and combine with one shuffle. Chunk carries
+// use the anchored look-back of the generic kernels (fixed association: deterministic).
+#pragma once
+
+namespace ltvqkv {
+
+constexpr int kFastTT = 64;   // tokens per tile
+constexpr int kFastSeg = 32;  // tokens per thread
+constexpr int kFastMaxDa = 8;
+
+LTVQKV_DEVICE void unpack8(const uint4& v, float (&f)[8]) {
+  const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 t = __bfloat1622float2(p[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+
+LTVQKV_DEVICE uint4 pack8(const float (&f)[8]) {
+  uint4 v;
+  __nv_bfloat162* p = reinterpret_cast<__nv_bfloat162*>(&v);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) p[i] = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+  return v;
+}
+
+struct FastFwdArgs {
+  const __nv_bfloat16* combined;
+  long long sc_b, sc_e;  // sc_t == 1
+  const __nv_bfloat16* inits;
+  const float* logit_bias;
+  __nv_bfloat16* out[3];
+  int B, T, NH, NKVH, Da, r, D, H, nchunks, use_sigmoid;
+  WorkspaceHeader* ws;
+  unsigned int* flags;
+  float* aggA;
+  float* aggX;
+  float* inclX;
+};
+
+struct FastBwdArgs {
+  const __nv_bfloat16* combined;
+  long long sc_b, sc_e;
+  const __nv_bfloat16* inits;
+  const float* logit_bias;
+  const __nv_bfloat16* h[3];
+  long long hs[3][3];  // b, head, t strides (d stride 1)
+  const __nv_bfloat16* gh[3];
+  long long gs[3][3];
+  __nv_bfloat16* grad_combined;
+  long long gc_b, gc_e;
+  __nv_bfloat16* grad_inits;
+  float* bias_part;
+  int B, T, NH, NKVH, Da, r, D, H, nchunks, use_sigmoid;
+  WorkspaceHeader* ws;
+  unsigned int* flags;
+  float* aggA;
+  float* aggX;
+  float* inclX;
+};
+
+// Waits (thread 0) for the flags of chunks [first, last) of row bh in the given visiting order.
+LTVQKV_DEVICE bool wait_flags_range(const unsigned int* flags, int BH, int bh, int nchunks, int m, int j, bool reverse,
+                                    unsigned int epoch, WorkspaceHeader* ws) {
+  bool timed_out = false;
+  for (int k = m; k < j && !timed_out; ++k) {
+    const int chunk = reverse ? nchunks - 1 - k : k;
+    wait_flag(&flags[(long long)chunk * BH + bh], epoch, ws, &timed_out);
+  }
+  return timed_out;
+}
+
+// ------------------------------------------------------------------------------------------
+// Forward
+// ------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(512) scan_fwd_fast_kernel(FastFwdArgs a) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int D = a.D, Da = a.Da;
+  __nv_bfloat16* out_s = reinterpret_cast<__nv_bfloat16*>(smem_raw);                 // [64][D]
+  float* alpha_s = reinterpret_cast<float*>(smem_raw + (size_t)kFastTT * D * 2);      // [Da][64]
+  float* shE = alpha_s + Da * kFastTT;                                                // [D]
+  __shared__ unsigned int sh_tile, sh_epoch;
+  __shared__ int sh_timeout;
+
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int c = tid >> 1, s = tid & 1;
+  if (tid == 0) {
+    sh_tile = draw_ticket(a.ws);
+    sh_epoch = *((volatile unsigned int*)&a.ws->epoch) & 0x3FFFFFFFu;
+  }
+  __syncthreads();
+  const unsigned int epoch = sh_epoch;
+  const int BH = a.B * a.H;
+  const int j = (int)(sh_tile / BH);
+  const int bh = (int)(sh_tile % BH);
+  const int b = bh / a.H, h = bh % a.H;
+  const int t0 = j * kFastTT;
+  const int tlen = min(kFastTT, a.T - t0);
+  const __nv_bfloat16* cb = a.combined + (long long)b * a.sc_b;
+  const int head_col = h * (D + Da);
+
+  for (int i = tid; i < Da * kFastTT; i += blockDim.x) {
+    const int gi = i / kFastTT, t = i % kFastTT;
+    float al = 0.f;  // tokens beyond T: identity steps
+    if (t < tlen) {
+      const float l = __bfloat162float(cb[(long long)(head_col + D + gi) * a.sc_e + t0 + t]) + a.logit_bias[h * Da + gi];
+      al = a.use_sigmoid ? sigmoid_f32(l) : l;
+    }
+    alpha_s[i] = al;
+  }
+  uint4 uv[4];
+  {
+    const __nv_bfloat16* urow = cb + (long long)(head_col + c) * a.sc_e + t0 + s * kFastSeg;
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      uv[k] = (s * kFastSeg + 8 * k < tlen) ? __ldg(reinterpret_cast<const uint4*>(urow + 8 * k)) : make_uint4(0, 0, 0, 0);
+  }
+  __syncthreads();
+  const float* al_row = alpha_s + (c / a.r) * kFastTT + s * kFastSeg;
+
+  float sa = 1.f, sx = 0.f;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    float f[8];
+    unpack8(uv[k], f);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float al = al_row[8 * k + e];
+      sx = (1.0f - al) * sx + al * f[e];
+      sa *= (1.0f - al);
+    }
+  }
+  // segment 0 lives in the even lane of each pair
+  const float a0 = __shfl_sync(0xffffffffu, sa, lane & ~1);
+  const float x0 = __shfl_sync(0xffffffffu, sx, lane & ~1);
+  const float tileA = a0 * sa, tileX = sa * x0 + sx;  // meaningful on s == 1
+
+  const long long tile_idx = (long long)j * BH + bh;
+  const bool is_anchor = (j % kAnchorStride) == 0;
+  if (j == 0) {
+    if (s == 1) shE[c] = __bfloat162float(a.inits[((long long)b * a.H + h) * D + c]);
+  } else {
+    if (!is_anchor) {
+      if (s == 1) {
+        a.aggX[tile_idx * D + c] = tileX;
+        if (c % a.r == 0) a.aggA[tile_idx * Da + c / a.r] = tileA;
+        __threadfence();
+      }
+      __syncthreads();
+      if (tid == 0) st_release_u32(&a.flags[tile_idx], (epoch << 2) | kFlagAgg);
+    }
+    const int m = (j - 1) / kAnchorStride * kAnchorStride;
+    if (tid == 0) sh_timeout = wait_flags_range(a.flags, BH, bh, a.nchunks, m, j, false, epoch, a.ws);
+    __syncthreads();
+    if (s == 1) {
+      float E = 0.f;
+      if (!sh_timeout) {
+        E = ld_cg_f32(&a.inclX[((long long)m * BH + bh) * D + c]);
+        for (int k = m + 1; k < j; ++k) {
+          const long long p = (long long)k * BH + bh;
+          E = ld_cg_f32(&a.aggA[p * Da + c / a.r]) * E + ld_cg_f32(&a.aggX[p * D + c]);
+        }
+      }
+      shE[c] = E;
+    }
+  }
+  if (is_anchor) {
+    if (s == 1) {
+      a.inclX[tile_idx * D + c] = tileA * shE[c] + tileX;
+      __threadfence();
+    }
+    __syncthreads();
+    if (tid == 0) st_release_u32(&a.flags[tile_idx], (epoch << 2) | kFlagIncl);
+  }
+  __syncthreads();
+
+  float carry = (s == 0) ? shE[c] : a0 * shE[c] + x0;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    float f[8];
+    unpack8(uv[k], f);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float al = al_row[8 * k + e];
+      carry = (1.0f - al) * carry + al * f[e];
+      out_s[(s * kFastSeg + 8 * k + e) * D + c] = __float2bfloat16_rn(carry);
+    }
+  }
+  __syncthreads();
+
+  int which, hloc, nheads;
+  split_head(h, a.NH, a.NKVH, which, hloc, nheads);
+  uint4* go = reinterpret_cast<uint4*>(a.out[which] + (((long long)b * nheads + hloc) * a.T + t0) * D);
+  const uint4* so = reinterpret_cast<const uint4*>(out_s);
+  const int n16 = tlen * D / 8;
+  for (int i = tid; i < n16; i += blockDim.x) go[i] = so[i];
+
+  if (tid == 0) finish_launch(a.ws, gridDim.x);
+}
+
+// ------------------------------------------------------------------------------------------
+// Backward
+// ------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(512) scan_bwd_fast_kernel(FastBwdArgs a) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int D = a.D, Da = a.Da;
+  __nv_bfloat16* G_s = reinterpret_cast<__nv_bfloat16*>(smem_raw);                        // [64][D] upstream grad
+  __nv_bfloat16* H_s = G_s + kFastTT * D;                                                 // [64][D] h_{t-1}
+  float* red = reinterpret_cast<float*>(H_s + kFastTT * D);                               // [64][D] dlogit terms
+  float* alpha_s = red + kFastTT * D;                                                     // [Da][65]
+  float* dlog_s = alpha_s + Da * (kFastTT + 1);                                           // [Da][64]
+  float* shE = dlog_s + Da * kFastTT;                                                     // [D]
+  __shared__ unsigned int sh_tile, sh_epoch;
+  __shared__ int sh_timeout;
+
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int c = tid >> 1, s = tid & 1;
+  if (tid == 0) {
+    sh_tile = draw_ticket(a.ws);
+    sh_epoch = *((volatile unsigned int*)&a.ws->epoch) & 0x3FFFFFFFu;
+  }
+  __syncthreads();
+  const unsigned int epoch = sh_epoch;
+  const int BH = a.B * a.H;
+  const int j = a.nchunks - 1 - (int)(sh_tile / BH);
+  const int bh = (int)(sh_tile % BH);
+  const int b = bh / a.H, h = bh % a.H;
+  const int t0 = j * kFastTT;
+  const int tlen = min(kFastTT, a.T - t0);
+  int which, hloc, nheads;
+  split_head(h, a.NH, a.NKVH, which, hloc, nheads);
+  const __nv_bfloat16* cb = a.combined + (long long)b * a.sc_b;
+  const int head_col = h * (D + Da);
+  const int ld_a = kFastTT + 1;
+
+  // gates alpha_{t0 + t}, t = 0..tlen (the first token of the next chunk included; 0 beyond T)
+  for (int i = tid; i < Da * ld_a; i += blockDim.x) {
+    const int gi = i / ld_a, t = i % ld_a;
+    float al = 0.f;
+    if (t <= tlen && t0 + t < a.T) {
+      const float l = __bfloat162float(cb[(long long)(head_col + D + gi) * a.sc_e + t0 + t]) + a.logit_bias[h * Da + gi];
+      al = a.use_sigmoid ? sigmoid_f32(l) : l;
+    }
+    alpha_s[i] = al;
+  }
+  // upstream gradient rows and h_{t-1} rows into shared memory (16-byte vectors)
+  {
+    const int vpr = D / 8;  // vectors per row
+    const long long* gs = a.gs[which];
+    const long long* hs = a.hs[which];
+    const __nv_bfloat16* gb = a.gh[which] + (long long)b * gs[0] + (long long)hloc * gs[1];
+    const __nv_bfloat16* hb = a.h[which] + (long long)b * hs[0] + (long long)hloc * hs[1];
+    const __nv_bfloat16* ib = a.inits + ((long long)b * a.H + h) * D;
+    uint4* Gv = reinterpret_cast<uint4*>(G_s);
+    uint4* Hv = reinterpret_cast<uint4*>(H_s);
+    for (int i = tid; i < kFastTT * vpr; i += blockDim.x) {
+      const int t = i / vpr, ch = i % vpr;
+      uint4 gv = make_uint4(0, 0, 0, 0), hv = make_uint4(0, 0, 0, 0);
+      if (t < tlen) {
+        gv = __ldg(reinterpret_cast<const uint4*>(gb + (long long)(t0 + t) * gs[2]) + ch);
+        const int tp = t0 + t - 1;
+        hv = tp >= 0 ? __ldg(reinterpret_cast<const uint4*>(hb + (long long)tp * hs[2]) + ch)
+                     : __ldg(reinterpret_cast<const uint4*>(ib) + ch);
+      }
+      Gv[i] = gv;
+      Hv[i] = hv;
+    }
+  }
+  uint4 uv[4];
+  const __nv_bfloat16* urow = cb + (long long)(head_col + c) * a.sc_e + t0 + s * kFastSeg;
+#pragma unroll
+  for (int k = 0; k < 4; ++k)
+    uv[k] = (s * kFastSeg + 8 * k < tlen) ? __ldg(reinterpret_cast<const uint4*>(urow + 8 * k)) : make_uint4(0, 0, 0, 0);
+  __syncthreads();
+
+  const int gi = c / a.r;
+  const float* al_row = alpha_s + gi * ld_a + s * kFastSeg;  // al_row[t] = alpha at local token s*32 + t
+  // reverse local scan of the segment (zero carry from the right)
+  float sa = 1.f, sx = 0.f;
+#pragma unroll
+  for (int t = kFastSeg - 1; t >= 0; --t) {
+    const float an = 1.0f - al_row[t + 1];
+    sx = an * sx + __bfloat162float(G_s[(s * kFastSeg + t) * D + c]);
+    sa *= an;
+  }
+  // segment 1 (odd lane) lies to the right of segment 0
+  const float a1 = __shfl_sync(0xffffffffu, sa, lane | 1);
+  const float x1 = __shfl_sync(0xffffffffu, sx, lane | 1);
+  const float tileA = sa * a1, tileX = sa * x1 + sx;  // meaningful on s == 0
+
+  const long long tile_idx = (long long)j * BH + bh;
+  const int rj = a.nchunks - 1 - j;
+  const bool is_anchor = (rj % kAnchorStride) == 0;
+  if (rj == 0) {
+    if (s == 0) shE[c] = 0.f;
+  } else {
+    if (!is_anchor) {
+      if (s == 0) {
+        a.aggX[tile_idx * D + c] = tileX;
+        if (c % a.r == 0) a.aggA[tile_idx * Da + gi] = tileA;
+        __threadfence();
+      }
+      __syncthreads();
+      if (tid == 0) st_release_u32(&a.flags[tile_idx], (epoch << 2) | kFlagAgg);
+    }
+    const int mr = (rj - 1) / kAnchorStride * kAnchorStride;
+    if (tid == 0) sh_timeout = wait_flags_range(a.flags, BH, bh, a.nchunks, mr, rj, true, epoch, a.ws);
+    __syncthreads();
+    if (s == 0) {
+      float E = 0.f;
+      if (!sh_timeout) {
+        E = ld_cg_f32(&a.inclX[((long long)(a.nchunks - 1 - mr) * BH + bh) * D + c]);
+        for (int rk = mr + 1; rk < rj; ++rk) {
+          const long long p = (long long)(a.nchunks - 1 - rk) * BH + bh;
+          E = ld_cg_f32(&a.aggA[p * Da + gi]) * E + ld_cg_f32(&a.aggX[p * D + c]);
+        }
+      }
+      shE[c] = E;
+    }
+  }
+  if (is_anchor) {
+    if (s == 0) {
+      a.inclX[tile_idx * D + c] = tileA * shE[c] + tileX;
+      __threadfence();
+    }
+    __syncthreads();
+    if (tid == 0) st_release_u32(&a.flags[tile_idx], (epoch << 2) | kFlagIncl);
+  }
+  __syncthreads();
+
+  // final reverse walk: g^_t for the segment, kept in registers
+  float ghat[kFastSeg];
+  {
+    float carry = (s == 1) ? shE[c] : a1 * shE[c] + x1;
+#pragma unroll
+    for (int t = kFastSeg - 1; t >= 0; --t) {
+      carry = (1.0f - al_row[t + 1]) * carry + __bfloat162float(G_s[(s * kFastSeg + t) * D + c]);
+      ghat[t] = carry;
+    }
+  }
+  if (t0 == 0 && s == 0)
+    a.grad_inits[((long long)b * a.H + h) * D + c] = __float2bfloat16_rn(ghat[0] * (1.0f - al_row[0]));
+
+  // elementwise: du (t-contiguous row of grad_combined) and the dlogit terms
+  __nv_bfloat16* grow = a.grad_combined + (long long)b * a.gc_b + (long long)(head_col + c) * a.gc_e + t0 + s * kFastSeg;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    float f[8], du[8];
+    unpack8(uv[k], f);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int t = 8 * k + e;
+      const float al = al_row[t];
+      const float gh = ghat[t];
+      du[e] = al * gh;
+      const float hp = __bfloat162float(H_s[(s * kFastSeg + t) * D + c]);
+      const float dalpha = (f[e] - hp) * gh;
+      red[(s * kFastSeg + t) * D + c] = a.use_sigmoid ? dalpha * (al * (1.0f - al)) : dalpha;
+    }
+    if (s * kFastSeg + 8 * k < tlen) *reinterpret_cast<uint4*>(grow + 8 * k) = pack8(du);
+  }
+  __syncthreads();
+
+  // group sums over the r channels of each (token, group): tpg = r / 32 threads per pair, each
+  // summing 32 channels in a lane-rotated order (conflict-free), then a fixed shuffle tree.
+  {
+    const int tpg = a.r / 32;
+    const int npairs = Da * kFastTT;
+    for (int base = 0; base < npairs * tpg; base += blockDim.x) {
+      const int w = base + tid;
+      const int pair = w / tpg, part = w % tpg;
+      float sum = 0.f;
+      if (pair < npairs) {
+        const int g = pair / kFastTT, t = pair % kFastTT;
+        const float* row = red + t * D + g * a.r + part * 32;
+        const int rot = (t + part * (32 / tpg)) & 31;  // distinct banks across the warp
+#pragma unroll 8
+        for (int i = 0; i < 32; ++i) sum += row[(i + rot) & 31];
+      }
+      for (int o = tpg >> 1; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      if (pair < npairs && part == 0) {
+        const int g = pair / kFastTT, t = pair % kFastTT;
+        dlog_s[g * kFastTT + t] = sum;
+        if (t < tlen)
+          a.grad_combined[(long long)b * a.gc_b + (long long)(head_col + D + g) * a.gc_e + t0 + t] =
+              __float2bfloat16_rn(sum);
+      }
+    }
+  }
+  __syncthreads();
+  // per-tile bias partial: warp g sums the tile's dlogit of group g in a fixed tree order
+  {
+    const int warp = tid >> 5;
+    for (int g = warp; g < Da; g += blockDim.x / 32) {
+      float v = 0.f;
+      for (int t = lane; t < kFastTT; t += 32) v += (t < tlen) ? dlog_s[g * kFastTT + t] : 0.f;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      if (lane == 0) a.bias_part[(((long long)b * a.nchunks + j) * a.H + h) * Da + g] = v;
+    }
+  }
+
+  if (tid == 0) finish_launch(a.ws, gridDim.x);
+}
+
+inline size_t fast_fwd_smem_bytes(int D, int Da) {
+  return (size_t)kFastTT * D * 2 + sizeof(float) * ((size_t)Da * kFastTT + D);
+}
+inline size_t fast_bwd_smem_bytes(int D, int Da) {
+  return (size_t)kFastTT * D * 2 * 2 + sizeof(float) * ((size_t)kFastTT * D + (size_t)Da * (kFastTT + 1) +
+                                                         (size_t)Da * kFastTT + D);
+}
+
+inline ScanGeometry fast_geometry(int B, int T, int NH, int NKVH, int Da, int r) {
+  ScanGeometry g;
+  g.B = B; g.T = T; g.NH = NH; g.NKVH = NKVH; g.Da = Da; g.r = r;
+  g.D = Da * r; g.H = NH + 2 * NKVH; g.F = g.H * (g.D + Da);
+  g.P = 2; g.L = kFastSeg; g.TT = kFastTT; g.nthreads = 2 * g.D;
+  g.nchunks = T > 0 ? (T + kFastTT - 1) / kFastTT : 0;
+  return g;
+}
+
+inline bool aligned16p(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Shape conditions shared by the fast kernels.
+inline bool fast_shape_ok(int T, int Da, int r) {
+  const int D = Da * r;
+  return T % 8 == 0 && D % 32 == 0 && D >= 32 && D <= 256 && Da <= kFastMaxDa;
+}
+
+}  // namespace ltvqkv

@@ -143,16 +143,25 @@ def _check_vs_oracle(dev, dtype, B, T, NH, NKVH, Da, r, seed, bias_shift=0.0, la
     assert not bad, f"max rel err above {tol}: {bad} (all: {errs})"
 
 
+# T = 700 takes the generic chunked kernels (T not a multiple of 8), T = 704 and 1000 the
+# vectorised bf16 kernels (704: eleven full 64-token chunks; 1000: a partial last chunk).
+@pytest.mark.parametrize("T", [700, 704, 1000])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 @pytest.mark.parametrize("Da,r", [(1, 128), (2, 64), (4, 32)])
-def test_scan_multichunk_vs_oracle(cuda_device, dtype, Da, r):
-    _check_vs_oracle(cuda_device, dtype, B=3, T=700, NH=2, NKVH=1, Da=Da, r=r, seed=Da)
+def test_scan_multichunk_vs_oracle(cuda_device, dtype, Da, r, T):
+    _check_vs_oracle(cuda_device, dtype, B=3, T=T, NH=2, NKVH=1, Da=Da, r=r, seed=Da)
 
 
+@pytest.mark.parametrize("T", [333, 336])
 @pytest.mark.parametrize("layout", ["bft", "btf"])
-def test_scan_layouts_and_transposed_grads(cuda_device, layout):
-    _check_vs_oracle(cuda_device, torch.bfloat16, B=2, T=333, NH=2, NKVH=2, Da=1, r=128, seed=5, layout=layout,
+def test_scan_layouts_and_transposed_grads(cuda_device, layout, T):
+    _check_vs_oracle(cuda_device, torch.bfloat16, B=2, T=T, NH=2, NKVH=2, Da=1, r=128, seed=5, layout=layout,
                      transposed_qk=True)
+
+
+def test_scan_head_dim_64_and_256(cuda_device):
+    _check_vs_oracle(cuda_device, torch.bfloat16, B=2, T=256, NH=1, NKVH=1, Da=1, r=64, seed=6)
+    _check_vs_oracle(cuda_device, torch.bfloat16, B=2, T=256, NH=1, NKVH=1, Da=2, r=128, seed=7)
 
 
 def test_scan_baseline_config2_full_size(cuda_device):
