@@ -170,6 +170,30 @@ LTVQKV_DEVICE void tma_load_3d(void* smem_dst, const CUtensorMap* m, uint64_t* b
       "l"(m), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
       : "memory");
 }
+LTVQKV_DEVICE void tma_load_2d(void* smem_dst, const CUtensorMap* m, uint64_t* bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(m), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+LTVQKV_DEVICE void tma_load_4d(void* smem_dst, const CUtensorMap* m, uint64_t* bar, int c0, int c1, int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(m), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+// Contiguous shared -> global bulk copy (16-byte aligned addresses, size a multiple of 16).
+LTVQKV_DEVICE void bulk_store(void* gdst, const void* smem_src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst), "r"(smem_u32(smem_src)),
+               "r"(bytes)
+               : "memory");
+}
+// Barrier among `count` threads (a multiple of 32) of the CTA, id 1..15 (0 is __syncthreads).
+LTVQKV_DEVICE void named_barrier(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
 LTVQKV_DEVICE void tma_store_3d(const CUtensorMap* m, const void* smem_src, int c0, int c1, int c2) {
   asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(m),
                "r"(smem_u32(smem_src)), "r"(c0), "r"(c1), "r"(c2)
@@ -261,6 +285,11 @@ __host__ __device__ constexpr uint32_t umma_idesc_bf16(int M, int N, int a_mn_ma
 // Host-side helpers shared by the .cu files
 // ------------------------------------------------------------------------------------------
 namespace ltvqkv_host {
+// Encodes a tiled TMA descriptor (cuTensorMapEncodeTiled through the driver entry point).
+// dims[0] is the innermost extent; strides_bytes holds the byte strides of dims 1..rank-1.
+bool encode_tiled_map(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base, const uint64_t* dims,
+                      const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swizzle);
+int num_sms();
 void set_last_cuda_error(cudaError_t e);
 int check_launch();  // returns LTVQKV_OK or LTVQKV_ERR_LAUNCH (and records the CUDA error text)
 inline bool valid_dtype(int dtype) { return dtype == LTVQKV_DTYPE_F32 || dtype == LTVQKV_DTYPE_BF16; }

@@ -19,10 +19,7 @@
 // long dW tiles are drawn first and the short dx tiles fill the remaining SMs.
 // Every mbarrier wait is bounded (2 s); a timeout records LTVQKV_ERR_TIMEOUT in the workspace
 // and all roles leave their loops, then TMEM is freed.
-#include <cudaTypedefs.h>
-
 #include <algorithm>
-#include <mutex>
 
 #include "ltvqkv_common.cuh"
 
@@ -412,43 +409,14 @@ using namespace ltvqkv;
 // ------------------------------------------------------------------------------------------
 namespace {
 
-PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, []() {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  });
-  return fn;
-}
-
 // 3-D tiled map: dims (d0 innermost, d1, d2), byte strides of d1 and d2, box (box0, box1, 1).
 bool make_map(CUtensorMap* m, bool f32, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1,
               uint64_t s2, uint32_t box0, uint32_t box1) {
-  auto enc = get_encode_fn();
-  if (!enc) return false;
-  cuuint64_t dims[3] = {d0, d1, d2};
-  cuuint64_t strides[2] = {s1, s2};
-  cuuint32_t box[3] = {box0, box1, 1};
-  cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = enc(m, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3,
-                   const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS;
-}
-
-int num_sms() {
-  static int n = 0;
-  if (n == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    if (n <= 0) n = 148;
-  }
-  return n;
+  const uint64_t dims[3] = {d0, d1, d2};
+  const uint64_t strides[2] = {s1, s2};
+  const uint32_t box[3] = {box0, box1, 1};
+  return ltvqkv_host::encode_tiled_map(m, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3,
+                                       base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 void finalize_problem(GemmProblem& p) {
@@ -467,7 +435,7 @@ int launch_tc(GemmParams& prm, const CUtensorMap* maps /*[6]*/, cudaStream_t s) 
     cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmemBytes);
     attr_set = true;
   }
-  int grid = std::min(prm.total_tiles, num_sms());
+  int grid = std::min(prm.total_tiles, ltvqkv_host::num_sms());
   gemm_tc_kernel<<<grid, kGemmThreads, kGemmSmemBytes, s>>>(maps[0], maps[1], maps[2], maps[3], maps[4], maps[5],
                                                           prm);
   return ltvqkv_host::check_launch();

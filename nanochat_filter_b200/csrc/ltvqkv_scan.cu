@@ -150,6 +150,7 @@ LTVQKV_DEVICE unsigned int wait_flag(const unsigned int* flag, unsigned int epoc
 }  // namespace ltvqkv
 
 #include "ltvqkv_scan_fast.cuh"
+#include "ltvqkv_scan_tma.cuh"
 
 namespace ltvqkv {
 
@@ -659,6 +660,40 @@ static int validate_scan_shape(int B, int T, int NH, int NKVH, int Da, int r) {
   return LTVQKV_OK;
 }
 
+namespace {
+constexpr size_t kMaxDynSmem = 227 * 1024;  // per-CTA dynamic shared memory limit of sm_100
+
+// Exact [B, F, T]-contiguous view of combined / grad_combined (what the projection produces).
+bool production_layout(const void* p, int64_t sb, int64_t st, int64_t se, int T, int F) {
+  return p != nullptr && aligned16p(p) && st == 1 && se == T && sb == (int64_t)F * T && T % 8 == 0;
+}
+
+bool bf16_map_2d(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows, uint32_t box_cols, uint32_t box_rows,
+                 bool swizzle) {
+  const uint64_t dims[2] = {cols, rows};
+  const uint64_t strides[1] = {cols * 2};
+  const uint32_t box[2] = {box_cols, box_rows};
+  return ltvqkv_host::encode_tiled_map(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box,
+                                       swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
+// [B, heads, T, D] tensor with d unit stride as a 4-D map (d, t, head, b), box (D, 64, 1, 1).
+bool bf16_map_rows(CUtensorMap* m, const void* base, const int64_t* st, int B, int heads, int T, int D) {
+  const uint64_t dims[4] = {(uint64_t)D, (uint64_t)T, (uint64_t)heads, (uint64_t)B};
+  const uint64_t strides[3] = {(uint64_t)st[2] * 2, (uint64_t)st[1] * 2, (uint64_t)st[0] * 2};
+  const uint32_t box[4] = {(uint32_t)D, (uint32_t)kFastTT, 1, 1};
+  return ltvqkv_host::encode_tiled_map(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, base, dims, strides, box,
+                                       CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
+int persistent_grid(const void* kernel, int threads, size_t smem, int ntiles) {
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem) != cudaSuccess || per_sm < 1)
+    per_sm = 1;
+  return std::max(1, std::min(ntiles, per_sm * ltvqkv_host::num_sms()));
+}
+}  // namespace
+
 extern "C" size_t ltvqkv_scan_workspace_bytes(int B, int T, int NH, int NKVH, int Da, int r) {
   if (validate_scan_shape(B, T, NH, NKVH, Da, r) != LTVQKV_OK) return 0;
   ScanGeometry gf = make_geometry(B, T, NH, NKVH, Da, r, kFwdBudget);
@@ -701,6 +736,31 @@ extern "C" int ltvqkv_scan_fwd(int dtype, const void* combined, int64_t sc_b, in
     e.B = B; e.T = T; e.NH = NH; e.NKVH = NKVH; e.Da = Da; e.r = r; e.D = g.D; e.H = g.H; e.use_sigmoid = use_sigmoid;
     int threads = (g.D + 31) / 32 * 32;
     scan_fwd_exact_kernel<<<(unsigned int)(B * g.H), threads, 0, s>>>(e);
+    return ltvqkv_host::check_launch();
+  }
+  if (dtype == LTVQKV_DTYPE_BF16 && fast_shape_ok(T, Da, r) && r % 32 == 0 &&
+      (long long)B * g.H >= 2LL * ltvqkv_host::num_sms() && tma_fwd_smem_bytes(g.D, Da) <= kMaxDynSmem &&
+      production_layout(combined, sc_b, sc_t, sc_e, T, g.F) && aligned16p(inits) &&
+      (NH == 0 || aligned16p(out_q)) && (NKVH == 0 || (aligned16p(out_k) && aligned16p(out_v)))) {
+    CUtensorMap tm_u, tm_l;
+    const uint64_t rows = (uint64_t)B * g.F;
+    if (!bf16_map_2d(&tm_u, combined, T, rows, kFastTT, g.D, true) ||
+        !bf16_map_2d(&tm_l, combined, T, rows, kFastTT, Da, false))
+      return LTVQKV_ERR_LAUNCH;
+    TmaFwdArgs f;
+    f.inits = reinterpret_cast<const __nv_bfloat16*>(inits); f.logit_bias = logit_bias;
+    f.out[0] = reinterpret_cast<__nv_bfloat16*>(out_q); f.out[1] = reinterpret_cast<__nv_bfloat16*>(out_k);
+    f.out[2] = reinterpret_cast<__nv_bfloat16*>(out_v);
+    f.B = B; f.T = T; f.NH = NH; f.NKVH = NKVH; f.Da = Da; f.r = r; f.D = g.D; f.H = g.H; f.F = g.F;
+    f.nchunks = (T + kFastTT - 1) / kFastTT; f.nrows = B * g.H; f.use_sigmoid = use_sigmoid;
+    f.ws = reinterpret_cast<WorkspaceHeader*>(ws);
+    const size_t tsm = tma_fwd_smem_bytes(g.D, Da);
+    const int threads = 2 * g.D + 32;
+    auto kern = threads <= 288 ? scan_fwd_rows_kernel<288> : scan_fwd_rows_kernel<544>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tsm) != cudaSuccess)
+      return ltvqkv_host::check_launch();
+    const int grid = persistent_grid((const void*)kern, threads, tsm, f.nrows);
+    kern<<<grid, threads, tsm, s>>>(tm_u, tm_l, f);
     return ltvqkv_host::check_launch();
   }
   if (dtype == LTVQKV_DTYPE_BF16 && sc_t == 1 && sc_e % 8 == 0 && sc_b % 8 == 0 && fast_shape_ok(T, Da, r) &&
@@ -818,6 +878,51 @@ extern "C" int ltvqkv_scan_bwd(int dtype, const void* combined, int64_t sc_b, in
     };
     const int tpg = r / 32;
     const bool r_ok = r % 32 == 0 && tpg >= 1 && (tpg & (tpg - 1)) == 0;
+    const int Fh = H * (D + Da);
+    if (dtype == LTVQKV_DTYPE_BF16 && r_ok && fast_shape_ok(T, Da, r) && tma_bwd_smem_bytes(D, Da) <= kMaxDynSmem &&
+        (long long)B * H >= 2LL * ltvqkv_host::num_sms() &&
+        production_layout(combined, sc_b, sc_t, sc_e, T, Fh) &&
+        production_layout(grad_combined, gc_b, gc_t, gc_e, T, Fh) && aligned16p(inits) &&
+        rows_ok(hq, hq_strides) && rows_ok(grad_hq, gq_strides) &&
+        (NKVH == 0 || (rows_ok(hk, hk_strides) && rows_ok(hv, hv_strides) && rows_ok(grad_hk, gk_strides) &&
+                       rows_ok(grad_hv, gv_strides)))) {
+      CUtensorMap tm_u, tm_l, tm_g[3], tm_h[3];
+      const uint64_t rows = (uint64_t)B * Fh;
+      bool ok = bf16_map_2d(&tm_u, combined, T, rows, kFastTT, D, true) &&
+                bf16_map_2d(&tm_l, combined, T, rows, kLogitBoxBwd, Da, false);
+      const void* hh[3] = {hq, hk, hv};
+      const void* gg[3] = {grad_hq, grad_hk, grad_hv};
+      const int64_t* hst[3] = {hq_strides, hk_strides, hv_strides};
+      const int64_t* gst[3] = {gq_strides, gk_strides, gv_strides};
+      const int heads[3] = {NH, NKVH, NKVH};
+      for (int i = 0; i < 3 && ok; ++i) {
+        const int src = heads[i] > 0 ? i : 0;  // unused groups reuse the q maps
+        ok = bf16_map_rows(&tm_g[i], gg[src], gst[src], B, heads[src], T, D) &&
+             bf16_map_rows(&tm_h[i], hh[src], hst[src], B, heads[src], T, D);
+      }
+      if (!ok) return LTVQKV_ERR_LAUNCH;
+      const ScanWorkspaceLayout wx = scan_ws_layout(fast_geometry(B, T, NH, NKVH, Da, r));
+      if (workspace_bytes < wx.total) return LTVQKV_ERR_WORKSPACE;
+      TmaBwdArgs f;
+      f.inits = reinterpret_cast<const __nv_bfloat16*>(inits); f.logit_bias = logit_bias;
+      f.grad_combined = reinterpret_cast<__nv_bfloat16*>(grad_combined);
+      f.grad_inits = reinterpret_cast<__nv_bfloat16*>(grad_inits);
+      f.bias_part = reinterpret_cast<float*>(ws + wx.bias_part);
+      f.B = B; f.T = T; f.NH = NH; f.NKVH = NKVH; f.Da = Da; f.r = r; f.D = D; f.H = H; f.F = Fh;
+      f.nchunks = (T + kFastTT - 1) / kFastTT; f.nrows = B * H; f.use_sigmoid = use_sigmoid;
+      f.ws = reinterpret_cast<WorkspaceHeader*>(ws);
+      const size_t tsm = tma_bwd_smem_bytes(D, Da);
+      const int threads = 2 * D + 32;
+      auto kern = threads <= 288 ? scan_bwd_rows_kernel<288> : scan_bwd_rows_kernel<544>;
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tsm) != cudaSuccess)
+        return ltvqkv_host::check_launch();
+      const int grid = persistent_grid((const void*)kern, threads, tsm, f.nrows);
+      kern<<<grid, threads, tsm, s>>>(tm_u, tm_l, tm_g[0], tm_g[1], tm_g[2], tm_h[0], tm_h[1], tm_h[2], f);
+      int rc = ltvqkv_host::check_launch();
+      if (rc != LTVQKV_OK) return rc;
+      bias_reduce_kernel<<<H * Da, kBiasReduceThreads, 0, s>>>(f.bias_part, grad_logit_bias, B, 1, H, Da);
+      return ltvqkv_host::check_launch();
+    }
     if (dtype == LTVQKV_DTYPE_BF16 && r_ok && fast_shape_ok(T, Da, r) && sc_t == 1 && sc_e % 8 == 0 &&
         sc_b % 8 == 0 && gc_t == 1 && gc_e % 8 == 0 && gc_b % 8 == 0 && aligned16p(combined) &&
         aligned16p(grad_combined) && aligned16p(inits) && rows_ok(hq, hq_strides) && rows_ok(grad_hq, gq_strides) &&

@@ -71,15 +71,43 @@ struct FastBwdArgs {
   float* inclX;
 };
 
-// Waits (thread 0) for the flags of chunks [first, last) of row bh in the given visiting order.
-LTVQKV_DEVICE bool wait_flags_range(const unsigned int* flags, int BH, int bh, int nchunks, int m, int j, bool reverse,
-                                    unsigned int epoch, WorkspaceHeader* ws) {
+// Warp 0 waits for the flags of chunk positions [m, j) of row bh (positions count from the end
+// when `reverse`), one lane per flag so the polls overlap; returns (to every lane of warp 0)
+// whether any wait gave up. j - m <= kAnchorStride <= 32.
+LTVQKV_DEVICE bool warp_wait_flags(const unsigned int* flags, int BH, int bh, int nchunks, int m, int j, bool reverse,
+                                   unsigned int epoch, WorkspaceHeader* ws, int lane) {
   bool timed_out = false;
-  for (int k = m; k < j && !timed_out; ++k) {
+  const int k = m + lane;
+  if (k < j) {
     const int chunk = reverse ? nchunks - 1 - k : k;
     wait_flag(&flags[(long long)chunk * BH + bh], epoch, ws, &timed_out);
   }
-  return timed_out;
+  return __any_sync(0xffffffffu, timed_out);
+}
+
+// Carry-in of a tile: the anchor's inclusive carry composed with the aggregates of the positions
+// between, in position order. All payload loads are issued before the composition.
+LTVQKV_DEVICE float compose_carry(const float* inclX, const float* aggA, const float* aggX, int BH, int bh,
+                                  int nchunks, int m, int j, bool reverse, int D, int Da, int c, int gi) {
+  float X[kAnchorStride], A[kAnchorStride];
+#pragma unroll
+  for (int q = 0; q < kAnchorStride; ++q) {
+    const int k = m + q;
+    const long long p = (long long)(reverse ? nchunks - 1 - k : k) * BH + bh;
+    X[q] = 0.f;
+    A[q] = 1.f;
+    if (q == 0) {
+      X[q] = ld_cg_f32(&inclX[p * D + c]);
+    } else if (k < j) {
+      X[q] = ld_cg_f32(&aggX[p * D + c]);
+      A[q] = ld_cg_f32(&aggA[p * Da + gi]);
+    }
+  }
+  float E = X[0];
+#pragma unroll
+  for (int q = 1; q < kAnchorStride; ++q)
+    if (m + q < j) E = A[q] * E + X[q];
+  return E;
 }
 
 // ------------------------------------------------------------------------------------------
@@ -162,19 +190,14 @@ __global__ void __launch_bounds__(512) scan_fwd_fast_kernel(FastFwdArgs a) {
       if (tid == 0) st_release_u32(&a.flags[tile_idx], (epoch << 2) | kFlagAgg);
     }
     const int m = (j - 1) / kAnchorStride * kAnchorStride;
-    if (tid == 0) sh_timeout = wait_flags_range(a.flags, BH, bh, a.nchunks, m, j, false, epoch, a.ws);
-    __syncthreads();
-    if (s == 1) {
-      float E = 0.f;
-      if (!sh_timeout) {
-        E = ld_cg_f32(&a.inclX[((long long)m * BH + bh) * D + c]);
-        for (int k = m + 1; k < j; ++k) {
-          const long long p = (long long)k * BH + bh;
-          E = ld_cg_f32(&a.aggA[p * Da + c / a.r]) * E + ld_cg_f32(&a.aggX[p * D + c]);
-        }
-      }
-      shE[c] = E;
+    if (tid < 32) {
+      const bool to = warp_wait_flags(a.flags, BH, bh, a.nchunks, m, j, false, epoch, a.ws, lane);
+      if (tid == 0) sh_timeout = to;
     }
+    __syncthreads();
+    if (s == 1)
+      shE[c] = sh_timeout ? 0.f
+                          : compose_carry(a.inclX, a.aggA, a.aggX, BH, bh, a.nchunks, m, j, false, D, Da, c, c / a.r);
   }
   if (is_anchor) {
     if (s == 1) {
@@ -316,19 +339,14 @@ __global__ void __launch_bounds__(512) scan_bwd_fast_kernel(FastBwdArgs a) {
       if (tid == 0) st_release_u32(&a.flags[tile_idx], (epoch << 2) | kFlagAgg);
     }
     const int mr = (rj - 1) / kAnchorStride * kAnchorStride;
-    if (tid == 0) sh_timeout = wait_flags_range(a.flags, BH, bh, a.nchunks, mr, rj, true, epoch, a.ws);
-    __syncthreads();
-    if (s == 0) {
-      float E = 0.f;
-      if (!sh_timeout) {
-        E = ld_cg_f32(&a.inclX[((long long)(a.nchunks - 1 - mr) * BH + bh) * D + c]);
-        for (int rk = mr + 1; rk < rj; ++rk) {
-          const long long p = (long long)(a.nchunks - 1 - rk) * BH + bh;
-          E = ld_cg_f32(&a.aggA[p * Da + gi]) * E + ld_cg_f32(&a.aggX[p * D + c]);
-        }
-      }
-      shE[c] = E;
+    if (tid < 32) {
+      const bool to = warp_wait_flags(a.flags, BH, bh, a.nchunks, mr, rj, true, epoch, a.ws, lane);
+      if (tid == 0) sh_timeout = to;
     }
+    __syncthreads();
+    if (s == 0)
+      shE[c] = sh_timeout ? 0.f
+                          : compose_carry(a.inclX, a.aggA, a.aggX, BH, bh, a.nchunks, mr, rj, true, D, Da, c, gi);
   }
   if (is_anchor) {
     if (s == 0) {
@@ -340,36 +358,31 @@ __global__ void __launch_bounds__(512) scan_bwd_fast_kernel(FastBwdArgs a) {
   }
   __syncthreads();
 
-  // final reverse walk: g^_t for the segment, kept in registers
-  float ghat[kFastSeg];
+  // final reverse walk fused with the elementwise part: g^_t, du (t-contiguous row of
+  // grad_combined) and the dlogit terms, one token at a time from the end of the segment
   {
+    __nv_bfloat16* grow =
+        a.grad_combined + (long long)b * a.gc_b + (long long)(head_col + c) * a.gc_e + t0 + s * kFastSeg;
     float carry = (s == 1) ? shE[c] : a1 * shE[c] + x1;
 #pragma unroll
-    for (int t = kFastSeg - 1; t >= 0; --t) {
-      carry = (1.0f - al_row[t + 1]) * carry + __bfloat162float(G_s[(s * kFastSeg + t) * D + c]);
-      ghat[t] = carry;
-    }
-  }
-  if (t0 == 0 && s == 0)
-    a.grad_inits[((long long)b * a.H + h) * D + c] = __float2bfloat16_rn(ghat[0] * (1.0f - al_row[0]));
-
-  // elementwise: du (t-contiguous row of grad_combined) and the dlogit terms
-  __nv_bfloat16* grow = a.grad_combined + (long long)b * a.gc_b + (long long)(head_col + c) * a.gc_e + t0 + s * kFastSeg;
+    for (int k = 3; k >= 0; --k) {
+      float f[8], du[8];
+      unpack8(uv[k], f);
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    float f[8], du[8];
-    unpack8(uv[k], f);
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const int t = 8 * k + e;
-      const float al = al_row[t];
-      const float gh = ghat[t];
-      du[e] = al * gh;
-      const float hp = __bfloat162float(H_s[(s * kFastSeg + t) * D + c]);
-      const float dalpha = (f[e] - hp) * gh;
-      red[(s * kFastSeg + t) * D + c] = a.use_sigmoid ? dalpha * (al * (1.0f - al)) : dalpha;
+      for (int e = 7; e >= 0; --e) {
+        const int t = 8 * k + e;
+        const int tl = s * kFastSeg + t;
+        carry = (1.0f - al_row[t + 1]) * carry + __bfloat162float(G_s[tl * D + c]);
+        const float al = al_row[t];
+        du[e] = al * carry;
+        const float hp = __bfloat162float(H_s[tl * D + c]);
+        const float dalpha = (f[e] - hp) * carry;
+        red[tl * D + c] = a.use_sigmoid ? dalpha * (al * (1.0f - al)) : dalpha;
+      }
+      if (s * kFastSeg + 8 * k < tlen) *reinterpret_cast<uint4*>(grow + 8 * k) = pack8(du);
     }
-    if (s * kFastSeg + 8 * k < tlen) *reinterpret_cast<uint4*>(grow + 8 * k) = pack8(du);
+    if (t0 == 0 && s == 0)
+      a.grad_inits[((long long)b * a.H + h) * D + c] = __float2bfloat16_rn(carry * (1.0f - al_row[0]));
   }
   __syncthreads();
 

@@ -223,3 +223,12 @@ def test_scan_is_deterministic_run_to_run(cuda_device):
         again = run_scan(tc, ti, tb, 2, 2, 1, 128, True, *tg)
         for a, e in zip(again, first):
             assert torch.equal(a, e)
+
+
+# Many (batch, head) rows (>= 2 per SM slot) take the row-streaming kernels: a CTA walks whole
+# rows chunk by chunk with the carry in registers.
+@pytest.mark.parametrize("T", [64, 200, 520])
+@pytest.mark.parametrize("Da,r", [(1, 128), (2, 64)])
+def test_scan_row_streaming_path_vs_oracle(cuda_device, T, Da, r):
+    _check_vs_oracle(cuda_device, torch.bfloat16, B=64, T=T, NH=2, NKVH=2, Da=Da, r=r, seed=T + Da,
+                     transposed_qk=True)
