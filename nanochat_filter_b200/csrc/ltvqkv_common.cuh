@@ -191,6 +191,15 @@ LTVQKV_DEVICE void bulk_store(void* gdst, const void* smem_src, uint32_t bytes) 
                : "memory");
 }
 // Barrier among `count` threads (a multiple of 32) of the CTA, id 1..15 (0 is __syncthreads).
+// Plain (untiled) bulk copy global -> this CTA's shared memory, completing on `bar`; both
+// addresses 16-byte aligned, size a multiple of 16.
+LTVQKV_DEVICE void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
 LTVQKV_DEVICE void named_barrier(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }

@@ -669,22 +669,40 @@ bool production_layout(const void* p, int64_t sb, int64_t st, int64_t se, int T,
 }
 
 bool bf16_map_2d(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows, uint32_t box_cols, uint32_t box_rows,
-                 bool swizzle) {
+                 CUtensorMapSwizzle swizzle) {
   const uint64_t dims[2] = {cols, rows};
   const uint64_t strides[1] = {cols * 2};
   const uint32_t box[2] = {box_cols, box_rows};
-  return ltvqkv_host::encode_tiled_map(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box,
-                                       swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE);
+  return ltvqkv_host::encode_tiled_map(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box, swizzle);
 }
 
-// [B, heads, T, D] tensor with d unit stride as a 4-D map (d, t, head, b), box (D, 64, 1, 1).
-bool bf16_map_rows(CUtensorMap* m, const void* base, const int64_t* st, int B, int heads, int T, int D) {
+// [B, heads, T, D] tensor with d unit stride as a 4-D map (d, t, head, b), box (D, tt, 1, 1).
+bool bf16_map_rows(CUtensorMap* m, const void* base, const int64_t* st, int B, int heads, int T, int D, int tt) {
   const uint64_t dims[4] = {(uint64_t)D, (uint64_t)T, (uint64_t)heads, (uint64_t)B};
   const uint64_t strides[3] = {(uint64_t)st[2] * 2, (uint64_t)st[1] * 2, (uint64_t)st[0] * 2};
-  const uint32_t box[4] = {(uint32_t)D, (uint32_t)kFastTT, 1, 1};
+  const uint32_t box[4] = {(uint32_t)D, (uint32_t)tt, 1, 1};
   return ltvqkv_host::encode_tiled_map(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, base, dims, strides, box,
                                        CU_TENSOR_MAP_SWIZZLE_NONE);
 }
+
+// Row kernels by head dim (64, 128 or 256) and chunk length (32 or 64 tokens).
+template <int kTT>
+decltype(&scan_fwd_rows_kernel<128, 32>) row_fwd_kernel(int D) {
+  return D == 64 ? scan_fwd_rows_kernel<64, kTT> : (D == 128 ? scan_fwd_rows_kernel<128, kTT> : scan_fwd_rows_kernel<256, kTT>);
+}
+template <int kTT>
+decltype(&scan_bwd_rows_kernel<128, 32>) row_bwd_kernel(int D) {
+  return D == 64 ? scan_bwd_rows_kernel<64, kTT> : (D == 128 ? scan_bwd_rows_kernel<128, kTT> : scan_bwd_rows_kernel<256, kTT>);
+}
+// Chunk length of the row kernels: 64 tokens (128-byte value-tile rows) when every group spans
+// at least 64 channels, else 32. Ring depths: forward 3 stages (a stage returns to the producer
+// one chunk after it was consumed), backward 2. At head dim 128 with 64-token chunks that is
+// 4 forward CTAs per SM (the config-2 row count, B * heads = 576, resident in one wave) and
+// 2 backward CTAs per SM; measured on B200 against 32-token chunks and deeper rings, which
+// lose more to fewer resident rows than they gain in prefetch distance.
+int row_chunk_tokens(int r) { return r >= 64 ? 64 : 32; }
+constexpr int kRowFwdStages = 3;
+constexpr int kRowBwdStages = 2;
 
 int persistent_grid(const void* kernel, int threads, size_t smem, int ntiles) {
   int per_sm = 0;
@@ -738,25 +756,29 @@ extern "C" int ltvqkv_scan_fwd(int dtype, const void* combined, int64_t sc_b, in
     scan_fwd_exact_kernel<<<(unsigned int)(B * g.H), threads, 0, s>>>(e);
     return ltvqkv_host::check_launch();
   }
-  if (dtype == LTVQKV_DTYPE_BF16 && fast_shape_ok(T, Da, r) && r % 32 == 0 &&
-      (long long)B * g.H >= 2LL * ltvqkv_host::num_sms() && tma_fwd_smem_bytes(g.D, Da) <= kMaxDynSmem &&
+  const int rtt = row_chunk_tokens(r);
+  const int rst = kRowFwdStages;
+  if (dtype == LTVQKV_DTYPE_BF16 && fast_shape_ok(T, Da, r) && r >= rtt && r % 32 == 0 &&
+      (g.D == 64 || g.D == 128 || g.D == 256) && g.H * Da <= kRowMaxBias &&
+      (long long)B * g.H >= 2LL * ltvqkv_host::num_sms() &&
+      row_fwd_smem_bytes(g.D, Da, g.H, rtt, rst) <= kMaxDynSmem &&
       production_layout(combined, sc_b, sc_t, sc_e, T, g.F) && aligned16p(inits) &&
       (NH == 0 || aligned16p(out_q)) && (NKVH == 0 || (aligned16p(out_k) && aligned16p(out_v)))) {
     CUtensorMap tm_u, tm_l;
     const uint64_t rows = (uint64_t)B * g.F;
-    if (!bf16_map_2d(&tm_u, combined, T, rows, kFastTT, g.D, true) ||
-        !bf16_map_2d(&tm_l, combined, T, rows, kFastTT, Da, false))
+    if (!bf16_map_2d(&tm_u, combined, T, rows, rtt, g.D, rtt == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B) ||
+        !bf16_map_2d(&tm_l, combined, T, rows, rtt, Da, CU_TENSOR_MAP_SWIZZLE_NONE))
       return LTVQKV_ERR_LAUNCH;
     TmaFwdArgs f;
     f.inits = reinterpret_cast<const __nv_bfloat16*>(inits); f.logit_bias = logit_bias;
     f.out[0] = reinterpret_cast<__nv_bfloat16*>(out_q); f.out[1] = reinterpret_cast<__nv_bfloat16*>(out_k);
     f.out[2] = reinterpret_cast<__nv_bfloat16*>(out_v);
     f.B = B; f.T = T; f.NH = NH; f.NKVH = NKVH; f.Da = Da; f.r = r; f.D = g.D; f.H = g.H; f.F = g.F;
-    f.nchunks = (T + kFastTT - 1) / kFastTT; f.nrows = B * g.H; f.use_sigmoid = use_sigmoid;
+    f.nchunks = (T + rtt - 1) / rtt; f.nrows = B * g.H; f.use_sigmoid = use_sigmoid; f.stages = rst;
     f.ws = reinterpret_cast<WorkspaceHeader*>(ws);
-    const size_t tsm = tma_fwd_smem_bytes(g.D, Da);
-    const int threads = 2 * g.D + 32;
-    auto kern = threads <= 288 ? scan_fwd_rows_kernel<288> : scan_fwd_rows_kernel<544>;
+    const size_t tsm = row_fwd_smem_bytes(g.D, Da, g.H, rtt, rst);
+    const int threads = g.D + 32;
+    auto kern = rtt == 64 ? row_fwd_kernel<64>(g.D) : row_fwd_kernel<32>(g.D);
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tsm) != cudaSuccess)
       return ltvqkv_host::check_launch();
     const int grid = persistent_grid((const void*)kern, threads, tsm, f.nrows);
@@ -879,7 +901,10 @@ extern "C" int ltvqkv_scan_bwd(int dtype, const void* combined, int64_t sc_b, in
     const int tpg = r / 32;
     const bool r_ok = r % 32 == 0 && tpg >= 1 && (tpg & (tpg - 1)) == 0;
     const int Fh = H * (D + Da);
-    if (dtype == LTVQKV_DTYPE_BF16 && r_ok && fast_shape_ok(T, Da, r) && tma_bwd_smem_bytes(D, Da) <= kMaxDynSmem &&
+    const int rtt = row_chunk_tokens(r);
+    const int rst = kRowBwdStages;
+    if (dtype == LTVQKV_DTYPE_BF16 && r_ok && r >= rtt && (D == 64 || D == 128 || D == 256) && H * Da <= kRowMaxBias &&
+        fast_shape_ok(T, Da, r) && row_bwd_smem_bytes(D, Da, H, rtt, rst) <= kMaxDynSmem &&
         (long long)B * H >= 2LL * ltvqkv_host::num_sms() &&
         production_layout(combined, sc_b, sc_t, sc_e, T, Fh) &&
         production_layout(grad_combined, gc_b, gc_t, gc_e, T, Fh) && aligned16p(inits) &&
@@ -888,8 +913,9 @@ extern "C" int ltvqkv_scan_bwd(int dtype, const void* combined, int64_t sc_b, in
                        rows_ok(grad_hv, gv_strides)))) {
       CUtensorMap tm_u, tm_l, tm_g[3], tm_h[3];
       const uint64_t rows = (uint64_t)B * Fh;
-      bool ok = bf16_map_2d(&tm_u, combined, T, rows, kFastTT, D, true) &&
-                bf16_map_2d(&tm_l, combined, T, rows, kLogitBoxBwd, Da, false);
+      bool ok = bf16_map_2d(&tm_u, combined, T, rows, rtt, D,
+                            rtt == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B) &&
+                bf16_map_2d(&tm_l, combined, T, rows, row_bwd_logit_box(rtt), Da, CU_TENSOR_MAP_SWIZZLE_NONE);
       const void* hh[3] = {hq, hk, hv};
       const void* gg[3] = {grad_hq, grad_hk, grad_hv};
       const int64_t* hst[3] = {hq_strides, hk_strides, hv_strides};
@@ -897,8 +923,8 @@ extern "C" int ltvqkv_scan_bwd(int dtype, const void* combined, int64_t sc_b, in
       const int heads[3] = {NH, NKVH, NKVH};
       for (int i = 0; i < 3 && ok; ++i) {
         const int src = heads[i] > 0 ? i : 0;  // unused groups reuse the q maps
-        ok = bf16_map_rows(&tm_g[i], gg[src], gst[src], B, heads[src], T, D) &&
-             bf16_map_rows(&tm_h[i], hh[src], hst[src], B, heads[src], T, D);
+        ok = bf16_map_rows(&tm_g[i], gg[src], gst[src], B, heads[src], T, D, rtt) &&
+             bf16_map_rows(&tm_h[i], hh[src], hst[src], B, heads[src], T, D, rtt);
       }
       if (!ok) return LTVQKV_ERR_LAUNCH;
       const ScanWorkspaceLayout wx = scan_ws_layout(fast_geometry(B, T, NH, NKVH, Da, r));
@@ -909,11 +935,11 @@ extern "C" int ltvqkv_scan_bwd(int dtype, const void* combined, int64_t sc_b, in
       f.grad_inits = reinterpret_cast<__nv_bfloat16*>(grad_inits);
       f.bias_part = reinterpret_cast<float*>(ws + wx.bias_part);
       f.B = B; f.T = T; f.NH = NH; f.NKVH = NKVH; f.Da = Da; f.r = r; f.D = D; f.H = H; f.F = Fh;
-      f.nchunks = (T + kFastTT - 1) / kFastTT; f.nrows = B * H; f.use_sigmoid = use_sigmoid;
+      f.nchunks = (T + rtt - 1) / rtt; f.nrows = B * H; f.use_sigmoid = use_sigmoid; f.stages = rst;
       f.ws = reinterpret_cast<WorkspaceHeader*>(ws);
-      const size_t tsm = tma_bwd_smem_bytes(D, Da);
-      const int threads = 2 * D + 32;
-      auto kern = threads <= 288 ? scan_bwd_rows_kernel<288> : scan_bwd_rows_kernel<544>;
+      const size_t tsm = row_bwd_smem_bytes(D, Da, H, rtt, rst);
+      const int threads = D + 32;
+      auto kern = rtt == 64 ? row_bwd_kernel<64>(D) : row_bwd_kernel<32>(D);
       if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tsm) != cudaSuccess)
         return ltvqkv_host::check_launch();
       const int grid = persistent_grid((const void*)kern, threads, tsm, f.nrows);

@@ -3,29 +3,36 @@
 // buffer, so one 2-D tensor map [B*F rows, T columns] addresses every head's value and logit rows.
 //
 // A persistent CTA owns whole (batch, head) rows, drawn from a ticket counter, and walks each row
-// chunk by chunk (64 tokens; forward in time order, backward in reverse). The carry never leaves
-// registers: thread (c, s) holds channel c, tokens [32 s, 32 s + 32) of a chunk, and the two
-// threads of a channel are adjacent lanes that hand the carry over with one shuffle — no
-// look-back, no inter-CTA communication, results fixed by construction. One producer warp
-// streams the row's chunks into a ring of shared-memory stages with cp.async.bulk.tensor
-// (mbarrier full/empty pairs), so the next chunks' loads are in flight while the consumers scan
-// the current one; forward outputs leave as one contiguous 16 KB bulk store per chunk, backward
-// gradients as 16-byte vector stores. Chosen when there are enough rows to fill the GPU
-// (B * heads >= 2 * SMs); fewer, longer rows take the chunk-parallel look-back kernels.
-// Every wait is bounded (2 s) and reports LTVQKV_ERR_TIMEOUT through the workspace.
+// chunk by chunk (kTT = 32 or 64 tokens; forward in time order, backward in reverse). Consumer
+// thread c owns channel c and walks all kTT tokens of a chunk, so the carry never leaves its
+// register: no look-back, no inter-CTA communication, results fixed by construction. One producer
+// warp streams the row's chunks into a ring of shared-memory stages with cp.async.bulk.tensor
+// (mbarrier full/empty pairs): the value tile (128- or 64-byte swizzle), the logit rows, and at a
+// row's first chunk the row's initial state (plain bulk copy). The logit bias of every head sits
+// in shared memory for the whole launch, so no global load is on a chunk's critical path.
+//
+// Forward: the chunk's output tile [kTT][D] is written over the value tile it came from (every
+// value row is in registers by then) and leaves as one contiguous bulk store; the stage is handed
+// back to the producer once that store has read it (one chunk later).
+// Backward: the adjoint walk keeps the per-token dalpha terms for the upper half of the chunk in
+// the value tile's space and the lower half in registers until every thread is done with the
+// gradient tile G, then over G; the per-(group, token) sums read that fp32 table.
+// Chosen when there are enough rows to fill the GPU (B * heads >= 2 * SMs); fewer, longer rows
+// take the chunk-parallel look-back kernels. Every wait is bounded (2 s) and reports
+// LTVQKV_ERR_TIMEOUT through the workspace.
 #pragma once
 
 namespace ltvqkv {
 
-constexpr int kTmaFwdStages = 4;
-constexpr int kTmaBwdStages = 3;
-constexpr int kLogitBoxBwd = 72;  // 64 tokens + the next chunk's first, padded to 16 bytes
+constexpr int kRowMaxStages = 8;
+constexpr int kRowMaxBias = 4096;  // heads * Da logit-bias entries held in shared memory
 
 struct TmaFwdArgs {
   const __nv_bfloat16* inits;
   const float* logit_bias;
   __nv_bfloat16* out[3];
   int B, T, NH, NKVH, Da, r, D, H, F, nchunks, nrows, use_sigmoid;
+  int stages;  // shared-memory ring depth (2..kRowMaxStages)
   WorkspaceHeader* ws;
 };
 
@@ -36,59 +43,108 @@ struct TmaBwdArgs {
   __nv_bfloat16* grad_inits;
   float* bias_part;  // [B][H][Da]: one partial per row
   int B, T, NH, NKVH, Da, r, D, H, F, nchunks, nrows, use_sigmoid;
+  int stages;  // shared-memory ring depth (2..kRowMaxStages)
   WorkspaceHeader* ws;
 };
 
-__host__ __device__ inline int tma_fwd_stage_bytes(int D, int Da) { return ((D + Da) * 128 + 1023) / 1024 * 1024; }
-__host__ __device__ inline int tma_bwd_logit_bytes(int Da) { return (Da * kLogitBoxBwd * 2 + 127) / 128 * 128; }
-__host__ __device__ inline int tma_bwd_stage_bytes(int D, int Da) {
-  return (D * 128 + tma_bwd_logit_bytes(Da) + 2 * kFastTT * D * 2 + 1023) / 1024 * 1024;
+struct RowTile {  // written by the producer for each staged chunk; row < 0 ends the stream
+  int row, b, h, j, t0, tlen, which, hloc, nheads;
+};
+
+__host__ __device__ constexpr int row_align(int v, int a) { return (v + a - 1) / a * a; }
+// Logit box of the backward: the chunk's kTT tokens plus the next chunk's first, padded to 16 bytes.
+__host__ __device__ constexpr int row_bwd_logit_box(int tt) { return tt + 8; }
+
+// Forward stage: value tile [D][kTT] (swizzled) | logits [Da][kTT] | initial state [D].
+__host__ __device__ constexpr int row_fwd_logit_off(int D, int tt) { return D * tt * 2; }
+__host__ __device__ constexpr int row_fwd_init_off(int D, int Da, int tt) {
+  return row_fwd_logit_off(D, tt) + row_align(Da * tt * 2, 128);
 }
-inline size_t tma_fwd_smem_bytes(int D, int Da) {
-  return 1024 + (size_t)kTmaFwdStages * tma_fwd_stage_bytes(D, Da) + 2 * (size_t)kFastTT * D * 2 +
-         sizeof(float) * (size_t)Da * kFastTT + 16 * kTmaFwdStages + 64;
+__host__ __device__ constexpr int row_fwd_stage_bytes(int D, int Da, int tt) {
+  return row_align(row_fwd_init_off(D, Da, tt) + D * 2, 1024);
 }
-inline size_t tma_bwd_smem_bytes(int D, int Da) {
-  return 1024 + (size_t)kTmaBwdStages * tma_bwd_stage_bytes(D, Da) +
-         sizeof(float) * ((size_t)kFastTT * D + (size_t)Da * (kFastTT + 1) + (size_t)Da * kFastTT) +
-         16 * kTmaBwdStages + 64;
+// Backward stage: value tile [D][kTT] | logits [Da][kTT + 8] | G [kTT][D] | H [kTT][D] | initial state [D].
+__host__ __device__ constexpr int row_bwd_logit_off(int D, int tt) { return D * tt * 2; }
+__host__ __device__ constexpr int row_bwd_g_off(int D, int Da, int tt) {
+  return row_bwd_logit_off(D, tt) + row_align(Da * row_bwd_logit_box(tt) * 2, 128);
+}
+__host__ __device__ constexpr int row_bwd_h_off(int D, int Da, int tt) { return row_bwd_g_off(D, Da, tt) + tt * D * 2; }
+__host__ __device__ constexpr int row_bwd_init_off(int D, int Da, int tt) {
+  return row_bwd_h_off(D, Da, tt) + tt * D * 2;
+}
+__host__ __device__ constexpr int row_bwd_stage_bytes(int D, int Da, int tt) {
+  return row_align(row_bwd_init_off(D, Da, tt) + D * 2, 1024);
 }
 
-// 16-byte chunk `chunk` of row `row` in a 128-byte-swizzled tile of 64 bf16 per row.
-LTVQKV_DEVICE const uint4* sw128_chunk(const uint8_t* tile, int row, int chunk) {
-  return reinterpret_cast<const uint4*>(tile + row * 128 + ((chunk ^ (row & 7)) << 4));
+inline size_t row_fwd_smem_bytes(int D, int Da, int H, int tt, int stages) {
+  return 1024 + (size_t)stages * row_fwd_stage_bytes(D, Da, tt) + (size_t)row_align(H * Da, 4) * 4 +
+         (size_t)8 * Da * tt + sizeof(RowTile) * stages + 16 + 16 * stages + 64;
+}
+inline size_t row_bwd_smem_bytes(int D, int Da, int H, int tt, int stages) {
+  return 1024 + (size_t)stages * row_bwd_stage_bytes(D, Da, tt) + (size_t)row_align(H * Da, 4) * 4 +
+         (size_t)16 * Da * tt + 4 * 32 + sizeof(RowTile) * stages + 16 + 16 * stages + 64;
+}
+
+// Occupancy targets (CTAs per SM) for __launch_bounds__, from the Da = 1 shared-memory footprint
+// and a floor of 64 (forward) / 96 (backward) registers per thread.
+constexpr int row_min_blocks(int smem, int threads, int regs) {
+  const int by_smem = (225 * 1024) / smem;
+  const int by_regs = 65536 / (threads * regs);
+  const int b = by_smem < by_regs ? by_smem : by_regs;
+  return b < 1 ? 1 : (b > 8 ? 8 : b);
+}
+constexpr int row_fwd_min_blocks(int D, int tt) {
+  return row_min_blocks(4 * row_fwd_stage_bytes(D, 1, tt) + 3072, D + 32, 64);
+}
+constexpr int row_bwd_min_blocks(int D, int tt) {
+  return row_min_blocks(2 * row_bwd_stage_bytes(D, 1, tt) + 3072, D + 32, 96);
+}
+
+// 16-byte chunk k of row `row` in a tile of kTT bf16 per row, as TMA writes it with the 128-byte
+// (kTT = 64) or 64-byte (kTT = 32) swizzle.
+template <int kTT>
+LTVQKV_DEVICE const uint4* swz_chunk(const uint8_t* tile, int row, int k) {
+  if constexpr (kTT == 64) {
+    return reinterpret_cast<const uint4*>(tile + row * 128 + ((k ^ (row & 7)) << 4));
+  } else {
+    return reinterpret_cast<const uint4*>(tile + row * 64 + ((k ^ ((row >> 1) & 3)) << 4));
+  }
 }
 
 // ------------------------------------------------------------------------------------------
 // Forward
 // ------------------------------------------------------------------------------------------
-template <int kMaxThreads>
-__global__ void __launch_bounds__(kMaxThreads, 2)
+template <int kD, int kTT>  // head dim = consumer threads; constants, so smem offsets are immediates
+__global__ void __launch_bounds__(kD + 32, row_fwd_min_blocks(kD, kTT))
     scan_fwd_rows_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_constant__ CUtensorMap tm_l,
                          const TmaFwdArgs a) {
-  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  extern __shared__ __align__(16) unsigned char smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const int D = a.D, Da = a.Da;
-  const int ncons = 2 * D;
-  const int sbytes = tma_fwd_stage_bytes(D, Da);
+  constexpr int D = kD, ncons = kD;
+  const int S = a.stages;
+  const int Da = a.Da;
+  const int sbytes = row_fwd_stage_bytes(D, Da, kTT);
+  constexpr int loff = row_fwd_logit_off(D, kTT);
+  const int ioff = row_fwd_init_off(D, Da, kTT);
+  const int nlb = a.H * Da;
   uint8_t* stages = base;
-  __nv_bfloat16* out_s = reinterpret_cast<__nv_bfloat16*>(stages + kTmaFwdStages * sbytes);  // [2][64][D]
-  float* alpha_s = reinterpret_cast<float*>(out_s + 2 * kFastTT * D);                       // [Da][64]
-  int* tile_slot = reinterpret_cast<int*>(alpha_s + Da * kFastTT);                          // [stages]
-  uint64_t* full = reinterpret_cast<uint64_t*>(
-      (reinterpret_cast<uintptr_t>(tile_slot + kTmaFwdStages) + 7) & ~uintptr_t(7));
-  uint64_t* empty = full + kTmaFwdStages;
+  float* lb_s = reinterpret_cast<float*>(stages + S * sbytes);               // [H][Da]
+  float2* gates = reinterpret_cast<float2*>(lb_s + row_align(nlb, 4));       // [Da][kTT]: (1 - a, a)
+  RowTile* info = reinterpret_cast<RowTile*>(gates + Da * kTT);              // [S]
+  uint64_t* full = reinterpret_cast<uint64_t*>((reinterpret_cast<uintptr_t>(info + S) + 15) & ~uintptr_t(15));
+  uint64_t* empty = full + S;
   __shared__ volatile int abort_flag;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
-    for (int i = 0; i < kTmaFwdStages; ++i) {
+    for (int i = 0; i < S; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], ncons / 32);
+      mbar_init(&empty[i], 1);  // released by thread 0 once the chunk's bulk store has read the stage
     }
     abort_flag = 0;
     fence_mbar_init();
   }
+  for (int q = tid; q < nlb; q += blockDim.x) lb_s[q] = a.logit_bias[q];
   __syncthreads();
 
   if (warp == ncons / 32) {
@@ -102,106 +158,87 @@ __global__ void __launch_bounds__(kMaxThreads, 2)
         int row = (int)draw_ticket(a.ws);
         if (row >= a.nrows) row = -1;
         const int nch = row < 0 ? 1 : a.nchunks;
+        const int b = row < 0 ? 0 : row / a.H, h = row < 0 ? 0 : row % a.H;
+        int which = 0, hloc = 0, nheads = 0;
+        if (row >= 0) split_head(h, a.NH, a.NKVH, which, hloc, nheads);
+        const int frow = b * a.F + h * (D + Da);
         for (int j = 0; j < nch; ++j, ++i) {
-          const int st = i % kTmaFwdStages;
-          const uint32_t ph = (uint32_t)(i / kTmaFwdStages) & 1u;
+          const int st = i % S;
+          const uint32_t ph = (uint32_t)(i / S) & 1u;
           if (!mbar_wait(&empty[st], ph ^ 1u, &abort_flag, a.ws, 0x7101)) { ok = false; break; }
+          RowTile& ti = info[st];
+          ti.row = row;
           if (row < 0) {
-            tile_slot[st] = -1;
             mbar_arrive(&full[st]);
             ok = false;
             break;
           }
-          tile_slot[st] = row * a.nchunks + j;
-          const int b = row / a.H, h = row % a.H;
-          const int frow = b * a.F + h * (D + Da);
+          ti.b = b; ti.h = h; ti.j = j; ti.t0 = j * kTT; ti.tlen = min(kTT, a.T - j * kTT);
+          ti.which = which; ti.hloc = hloc; ti.nheads = nheads;
           uint8_t* sb = stages + st * sbytes;
-          mbar_arrive_expect_tx(&full[st], (uint32_t)((D + Da) * 128));
-          tma_load_2d(sb, &tm_u, &full[st], j * kFastTT, frow);
-          tma_load_2d(sb + D * 128, &tm_l, &full[st], j * kFastTT, frow + D);
+          const uint32_t bytes = (uint32_t)((D + Da) * kTT * 2 + (j == 0 ? D * 2 : 0));
+          mbar_arrive_expect_tx(&full[st], bytes);
+          tma_load_2d(sb, &tm_u, &full[st], j * kTT, frow);
+          tma_load_2d(sb + loff, &tm_l, &full[st], j * kTT, frow + D);
+          if (j == 0) bulk_load(sb + ioff, a.inits + ((long long)b * a.H + h) * D, D * 2, &full[st]);
         }
       }
     }
     __syncwarp();
   } else {
-    // ---------------- consumers ----------------
-    const int c = tid >> 1, s = tid & 1;
-    int buf = 0;
-    float E = 0.f;  // row carry (h at the end of the previous chunk), held by the s == 1 lane
+    // ---------------- consumers: thread c = channel ----------------
+    const int c = tid;
+    const int gi = c / a.r;
+    float E = 0.f;  // row carry: h at the last token of the previous chunk
     for (int i = 0;; ++i) {
-      const int st = i % kTmaFwdStages;
-      const uint32_t ph = (uint32_t)(i / kTmaFwdStages) & 1u;
+      const int st = i % S;
+      const uint32_t ph = (uint32_t)(i / S) & 1u;
       if (!mbar_wait(&full[st], ph, &abort_flag, a.ws, 0x7102)) break;
-      const int tile = tile_slot[st];
-      if (tile < 0) break;
-      const int row = tile / a.nchunks, j = tile % a.nchunks;
-      const int b = row / a.H, h = row % a.H;
-      const int t0 = j * kFastTT;
-      const int tlen = min(kFastTT, a.T - t0);
-      const uint8_t* sb = stages + st * sbytes;
-      if (j == 0 && s == 1) E = __bfloat162float(a.inits[((long long)b * a.H + h) * D + c]);
-      if (tid < Da * kFastTT) {
-        const int g = tid / kFastTT, t = tid % kFastTT;
-        float al = 0.f;
-        if (t < tlen) {
-          const float l = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(sb + D * 128 + g * 128)[t]) +
-                          a.logit_bias[h * Da + g];
+      const RowTile ti = info[st];
+      if (ti.row < 0) break;
+      uint8_t* sb = stages + st * sbytes;
+      if (ti.j == 0) E = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(sb + ioff)[c]);
+      if (tid < Da * kTT) {
+        const int g = tid / kTT, t = tid % kTT;
+        float al = 0.f;  // beyond T: identity steps
+        if (t < ti.tlen) {
+          const float l = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(sb + loff)[g * kTT + t]) +
+                          lb_s[ti.h * Da + g];
           al = a.use_sigmoid ? sigmoid_f32(l) : l;
         }
-        alpha_s[tid] = al;
+        gates[tid] = make_float2(1.0f - al, al);
       }
-      uint4 uv[4];
+      uint4 uv[kTT / 8];
 #pragma unroll
-      for (int k = 0; k < 4; ++k) uv[k] = *sw128_chunk(sb, c, 4 * s + k);
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[st]);
-      // out_s[buf] was last read by the bulk store issued two chunks ago
-      if (tid == 0) tma_store_wait_read1();
-      named_barrier(1, ncons);
+      for (int k = 0; k < kTT / 8; ++k) uv[k] = *swz_chunk<kTT>(sb, c, k);
+      named_barrier(1, ncons);  // gates ready; every value row is in registers
 
-      const float* al_row = alpha_s + (c / a.r) * kFastTT + s * kFastSeg;
-      float sa = 1.f, sx = 0.f;
-      if (s == 0) {  // the first segment's aggregate carries the chunk's entry value to its partner
+      // the output tile [kTT][D] overwrites the value tile
+      const float2* grow = gates + gi * kTT;
+      __nv_bfloat16* ob = reinterpret_cast<__nv_bfloat16*>(sb) + c;
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          float f[8];
-          unpack8(uv[k], f);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const float al = al_row[8 * k + e];
-            sx = (1.0f - al) * sx + al * f[e];
-            sa *= (1.0f - al);
-          }
-        }
-      }
-      const float a0 = __shfl_sync(0xffffffffu, sa, lane & ~1);
-      const float x0 = __shfl_sync(0xffffffffu, sx, lane & ~1);
-      const float Ec = __shfl_sync(0xffffffffu, E, lane | 1);
-      float carry = (s == 0) ? Ec : a0 * Ec + x0;
-
-      __nv_bfloat16* ob = out_s + buf * kFastTT * D;
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
+      for (int k = 0; k < kTT / 8; ++k) {
         float f[8];
         unpack8(uv[k], f);
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-          const float al = al_row[8 * k + e];
-          carry = (1.0f - al) * carry + al * f[e];
-          ob[(s * kFastSeg + 8 * k + e) * D + c] = __float2bfloat16_rn(carry);
+          const float2 g2 = grow[8 * k + e];
+          E = g2.x * E + g2.y * f[e];
+          ob[(8 * k + e) * D] = __float2bfloat16_rn(E);
         }
       }
-      if (s == 1) E = carry;
       fence_proxy_async_smem();
       named_barrier(1, ncons);
       if (tid == 0) {
-        int which, hloc, nheads;
-        split_head(h, a.NH, a.NKVH, which, hloc, nheads);
-        __nv_bfloat16* go = a.out[which] + (((long long)b * nheads + hloc) * a.T + t0) * D;
-        bulk_store(go, ob, (uint32_t)(tlen * D * 2));
+        __nv_bfloat16* o0 = ti.which == 0 ? a.out[0] : (ti.which == 1 ? a.out[1] : a.out[2]);
+        __nv_bfloat16* go = o0 + (((long long)ti.b * ti.nheads + ti.hloc) * a.T + ti.t0) * D;
+        bulk_store(go, sb, (uint32_t)(ti.tlen * D * 2));
         tma_store_commit();
+        if (i > 0) {  // the previous chunk's store has read its stage: hand it back
+          tma_store_wait_read1();
+          mbar_arrive(&empty[(i - 1) % S]);
+        }
       }
-      buf ^= 1;
     }
     if (tid == 0) tma_store_wait0();
   }
@@ -212,40 +249,42 @@ __global__ void __launch_bounds__(kMaxThreads, 2)
 // ------------------------------------------------------------------------------------------
 // Backward
 // ------------------------------------------------------------------------------------------
-template <int kMaxThreads>
-__global__ void __launch_bounds__(kMaxThreads, 1)
+template <int kD, int kTT>
+__global__ void __launch_bounds__(kD + 32, row_bwd_min_blocks(kD, kTT))
     scan_bwd_rows_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_constant__ CUtensorMap tm_l,
                          const __grid_constant__ CUtensorMap tm_gq, const __grid_constant__ CUtensorMap tm_gk,
                          const __grid_constant__ CUtensorMap tm_gv, const __grid_constant__ CUtensorMap tm_hq,
                          const __grid_constant__ CUtensorMap tm_hk, const __grid_constant__ CUtensorMap tm_hv,
                          const TmaBwdArgs a) {
-  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  extern __shared__ __align__(16) unsigned char smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const int D = a.D, Da = a.Da;
-  const int ncons = 2 * D;
-  const int sbytes = tma_bwd_stage_bytes(D, Da);
-  const int lbytes = tma_bwd_logit_bytes(Da);
+  constexpr int D = kD, ncons = kD, LB = row_bwd_logit_box(kTT);
+  const int S = a.stages;
+  const int Da = a.Da;
+  const int sbytes = row_bwd_stage_bytes(D, Da, kTT);
+  constexpr int loff = row_bwd_logit_off(D, kTT);
+  const int goff = row_bwd_g_off(D, Da, kTT), hoff = row_bwd_h_off(D, Da, kTT), ioff = row_bwd_init_off(D, Da, kTT);
+  const int nlb = a.H * Da;
   uint8_t* stages = base;
-  float* red = reinterpret_cast<float*>(stages + kTmaBwdStages * sbytes);  // [64][D]
-  float* alpha_s = red + kFastTT * D;                                      // [Da][65]
-  float* dlog_s = alpha_s + Da * (kFastTT + 1);                            // [Da][64]
-  int* tile_slot = reinterpret_cast<int*>(dlog_s + Da * kFastTT);
-  uint64_t* full = reinterpret_cast<uint64_t*>(
-      (reinterpret_cast<uintptr_t>(tile_slot + kTmaBwdStages) + 7) & ~uintptr_t(7));
-  uint64_t* empty = full + kTmaBwdStages;
+  float* lb_s = reinterpret_cast<float*>(stages + S * sbytes);               // [H][Da]
+  float4* gates = reinterpret_cast<float4*>(lb_s + row_align(nlb, 4));       // [Da][kTT]
+  float* wsum = reinterpret_cast<float*>(gates + Da * kTT);                  // [ncons / 32]
+  RowTile* info = reinterpret_cast<RowTile*>(wsum + 32);                     // [S]
+  uint64_t* full = reinterpret_cast<uint64_t*>((reinterpret_cast<uintptr_t>(info + S) + 15) & ~uintptr_t(15));
+  uint64_t* empty = full + S;
   __shared__ volatile int abort_flag;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
-    for (int i = 0; i < kTmaBwdStages; ++i) {
+    for (int i = 0; i < S; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], ncons / 32);
     }
     abort_flag = 0;
     fence_mbar_init();
   }
+  for (int q = tid; q < nlb; q += blockDim.x) lb_s[q] = a.logit_bias[q];
   __syncthreads();
-  const int ld_a = kFastTT + 1;
 
   if (warp == ncons / 32) {
     // ---------------- producer: rows from the ticket counter, chunks in reverse time order ----------------
@@ -258,148 +297,147 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
         int row = (int)draw_ticket(a.ws);
         if (row >= a.nrows) row = -1;
         const int nch = row < 0 ? 1 : a.nchunks;
+        const int b = row < 0 ? 0 : row / a.H, h = row < 0 ? 0 : row % a.H;
+        int which = 0, hloc = 0, nheads = 0;
+        if (row >= 0) split_head(h, a.NH, a.NKVH, which, hloc, nheads);
+        const int frow = b * a.F + h * (D + Da);
+        const CUtensorMap* mg = which == 0 ? &tm_gq : (which == 1 ? &tm_gk : &tm_gv);
+        const CUtensorMap* mh = which == 0 ? &tm_hq : (which == 1 ? &tm_hk : &tm_hv);
         for (int q = 0; q < nch; ++q, ++i) {
-          const int st = i % kTmaBwdStages;
-          const uint32_t ph = (uint32_t)(i / kTmaBwdStages) & 1u;
+          const int st = i % S;
+          const uint32_t ph = (uint32_t)(i / S) & 1u;
           if (!mbar_wait(&empty[st], ph ^ 1u, &abort_flag, a.ws, 0x7201)) { ok = false; break; }
+          RowTile& ti = info[st];
+          ti.row = row;
           if (row < 0) {
-            tile_slot[st] = -1;
             mbar_arrive(&full[st]);
             ok = false;
             break;
           }
           const int j = a.nchunks - 1 - q;
-          tile_slot[st] = row * a.nchunks + j;
-          const int b = row / a.H, h = row % a.H;
-          int which, hloc, nheads;
-          split_head(h, a.NH, a.NKVH, which, hloc, nheads);
-          const int frow = b * a.F + h * (D + Da);
-          const int t0 = j * kFastTT;
+          const int t0 = j * kTT;
+          ti.b = b; ti.h = h; ti.j = j; ti.t0 = t0; ti.tlen = min(kTT, a.T - t0);
+          ti.which = which; ti.hloc = hloc; ti.nheads = nheads;
           uint8_t* sb = stages + st * sbytes;
-          uint8_t* sl = sb + D * 128;
-          uint8_t* sg = sl + lbytes;
-          uint8_t* shh = sg + kFastTT * D * 2;
-          const CUtensorMap* mg = which == 0 ? &tm_gq : (which == 1 ? &tm_gk : &tm_gv);
-          const CUtensorMap* mh = which == 0 ? &tm_hq : (which == 1 ? &tm_hk : &tm_hv);
-          mbar_arrive_expect_tx(&full[st], (uint32_t)(D * 128 + Da * kLogitBoxBwd * 2 + 2 * kFastTT * D * 2));
+          const uint32_t bytes = (uint32_t)(D * kTT * 2 + Da * LB * 2 + 2 * kTT * D * 2 + (q == 0 ? D * 2 : 0));
+          mbar_arrive_expect_tx(&full[st], bytes);
           tma_load_2d(sb, &tm_u, &full[st], t0, frow);
-          tma_load_2d(sl, &tm_l, &full[st], t0, frow + D);
-          tma_load_4d(sg, mg, &full[st], 0, t0, hloc, b);
-          tma_load_4d(shh, mh, &full[st], 0, t0 - 1, hloc, b);
+          tma_load_2d(sb + loff, &tm_l, &full[st], t0, frow + D);
+          tma_load_4d(sb + goff, mg, &full[st], 0, t0, hloc, b);
+          tma_load_4d(sb + hoff, mh, &full[st], 0, t0 - 1, hloc, b);
+          if (q == 0) bulk_load(sb + ioff, a.inits + ((long long)b * a.H + h) * D, D * 2, &full[st]);
         }
       }
     }
     __syncwarp();
   } else {
-    // ---------------- consumers ----------------
-    const int c = tid >> 1, s = tid & 1;
+    // ---------------- consumers: thread c = channel ----------------
+    const int c = tid;
     const int gi = c / a.r;
-    float Eg = 0.f;        // g^ at the first token of the previously processed chunk (s == 0 lane)
-    float bias_acc = 0.f;  // lane 0 of warp g < Da: the row's logit-bias gradient of group g
+    const int tpp = a.r / kTT;  // threads per (group, token) pair in the group sums
+    const int pair = tid / tpp, part = tid % tpp;
+    const int pg = pair / kTT, pt = pair % kTT;
+    float carry = 0.f;   // adjoint of h at the first token of the previously processed chunk
+    __nv_bfloat16 init_c = __float2bfloat16_rn(0.f);  // h_{-1} of this channel
+    float bias_t = 0.f;  // part == 0: this row's sum of dlogit at token offset pt of group pg
     for (int i = 0;; ++i) {
-      const int st = i % kTmaBwdStages;
-      const uint32_t ph = (uint32_t)(i / kTmaBwdStages) & 1u;
+      const int st = i % S;
+      const uint32_t ph = (uint32_t)(i / S) & 1u;
       if (!mbar_wait(&full[st], ph, &abort_flag, a.ws, 0x7202)) break;
-      const int tile = tile_slot[st];
-      if (tile < 0) break;
-      const int row = tile / a.nchunks, j = tile % a.nchunks;
-      const int b = row / a.H, h = row % a.H;
-      const int t0 = j * kFastTT;
-      const int tlen = min(kFastTT, a.T - t0);
-      if (j == a.nchunks - 1) {
-        Eg = 0.f;
-        bias_acc = 0.f;
+      const RowTile ti = info[st];
+      if (ti.row < 0) break;
+      const long long rowbase = (long long)ti.b * a.H + ti.h;
+      uint8_t* sb = stages + st * sbytes;
+      if (ti.j == a.nchunks - 1) {
+        carry = 0.f;
+        bias_t = 0.f;
+        init_c = reinterpret_cast<const __nv_bfloat16*>(sb + ioff)[c];
       }
-      const uint8_t* sb = stages + st * sbytes;
-      const __nv_bfloat16* L_s = reinterpret_cast<const __nv_bfloat16*>(sb + D * 128);
-      const __nv_bfloat16* G_s = reinterpret_cast<const __nv_bfloat16*>(sb + D * 128 + lbytes);
-      const __nv_bfloat16* H_s = G_s + kFastTT * D;
-      for (int q = tid; q < Da * ld_a; q += ncons) {
-        const int g = q / ld_a, t = q % ld_a;
-        float al = 0.f;
-        if (t <= tlen && t0 + t < a.T) {
-          const float l = __bfloat162float(L_s[g * kLogitBoxBwd + t]) + a.logit_bias[h * Da + g];
+      const __nv_bfloat16* L_s = reinterpret_cast<const __nv_bfloat16*>(sb + loff);
+      const __nv_bfloat16* G_s = reinterpret_cast<const __nv_bfloat16*>(sb + goff);
+      __nv_bfloat16* H_s = reinterpret_cast<__nv_bfloat16*>(sb + hoff);
+      // h_{t-1} of the row's first token is the initial state (the tile's row -1 was filled with 0)
+      if (ti.t0 == 0) H_s[c] = init_c;
+      for (int q = tid; q < Da * kTT; q += ncons) {
+        const int g = q / kTT, t = q % kTT;
+        const float lb = lb_s[ti.h * Da + g];
+        float al = 0.f, an = 0.f;  // alpha_t and alpha_{t+1}; identity steps beyond T
+        if (t < ti.tlen) {
+          const float l = __bfloat162float(L_s[g * LB + t]) + lb;
           al = a.use_sigmoid ? sigmoid_f32(l) : l;
         }
-        alpha_s[q] = al;
+        if (ti.t0 + t + 1 < a.T) {
+          const float l = __bfloat162float(L_s[g * LB + t + 1]) + lb;
+          an = a.use_sigmoid ? sigmoid_f32(l) : l;
+        }
+        gates[q] = make_float4(1.0f - an, al, a.use_sigmoid ? al * (1.0f - al) : 1.0f, 0.f);
       }
-      uint4 uv[4];
+      uint4 uv[kTT / 8];
 #pragma unroll
-      for (int k = 0; k < 4; ++k) uv[k] = *sw128_chunk(sb, c, 4 * s + k);
+      for (int k = 0; k < kTT / 8; ++k) uv[k] = *swz_chunk<kTT>(sb, c, k);
+      named_barrier(1, ncons);  // gates ready; every value row is in registers
+
+      // reverse walk: adjoint carry, du, and the per-token dalpha terms
+      const float4* grow = gates + gi * kTT;
+      __nv_bfloat16* urow = a.grad_combined + ((long long)ti.b * a.F + ti.h * (D + Da) + c) * a.T + ti.t0;
+      float* red_hi = reinterpret_cast<float*>(sb);         // [kTT/2][D]: tokens kTT/2.. over the value tile
+      float* red_lo = reinterpret_cast<float*>(sb + goff);  // [kTT/2][D]: tokens 0..kTT/2-1 over G
+      float da[kTT / 2];
+#pragma unroll
+      for (int k = kTT / 8 - 1; k >= 0; --k) {
+        float f[8], du[8];
+        unpack8(uv[k], f);
+#pragma unroll
+        for (int e = 7; e >= 0; --e) {
+          const int t = 8 * k + e;
+          const float4 gv = grow[t];
+          carry = gv.x * carry + __bfloat162float(G_s[t * D + c]);
+          du[e] = gv.y * carry;
+          const float d = (f[e] - __bfloat162float(H_s[t * D + c])) * carry * gv.z;
+          if (t >= kTT / 2) red_hi[(t - kTT / 2) * D + c] = d;
+          else da[t] = d;
+        }
+        if (8 * k < ti.tlen) *reinterpret_cast<uint4*>(urow + 8 * k) = pack8(du);
+      }
+      if (ti.t0 == 0) a.grad_inits[rowbase * D + c] = __float2bfloat16_rn(carry * (1.0f - grow[0].y));
+      named_barrier(1, ncons);  // every thread is done with G
+#pragma unroll
+      for (int t = 0; t < kTT / 2; ++t) red_lo[t * D + c] = da[t];
       named_barrier(1, ncons);
 
-      const float* al_row = alpha_s + gi * ld_a + s * kFastSeg;
-      float sa = 1.f, sx = 0.f;
-      if (s == 1) {  // the second segment's aggregate carries the chunk's exit value to its partner
-#pragma unroll
-        for (int t = kFastSeg - 1; t >= 0; --t) {
-          const float an = 1.0f - al_row[t + 1];
-          sx = an * sx + __bfloat162float(G_s[(s * kFastSeg + t) * D + c]);
-          sa *= an;
-        }
-      }
-      const float a1 = __shfl_sync(0xffffffffu, sa, lane | 1);
-      const float x1 = __shfl_sync(0xffffffffu, sx, lane | 1);
-      const float Ec = __shfl_sync(0xffffffffu, Eg, lane & ~1);
-
-      // final reverse walk fused with the elementwise part (g^_t, du, dlogit terms)
       {
-        const float init_c = __bfloat162float(a.inits[((long long)b * a.H + h) * D + c]);
-        __nv_bfloat16* grow = a.grad_combined + (long long)(b * a.F + h * (D + Da) + c) * a.T + t0 + s * kFastSeg;
-        float carry = (s == 1) ? Ec : a1 * Ec + x1;
+        const float* rbase = pt >= kTT / 2 ? red_hi + (pt - kTT / 2) * D : red_lo + pt * D;
+        const float4* rrow = reinterpret_cast<const float4*>(rbase + pg * a.r + part * kTT);
+        float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
 #pragma unroll
-        for (int k = 3; k >= 0; --k) {
-          float f[8], du[8];
-          unpack8(uv[k], f);
-#pragma unroll
-          for (int e = 7; e >= 0; --e) {
-            const int t = 8 * k + e;
-            const int tl = s * kFastSeg + t;
-            carry = (1.0f - al_row[t + 1]) * carry + __bfloat162float(G_s[tl * D + c]);
-            const float al = al_row[t];
-            du[e] = al * carry;
-            const float hp = (t0 + tl == 0) ? init_c : __bfloat162float(H_s[tl * D + c]);
-            const float dalpha = (f[e] - hp) * carry;
-            red[tl * D + c] = a.use_sigmoid ? dalpha * (al * (1.0f - al)) : dalpha;
-          }
-          if (s * kFastSeg + 8 * k < tlen) *reinterpret_cast<uint4*>(grow + 8 * k) = pack8(du);
+        for (int q = 0; q < kTT / 4; ++q) {
+          const float4 v = rrow[(q + lane) & (kTT / 4 - 1)];
+          s0 += v.x; s1 += v.y; s2 += v.z; s3 += v.w;
         }
-        if (s == 0) Eg = carry;
-        if (t0 == 0 && s == 0)
-          a.grad_inits[((long long)b * a.H + h) * D + c] = __float2bfloat16_rn(carry * (1.0f - al_row[0]));
+        float sum = (s0 + s1) + (s2 + s3);
+        for (int o = tpp >> 1; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        if (part == 0 && pt < ti.tlen) {
+          a.grad_combined[((long long)ti.b * a.F + ti.h * (D + Da) + D + pg) * a.T + ti.t0 + pt] =
+              __float2bfloat16_rn(sum);
+          bias_t += sum;
+        }
       }
+      fence_proxy_async_smem();  // order this thread's writes into the stage before the next TMA fill
       __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[st]);
-      named_barrier(1, ncons);
+      if (lane == 0) mbar_arrive(&empty[st]);  // the stage (and the dalpha table in it) is free
 
-      {
-        const int tpg = a.r / 32;
-        const int npairs = Da * kFastTT;
-        const int pair = tid / tpg, part = tid % tpg;
-        float sum = 0.f;
-        if (pair < npairs) {
-          const int g = pair / kFastTT, t = pair % kFastTT;
-          const float* rrow = red + t * D + g * a.r + part * 32;
-          const int rot = (t + part * (32 / tpg)) & 31;
-#pragma unroll 8
-          for (int q = 0; q < 32; ++q) sum += rrow[(q + rot) & 31];
-        }
-        for (int o = tpg >> 1; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-        if (pair < npairs && part == 0) {
-          const int g = pair / kFastTT, t = pair % kFastTT;
-          dlog_s[g * kFastTT + t] = sum;
-          if (t < tlen)
-            a.grad_combined[(long long)(b * a.F + h * (D + Da) + D + g) * a.T + t0 + t] = __float2bfloat16_rn(sum);
-        }
-      }
-      named_barrier(1, ncons);
-      if (warp < Da) {
-        float v = 0.f;
-        for (int t = lane; t < kFastTT; t += 32) v += (t < tlen) ? dlog_s[warp * kFastTT + t] : 0.f;
+      if (ti.j == 0) {  // row done: this row's logit-bias partials, a fixed-order sum per group
+        float v = part == 0 ? bias_t : 0.f;
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-        bias_acc += v;
-        if (j == 0 && lane == 0) a.bias_part[((long long)b * a.H + h) * Da + warp] = bias_acc;
+        if (lane == 0) wsum[warp] = v;
+        named_barrier(1, ncons);
+        if (tid < Da) {
+          const int wpg = a.r / 32;  // warps per group
+          float t = 0.f;
+          for (int w = 0; w < wpg; ++w) t += wsum[tid * wpg + w];
+          a.bias_part[rowbase * Da + tid] = t;
+        }
       }
     }
   }

@@ -228,7 +228,13 @@ def test_scan_is_deterministic_run_to_run(cuda_device):
 # Many (batch, head) rows (>= 2 per SM slot) take the row-streaming kernels: a CTA walks whole
 # rows chunk by chunk with the carry in registers.
 @pytest.mark.parametrize("T", [64, 200, 520])
-@pytest.mark.parametrize("Da,r", [(1, 128), (2, 64)])
+@pytest.mark.parametrize("Da,r", [(1, 128), (2, 64), (4, 32), (1, 64), (2, 128), (1, 256)])
 def test_scan_row_streaming_path_vs_oracle(cuda_device, T, Da, r):
     _check_vs_oracle(cuda_device, torch.bfloat16, B=64, T=T, NH=2, NKVH=2, Da=Da, r=r, seed=T + Da,
                      transposed_qk=True)
+
+
+# A ragged last chunk (1000 = 15 * 64 + 40) on the row-streaming path, head dim 128.
+def test_scan_row_streaming_ragged_tail(cuda_device):
+    _check_vs_oracle(cuda_device, torch.bfloat16, B=60, T=1000, NH=3, NKVH=1, Da=1, r=128, seed=5,
+                     transposed_qk=False)
