@@ -362,7 +362,7 @@ def run_ours(args, cfg):
                 "d2h_bytes_per_step": d2h_bytes, "steps": K2,
                 "path": "LtvCudaFusedConcatHeadMajorRegisterCastBlellochScanQkvFilter forward + autograd backward"},
         "gpu_launches": 5 * K,
-        "roofline": {"bound": "tensor", "kernel": "gemm_tc_kernel (projection backward: dx + dW)",
+        "roofline": {"bound": "tensor", "kernel": "gemm_pair_kernel (projection backward: dW + dx, CTA pairs)",
                      "achieved": round(achieved, 1), "peak": tc_peak, "unit": "TFLOP/s",
                      "frac": round(achieved / tc_peak, 4),
                      "traffic": traffic,

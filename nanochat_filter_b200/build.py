@@ -19,7 +19,7 @@ LIB_NAME = "libltvqkv.so"
 LIB_PATH = os.path.join(HERE, LIB_NAME)
 
 SOURCES = ["ltvqkv_abi.cu", "ltvqkv_scan.cu", "ltvqkv_gemm.cu", "ltvqkv_decode.cu"]
-HEADERS = ["ltvqkv_common.cuh"]
+HEADERS = sorted(f for f in os.listdir(CSRC) if f.endswith(".cuh"))
 
 NVCC_FLAGS = [
     "-gencode",

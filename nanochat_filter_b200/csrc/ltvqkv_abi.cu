@@ -44,6 +44,21 @@ bool encode_tiled_map(CUtensorMap* map, CUtensorMapDataType dtype, int rank, con
   }
   CUresult r = enc(map, dtype, (cuuint32_t)rank, const_cast<void*>(base), d, st, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
                    swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r == CUDA_ERROR_INVALID_CONTEXT) {
+    // A thread that has made no context-binding runtime call yet (e.g. an autograd worker thread)
+    // has no current context for the driver call: bind the runtime's primary context and retry.
+    cudaFree(nullptr);
+    r = enc(map, dtype, (cuuint32_t)rank, const_cast<void*>(base), d, st, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  }
+  if (r != CUDA_SUCCESS) {
+    // the status alone says "launch error"; keep what the driver rejected for the error text
+    snprintf(g_last_cuda_error, sizeof(g_last_cuda_error),
+             "cuTensorMapEncodeTiled: CUresult %d (rank %d, dims %llu x %llu x %llu, box %u x %u, swizzle %d)", (int)r,
+             rank, (unsigned long long)d[0], (unsigned long long)(rank > 1 ? d[1] : 1),
+             (unsigned long long)(rank > 2 ? d[2] : 1), (unsigned)bx[0], (unsigned)(rank > 1 ? bx[1] : 1),
+             (int)swizzle);
+  }
   return r == CUDA_SUCCESS;
 }
 

@@ -93,6 +93,44 @@ def test_gemm_fp32_master_weight_grad(cuda_device):
     assert max_rel_err(w.grad.cpu().numpy(), egw.cpu().numpy(), 1.0) <= 1e-5
 
 
+# Ragged tile edges: token counts and channel counts that are not multiples of the 256-row tiles
+# or 64-wide k-blocks, head-dim totals F that leave a narrow last column tile, odd batch counts
+# (the fp32 weight gradient is then reduced in one pass instead of two halves), both layouts.
+@pytest.mark.parametrize("B,T,K,F,grad_layout", [(5, 264, 200, 130, "contiguous"), (6, 136, 72, 40, "transposed"),
+                                                 (2, 1024, 768, 2322, "transposed"), (1, 8, 8, 8, "contiguous")])
+def test_gemm_ragged_shapes_fp32_weight_grad(cuda_device, B, T, K, F, grad_layout):
+    gen = torch.Generator(device=cuda_device).manual_seed(B + T + K + F)
+    x = (torch.randn(B, T, K, device=cuda_device, generator=gen) / K**0.5).to(torch.bfloat16)
+    w = (torch.randn(F, K, device=cuda_device, generator=gen) / K**0.5).to(torch.bfloat16)
+    g = torch.randn(B, F, T, device=cuda_device, generator=gen).to(torch.bfloat16)
+    if grad_layout == "transposed":
+        g = g.transpose(1, 2).contiguous().transpose(1, 2)
+    out = FLT(x, w)
+    gx = torch.empty_like(x)
+    gw = torch.full((F, K), float("nan"), device=cuda_device)  # fp32: every entry must be written
+    BWD(x, w, g, gx, gw)
+    eo, egx, egw = _reference(x, w, g)
+    assert max_rel_err(out.float().cpu().numpy(), eo.cpu().numpy()) <= 2e-2
+    assert max_rel_err(gx.float().cpu().numpy(), egx.cpu().numpy()) <= 2e-2
+    assert max_rel_err(gw.cpu().numpy(), egw.cpu().numpy(), 1.0) <= 1e-5
+
+
+def test_gemm_weight_grad_deterministic(cuda_device):
+    """The fp32 weight gradient taken in two batch halves is the same on every run."""
+    B, T, K, F = 8, 512, 768, 2322
+    gen = torch.Generator(device=cuda_device).manual_seed(3)
+    x = (torch.randn(B, T, K, device=cuda_device, generator=gen) / K**0.5).to(torch.bfloat16)
+    w = (torch.randn(F, K, device=cuda_device, generator=gen) / K**0.5).to(torch.bfloat16)
+    g = torch.randn(B, F, T, device=cuda_device, generator=gen).to(torch.bfloat16)
+    gx = torch.empty_like(x)
+    first = torch.empty(F, K, device=cuda_device)
+    BWD(x, w, g, gx, first)
+    for _ in range(3):
+        again = torch.empty(F, K, device=cuda_device)
+        BWD(x, w, g, gx, again)
+        assert torch.equal(again, first)
+
+
 def test_gemm_fp32_config1(cuda_device):
     """Config-1 projection shape in fp32 (CUDA-core fp32 products): max rel err <= 1e-5."""
     B, T, K, F = 2, 256, 768, 2322
