@@ -118,6 +118,14 @@ LTVQKV_DEVICE uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic
 // ------------------------------------------------------------------------------------------
 // mbarrier
 // ------------------------------------------------------------------------------------------
+// `p` advanced to the next multiple of `align` bytes (a power of two) of the shared window, by
+// pointer arithmetic: an integer round trip would hide from the compiler that the result points
+// into shared memory, turning every access through it into a generic one.
+template <typename T>
+LTVQKV_DEVICE T* smem_align(void* p, uint32_t align) {
+  unsigned char* c = reinterpret_cast<unsigned char*>(p);
+  return reinterpret_cast<T*>(c + ((align - (smem_u32(c) & (align - 1))) & (align - 1)));
+}
 LTVQKV_DEVICE void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
 }
@@ -202,6 +210,11 @@ LTVQKV_DEVICE void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, u
 }
 LTVQKV_DEVICE void named_barrier(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+LTVQKV_DEVICE void tma_store_2d(const CUtensorMap* m, const void* smem_src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(m),
+               "r"(smem_u32(smem_src)), "r"(c0), "r"(c1)
+               : "memory");
 }
 LTVQKV_DEVICE void tma_store_3d(const CUtensorMap* m, const void* smem_src, int c0, int c1, int c2) {
   asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(m),

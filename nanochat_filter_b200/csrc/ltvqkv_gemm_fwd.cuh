@@ -42,7 +42,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     gemm_fwd_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                     const __grid_constant__ CUtensorMap tmOut, const __grid_constant__ FwdParams prm) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* smem = smem_align<unsigned char>(smem_raw, 1024);
   unsigned char* stages = smem;
   unsigned char* epi = stages + kFwdStages * kFwdStageBytes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(epi + 4 * 2 * kFwdEpiBufBytes);

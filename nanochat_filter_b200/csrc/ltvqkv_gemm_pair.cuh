@@ -99,7 +99,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                      const __grid_constant__ CUtensorMap tmA1, const __grid_constant__ CUtensorMap tmB1,
                      const __grid_constant__ PairParams prm) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* smem = smem_align<unsigned char>(smem_raw, 1024);
   unsigned char* stages = smem;
   uint64_t* bars = reinterpret_cast<uint64_t*>(stages + kPairStages * kPairStageBytes);
   uint64_t* full_bar = bars;                           // [kPairStages] (leader's counts the pair's bytes)

@@ -694,13 +694,13 @@ template <int kTT>
 decltype(&scan_bwd_rows_kernel<128, 32>) row_bwd_kernel(int D) {
   return D == 64 ? scan_bwd_rows_kernel<64, kTT> : (D == 128 ? scan_bwd_rows_kernel<128, kTT> : scan_bwd_rows_kernel<256, kTT>);
 }
-// Chunk length of the row kernels: 64 tokens (128-byte value-tile rows) when every group spans
-// at least 64 channels, else 32. Ring depths: forward 3 stages (a stage returns to the producer
-// one chunk after it was consumed), backward 2. At head dim 128 with 64-token chunks that is
-// 4 forward CTAs per SM (the config-2 row count, B * heads = 576, resident in one wave) and
-// 2 backward CTAs per SM; measured on B200 against 32-token chunks and deeper rings, which
-// lose more to fewer resident rows than they gain in prefetch distance.
-int row_chunk_tokens(int r) { return r >= 64 ? 64 : 32; }
+// Chunk lengths and ring depths of the row kernels, measured on B200 at config 2 (576 rows, head
+// dim 128). Forward: 64-token chunks (128-byte value-tile rows; 32 when a decay group is narrower
+// than 64 channels) in a 3-stage ring, 4 CTAs per SM, so all rows are resident in one wave.
+// Backward: 32-token chunks in a 2-stage ring, 4 CTAs per SM; 64-token chunks fit only 2 CTAs per
+// SM (two waves of rows) and measured slower.
+int row_fwd_chunk_tokens(int r) { return r >= 64 ? 64 : 32; }
+int row_bwd_chunk_tokens(int /*r*/) { return 32; }
 constexpr int kRowFwdStages = 3;
 constexpr int kRowBwdStages = 2;
 
@@ -710,6 +710,119 @@ int persistent_grid(const void* kernel, int threads, size_t smem, int ntiles) {
     per_sm = 1;
   return std::max(1, std::min(ntiles, per_sm * ltvqkv_host::num_sms()));
 }
+// Whether the forward takes the row-streaming kernel (bf16, production layout, enough rows).
+bool row_fwd_applies(int dtype, const void* combined, int64_t sc_b, int64_t sc_t, int64_t sc_e, const void* inits,
+                     const void* out_q, const void* out_k, const void* out_v, int B, int T, int NH, int NKVH, int Da,
+                     int r) {
+  const int D = Da * r, H = NH + 2 * NKVH, F = H * (D + Da);
+  const int rtt = row_fwd_chunk_tokens(r);
+  return dtype == LTVQKV_DTYPE_BF16 && fast_shape_ok(T, Da, r) && r >= rtt && r % 32 == 0 &&
+         (D == 64 || D == 128 || D == 256) && H * Da <= kRowMaxBias &&
+         (long long)B * H >= 2LL * ltvqkv_host::num_sms() &&
+         row_fwd_smem_bytes(D, Da, H, rtt, kRowFwdStages) <= kMaxDynSmem &&
+         production_layout(combined, sc_b, sc_t, sc_e, T, F) && aligned16p(inits) &&
+         (NH == 0 || aligned16p(out_q)) && (NKVH == 0 || (aligned16p(out_k) && aligned16p(out_v)));
+}
+
+// Row-streaming forward when its conditions hold; `used` reports whether it ran.
+int try_row_fwd(bool& used, int dtype, const void* combined, int64_t sc_b, int64_t sc_t, int64_t sc_e,
+                const void* inits, const float* logit_bias, void* out_q, void* out_k, void* out_v, int B, int T, int NH,
+                int NKVH, int Da, int r, int use_sigmoid, char* ws, cudaStream_t s) {
+  used = false;
+  const int D = Da * r, H = NH + 2 * NKVH, F = H * (D + Da);
+  const int rtt = row_fwd_chunk_tokens(r);
+  const int rst = kRowFwdStages;
+  if (!row_fwd_applies(dtype, combined, sc_b, sc_t, sc_e, inits, out_q, out_k, out_v, B, T, NH, NKVH, Da, r)) return LTVQKV_OK;
+  used = true;
+  CUtensorMap tm_u, tm_l;
+  const uint64_t rows = (uint64_t)B * F;
+  if (!bf16_map_2d(&tm_u, combined, T, rows, rtt, D, rtt == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B) ||
+      !bf16_map_2d(&tm_l, combined, T, rows, rtt, Da, CU_TENSOR_MAP_SWIZZLE_NONE))
+    return LTVQKV_ERR_LAUNCH;
+  TmaFwdArgs f;
+  f.inits = reinterpret_cast<const __nv_bfloat16*>(inits); f.logit_bias = logit_bias;
+  f.out[0] = reinterpret_cast<__nv_bfloat16*>(out_q); f.out[1] = reinterpret_cast<__nv_bfloat16*>(out_k);
+  f.out[2] = reinterpret_cast<__nv_bfloat16*>(out_v);
+  f.B = B; f.T = T; f.NH = NH; f.NKVH = NKVH; f.Da = Da; f.r = r; f.D = D; f.H = H; f.F = F;
+  f.nchunks = (T + rtt - 1) / rtt; f.nrows = B * H; f.use_sigmoid = use_sigmoid; f.stages = rst;
+  f.ws = reinterpret_cast<WorkspaceHeader*>(ws);
+  const size_t tsm = row_fwd_smem_bytes(D, Da, H, rtt, rst);
+  const int threads = D + 32;
+  auto kern = rtt == 64 ? row_fwd_kernel<64>(D) : row_fwd_kernel<32>(D);
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tsm) != cudaSuccess)
+    return ltvqkv_host::check_launch();
+  const int grid = persistent_grid((const void*)kern, threads, tsm, f.nrows);
+  kern<<<grid, threads, tsm, s>>>(tm_u, tm_l, f);
+  return ltvqkv_host::check_launch();
+}
+
+// Row-streaming backward when its conditions hold; `used` reports whether it ran.
+int try_row_bwd(bool& used, int dtype, const void* combined, int64_t sc_b, int64_t sc_t, int64_t sc_e,
+                const void* inits, const float* logit_bias, const void* hq, const int64_t* hq_strides, const void* hk,
+                const int64_t* hk_strides, const void* hv, const int64_t* hv_strides, const void* grad_hq,
+                const int64_t* gq_strides, const void* grad_hk, const int64_t* gk_strides, const void* grad_hv,
+                const int64_t* gv_strides, void* grad_combined, int64_t gc_b, int64_t gc_t, int64_t gc_e,
+                void* grad_inits, float* grad_logit_bias, int B, int T, int NH, int NKVH, int Da, int r,
+                int use_sigmoid, char* ws, size_t workspace_bytes, cudaStream_t s) {
+  used = false;
+  auto rows_ok = [&](const void* p, const int64_t* st) {
+    return p == nullptr || (aligned16p(p) && st[3] == 1 && st[0] % 8 == 0 && st[1] % 8 == 0 && st[2] % 8 == 0);
+  };
+  const int H = NH + 2 * NKVH, D = Da * r;
+  const int tpg = r / 32;
+  const bool r_ok = r % 32 == 0 && tpg >= 1 && (tpg & (tpg - 1)) == 0;
+  const int Fh = H * (D + Da);
+  const int rtt = row_bwd_chunk_tokens(r);
+  const int rst = kRowBwdStages;
+  const size_t tsm = row_bwd_smem_bytes(D, Da, H, rtt, rst);
+  if (!(dtype == LTVQKV_DTYPE_BF16 && r_ok && r >= rtt && (D == 64 || D == 128 || D == 256) &&
+        H * Da <= kRowMaxBias && fast_shape_ok(T, Da, r) && tsm <= kMaxDynSmem &&
+        (long long)B * H >= 2LL * ltvqkv_host::num_sms() && production_layout(combined, sc_b, sc_t, sc_e, T, Fh) &&
+        production_layout(grad_combined, gc_b, gc_t, gc_e, T, Fh) && aligned16p(inits) &&
+        rows_ok(hq, hq_strides) && rows_ok(grad_hq, gq_strides) &&
+        (NKVH == 0 || (rows_ok(hk, hk_strides) && rows_ok(hv, hv_strides) && rows_ok(grad_hk, gk_strides) &&
+                       rows_ok(grad_hv, gv_strides)))))
+    return LTVQKV_OK;
+  used = true;
+  CUtensorMap tm_u, tm_du, tm_l, tm_g[3], tm_h[3];
+  const uint64_t rows = (uint64_t)B * Fh;
+  const CUtensorMapSwizzle tile_swz = rtt == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  bool ok = bf16_map_2d(&tm_u, combined, T, rows, rtt, D, tile_swz) &&
+            bf16_map_2d(&tm_du, grad_combined, T, rows, rtt, D, tile_swz) &&
+            bf16_map_2d(&tm_l, combined, T, rows, row_bwd_logit_box(rtt), Da, CU_TENSOR_MAP_SWIZZLE_NONE);
+  const void* hh[3] = {hq, hk, hv};
+  const void* gg[3] = {grad_hq, grad_hk, grad_hv};
+  const int64_t* hst[3] = {hq_strides, hk_strides, hv_strides};
+  const int64_t* gst[3] = {gq_strides, gk_strides, gv_strides};
+  const int heads[3] = {NH, NKVH, NKVH};
+  for (int i = 0; i < 3 && ok; ++i) {
+    const int src = heads[i] > 0 ? i : 0;  // unused groups reuse the q maps
+    ok = bf16_map_rows(&tm_g[i], gg[src], gst[src], B, heads[src], T, D, rtt) &&
+         bf16_map_rows(&tm_h[i], hh[src], hst[src], B, heads[src], T, D, rtt);
+  }
+  if (!ok) return LTVQKV_ERR_LAUNCH;
+  const ScanWorkspaceLayout wx = scan_ws_layout(fast_geometry(B, T, NH, NKVH, Da, r));
+  if (workspace_bytes < wx.total) return LTVQKV_ERR_WORKSPACE;
+  TmaBwdArgs f;
+  f.inits = reinterpret_cast<const __nv_bfloat16*>(inits); f.logit_bias = logit_bias;
+  f.grad_combined = reinterpret_cast<__nv_bfloat16*>(grad_combined);
+  f.grad_inits = reinterpret_cast<__nv_bfloat16*>(grad_inits);
+  f.bias_part = reinterpret_cast<float*>(ws + wx.bias_part);
+  f.B = B; f.T = T; f.NH = NH; f.NKVH = NKVH; f.Da = Da; f.r = r; f.D = D; f.H = H; f.F = Fh;
+  f.nchunks = (T + rtt - 1) / rtt; f.nrows = B * H; f.use_sigmoid = use_sigmoid; f.stages = rst;
+  f.ws = reinterpret_cast<WorkspaceHeader*>(ws);
+  const int threads = D + 32;
+  auto kern = rtt == 64 ? row_bwd_kernel<64>(D) : row_bwd_kernel<32>(D);
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tsm) != cudaSuccess)
+    return ltvqkv_host::check_launch();
+  const int grid = persistent_grid((const void*)kern, threads, tsm, f.nrows);
+  kern<<<grid, threads, tsm, s>>>(tm_u, tm_l, tm_du, tm_g[0], tm_g[1], tm_g[2], tm_h[0], tm_h[1], tm_h[2], f);
+  int rc = ltvqkv_host::check_launch();
+  if (rc != LTVQKV_OK) return rc;
+  bias_reduce_kernel<<<H * Da, kBiasReduceThreads, 0, s>>>(f.bias_part, grad_logit_bias, B, 1, H, Da);
+  return ltvqkv_host::check_launch();
+}
+
 }  // namespace
 
 extern "C" size_t ltvqkv_scan_workspace_bytes(int B, int T, int NH, int NKVH, int Da, int r) {
@@ -756,34 +869,11 @@ extern "C" int ltvqkv_scan_fwd(int dtype, const void* combined, int64_t sc_b, in
     scan_fwd_exact_kernel<<<(unsigned int)(B * g.H), threads, 0, s>>>(e);
     return ltvqkv_host::check_launch();
   }
-  const int rtt = row_chunk_tokens(r);
-  const int rst = kRowFwdStages;
-  if (dtype == LTVQKV_DTYPE_BF16 && fast_shape_ok(T, Da, r) && r >= rtt && r % 32 == 0 &&
-      (g.D == 64 || g.D == 128 || g.D == 256) && g.H * Da <= kRowMaxBias &&
-      (long long)B * g.H >= 2LL * ltvqkv_host::num_sms() &&
-      row_fwd_smem_bytes(g.D, Da, g.H, rtt, rst) <= kMaxDynSmem &&
-      production_layout(combined, sc_b, sc_t, sc_e, T, g.F) && aligned16p(inits) &&
-      (NH == 0 || aligned16p(out_q)) && (NKVH == 0 || (aligned16p(out_k) && aligned16p(out_v)))) {
-    CUtensorMap tm_u, tm_l;
-    const uint64_t rows = (uint64_t)B * g.F;
-    if (!bf16_map_2d(&tm_u, combined, T, rows, rtt, g.D, rtt == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B) ||
-        !bf16_map_2d(&tm_l, combined, T, rows, rtt, Da, CU_TENSOR_MAP_SWIZZLE_NONE))
-      return LTVQKV_ERR_LAUNCH;
-    TmaFwdArgs f;
-    f.inits = reinterpret_cast<const __nv_bfloat16*>(inits); f.logit_bias = logit_bias;
-    f.out[0] = reinterpret_cast<__nv_bfloat16*>(out_q); f.out[1] = reinterpret_cast<__nv_bfloat16*>(out_k);
-    f.out[2] = reinterpret_cast<__nv_bfloat16*>(out_v);
-    f.B = B; f.T = T; f.NH = NH; f.NKVH = NKVH; f.Da = Da; f.r = r; f.D = g.D; f.H = g.H; f.F = g.F;
-    f.nchunks = (T + rtt - 1) / rtt; f.nrows = B * g.H; f.use_sigmoid = use_sigmoid; f.stages = rst;
-    f.ws = reinterpret_cast<WorkspaceHeader*>(ws);
-    const size_t tsm = row_fwd_smem_bytes(g.D, Da, g.H, rtt, rst);
-    const int threads = g.D + 32;
-    auto kern = rtt == 64 ? row_fwd_kernel<64>(g.D) : row_fwd_kernel<32>(g.D);
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tsm) != cudaSuccess)
-      return ltvqkv_host::check_launch();
-    const int grid = persistent_grid((const void*)kern, threads, tsm, f.nrows);
-    kern<<<grid, threads, tsm, s>>>(tm_u, tm_l, f);
-    return ltvqkv_host::check_launch();
+  {
+    bool used = false;
+    const int rc = try_row_fwd(used, dtype, combined, sc_b, sc_t, sc_e, inits, logit_bias, out_q, out_k, out_v, B, T,
+                               NH, NKVH, Da, r, use_sigmoid, ws, s);
+    if (used) return rc;
   }
   if (dtype == LTVQKV_DTYPE_BF16 && sc_t == 1 && sc_e % 8 == 0 && sc_b % 8 == 0 && fast_shape_ok(T, Da, r) &&
       aligned16p(combined) && aligned16p(inits) && (NH == 0 || aligned16p(out_q)) &&
@@ -900,54 +990,13 @@ extern "C" int ltvqkv_scan_bwd(int dtype, const void* combined, int64_t sc_b, in
     };
     const int tpg = r / 32;
     const bool r_ok = r % 32 == 0 && tpg >= 1 && (tpg & (tpg - 1)) == 0;
-    const int Fh = H * (D + Da);
-    const int rtt = row_chunk_tokens(r);
-    const int rst = kRowBwdStages;
-    if (dtype == LTVQKV_DTYPE_BF16 && r_ok && r >= rtt && (D == 64 || D == 128 || D == 256) && H * Da <= kRowMaxBias &&
-        fast_shape_ok(T, Da, r) && row_bwd_smem_bytes(D, Da, H, rtt, rst) <= kMaxDynSmem &&
-        (long long)B * H >= 2LL * ltvqkv_host::num_sms() &&
-        production_layout(combined, sc_b, sc_t, sc_e, T, Fh) &&
-        production_layout(grad_combined, gc_b, gc_t, gc_e, T, Fh) && aligned16p(inits) &&
-        rows_ok(hq, hq_strides) && rows_ok(grad_hq, gq_strides) &&
-        (NKVH == 0 || (rows_ok(hk, hk_strides) && rows_ok(hv, hv_strides) && rows_ok(grad_hk, gk_strides) &&
-                       rows_ok(grad_hv, gv_strides)))) {
-      CUtensorMap tm_u, tm_l, tm_g[3], tm_h[3];
-      const uint64_t rows = (uint64_t)B * Fh;
-      bool ok = bf16_map_2d(&tm_u, combined, T, rows, rtt, D,
-                            rtt == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B) &&
-                bf16_map_2d(&tm_l, combined, T, rows, row_bwd_logit_box(rtt), Da, CU_TENSOR_MAP_SWIZZLE_NONE);
-      const void* hh[3] = {hq, hk, hv};
-      const void* gg[3] = {grad_hq, grad_hk, grad_hv};
-      const int64_t* hst[3] = {hq_strides, hk_strides, hv_strides};
-      const int64_t* gst[3] = {gq_strides, gk_strides, gv_strides};
-      const int heads[3] = {NH, NKVH, NKVH};
-      for (int i = 0; i < 3 && ok; ++i) {
-        const int src = heads[i] > 0 ? i : 0;  // unused groups reuse the q maps
-        ok = bf16_map_rows(&tm_g[i], gg[src], gst[src], B, heads[src], T, D, rtt) &&
-             bf16_map_rows(&tm_h[i], hh[src], hst[src], B, heads[src], T, D, rtt);
-      }
-      if (!ok) return LTVQKV_ERR_LAUNCH;
-      const ScanWorkspaceLayout wx = scan_ws_layout(fast_geometry(B, T, NH, NKVH, Da, r));
-      if (workspace_bytes < wx.total) return LTVQKV_ERR_WORKSPACE;
-      TmaBwdArgs f;
-      f.inits = reinterpret_cast<const __nv_bfloat16*>(inits); f.logit_bias = logit_bias;
-      f.grad_combined = reinterpret_cast<__nv_bfloat16*>(grad_combined);
-      f.grad_inits = reinterpret_cast<__nv_bfloat16*>(grad_inits);
-      f.bias_part = reinterpret_cast<float*>(ws + wx.bias_part);
-      f.B = B; f.T = T; f.NH = NH; f.NKVH = NKVH; f.Da = Da; f.r = r; f.D = D; f.H = H; f.F = Fh;
-      f.nchunks = (T + rtt - 1) / rtt; f.nrows = B * H; f.use_sigmoid = use_sigmoid; f.stages = rst;
-      f.ws = reinterpret_cast<WorkspaceHeader*>(ws);
-      const size_t tsm = row_bwd_smem_bytes(D, Da, H, rtt, rst);
-      const int threads = D + 32;
-      auto kern = rtt == 64 ? row_bwd_kernel<64>(D) : row_bwd_kernel<32>(D);
-      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tsm) != cudaSuccess)
-        return ltvqkv_host::check_launch();
-      const int grid = persistent_grid((const void*)kern, threads, tsm, f.nrows);
-      kern<<<grid, threads, tsm, s>>>(tm_u, tm_l, tm_g[0], tm_g[1], tm_g[2], tm_h[0], tm_h[1], tm_h[2], f);
-      int rc = ltvqkv_host::check_launch();
-      if (rc != LTVQKV_OK) return rc;
-      bias_reduce_kernel<<<H * Da, kBiasReduceThreads, 0, s>>>(f.bias_part, grad_logit_bias, B, 1, H, Da);
-      return ltvqkv_host::check_launch();
+    {
+      bool used = false;
+      const int rc = try_row_bwd(used, dtype, combined, sc_b, sc_t, sc_e, inits, logit_bias, hq, hq_strides, hk,
+                                 hk_strides, hv, hv_strides, grad_hq, gq_strides, grad_hk, gk_strides, grad_hv,
+                                 gv_strides, grad_combined, gc_b, gc_t, gc_e, grad_inits, grad_logit_bias, B, T, NH,
+                                 NKVH, Da, r, use_sigmoid, ws, workspace_bytes, s);
+      if (used) return rc;
     }
     if (dtype == LTVQKV_DTYPE_BF16 && r_ok && fast_shape_ok(T, Da, r) && sc_t == 1 && sc_e % 8 == 0 &&
         sc_b % 8 == 0 && gc_t == 1 && gc_e % 8 == 0 && gc_b % 8 == 0 && aligned16p(combined) &&
@@ -1000,6 +1049,7 @@ extern "C" int ltvqkv_scan_bwd(int dtype, const void* combined, int64_t sc_b, in
   bias_reduce_kernel<<<H * Da, kBiasReduceThreads, 0, s>>>(a.bias_part, grad_logit_bias, B, g.nchunks, H, Da);
   return ltvqkv_host::check_launch();
 }
+
 
 // ------------------------------------------------------------------------------------------
 // Allocation-free forward scan.

@@ -14,9 +14,11 @@
 // Forward: the chunk's output tile [kTT][D] is written over the value tile it came from (every
 // value row is in registers by then) and leaves as one contiguous bulk store; the stage is handed
 // back to the producer once that store has read it (one chunk later).
-// Backward: the adjoint walk keeps the per-token dalpha terms for the upper half of the chunk in
-// the value tile's space and the lower half in registers until every thread is done with the
-// gradient tile G, then over G; the per-(group, token) sums read that fp32 table.
+// Backward: thread c alone reads its channel's slots of the chunk's value tile (16 bytes per 8
+// tokens), gradient tile G and state tile H (2 bytes per token each), so once it has read them it
+// reuses them: du goes back into the value-tile slot (the tile then leaves as one bulk tensor store
+// into grad_combined) and dalpha(t, c) as an fp32 split into its high and low halves into G[t][c]
+// and H[t][c]; the per-(group, token) sums read that table after one barrier.
 // Chosen when there are enough rows to fill the GPU (B * heads >= 2 * SMs); fewer, longer rows
 // take the chunk-parallel look-back kernels. Every wait is bounded (2 s) and reports
 // LTVQKV_ERR_TIMEOUT through the workspace.
@@ -85,6 +87,7 @@ inline size_t row_bwd_smem_bytes(int D, int Da, int H, int tt, int stages) {
          (size_t)16 * Da * tt + 4 * 32 + sizeof(RowTile) * stages + 16 + 16 * stages + 64;
 }
 
+
 // Occupancy targets (CTAs per SM) for __launch_bounds__, from the Da = 1 shared-memory footprint
 // and a floor of 64 (forward) / 96 (backward) registers per thread.
 constexpr int row_min_blocks(int smem, int threads, int regs) {
@@ -99,6 +102,7 @@ constexpr int row_fwd_min_blocks(int D, int tt) {
 constexpr int row_bwd_min_blocks(int D, int tt) {
   return row_min_blocks(2 * row_bwd_stage_bytes(D, 1, tt) + 3072, D + 32, 96);
 }
+
 
 // 16-byte chunk k of row `row` in a tile of kTT bf16 per row, as TMA writes it with the 128-byte
 // (kTT = 64) or 64-byte (kTT = 32) swizzle.
@@ -119,7 +123,7 @@ __global__ void __launch_bounds__(kD + 32, row_fwd_min_blocks(kD, kTT))
     scan_fwd_rows_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_constant__ CUtensorMap tm_l,
                          const TmaFwdArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* base = smem_align<uint8_t>(smem_raw, 1024);
   constexpr int D = kD, ncons = kD;
   const int S = a.stages;
   const int Da = a.Da;
@@ -131,7 +135,7 @@ __global__ void __launch_bounds__(kD + 32, row_fwd_min_blocks(kD, kTT))
   float* lb_s = reinterpret_cast<float*>(stages + S * sbytes);               // [H][Da]
   float2* gates = reinterpret_cast<float2*>(lb_s + row_align(nlb, 4));       // [Da][kTT]: (1 - a, a)
   RowTile* info = reinterpret_cast<RowTile*>(gates + Da * kTT);              // [S]
-  uint64_t* full = reinterpret_cast<uint64_t*>((reinterpret_cast<uintptr_t>(info + S) + 15) & ~uintptr_t(15));
+  uint64_t* full = smem_align<uint64_t>(info + S, 16);
   uint64_t* empty = full + S;
   __shared__ volatile int abort_flag;
 
@@ -223,7 +227,7 @@ __global__ void __launch_bounds__(kD + 32, row_fwd_min_blocks(kD, kTT))
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
           const float2 g2 = grow[8 * k + e];
-          E = g2.x * E + g2.y * f[e];
+          E = __fmaf_rn(g2.x, E, __fmul_rn(g2.y, f[e]));
           ob[(8 * k + e) * D] = __float2bfloat16_rn(E);
         }
       }
@@ -252,12 +256,13 @@ __global__ void __launch_bounds__(kD + 32, row_fwd_min_blocks(kD, kTT))
 template <int kD, int kTT>
 __global__ void __launch_bounds__(kD + 32, row_bwd_min_blocks(kD, kTT))
     scan_bwd_rows_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_constant__ CUtensorMap tm_l,
+                         const __grid_constant__ CUtensorMap tm_du,
                          const __grid_constant__ CUtensorMap tm_gq, const __grid_constant__ CUtensorMap tm_gk,
                          const __grid_constant__ CUtensorMap tm_gv, const __grid_constant__ CUtensorMap tm_hq,
                          const __grid_constant__ CUtensorMap tm_hk, const __grid_constant__ CUtensorMap tm_hv,
                          const TmaBwdArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* base = smem_align<uint8_t>(smem_raw, 1024);
   constexpr int D = kD, ncons = kD, LB = row_bwd_logit_box(kTT);
   const int S = a.stages;
   const int Da = a.Da;
@@ -270,7 +275,7 @@ __global__ void __launch_bounds__(kD + 32, row_bwd_min_blocks(kD, kTT))
   float4* gates = reinterpret_cast<float4*>(lb_s + row_align(nlb, 4));       // [Da][kTT]
   float* wsum = reinterpret_cast<float*>(gates + Da * kTT);                  // [ncons / 32]
   RowTile* info = reinterpret_cast<RowTile*>(wsum + 32);                     // [S]
-  uint64_t* full = reinterpret_cast<uint64_t*>((reinterpret_cast<uintptr_t>(info + S) + 15) & ~uintptr_t(15));
+  uint64_t* full = smem_align<uint64_t>(info + S, 16);
   uint64_t* empty = full + S;
   __shared__ volatile int abort_flag;
 
@@ -354,7 +359,6 @@ __global__ void __launch_bounds__(kD + 32, row_bwd_min_blocks(kD, kTT))
         init_c = reinterpret_cast<const __nv_bfloat16*>(sb + ioff)[c];
       }
       const __nv_bfloat16* L_s = reinterpret_cast<const __nv_bfloat16*>(sb + loff);
-      const __nv_bfloat16* G_s = reinterpret_cast<const __nv_bfloat16*>(sb + goff);
       __nv_bfloat16* H_s = reinterpret_cast<__nv_bfloat16*>(sb + hoff);
       // h_{t-1} of the row's first token is the initial state (the tile's row -1 was filled with 0)
       if (ti.t0 == 0) H_s[c] = init_c;
@@ -372,49 +376,60 @@ __global__ void __launch_bounds__(kD + 32, row_bwd_min_blocks(kD, kTT))
         }
         gates[q] = make_float4(1.0f - an, al, a.use_sigmoid ? al * (1.0f - al) : 1.0f, 0.f);
       }
-      uint4 uv[kTT / 8];
-#pragma unroll
-      for (int k = 0; k < kTT / 8; ++k) uv[k] = *swz_chunk<kTT>(sb, c, k);
-      named_barrier(1, ncons);  // gates ready; every value row is in registers
+      named_barrier(1, ncons);  // gates ready
 
-      // reverse walk: adjoint carry, du, and the per-token dalpha terms
+      // reverse walk: adjoint carry, du, and the per-token dalpha terms. Thread c alone reads the
+      // 16-bit slots G[t][c] and H[t][c]; once it has, it stores dalpha(t, c) there as an fp32 split
+      // into its high and low halves, so the table needs no space, registers or barrier of its own.
       const float4* grow = gates + gi * kTT;
-      __nv_bfloat16* urow = a.grad_combined + ((long long)ti.b * a.F + ti.h * (D + Da) + c) * a.T + ti.t0;
-      float* red_hi = reinterpret_cast<float*>(sb);         // [kTT/2][D]: tokens kTT/2.. over the value tile
-      float* red_lo = reinterpret_cast<float*>(sb + goff);  // [kTT/2][D]: tokens 0..kTT/2-1 over G
-      float da[kTT / 2];
-#pragma unroll
+      uint16_t* G16 = reinterpret_cast<uint16_t*>(sb + goff);
+      uint16_t* H16 = reinterpret_cast<uint16_t*>(sb + hoff);
+      // one 8-token block per iteration: unrolling across blocks would let every block's loads be
+      // hoisted to the top and spill
+#pragma unroll 1
       for (int k = kTT / 8 - 1; k >= 0; --k) {
         float f[8], du[8];
-        unpack8(uv[k], f);
+        uint4* slot = const_cast<uint4*>(swz_chunk<kTT>(sb, c, k));  // read by thread c alone
+        unpack8(*slot, f);
 #pragma unroll
         for (int e = 7; e >= 0; --e) {
           const int t = 8 * k + e;
           const float4 gv = grow[t];
-          carry = gv.x * carry + __bfloat162float(G_s[t * D + c]);
+          carry = gv.x * carry + __uint_as_float((uint32_t)G16[t * D + c] << 16);
           du[e] = gv.y * carry;
-          const float d = (f[e] - __bfloat162float(H_s[t * D + c])) * carry * gv.z;
-          if (t >= kTT / 2) red_hi[(t - kTT / 2) * D + c] = d;
-          else da[t] = d;
+          const float d = (f[e] - __uint_as_float((uint32_t)H16[t * D + c] << 16)) * carry * gv.z;
+          const uint32_t bits = __float_as_uint(d);
+          G16[t * D + c] = (uint16_t)(bits >> 16);
+          H16[t * D + c] = (uint16_t)(bits & 0xffffu);
         }
-        if (8 * k < ti.tlen) *reinterpret_cast<uint4*>(urow + 8 * k) = pack8(du);
+        *slot = pack8(du);  // du takes the value tile's place: the tile leaves as one bulk store
       }
       if (ti.t0 == 0) a.grad_inits[rowbase * D + c] = __float2bfloat16_rn(carry * (1.0f - grow[0].y));
-      named_barrier(1, ncons);  // every thread is done with G
-#pragma unroll
-      for (int t = 0; t < kTT / 2; ++t) red_lo[t * D + c] = da[t];
-      named_barrier(1, ncons);
+      fence_proxy_async_smem();
+      named_barrier(1, ncons);  // the dalpha table and the du tile are complete
+      if (tid == 0) {
+        tma_store_2d(&tm_du, sb, ti.t0, ti.b * a.F + ti.h * (D + Da));  // columns beyond T are clipped
+        tma_store_commit();
+      }
 
       {
-        const float* rbase = pt >= kTT / 2 ? red_hi + (pt - kTT / 2) * D : red_lo + pt * D;
-        const float4* rrow = reinterpret_cast<const float4*>(rbase + pg * a.r + part * kTT);
-        float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+        // this thread's kTT channels of token pt of group pg: 16-byte pieces, rotated by lane so the
+        // 8 lanes of a shared-memory phase hit 8 different bank groups
+        const uint4* ghi = reinterpret_cast<const uint4*>(G16 + pt * D + pg * a.r + part * kTT);
+        const uint4* glo = reinterpret_cast<const uint4*>(H16 + pt * D + pg * a.r + part * kTT);
+        float s0 = 0.f, s1 = 0.f;
 #pragma unroll
-        for (int q = 0; q < kTT / 4; ++q) {
-          const float4 v = rrow[(q + lane) & (kTT / 4 - 1)];
-          s0 += v.x; s1 += v.y; s2 += v.z; s3 += v.w;
+        for (int q = 0; q < kTT / 8; ++q) {
+          const int qq = (q + lane) & (kTT / 8 - 1);
+          const uint4 hi = ghi[qq], lo = glo[qq];
+          const uint32_t hw[4] = {hi.x, hi.y, hi.z, hi.w}, lw[4] = {lo.x, lo.y, lo.z, lo.w};
+#pragma unroll
+          for (int w = 0; w < 4; ++w) {
+            s0 += __uint_as_float((hw[w] << 16) | (lw[w] & 0xffffu));
+            s1 += __uint_as_float((hw[w] & 0xffff0000u) | (lw[w] >> 16));
+          }
         }
-        float sum = (s0 + s1) + (s2 + s3);
+        float sum = s0 + s1;
         for (int o = tpp >> 1; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
         if (part == 0 && pt < ti.tlen) {
           a.grad_combined[((long long)ti.b * a.F + ti.h * (D + Da) + D + pg) * a.T + ti.t0 + pt] =
@@ -423,6 +438,7 @@ __global__ void __launch_bounds__(kD + 32, row_bwd_min_blocks(kD, kTT))
         }
       }
       fence_proxy_async_smem();  // order this thread's writes into the stage before the next TMA fill
+      if (tid == 0) tma_store_wait_read0();  // the du tile has left the stage
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[st]);  // the stage (and the dalpha table in it) is free
 
@@ -440,6 +456,7 @@ __global__ void __launch_bounds__(kD + 32, row_bwd_min_blocks(kD, kTT))
         }
       }
     }
+    if (tid == 0) tma_store_wait0();
   }
   __syncthreads();
   if (tid == 0) finish_launch(a.ws, gridDim.x);

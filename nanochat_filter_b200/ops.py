@@ -363,6 +363,7 @@ torch.library.impl("nanochat_cuda::fused_linear_transpose_backward_kernel", "CUD
 torch.library.impl("nanochat_cuda::ltv_decode_step", "CUDA", _decode_step)
 
 
+
 # ------------------------------------------------------------------------------------------
 # Functional wrappers (reference nanochat/ops/ltv_cuda_ops.py:256-299)
 # ------------------------------------------------------------------------------------------

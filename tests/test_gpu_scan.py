@@ -238,3 +238,4 @@ def test_scan_row_streaming_path_vs_oracle(cuda_device, T, Da, r):
 def test_scan_row_streaming_ragged_tail(cuda_device):
     _check_vs_oracle(cuda_device, torch.bfloat16, B=60, T=1000, NH=3, NKVH=1, Da=1, r=128, seed=5,
                      transposed_qk=False)
+
