@@ -53,8 +53,15 @@ def _load():
         lib.oracle_gemm_fwd.argtypes = [f, f, f, i, i, i, i, i]
         lib.oracle_gemm_bwd.argtypes = [f, f, f, f, f, i, i, i, i, i, i]
         lib.oracle_round_bf16.argtypes = [f, ll]
+        lib.oracle_set_threads.argtypes = [i]
+        lib.oracle_set_threads.restype = i
         _lib = lib
     return _lib
+
+
+def set_threads(n: int) -> int:
+    """Sets the oracle's OpenMP thread count (n > 0) and returns the count in effect."""
+    return int(_load().oracle_set_threads(int(n)))
 
 
 def _p(a: np.ndarray):

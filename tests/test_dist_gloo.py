@@ -95,3 +95,55 @@ def test_two_rank_gradient_average_matches_full_batch():
         np.testing.assert_allclose(rw, gw / 2, rtol=1e-5, atol=1e-6)
         np.testing.assert_allclose(rb, gb / 2, rtol=1e-5, atol=1e-6)
         np.testing.assert_allclose(ri, gi / 2, rtol=1e-5, atol=1e-6)
+
+
+def _worker_async(rank, world, port, out_q):
+    import sys
+    sys.path.insert(0, ROOT)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from nanochat_filter_b200 import LtvCombinedHeadMajorQkvFilter
+        from nanochat_filter_b200.dist import GradBucket, filter_parameters
+
+        p = _problem()
+        B = p["x"].shape[0]
+        shard = slice(rank * B // world, (rank + 1) * B // world)
+        f = LtvCombinedHeadMajorQkvFilter(p["NH"], p["NKVH"], p["Da"] * p["r"], p["r"])
+        bucket = GradBucket(filter_parameters([f]))
+        gw, gb, gi = _grads(p, shard)
+        # step 1's gradients go out, then step 2 overwrites .grad before step 1's reduction is awaited
+        f.c.weight.grad, f.logit_bias.grad, f.init_param.grad = (torch.from_numpy(a) for a in (gw, gb, gi))
+        h1 = bucket.start()
+        f.c.weight.grad, f.logit_bias.grad, f.init_param.grad = (torch.from_numpy(2 * a) for a in (gw, gb, gi))
+        h2 = bucket.start()
+        h1.wait(copy_back=False)
+        flat1 = bucket.buffers[h1.slot][torch.float32].numpy().copy()
+        h2.wait(copy_back=True)
+        out_q.put((rank, flat1, f.c.weight.grad.numpy().copy(), f.logit_bias.grad.numpy().copy(),
+                   f.init_param.grad.numpy().copy()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_overlapped_reductions_keep_their_own_gradients():
+    """Two reductions in flight (GradBucket.start): each averages the gradients it was started with."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_async, args=(r, 2, port, q)) for r in range(2)]
+    for pr in procs:
+        pr.start()
+    results = [q.get(timeout=240) for _ in range(2)]
+    for pr in procs:
+        pr.join(timeout=60)
+        assert pr.exitcode == 0
+    p = _problem()
+    gw, gb, gi = _grads(p, slice(None))
+    flat_expect = np.concatenate([gw.reshape(-1), gb.reshape(-1), gi.reshape(-1)]) / 2
+    for _, flat1, rw, rb, ri in results:
+        np.testing.assert_allclose(flat1, flat_expect, rtol=1e-5, atol=1e-6)
+        np.testing.assert_allclose(rw, gw, rtol=1e-5, atol=1e-6)   # average of 2x the shard sums
+        np.testing.assert_allclose(rb, gb, rtol=1e-5, atol=1e-6)
+        np.testing.assert_allclose(ri, gi, rtol=1e-5, atol=1e-6)
