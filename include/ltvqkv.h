@@ -151,6 +151,21 @@ LTVQKV_API int ltvqkv_gemm_fwd(int dtype, const void* x, const void* weight, voi
                     int B, int T, int K, int F,
                     void* workspace, size_t workspace_bytes, void* stream);
 
+/* Projection and scan forward in one call: ltvqkv_gemm_fwd(x, weight -> combined) followed by
+ * ltvqkv_scan_fwd(combined viewed [B, T, F] -> q, k, v), as the reference's filter forward calls
+ * them (nanochat/ltv_cuda_fused_concat_head_major_register_cast_blelloch_scan_qkv_filter.py:24-73:
+ * fused_linear_transpose, then the scan op); no single reference function corresponds. x [B, T, C],
+ * weight [F, C], combined [B, F, T] (written, as ltvqkv_gemm_fwd writes it), inits [B, H, D],
+ * logit_bias [H, Da] fp32, q/k/v [B, heads, T, D], all contiguous. bf16 with D = 128, Da = 1,
+ * T % 32 == 0, C % 8 == 0 and B * H >= 2 * (SM count) runs fused (the head's value rows go from the tensor cores' TMEM
+ * accumulator straight into the scan; the decay-logit rows are projected first); other cases run
+ * the two entry points in sequence. Results equal the two-call sequence bit for bit. The workspace
+ * is the scan's (ltvqkv_scan_workspace_bytes). */
+LTVQKV_API int ltvqkv_proj_scan_fwd(int dtype, const void* x, const void* weight, const void* inits,
+                    const float* logit_bias, void* combined, void* out_q, void* out_k, void* out_v,
+                    int B, int T, int C, int NH, int NKVH, int Da, int r, int use_sigmoid,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
 /* Projection backward: replaces cpp_ewma_cuda.fused_linear_transpose_backward
  * (reference cpp_ewma/src/fused_linear_transpose_backward.cu:22-132; called from
  * nanochat/ops/fused_linear_transpose.py:84-101).

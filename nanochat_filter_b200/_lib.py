@@ -35,6 +35,7 @@ EXPORTED_SYMBOLS = (
     "ltvqkv_workspace_error",
     "ltvqkv_debug_wait_timeout",
     "ltvqkv_scan_fwd_noalloc",
+    "ltvqkv_proj_scan_fwd",
 )
 
 _lib: Optional[ctypes.CDLL] = None
@@ -70,6 +71,9 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.ltvqkv_gemm_workspace_bytes.argtypes = []
     lib.ltvqkv_gemm_fwd.restype = _i
     lib.ltvqkv_gemm_fwd.argtypes = [_i, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _sz, _vp]
+    lib.ltvqkv_proj_scan_fwd.restype = _i
+    lib.ltvqkv_proj_scan_fwd.argtypes = [_i, _vp, _vp, _vp, _pf, _vp, _vp, _vp, _vp,
+                                         _i, _i, _i, _i, _i, _i, _i, _i, _vp, _sz, _vp]
     lib.ltvqkv_gemm_bwd.restype = _i
     lib.ltvqkv_gemm_bwd.argtypes = [_i, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _vp, _i,
                                     _i, _i, _i, _i, _vp, _sz, _vp]

@@ -118,6 +118,13 @@ LTVQKV_DEVICE uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic
 // ------------------------------------------------------------------------------------------
 // mbarrier
 // ------------------------------------------------------------------------------------------
+// Which output tensor and local head a global head index maps to (Q heads, K heads, V heads).
+LTVQKV_DEVICE void split_head(int h, int NH, int NKVH, int& which, int& hloc, int& nheads) {
+  if (h < NH) { which = 0; hloc = h; nheads = NH; }
+  else if (h < NH + NKVH) { which = 1; hloc = h - NH; nheads = NKVH; }
+  else { which = 2; hloc = h - NH - NKVH; nheads = NKVH; }
+}
+
 // `p` advanced to the next multiple of `align` bytes (a power of two) of the shared window, by
 // pointer arithmetic: an integer round trip would hide from the compiler that the result points
 // into shared memory, turning every access through it into a generic one.
@@ -210,6 +217,17 @@ LTVQKV_DEVICE void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, u
 }
 LTVQKV_DEVICE void named_barrier(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+// Named barrier that also ORs a predicate over the participating threads: every thread gets the
+// same answer, so a group can leave a loop together when any of its threads saw a wait time out.
+LTVQKV_DEVICE bool named_barrier_or(int id, int count, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, %2, %3, p;\n selp.u32 %0, 1, 0, q;\n}"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "r"(id), "r"(count)
+      : "memory");
+  return r != 0;
 }
 LTVQKV_DEVICE void tma_store_2d(const CUtensorMap* m, const void* smem_src, int c0, int c1) {
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(m),

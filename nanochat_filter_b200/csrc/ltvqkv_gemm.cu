@@ -13,10 +13,13 @@
 // The backward's tensor-core kernel (CTA pairs, tcgen05 cta_group::2) is in ltvqkv_gemm_pair.cuh.
 #include <algorithm>
 #include <mutex>
+#include <set>
+#include <utility>
 
 #include "ltvqkv_common.cuh"
 #include "ltvqkv_gemm_fwd.cuh"
 #include "ltvqkv_gemm_pair.cuh"
+#include "ltvqkv_proj_scan.cuh"
 
 namespace ltvqkv {
 
@@ -159,6 +162,56 @@ int launch_pair(PairParams& prm, const CUtensorMap* maps /*[4]*/, cudaStream_t s
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Opts `kernel` into `bytes` of dynamic shared memory on the current device (once per device).
+int smem_opt_in(const void* kernel, size_t bytes) {
+  static std::mutex mu;
+  static std::set<std::pair<int, const void*>> done;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return ltvqkv_host::check_launch();
+  std::lock_guard<std::mutex> lock(mu);
+  if (done.count({dev, kernel})) return LTVQKV_OK;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) != cudaSuccess)
+    return ltvqkv_host::check_launch();
+  done.insert({dev, kernel});
+  return LTVQKV_OK;
+}
+
+// Resident clusters of the fused projection + scan kernel on the current device (cached); 0 on a
+// CUDA error.
+int ps_clusters() {
+  static std::mutex mu;
+  static int by_device[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+  std::lock_guard<std::mutex> lock(mu);
+  if (by_device[dev] == 0) {
+    if (cudaFuncSetAttribute(proj_scan_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPsSmemBytes) !=
+        cudaSuccess)
+      return 0;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * (ltvqkv_host::num_sms() / 2), 1, 1);
+    cfg.blockDim = dim3(kPsThreads, 1, 1);
+    cfg.dynamicSmemBytes = kPsSmemBytes;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, proj_scan_fwd_kernel, &cfg) != cudaSuccess || n < 1) {
+      cudaGetLastError();
+      n = ltvqkv_host::num_sms() / 2;
+    }
+    by_device[dev] = n;
+  }
+  return by_device[dev];
+}
+
+// The forward GEMM kernel on prepared maps (out rows = prm.F).
+int launch_gemm_fwd(const CUtensorMap& tmW, const CUtensorMap& tmX, const CUtensorMap& tmOut, const FwdParams& prm,
+                    cudaStream_t s) {
+  const int rc = smem_opt_in((const void*)gemm_fwd_kernel, kFwdSmemBytes);
+  if (rc != LTVQKV_OK) return rc;
+  const int grid = std::min(prm.num_tiles, ltvqkv_host::num_sms());
+  gemm_fwd_kernel<<<grid, kFwdThreads, kFwdSmemBytes, s>>>(tmW, tmX, tmOut, prm);
+  return ltvqkv_host::check_launch();
+}
+
 template <typename Tin, typename Tout>
 int launch_simt(const SimtArgs& a, int out_batches, cudaStream_t s) {
   if (a.M == 0 || a.N == 0 || out_batches == 0) return LTVQKV_OK;
@@ -207,22 +260,77 @@ extern "C" int ltvqkv_gemm_fwd(int dtype, const void* x, const void* weight, voi
       !make_map(&tmX, false, x, K, T, B, (uint64_t)K * 2, (uint64_t)K * T * 2, 64, kFwdBN) ||
       !make_map(&tmOut, false, out, T, F, B, (uint64_t)T * 2, (uint64_t)T * F * 2, 64, 32))
     return LTVQKV_ERR_LAUNCH;
-  {
-    // the shared-memory opt-in is per device
-    static std::mutex mu;
-    static bool done[64] = {};
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return ltvqkv_host::check_launch();
-    std::lock_guard<std::mutex> lock(mu);
-    if (!done[dev]) {
-      if (cudaFuncSetAttribute(gemm_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kFwdSmemBytes) !=
-          cudaSuccess)
-        return ltvqkv_host::check_launch();
-      done[dev] = true;
-    }
+  return launch_gemm_fwd(tmW, tmX, tmOut, prm, s);
+}
+
+extern "C" int ltvqkv_proj_scan_fwd(int dtype, const void* x, const void* weight, const void* inits,
+                                    const float* logit_bias, void* combined, void* out_q, void* out_k, void* out_v,
+                                    int B, int T, int C, int NH, int NKVH, int Da, int r, int use_sigmoid,
+                                    void* workspace, size_t workspace_bytes, void* stream) {
+  if (!ltvqkv_host::valid_dtype(dtype)) return LTVQKV_ERR_DTYPE;
+  if (B < 0 || T < 0 || C < 0 || NH < 0 || NKVH < 0 || Da < 1 || r < 1) return LTVQKV_ERR_SHAPE;
+  const int H = NH + 2 * NKVH, D = Da * r, F = H * (D + Da);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  // Fused when the scan operator would take its row-streaming kernel for these shapes (at least
+  // two (batch, head) rows per SM), whose arithmetic the fused epilogue repeats step for step.
+  const bool fused = dtype == LTVQKV_DTYPE_BF16 && D == kPsD && Da == 1 && H >= 1 && H <= kFwdBM && B > 0 &&
+                     (long long)B * H >= 2LL * ltvqkv_host::num_sms() &&
+                     T > 0 && T % 32 == 0 && C > 0 && C % 8 == 0 && x && weight && inits && logit_bias &&
+                     combined && aligned16(x) && aligned16(weight) && aligned16(combined) &&
+                     (NH == 0 || (out_q && aligned16(out_q))) &&
+                     (NKVH == 0 || (out_k && out_v && aligned16(out_k) && aligned16(out_v)));
+  if (!fused) {
+    // the two operators in sequence: projection into `combined`, then the scan reading it
+    int rc = ltvqkv_gemm_fwd(dtype, x, weight, combined, B, T, C, F, workspace, workspace_bytes, stream);
+    if (rc != LTVQKV_OK) return rc;
+    return ltvqkv_scan_fwd(dtype, combined, (int64_t)F * T, 1, T, inits, logit_bias, out_q, out_k, out_v, B, T, NH,
+                           NKVH, Da, r, use_sigmoid, workspace, workspace_bytes, stream);
   }
-  const int grid = std::min(prm.num_tiles, ltvqkv_host::num_sms());
-  gemm_fwd_kernel<<<grid, kFwdThreads, kFwdSmemBytes, s>>>(tmW, tmX, tmOut, prm);
+  if (!workspace || workspace_bytes < ltvqkv_gemm_workspace_bytes()) return LTVQKV_ERR_WORKSPACE;
+  WorkspaceHeader* ws = reinterpret_cast<WorkspaceHeader*>(workspace);
+  const char* wb = reinterpret_cast<const char*>(weight);
+  char* cb = reinterpret_cast<char*>(combined);
+  // 1. the H decay-logit rows (row h*(D+1) + D of W and of `combined`) through the forward GEMM:
+  //    strided 2-D views that skip the value rows; rows beyond H read zeros and are not stored
+  FwdParams lp = {};
+  lp.F = H; lp.T = T; lp.B = B;
+  lp.m_tiles = 1;
+  lp.n_tiles = (T + kFwdBN - 1) / kFwdBN;
+  lp.k_blocks = (C + kFwdBK - 1) / kFwdBK;
+  lp.num_tiles = B * lp.n_tiles;
+  lp.ws = ws;
+  CUtensorMap tmWl, tmX, tmOl;
+  if (!make_map(&tmWl, false, wb + (size_t)D * C * 2, C, H, 1, (uint64_t)(D + 1) * C * 2, (uint64_t)F * C * 2, 64,
+                kFwdBM) ||
+      !make_map(&tmX, false, x, C, T, B, (uint64_t)C * 2, (uint64_t)C * T * 2, 64, kFwdBN) ||
+      !make_map(&tmOl, false, cb + (size_t)D * T * 2, T, H, B, (uint64_t)(D + 1) * T * 2, (uint64_t)F * T * 2, 64,
+                32))
+    return LTVQKV_ERR_LAUNCH;
+  int rc = launch_gemm_fwd(tmWl, tmX, tmOl, lp, s);
+  if (rc != LTVQKV_OK) return rc;
+  // 2. value rows and the scan, one head pair per ticket on a CTA pair
+  PsParams pp = {};
+  pp.B = B; pp.T = T; pp.H = H; pp.NH = NH; pp.NKVH = NKVH; pp.F = F;
+  pp.n_tiles = (T + kPsBN - 1) / kPsBN;
+  pp.k_blocks = lp.k_blocks;
+  pp.npairs = B * ((H + 1) / 2);
+  pp.use_sigmoid = use_sigmoid;
+  pp.combined = reinterpret_cast<__nv_bfloat16*>(combined);
+  pp.inits = reinterpret_cast<const __nv_bfloat16*>(inits);
+  pp.logit_bias = logit_bias;
+  pp.out[0] = reinterpret_cast<__nv_bfloat16*>(out_q);
+  pp.out[1] = reinterpret_cast<__nv_bfloat16*>(out_k);
+  pp.out[2] = reinterpret_cast<__nv_bfloat16*>(out_v);
+  pp.ws = ws;
+  CUtensorMap tmW, tmXh;
+  if (!make_map(&tmW, false, weight, C, F, 1, (uint64_t)C * 2, (uint64_t)C * F * 2, 64, 128) ||
+      !make_map(&tmXh, false, x, C, T, B, (uint64_t)C * 2, (uint64_t)C * T * 2, 64, kPsBN / 2))
+    return LTVQKV_ERR_LAUNCH;
+  const int nclusters = ps_clusters();
+  if (nclusters < 1) return ltvqkv_host::check_launch();
+  // two head pairs per cluster at a time
+  const int grid = 2 * std::max(1, std::min(nclusters, (pp.npairs + 1) / 2));
+  proj_scan_fwd_kernel<<<grid, kPsThreads, kPsSmemBytes, s>>>(tmW, tmXh, pp);
   return ltvqkv_host::check_launch();
 }
 

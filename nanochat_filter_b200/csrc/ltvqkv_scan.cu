@@ -120,12 +120,6 @@ struct ScanBwdArgs {
   float* bias_part;
 };
 
-// Which output tensor and local head a global head index maps to (Q heads, K heads, V heads).
-LTVQKV_DEVICE void split_head(int h, int NH, int NKVH, int& which, int& hloc, int& nheads) {
-  if (h < NH) { which = 0; hloc = h; nheads = NH; }
-  else if (h < NH + NKVH) { which = 1; hloc = h - NH; nheads = NKVH; }
-  else { which = 2; hloc = h - NH - NKVH; nheads = NKVH; }
-}
 
 // Spin (one thread) until the flag of a predecessor tile carries the current epoch and a
 // state; returns the state, or kFlagIncl with *timed_out set when the wait gave up.

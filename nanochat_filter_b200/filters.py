@@ -106,10 +106,11 @@ class LtvCombinedHeadMajorQkvFilter(LtvCombinedQkvFilterBase):
 
 
 class LtvCudaFusedConcatHeadMajorRegisterCastBlellochScanQkvFilter(LtvCombinedHeadMajorQkvFilter):
-    """CUDA filter: tcgen05 projection into [B, F, T], then the look-back carried scan.
+    """CUDA filter: tcgen05 projection into [B, F, T], then the scan.
 
-    Decode steps (T == 1 with cached state, no autograd) take the one-launch
-    `ltv_decode_step` path; everything else follows the reference's two-op composition.
+    Decode steps (T == 1 with cached state, no autograd) take the one-launch `ltv_decode_step`
+    path; bf16/fp16 sequences take `ltv_proj_scan` (projection and scan forward in one call);
+    fp32 runs follow the reference's two-op composition.
     """
 
     use_decode_kernel: bool = True
@@ -122,6 +123,14 @@ class LtvCudaFusedConcatHeadMajorRegisterCastBlellochScanQkvFilter(LtvCombinedHe
         if (self.use_decode_kernel and T == 1 and not run_ltv_in_fp32 and x.is_cuda
                 and not (torch.is_grad_enabled() and (x.requires_grad or self.c.weight.requires_grad))):
             return self._decode(x, previous_values)
+
+        if not run_ltv_in_fp32:
+            # projection + scan in one call (tensor-core accumulator straight into the recurrence);
+            # outputs and gradients equal the two-op composition below bit for bit
+            inits = resolve_inits_original_dtype(B, self.init_param, previous_values).to(dtype=x.dtype).contiguous()
+            _, hq, hk, hv = _ops.ltv_proj_scan(x.contiguous(), self.c.weight, inits, self.logit_bias.contiguous(),
+                                               self.n_head, self.n_kv_head, self.num_alpha_groups, self.r, True)
+            return hq.transpose(1, 2), hk.transpose(1, 2), hv.transpose(1, 2)
 
         out_buf = _ops.fused_linear_transpose(x.float() if run_ltv_in_fp32 else x,
                                               self.c.weight.float() if run_ltv_in_fp32 else self.c.weight)

@@ -13,7 +13,9 @@ so code written against the reference's `torch.ops.nanochat_cuda.*` runs unchang
   fused_linear_transpose
   fused_linear_transpose_backward_kernel
 
-plus one op the reference does not have, `ltv_decode_step` (one-launch decode update).
+plus ops the reference does not have: `ltv_decode_step` (one-launch decode update) and
+`ltv_proj_scan_cuda_op` / `ltv_proj_scan_forward_kernel` (projection and scan forward in one
+call, the composition the reference's filter runs as two ops; same outputs bit for bit).
 
 The CUDA implementations call libltvqkv.so through its C ABI; only "CUDA" and "Meta"
 dispatch keys are registered, so CPU tensors raise NotImplementedError from the dispatcher —
@@ -70,6 +72,17 @@ lib.define(
     "fused_linear_transpose_backward_kernel("
     "Tensor x, Tensor weight, Tensor grad_out, Tensor(a!) grad_x, Tensor(b!) grad_weight"
     ") -> ()"
+)
+lib.define(
+    "ltv_proj_scan_forward_kernel("
+    "Tensor x, Tensor weight, Tensor inits, Tensor logit_bias, Tensor(a!) combined, "
+    "Tensor(b!) out_q, Tensor(c!) out_k, Tensor(d!) out_v, int NH, int NKVH, int da, int r, bool use_sigmoid"
+    ") -> ()"
+)
+lib.define(
+    "ltv_proj_scan_cuda_op("
+    "Tensor x, Tensor weight, Tensor inits, Tensor logit_bias, int NH, int NKVH, int da, int r, bool use_sigmoid"
+    ") -> (Tensor, Tensor, Tensor, Tensor)"
 )
 lib.define(
     "ltv_decode_step("
@@ -308,6 +321,106 @@ def _flt_bwd_fake(x, weight, grad_out, grad_x, grad_weight):
 
 
 # ------------------------------------------------------------------------------------------
+# Projection + scan forward in one call
+# ------------------------------------------------------------------------------------------
+def _proj_scan_forward_kernel(x, weight, inits, logit_bias, combined, out_q, out_k, out_v, NH, NKVH, da, r,
+                              use_sigmoid):
+    """fused_linear_transpose(x, weight) -> combined [B, F, T], then the scan over combined^T.
+
+    Equals `fused_linear_transpose` followed by the scan forward kernel on `combined.transpose(1, 2)`
+    (the reference filter's composition,
+    nanochat/ltv_cuda_fused_concat_head_major_register_cast_blelloch_scan_qkv_filter.py:24-73).
+    """
+    if not x.is_contiguous() or x.dim() != 3:
+        raise RuntimeError("ltv_proj_scan requires a contiguous [B, T, C] x")
+    L = _lib.load()
+    B, T, C = x.shape
+    H = NH + 2 * NKVH
+    D = da * r
+    F = H * (D + da)
+    w = (weight if weight.dtype == x.dtype else weight.to(x.dtype)).contiguous()
+    if tuple(w.shape) != (F, C):
+        raise RuntimeError(f"weight must be [{F}, {C}], got {tuple(w.shape)}")
+    if tuple(combined.shape) != (B, F, T) or not combined.is_contiguous() or combined.dtype != x.dtype:
+        raise RuntimeError("combined must be a contiguous [B, F, T] tensor of x's dtype")
+    _check_scan_inputs(combined.transpose(1, 2), inits, logit_bias, NH, NKVH, da, r)
+    inits = inits.contiguous()
+    logit_bias = logit_bias.contiguous()
+    for o, n in ((out_q, NH), (out_k, NKVH), (out_v, NKVH)):
+        if not o.is_contiguous() or o.dtype != x.dtype or tuple(o.shape) != (B, n, T, D):
+            raise RuntimeError("out_q/out_k/out_v must be contiguous [B, heads, T, D] of x's dtype")
+    nbytes = max(L.ltvqkv_scan_workspace_bytes(B, T, NH, NKVH, da, r), L.ltvqkv_gemm_workspace_bytes())
+    ws = _lib.workspace(x.device, nbytes)
+    rc = L.ltvqkv_proj_scan_fwd(_lib.dtype_code(x.dtype), x.data_ptr(), w.data_ptr(), inits.data_ptr(),
+                                logit_bias.data_ptr(), combined.data_ptr(), out_q.data_ptr(), out_k.data_ptr(),
+                                out_v.data_ptr(), B, T, C, NH, NKVH, da, r, int(bool(use_sigmoid)), ws.data_ptr(),
+                                ws.numel(), _lib.stream_handle(x.device))
+    _lib.check(rc, "ltvqkv_proj_scan_fwd")
+
+
+def _proj_scan_op(x, weight, inits, logit_bias, NH, NKVH, da, r, use_sigmoid):
+    B, T, _ = x.shape
+    D = da * r
+    F = (NH + 2 * NKVH) * (D + da)
+    kw = dict(device=x.device, dtype=x.dtype)
+    combined = torch.empty((B, F, T), **kw)
+    out_q = torch.empty((B, NH, T, D), **kw)
+    out_k = torch.empty((B, NKVH, T, D), **kw)
+    out_v = torch.empty((B, NKVH, T, D), **kw)
+    _proj_scan_forward_kernel(x, weight, inits, logit_bias, combined, out_q, out_k, out_v, NH, NKVH, da, r,
+                              use_sigmoid)
+    return combined, out_q, out_k, out_v
+
+
+def _ps_setup(ctx, inputs, output):
+    x, weight, inits, logit_bias, NH, NKVH, da, r, use_sigmoid = inputs
+    combined, hq, hk, hv = output
+    ctx.save_for_backward(x, weight, combined, inits, logit_bias, hq, hk, hv)
+    ctx.args = (NH, NKVH, da, r)
+    ctx.use_sigmoid = use_sigmoid
+
+
+def _ps_backward(ctx, grad_comb, grad_hq, grad_hk, grad_hv):
+    # the two reference backward kernels in sequence: scan backward into grad_combined (whose
+    # [B, F, T] memory is the projection's grad_out), then the projection backward
+    x, weight, comb, inits, logit_bias, hq, hk, hv = ctx.saved_tensors
+    combined = comb.transpose(1, 2)
+    grad_hq = torch.zeros_like(hq) if grad_hq is None else grad_hq
+    grad_hk = torch.zeros_like(hk) if grad_hk is None else grad_hk
+    grad_hv = torch.zeros_like(hv) if grad_hv is None else grad_hv
+    grad_combined = torch.empty_like(combined)
+    grad_inits = torch.empty_like(inits, memory_format=torch.contiguous_format)
+    grad_logit_bias = torch.zeros_like(logit_bias, memory_format=torch.contiguous_format)
+    torch.ops.nanochat_cuda.ltv_fused_concat_head_major_register_cast_blelloch_scan_cuda_backward_kernel(
+        combined, inits, logit_bias, hq, hk, hv, grad_hq, grad_hk, grad_hv, grad_combined, grad_inits,
+        grad_logit_bias, *ctx.args, 32, 2, 8, ctx.use_sigmoid)
+    grad_out = grad_combined.transpose(1, 2)
+    if grad_comb is not None:
+        grad_out = grad_out + grad_comb
+    grad_x = torch.empty_like(x, memory_format=torch.contiguous_format)
+    grad_weight = torch.empty_like(weight, memory_format=torch.contiguous_format)
+    torch.ops.nanochat_cuda.fused_linear_transpose_backward_kernel(x, weight, grad_out, grad_x, grad_weight)
+    return (grad_x, grad_weight, grad_inits, grad_logit_bias) + (None,) * 5
+
+
+torch.library.register_autograd("nanochat_cuda::ltv_proj_scan_cuda_op", _ps_backward, setup_context=_ps_setup)
+
+
+@torch.library.register_fake("nanochat_cuda::ltv_proj_scan_cuda_op")
+def _proj_scan_fake(x, weight, inits, logit_bias, NH, NKVH, da, r, use_sigmoid):
+    B, T, _ = x.shape
+    D = da * r
+    F = (NH + 2 * NKVH) * (D + da)
+    return (x.new_empty((B, F, T)), x.new_empty((B, NH, T, D)), x.new_empty((B, NKVH, T, D)),
+            x.new_empty((B, NKVH, T, D)))
+
+
+@torch.library.register_fake("nanochat_cuda::ltv_proj_scan_forward_kernel")
+def _proj_scan_kernel_fake(*args):
+    return None
+
+
+# ------------------------------------------------------------------------------------------
 # Decode step
 # ------------------------------------------------------------------------------------------
 def _decode_step(x, weight, logit_bias, prev_q, prev_k, prev_v, init_param, NH, NKVH, da, r, use_sigmoid):
@@ -361,6 +474,8 @@ torch.library.impl("nanochat_cuda::fused_linear_transpose", "CUDA", _fused_linea
 torch.library.impl("nanochat_cuda::fused_linear_transpose_cuda_op", "CUDA", _fused_linear_transpose_op)
 torch.library.impl("nanochat_cuda::fused_linear_transpose_backward_kernel", "CUDA", _fused_linear_transpose_backward_kernel)
 torch.library.impl("nanochat_cuda::ltv_decode_step", "CUDA", _decode_step)
+torch.library.impl("nanochat_cuda::ltv_proj_scan_forward_kernel", "CUDA", _proj_scan_forward_kernel)
+torch.library.impl("nanochat_cuda::ltv_proj_scan_cuda_op", "CUDA", _proj_scan_op)
 
 
 
@@ -387,3 +502,9 @@ def ltv_decode_step(x: torch.Tensor, weight: torch.Tensor, logit_bias: torch.Ten
     """One incremental filter step for x [B, C] (or [B, 1, C]); returns the new states."""
     return torch.ops.nanochat_cuda.ltv_decode_step(x, weight, logit_bias, prev_q, prev_k, prev_v, init_param, NH,
                                                     NKVH, da, r, use_sigmoid)
+
+
+def ltv_proj_scan(x: torch.Tensor, weight: torch.Tensor, inits: torch.Tensor, logit_bias: torch.Tensor, NH: int,
+                  NKVH: int, da: int, r: int, use_sigmoid: bool = True):
+    """Projection and scan forward in one call; returns (combined [B, F, T], q, k, v [B, heads, T, D])."""
+    return torch.ops.nanochat_cuda.ltv_proj_scan_cuda_op(x, weight, inits, logit_bias, NH, NKVH, da, r, use_sigmoid)

@@ -1,0 +1,145 @@
+"""GPU parity of the one-call projection + scan forward (`ltv_proj_scan_cuda_op`).
+
+The op must equal the reference filter's two-op composition
+(nanochat/ltv_cuda_fused_concat_head_major_register_cast_blelloch_scan_qkv_filter.py:24-73:
+fused_linear_transpose, then the scan op on combined^T) bit for bit — both the projection
+`combined` it writes and q/k/v — so the comparison here is exact equality with this library's
+own two operators, whose parity with the reference is covered by the GEMM and scan tests; the
+oracle check below anchors the fused path to the CPU restatement directly as well. Shapes cover
+the fused case (bf16, D = 128, Da = 1, T % 32 == 0) with T not a multiple of the 256-token tile,
+C not a multiple of the 64-wide k block, heads without K/V, and the sequential fallback cases
+(fp32, T % 32 != 0, Da > 1).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import nanochat_filter_b200  # noqa: F401
+from nanochat_filter_b200.filters import LtvCudaFusedConcatHeadMajorRegisterCastBlellochScanQkvFilter
+from nanochat_filter_b200.util import LtvInitValues
+from conftest import max_rel_err
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+OPS = torch.ops.nanochat_cuda
+
+
+def _inputs(dev, B, T, C, NH, NKVH, Da, r, dtype, seed):
+    H = NH + 2 * NKVH
+    D = Da * r
+    F = H * (D + Da)
+    g = torch.Generator(device=dev).manual_seed(seed)
+    x = (torch.randn((B, T, C), generator=g, device=dev) * 0.5).to(dtype)
+    w = (torch.rand((F, C), generator=g, device=dev) * 2 - 1).mul(C ** -0.5).to(dtype)
+    inits = (torch.rand((B, H, D), generator=g, device=dev) * 2 - 1).mul(0.5).to(dtype)
+    bias = torch.rand((H, Da), generator=g, device=dev) * 2 - 1
+    return x, w, inits, bias
+
+
+def _two_ops(x, w, inits, bias, NH, NKVH, Da, r, use_sigmoid):
+    comb = OPS.fused_linear_transpose_cuda_op(x, w)
+    q, k, v = OPS.ltv_fused_concat_head_major_register_cast_blelloch_scan_cuda_op(
+        comb.transpose(1, 2), inits, bias, NH, NKVH, Da, r, 8, 8, 4, 32, 2, 8, use_sigmoid)
+    return comb, q, k, v
+
+
+# The fused kernel runs when B * H >= 2 * SMs (296 (batch, head) rows on a 148-SM B200), the
+# shapes for which the scan operator takes its row-streaming kernel; other cases run the two
+# entry points in sequence and must equal them trivially.
+CASES = [
+    # B, T, C, NH, NKVH, Da, r
+    (32, 1024, 768, 6, 6, 1, 128),    # the d=12 training shape (config 2)
+    (17, 544, 200, 6, 6, 1, 128),     # T % 256 != 0, C % 64 != 0
+    (150, 32, 64, 2, 0, 1, 128),      # one token tile, Q heads only
+    (60, 96, 136, 1, 2, 1, 128),      # K/V-heavy
+    (2, 2048, 768, 6, 6, 1, 128),     # few rows: sequential
+    (20, 1000, 256, 6, 6, 1, 128),    # T % 32 != 0: sequential
+    (40, 256, 128, 6, 6, 2, 64),      # Da > 1: sequential
+]
+
+
+@pytest.mark.parametrize("B,T,C,NH,NKVH,Da,r", CASES)
+@pytest.mark.parametrize("use_sigmoid", [True, False])
+def test_proj_scan_equals_two_ops(cuda_device, B, T, C, NH, NKVH, Da, r, use_sigmoid):
+    x, w, inits, bias = _inputs(cuda_device, B, T, C, NH, NKVH, Da, r, torch.bfloat16, B * 131 + T + C)
+    if not use_sigmoid:
+        bias = bias * 0.05 + 0.3  # raw alphas in (0.25, 0.35) keep the recurrence bounded
+        w = w * 0.05
+    ref = _two_ops(x, w, inits, bias, NH, NKVH, Da, r, use_sigmoid)
+    got = OPS.ltv_proj_scan_cuda_op(x, w, inits, bias, NH, NKVH, Da, r, use_sigmoid)
+    torch.cuda.synchronize()
+    for a, b, n in zip(got, ref, ("combined", "q", "k", "v")):
+        assert a.shape == b.shape, n
+        assert torch.equal(a, b), f"{n}: {(a.float() - b.float()).abs().max().item()}"
+
+
+def test_proj_scan_fp32_fallback(cuda_device):
+    x, w, inits, bias = _inputs(cuda_device, 2, 256, 128, 2, 1, 1, 128, torch.float32, 7)
+    ref = _two_ops(x, w, inits, bias, 2, 1, 1, 128, True)
+    got = OPS.ltv_proj_scan_cuda_op(x, w, inits, bias, 2, 1, 1, 128, True)
+    for a, b in zip(got, ref):
+        assert torch.equal(a, b)
+
+
+def test_proj_scan_against_oracle(cuda_device):
+    """The fused path against the CPU restatement of the scan on the kernel's own `combined`."""
+    B, T, C, NH, NKVH, Da, r = 300, 64, 192, 1, 0, 1, 128   # 300 rows: the fused kernel
+    x, w, inits, bias = _inputs(cuda_device, B, T, C, NH, NKVH, Da, r, torch.bfloat16, 99)
+    comb, q, k, v = OPS.ltv_proj_scan_cuda_op(x, w, inits, bias, NH, NKVH, Da, r, True)
+    # projection: fp32 contraction of the same bf16 values, rounded once
+    ref_comb = torch.matmul(w.float(), x.float().transpose(1, 2))
+    np.testing.assert_allclose(comb.float().cpu().numpy(), ref_comb.cpu().numpy(), rtol=1e-2, atol=1e-2)
+    # scan: the oracle fed the kernel's bf16 projection (bf16 state rounding, same bound as the
+    # scan operator's own oracle test)
+    f32 = lambda t: t.float().contiguous().cpu().numpy()  # noqa: E731
+    oq, ok, ov = O.scan_fwd(f32(comb.transpose(1, 2)), f32(inits), f32(bias), NH, NKVH, Da, r, True, True)
+    for got, want, n in ((q, oq, "q"), (k, ok, "k"), (v, ov, "v")):
+        err = max_rel_err(f32(got), want, 1e-2)
+        assert err <= 2e-2, f"{n}: {err}"
+
+
+def test_proj_scan_autograd_equals_two_ops(cuda_device):
+    B, T, C, NH, NKVH, Da, r = 100, 288, 192, 2, 1, 1, 128
+    x, w, inits, bias = _inputs(cuda_device, B, T, C, NH, NKVH, Da, r, torch.bfloat16, 5)
+    wf = w.float()
+    gen = torch.Generator(device=cuda_device).manual_seed(3)
+    grads = [torch.randn((B, n, T, 128), generator=gen, device=cuda_device).to(torch.bfloat16)
+             for n in (NH, NKVH, NKVH)]
+
+    def run(fused):
+        xx = x.clone().requires_grad_(True)
+        ww = wf.clone().requires_grad_(True)
+        ii = inits.clone().requires_grad_(True)
+        bb = bias.clone().requires_grad_(True)
+        if fused:
+            _, q, k, v = OPS.ltv_proj_scan_cuda_op(xx, ww, ii, bb, NH, NKVH, Da, r, True)
+        else:
+            comb = OPS.fused_linear_transpose_cuda_op(xx, ww)  # fp32 master weight, as the filter passes it
+            q, k, v = OPS.ltv_fused_concat_head_major_register_cast_blelloch_scan_cuda_op(
+                comb.transpose(1, 2), ii, bb, NH, NKVH, Da, r, 8, 8, 4, 32, 2, 8, True)
+        torch.autograd.backward((q, k, v), grads)
+        return (q, k, v, xx.grad, ww.grad, ii.grad, bb.grad)
+
+    got, ref = run(True), run(False)
+    names = ("q", "k", "v", "grad_x", "grad_w", "grad_inits", "grad_bias")
+    for a, b, n in zip(got, ref, names):
+        assert a.dtype == b.dtype and torch.equal(a, b), n
+
+
+def test_filter_module_fused_forward(cuda_device):
+    """The module's bf16 forward (one-call path) equals its fp32-free two-op composition."""
+    torch.manual_seed(0)
+    f = LtvCudaFusedConcatHeadMajorRegisterCastBlellochScanQkvFilter(6, 6, 128, 128).to(cuda_device)
+    f.init_weights(2.0, 0.05, 0.5, 0.5)
+    B = 17
+    x = (torch.randn(B, 320, 768, device=cuda_device) * 0.5).to(torch.bfloat16)
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        q, k, v = f(x, LtvInitValues())
+    inits = f.init_param.to(torch.bfloat16).unsqueeze(0).expand(B, -1, -1).contiguous()
+    _, rq, rk, rv = _two_ops(x, f.c.weight.to(torch.bfloat16), inits, f.logit_bias.detach(), 6, 6, 1, 128, True)
+    for a, b in ((q, rq), (k, rk), (v, rv)):
+        assert torch.equal(a, b.transpose(1, 2))
