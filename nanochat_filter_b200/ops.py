@@ -375,6 +375,8 @@ def _proj_scan_op(x, weight, inits, logit_bias, NH, NKVH, da, r, use_sigmoid):
 def _ps_setup(ctx, inputs, output):
     x, weight, inits, logit_bias, NH, NKVH, da, r, use_sigmoid = inputs
     combined, hq, hk, hv = output
+    # `combined` is usually not used downstream: keep its gradient None instead of a zero tensor
+    ctx.set_materialize_grads(False)
     ctx.save_for_backward(x, weight, combined, inits, logit_bias, hq, hk, hv)
     ctx.args = (NH, NKVH, da, r)
     ctx.use_sigmoid = use_sigmoid
