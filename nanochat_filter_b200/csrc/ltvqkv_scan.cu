@@ -684,9 +684,8 @@ template <int kTT>
 decltype(&scan_fwd_rows_kernel<128, 32>) row_fwd_kernel(int D) {
   return D == 64 ? scan_fwd_rows_kernel<64, kTT> : (D == 128 ? scan_fwd_rows_kernel<128, kTT> : scan_fwd_rows_kernel<256, kTT>);
 }
-template <int kTT>
 decltype(&scan_bwd_rows_kernel<128, 32>) row_bwd_kernel(int D) {
-  return D == 64 ? scan_bwd_rows_kernel<64, kTT> : (D == 128 ? scan_bwd_rows_kernel<128, kTT> : scan_bwd_rows_kernel<256, kTT>);
+  return D == 64 ? scan_bwd_rows_kernel<64, 32> : (D == 128 ? scan_bwd_rows_kernel<128, 32> : scan_bwd_rows_kernel<256, 32>);
 }
 // Chunk lengths and ring depths of the row kernels, measured on B200 at config 2 (576 rows, head
 // dim 128). Forward: 64-token chunks (128-byte value-tile rows; 32 when a decay group is narrower
@@ -805,8 +804,8 @@ int try_row_bwd(bool& used, int dtype, const void* combined, int64_t sc_b, int64
   f.B = B; f.T = T; f.NH = NH; f.NKVH = NKVH; f.Da = Da; f.r = r; f.D = D; f.H = H; f.F = Fh;
   f.nchunks = (T + rtt - 1) / rtt; f.nrows = B * H; f.use_sigmoid = use_sigmoid; f.stages = rst;
   f.ws = reinterpret_cast<WorkspaceHeader*>(ws);
-  const int threads = D + 32;
-  auto kern = rtt == 64 ? row_bwd_kernel<64>(D) : row_bwd_kernel<32>(D);
+  const int threads = D / 2 + 32;  // consumers own channel pairs, plus the producer warp
+  auto kern = row_bwd_kernel(D);  // 32-token chunks
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tsm) != cudaSuccess)
     return ltvqkv_host::check_launch();
   const int grid = persistent_grid((const void*)kern, threads, tsm, f.nrows);

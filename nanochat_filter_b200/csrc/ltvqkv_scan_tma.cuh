@@ -84,7 +84,8 @@ inline size_t row_fwd_smem_bytes(int D, int Da, int H, int tt, int stages) {
 }
 inline size_t row_bwd_smem_bytes(int D, int Da, int H, int tt, int stages) {
   return 1024 + (size_t)stages * row_bwd_stage_bytes(D, Da, tt) + (size_t)row_align(H * Da, 4) * 4 +
-         (size_t)16 * Da * tt + 4 * 32 + sizeof(RowTile) * stages + 16 + 16 * stages + 64;
+         (size_t)16 * Da * tt + (size_t)4 * (D / 32) * tt + (size_t)4 * Da * tt + sizeof(RowTile) * stages + 16 +
+         16 * stages + 64;
 }
 
 
@@ -100,7 +101,7 @@ constexpr int row_fwd_min_blocks(int D, int tt) {
   return row_min_blocks(4 * row_fwd_stage_bytes(D, 1, tt) + 3072, D + 32, 64);
 }
 constexpr int row_bwd_min_blocks(int D, int tt) {
-  return row_min_blocks(2 * row_bwd_stage_bytes(D, 1, tt) + 3072, D + 32, 96);
+  return row_min_blocks(2 * row_bwd_stage_bytes(D, 1, tt) + 3072, D / 2 + 32, 128);
 }
 
 
@@ -254,7 +255,7 @@ __global__ void __launch_bounds__(kD + 32, row_fwd_min_blocks(kD, kTT))
 // Backward
 // ------------------------------------------------------------------------------------------
 template <int kD, int kTT>
-__global__ void __launch_bounds__(kD + 32, row_bwd_min_blocks(kD, kTT))
+__global__ void __launch_bounds__(kD / 2 + 32, row_bwd_min_blocks(kD, kTT))
     scan_bwd_rows_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_constant__ CUtensorMap tm_l,
                          const __grid_constant__ CUtensorMap tm_du,
                          const __grid_constant__ CUtensorMap tm_gq, const __grid_constant__ CUtensorMap tm_gk,
@@ -263,7 +264,7 @@ __global__ void __launch_bounds__(kD + 32, row_bwd_min_blocks(kD, kTT))
                          const TmaBwdArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   uint8_t* base = smem_align<uint8_t>(smem_raw, 1024);
-  constexpr int D = kD, ncons = kD, LB = row_bwd_logit_box(kTT);
+  constexpr int D = kD, ncons = kD / 2, LB = row_bwd_logit_box(kTT);  // a consumer owns two channels
   const int S = a.stages;
   const int Da = a.Da;
   const int sbytes = row_bwd_stage_bytes(D, Da, kTT);
@@ -273,8 +274,10 @@ __global__ void __launch_bounds__(kD + 32, row_bwd_min_blocks(kD, kTT))
   uint8_t* stages = base;
   float* lb_s = reinterpret_cast<float*>(stages + S * sbytes);               // [H][Da]
   float4* gates = reinterpret_cast<float4*>(lb_s + row_align(nlb, 4));       // [Da][kTT]
-  float* wsum = reinterpret_cast<float*>(gates + Da * kTT);                  // [ncons / 32]
-  RowTile* info = reinterpret_cast<RowTile*>(wsum + 32);                     // [S]
+  // dalpha partial sums per lane segment (see below) and per-row logit-bias sums
+  float* part = reinterpret_cast<float*>(gates + Da * kTT);                  // [D / 32][kTT]
+  float* bsum = part + (D / 32) * kTT;                                        // [Da][kTT]
+  RowTile* info = reinterpret_cast<RowTile*>(bsum + Da * kTT);               // [S]
   uint64_t* full = smem_align<uint64_t>(info + S, 16);
   uint64_t* empty = full + S;
   __shared__ volatile int abort_flag;
@@ -336,15 +339,26 @@ __global__ void __launch_bounds__(kD + 32, row_bwd_min_blocks(kD, kTT))
     }
     __syncwarp();
   } else {
-    // ---------------- consumers: thread c = channel ----------------
-    const int c = tid;
-    const int gi = c / a.r;
-    const int tpp = a.r / kTT;  // threads per (group, token) pair in the group sums
-    const int pair = tid / tpp, part = tid % tpp;
-    const int pg = pair / kTT, pt = pair % kTT;
-    float carry = 0.f;   // adjoint of h at the first token of the previously processed chunk
-    __nv_bfloat16 init_c = __float2bfloat16_rn(0.f);  // h_{-1} of this channel
-    float bias_t = 0.f;  // part == 0: this row's sum of dlogit at token offset pt of group pg
+    // ---------------- consumers: thread = channel pair (2 tid, 2 tid + 1) ----------------
+    // Two adjacent channels per thread: every 16-bit G/H access of the walk becomes one 32-bit
+    // access, a full 128-byte shared-memory wavefront per warp instead of half of one.
+    static_assert(kTT == 32, "the backward walks 32-token chunks (four 8-token blocks)");
+    const int gi = (2 * tid) / a.r;  // r is even, so both channels share the decay group
+    // dalpha group sums: a "segment" of lanes covers min(r, 64) channels of one group; within a
+    // warp, each 8-token block is reduced by a transposing butterfly (three halving rounds, then
+    // plain rounds), so lane l ends with the segment's sum of token (l / (seg/8)) & 7 of the block.
+    const int seg = a.r >= 64 ? 32 : a.r / 2;        // lanes per segment (16 or 32)
+    const int m1 = seg / 2, m2 = seg / 4, m3 = seg / 8;
+    const int tloc = ((lane & m1) ? 4 : 0) + ((lane & m2) ? 2 : 0) + ((lane & m3) ? 1 : 0);
+    const bool canon = (lane & (m3 - 1)) == 0;        // one lane per (segment, token) writes
+    const int segid = warp * (32 / seg) + lane / seg;
+    const int spg = a.r / (2 * seg);                  // segments per group
+    // value-tile rows 2 tid and 2 tid + 1 are read in lane-dependent order, so that the 8 lanes of
+    // a shared-memory phase hit 8 different 16-byte bank groups under the tile's swizzle
+    const int sw = (lane >> 2) & 1;
+    float carry0 = 0.f, carry1 = 0.f;  // adjoints of h at the first token of the previous chunk
+    uint32_t init2 = 0;                 // h_{-1} of both channels (bf16 pair)
+    float bias_q[2] = {0.f, 0.f};       // this row's dlogit sums of (group, token) entries q = tid + i*ncons
     for (int i = 0;; ++i) {
       const int st = i % S;
       const uint32_t ph = (uint32_t)(i / S) & 1u;
@@ -354,14 +368,15 @@ __global__ void __launch_bounds__(kD + 32, row_bwd_min_blocks(kD, kTT))
       const long long rowbase = (long long)ti.b * a.H + ti.h;
       uint8_t* sb = stages + st * sbytes;
       if (ti.j == a.nchunks - 1) {
-        carry = 0.f;
-        bias_t = 0.f;
-        init_c = reinterpret_cast<const __nv_bfloat16*>(sb + ioff)[c];
+        carry0 = carry1 = 0.f;
+        bias_q[0] = bias_q[1] = 0.f;
+        init2 = reinterpret_cast<const uint32_t*>(sb + ioff)[tid];
       }
       const __nv_bfloat16* L_s = reinterpret_cast<const __nv_bfloat16*>(sb + loff);
-      __nv_bfloat16* H_s = reinterpret_cast<__nv_bfloat16*>(sb + hoff);
+      const uint32_t* G32 = reinterpret_cast<const uint32_t*>(sb + goff);
+      uint32_t* H32 = reinterpret_cast<uint32_t*>(sb + hoff);
       // h_{t-1} of the row's first token is the initial state (the tile's row -1 was filled with 0)
-      if (ti.t0 == 0) H_s[c] = init_c;
+      if (ti.t0 == 0) H32[tid] = init2;
       for (int q = tid; q < Da * kTT; q += ncons) {
         const int g = q / kTT, t = q % kTT;
         const float lb = lb_s[ti.h * Da + g];
@@ -378,82 +393,104 @@ __global__ void __launch_bounds__(kD + 32, row_bwd_min_blocks(kD, kTT))
       }
       named_barrier(1, ncons);  // gates ready
 
-      // reverse walk: adjoint carry, du, and the per-token dalpha terms. Thread c alone reads the
-      // 16-bit slots G[t][c] and H[t][c]; once it has, it stores dalpha(t, c) there as an fp32 split
-      // into its high and low halves, so the table needs no space, registers or barrier of its own.
+      // reverse walk: adjoint carries, du, and the per-token dalpha terms of both channels
       const float4* grow = gates + gi * kTT;
-      uint16_t* G16 = reinterpret_cast<uint16_t*>(sb + goff);
-      uint16_t* H16 = reinterpret_cast<uint16_t*>(sb + hoff);
       // one 8-token block per iteration: unrolling across blocks would let every block's loads be
       // hoisted to the top and spill
 #pragma unroll 1
       for (int k = kTT / 8 - 1; k >= 0; --k) {
-        float f[8], du[8];
-        uint4* slot = const_cast<uint4*>(swz_chunk<kTT>(sb, c, k));  // read by thread c alone
-        unpack8(*slot, f);
+        uint4* slotA = const_cast<uint4*>(swz_chunk<kTT>(sb, 2 * tid + sw, k));
+        uint4* slotB = const_cast<uint4*>(swz_chunk<kTT>(sb, 2 * tid + 1 - sw, k));
+        const uint4 vA = *slotA, vB = *slotB;
+        float f0[8], f1[8], du0[8], du1[8], ds[8];
+        unpack8(sw ? vB : vA, f0);
+        unpack8(sw ? vA : vB, f1);
 #pragma unroll
         for (int e = 7; e >= 0; --e) {
           const int t = 8 * k + e;
           const float4 gv = grow[t];
-          carry = gv.x * carry + __uint_as_float((uint32_t)G16[t * D + c] << 16);
-          du[e] = gv.y * carry;
-          const float d = (f[e] - __uint_as_float((uint32_t)H16[t * D + c] << 16)) * carry * gv.z;
-          const uint32_t bits = __float_as_uint(d);
-          G16[t * D + c] = (uint16_t)(bits >> 16);
-          H16[t * D + c] = (uint16_t)(bits & 0xffffu);
+          const uint32_t g2 = G32[t * (D / 2) + tid], h2 = H32[t * (D / 2) + tid];
+          carry0 = gv.x * carry0 + __uint_as_float(g2 << 16);
+          carry1 = gv.x * carry1 + __uint_as_float(g2 & 0xffff0000u);
+          du0[e] = gv.y * carry0;
+          du1[e] = gv.y * carry1;
+          const float d0 = (f0[e] - __uint_as_float(h2 << 16)) * carry0 * gv.z;
+          const float d1 = (f1[e] - __uint_as_float(h2 & 0xffff0000u)) * carry1 * gv.z;
+          ds[e] = d0 + d1;
         }
-        *slot = pack8(du);  // du takes the value tile's place: the tile leaves as one bulk store
+        // du takes the value tile's place: the tile leaves as one bulk store
+        const uint4 p0 = pack8(du0), p1 = pack8(du1);
+        *slotA = sw ? p1 : p0;
+        *slotB = sw ? p0 : p1;
+        // the block's 8 dalpha terms summed over the segment's lanes: halving rounds keep the
+        // upper half of the values in the lanes with the round's mask bit set
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const bool up = (lane & m1) != 0;
+          const float send = up ? ds[j] : ds[j + 4];
+          const float keep = up ? ds[j + 4] : ds[j];
+          ds[j] = keep + __shfl_xor_sync(0xffffffffu, send, m1);
+        }
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const bool up = (lane & m2) != 0;
+          const float send = up ? ds[j] : ds[j + 2];
+          const float keep = up ? ds[j + 2] : ds[j];
+          ds[j] = keep + __shfl_xor_sync(0xffffffffu, send, m2);
+        }
+        {
+          const bool up = (lane & m3) != 0;
+          const float send = up ? ds[0] : ds[1];
+          const float keep = up ? ds[1] : ds[0];
+          ds[0] = keep + __shfl_xor_sync(0xffffffffu, send, m3);
+        }
+        for (int o = m3 >> 1; o > 0; o >>= 1) ds[0] += __shfl_xor_sync(0xffffffffu, ds[0], o);
+        if (canon) part[segid * kTT + 8 * k + tloc] = ds[0];
       }
-      if (ti.t0 == 0) a.grad_inits[rowbase * D + c] = __float2bfloat16_rn(carry * (1.0f - grow[0].y));
+      if (ti.t0 == 0) {
+        const __nv_bfloat162 gi2 =
+            __floats2bfloat162_rn(carry0 * (1.0f - grow[0].y), carry1 * (1.0f - grow[0].y));
+        reinterpret_cast<__nv_bfloat162*>(a.grad_inits + rowbase * D)[tid] = gi2;
+      }
       fence_proxy_async_smem();
-      named_barrier(1, ncons);  // the dalpha table and the du tile are complete
+      named_barrier(1, ncons);  // the du tile and the segment sums are complete
       if (tid == 0) {
         tma_store_2d(&tm_du, sb, ti.t0, ti.b * a.F + ti.h * (D + Da));  // columns beyond T are clipped
         tma_store_commit();
       }
-
-      {
-        // this thread's kTT channels of token pt of group pg: 16-byte pieces, rotated by lane so the
-        // 8 lanes of a shared-memory phase hit 8 different bank groups
-        const uint4* ghi = reinterpret_cast<const uint4*>(G16 + pt * D + pg * a.r + part * kTT);
-        const uint4* glo = reinterpret_cast<const uint4*>(H16 + pt * D + pg * a.r + part * kTT);
-        float s0 = 0.f, s1 = 0.f;
+      // dlogit of each (group, token): the group's segment sums in a fixed order
 #pragma unroll
-        for (int q = 0; q < kTT / 8; ++q) {
-          const int qq = (q + lane) & (kTT / 8 - 1);
-          const uint4 hi = ghi[qq], lo = glo[qq];
-          const uint32_t hw[4] = {hi.x, hi.y, hi.z, hi.w}, lw[4] = {lo.x, lo.y, lo.z, lo.w};
-#pragma unroll
-          for (int w = 0; w < 4; ++w) {
-            s0 += __uint_as_float((hw[w] << 16) | (lw[w] & 0xffffu));
-            s1 += __uint_as_float((hw[w] & 0xffff0000u) | (lw[w] >> 16));
+      for (int qi = 0; qi < 2; ++qi) {
+        const int q = tid + qi * ncons;
+        if (q < Da * kTT) {
+          const int g = q / kTT, t = q % kTT;
+          float sum = 0.f;
+          for (int j = 0; j < spg; ++j) sum += part[(g * spg + j) * kTT + t];
+          if (t < ti.tlen) {
+            a.grad_combined[((long long)ti.b * a.F + ti.h * (D + Da) + D + g) * a.T + ti.t0 + t] =
+                __float2bfloat16_rn(sum);
+            bias_q[qi] += sum;
           }
-        }
-        float sum = s0 + s1;
-        for (int o = tpp >> 1; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-        if (part == 0 && pt < ti.tlen) {
-          a.grad_combined[((long long)ti.b * a.F + ti.h * (D + Da) + D + pg) * a.T + ti.t0 + pt] =
-              __float2bfloat16_rn(sum);
-          bias_t += sum;
         }
       }
       fence_proxy_async_smem();  // order this thread's writes into the stage before the next TMA fill
       if (tid == 0) tma_store_wait_read0();  // the du tile has left the stage
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[st]);  // the stage (and the dalpha table in it) is free
+      named_barrier(1, ncons);   // every segment sum has been read (`part` is rewritten next chunk)
+      if (lane == 0) mbar_arrive(&empty[st]);  // the stage is free
 
       if (ti.j == 0) {  // row done: this row's logit-bias partials, a fixed-order sum per group
-        float v = part == 0 ? bias_t : 0.f;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-        if (lane == 0) wsum[warp] = v;
+        for (int qi = 0; qi < 2; ++qi) {
+          const int q = tid + qi * ncons;
+          if (q < Da * kTT) bsum[q] = bias_q[qi];
+        }
         named_barrier(1, ncons);
         if (tid < Da) {
-          const int wpg = a.r / 32;  // warps per group
           float t = 0.f;
-          for (int w = 0; w < wpg; ++w) t += wsum[tid * wpg + w];
+          for (int j = 0; j < kTT; ++j) t += bsum[tid * kTT + j];
           a.bias_part[rowbase * Da + tid] = t;
         }
+        named_barrier(1, ncons);  // bsum is free again
       }
     }
     if (tid == 0) tma_store_wait0();
