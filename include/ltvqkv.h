@@ -137,6 +137,40 @@ LTVQKV_API int ltvqkv_scan_bwd(int dtype,
                     void* workspace, size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------------------------
+ * Look-back scan: replaces cpp_ewma_cuda.ltv_look_back_fused_concat_head_major_register_cast_
+ * {blelloch,sequential}_scan_cuda_{forward,backward} (reference cpp_ewma/src/ltv_look_back_*.cu;
+ * semantics nanochat/ops/ltv_reference_ops.py:37-124). Tokens are split into chunks [0, P),
+ * [P + (i-1) Q, P + i Q); each chunk's outputs come from the recurrence restarted from the initial
+ * state K - 1 tokens before the chunk (those warm-up states are not output). P >= T is the plain
+ * scan. Arguments as ltvqkv_scan_fwd / ltvqkv_scan_bwd plus P, Q, K (>= 1); outputs q/k/v are
+ * contiguous [B, heads, T, D]; D = Da * r <= 1024. The backward's workspace holds per-(batch,
+ * head) bias partials (ltvqkv_lookback_workspace_bytes); grad_logit_bias is accumulated into
+ * (zero it first), grad_combined and grad_inits are overwritten. fp32 follows the reference
+ * oracle's operation order (separately rounded products and sums, later chunks' contributions
+ * first). A warm-up prefix longer than about 13k tokens (D = 128) returns LTVQKV_ERR_TOO_LARGE. */
+LTVQKV_API size_t ltvqkv_lookback_workspace_bytes(int B, int NH, int NKVH, int Da);
+LTVQKV_API int ltvqkv_lookback_scan_fwd(int dtype,
+                    const void* combined, int64_t sc_b, int64_t sc_t, int64_t sc_e,
+                    const void* inits, const float* logit_bias,
+                    void* out_q, void* out_k, void* out_v,
+                    int B, int T, int NH, int NKVH, int Da, int r,
+                    int64_t P, int64_t Q, int64_t K, int use_sigmoid, void* stream);
+LTVQKV_API int ltvqkv_lookback_scan_bwd(int dtype,
+                    const void* combined, int64_t sc_b, int64_t sc_t, int64_t sc_e,
+                    const void* inits, const float* logit_bias,
+                    const void* hq, const int64_t* hq_strides,
+                    const void* hk, const int64_t* hk_strides,
+                    const void* hv, const int64_t* hv_strides,
+                    const void* grad_hq, const int64_t* gq_strides,
+                    const void* grad_hk, const int64_t* gk_strides,
+                    const void* grad_hv, const int64_t* gv_strides,
+                    void* grad_combined, int64_t gc_b, int64_t gc_t, int64_t gc_e,
+                    void* grad_inits, float* grad_logit_bias,
+                    int B, int T, int NH, int NKVH, int Da, int r,
+                    int64_t P, int64_t Q, int64_t K, int use_sigmoid,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------------------------
  * Projection ("fused linear transpose"): replaces cpp_ewma_cuda.fused_linear_transpose
  * (reference cpp_ewma/src/fused_linear_transpose_forward.cu:23-58; called from
  * nanochat/ops/fused_linear_transpose.py:20-41).

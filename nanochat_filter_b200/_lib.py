@@ -36,6 +36,9 @@ EXPORTED_SYMBOLS = (
     "ltvqkv_debug_wait_timeout",
     "ltvqkv_scan_fwd_noalloc",
     "ltvqkv_proj_scan_fwd",
+    "ltvqkv_lookback_workspace_bytes",
+    "ltvqkv_lookback_scan_fwd",
+    "ltvqkv_lookback_scan_bwd",
 )
 
 _lib: Optional[ctypes.CDLL] = None
@@ -67,6 +70,17 @@ def _declare(lib: ctypes.CDLL) -> None:
                                     _vp, _pi64, _vp, _pi64, _vp, _pi64,
                                     _vp, _i64, _i64, _i64, _vp, _pf,
                                     _i, _i, _i, _i, _i, _i, _i, _vp, _sz, _vp]
+    lib.ltvqkv_lookback_workspace_bytes.restype = _sz
+    lib.ltvqkv_lookback_workspace_bytes.argtypes = [_i, _i, _i, _i]
+    lib.ltvqkv_lookback_scan_fwd.restype = _i
+    lib.ltvqkv_lookback_scan_fwd.argtypes = [_i, _vp, _i64, _i64, _i64, _vp, _pf, _vp, _vp, _vp,
+                                             _i, _i, _i, _i, _i, _i, _i64, _i64, _i64, _i, _vp]
+    lib.ltvqkv_lookback_scan_bwd.restype = _i
+    lib.ltvqkv_lookback_scan_bwd.argtypes = [_i, _vp, _i64, _i64, _i64, _vp, _pf,
+                                             _vp, _pi64, _vp, _pi64, _vp, _pi64,
+                                             _vp, _pi64, _vp, _pi64, _vp, _pi64,
+                                             _vp, _i64, _i64, _i64, _vp, _pf,
+                                             _i, _i, _i, _i, _i, _i, _i64, _i64, _i64, _i, _vp, _sz, _vp]
     lib.ltvqkv_gemm_workspace_bytes.restype = _sz
     lib.ltvqkv_gemm_workspace_bytes.argtypes = []
     lib.ltvqkv_gemm_fwd.restype = _i

@@ -1,0 +1,340 @@
+// Look-back (chunk-restarting) scan, forward and backward.
+//
+// The reference's look-back scans (nanochat/ops/ltv_cuda_look_back_fused_concat_head_major_register_cast_
+// {blelloch,sequential}_scan.py; semantics in nanochat/ops/ltv_reference_ops.py:37-124) split the
+// T tokens into chunks — [0, P), then [P + (i-1) Q, P + i Q) — and compute every chunk's outputs
+// with the same recurrence h_t = (1 - a_t) h_{t-1} + a_t u_t, restarted from the initial state
+// K - 1 tokens before the chunk (a warm-up prefix whose states are not output). P >= T is the
+// plain scan; K = 1 restarts exactly at each chunk.
+//
+// B200 layout: one CTA per (batch, head) row, thread c = channel c, tokens walked in order with
+// the state in a register; the decay of channel c's group is evaluated by the thread itself. The
+// backward walks the chunks in reverse, and inside a chunk first the chunk's own tokens (h_{t-1}
+// read from the saved outputs, which are that chunk's states rounded to the storage dtype) and
+// then the warm-up prefix, whose states are replayed in 32-token blocks from checkpoints kept in
+// shared memory. Contributions of overlapping prefixes to one element of grad_combined are added
+// in the reference autograd graph's order — later chunks first, each rounded to the storage dtype
+// and summed in it — and the per-token group sums of dalpha are sequential in the channel index,
+// so fp32 results follow the reference oracle's operation order (separately rounded multiplies
+// and adds, no FMA contraction). Every grad_combined element is written by exactly one thread.
+#include "ltvqkv_common.cuh"
+
+namespace ltvqkv {
+namespace {
+
+constexpr int kLbBlock = 32;  // prefix replay block (tokens)
+
+struct LbArgs {
+  const void* combined;
+  long long sc_b, sc_t, sc_e;
+  const void* inits;
+  const float* logit_bias;
+  void* out[3];
+  const void* h[3];
+  long long hs[3][4];
+  const void* gh[3];
+  long long gs[3][4];
+  void* grad_combined;
+  long long gc_b, gc_t, gc_e;
+  void* grad_inits;
+  float* bias_part;  // [B][H][Da]
+  int B, T, NH, NKVH, Da, r, D, H, use_sigmoid;
+  long long P, Q, K;
+  int nchunks, ncp;  // chunks per row; prefix checkpoints
+};
+
+template <typename S>
+LTVQKV_DEVICE float ld(const void* p, long long i) {
+  if constexpr (sizeof(S) == 4) return reinterpret_cast<const float*>(p)[i];
+  else return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+}
+template <typename S>
+LTVQKV_DEVICE void st(void* p, long long i, float v) {
+  if constexpr (sizeof(S) == 4) reinterpret_cast<float*>(p)[i] = v;
+  else reinterpret_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
+}
+// Rounding to the storage dtype (identity for fp32).
+template <typename S>
+LTVQKV_DEVICE float qz(float v) {
+  if constexpr (sizeof(S) == 4) return v;
+  else return __bfloat162float(__float2bfloat16_rn(v));
+}
+
+LTVQKV_DEVICE void chunk_bounds(const LbArgs& a, int ci, int& t_start, int& t_end, int& t_pref) {
+  long long s = ci == 0 ? 0 : a.P + (long long)(ci - 1) * a.Q;
+  long long e = ci == 0 ? a.P : a.P + (long long)ci * a.Q;
+  if (e > a.T) e = a.T;
+  long long p = s - (a.K - 1);
+  t_start = (int)s;
+  t_end = (int)e;
+  t_pref = p < 0 ? 0 : (int)p;
+}
+
+template <typename S>
+LTVQKV_DEVICE float lb_alpha(const LbArgs& a, long long cb, int t, int col, int h, int g) {
+  const float raw = __fadd_rn(ld<S>(a.combined, cb + (long long)t * a.sc_t + (long long)(col + a.D + g) * a.sc_e),
+                              a.logit_bias[h * a.Da + g]);
+  if (!a.use_sigmoid) return raw;
+  if constexpr (sizeof(S) == 4) return sigmoid_f32_exact(raw);
+  else return sigmoid_f32(raw);
+}
+
+// s' = (1 - a) s + a u, each product and the sum rounded once
+LTVQKV_DEVICE float lb_step(float s, float al, float u) {
+  return __fadd_rn(__fmul_rn(__fsub_rn(1.0f, al), s), __fmul_rn(al, u));
+}
+
+template <typename S>
+__global__ void __launch_bounds__(1024) lookback_fwd_kernel(LbArgs a) {
+  const int b = blockIdx.x / a.H, h = blockIdx.x % a.H;
+  const int c = threadIdx.x;
+  if (c >= a.D) return;
+  int which, hloc, nheads;
+  split_head(h, a.NH, a.NKVH, which, hloc, nheads);
+  const long long cb = (long long)b * a.sc_b;
+  const int col = h * (a.D + a.Da);
+  const int g = c / a.r;
+  const float init = ld<S>(a.inits, ((long long)b * a.H + h) * a.D + c);
+  const long long ob = ((long long)b * nheads + hloc) * (long long)a.T * a.D + c;
+  for (int ci = 0; ci < a.nchunks; ++ci) {
+    int t_start, t_end, t_pref;
+    chunk_bounds(a, ci, t_start, t_end, t_pref);
+    float s = init;
+    for (int t = t_pref; t < t_end; ++t) {
+      const float al = lb_alpha<S>(a, cb, t, col, h, g);
+      s = lb_step(s, al, ld<S>(a.combined, cb + (long long)t * a.sc_t + (long long)(col + c) * a.sc_e));
+      if (t >= t_start) st<S>(a.out[which], ob + (long long)t * a.D, s);
+    }
+  }
+}
+
+// One token of the reverse sweep: du and dlogit contributions of this chunk (rounded to the
+// storage dtype and added to what later chunks left, or stored when no later chunk reached the
+// token), the group sums of dalpha, and the adjoint carry. All threads of the CTA call it.
+template <typename S>
+LTVQKV_DEVICE void lb_bwd_token(const LbArgs& a, float* red, long long cb, long long gcb, int col, int h, int g,
+                                bool active, int c, int t, float sprev, bool first, float& gacc, float& bias_acc) {
+  float al = 0.f;
+  if (active) {
+    al = lb_alpha<S>(a, cb, t, col, h, g);
+    const float u = ld<S>(a.combined, cb + (long long)t * a.sc_t + (long long)(col + c) * a.sc_e);
+    const long long gi = gcb + (long long)t * a.gc_t + (long long)(col + c) * a.gc_e;
+    const float du = qz<S>(__fmul_rn(gacc, al));
+    st<S>(a.grad_combined, gi, first ? du : __fadd_rn(ld<S>(a.grad_combined, gi), du));
+    red[c] = __fmul_rn(gacc, __fsub_rn(u, sprev));
+  }
+  __syncthreads();
+  if (c < a.Da) {
+    float ga = 0.f;
+    for (int k = 0; k < a.r; ++k) ga = __fadd_rn(ga, red[c * a.r + k]);
+    const float ag = lb_alpha<S>(a, cb, t, col, h, c);
+    const float graw = a.use_sigmoid ? __fmul_rn(__fmul_rn(ga, __fsub_rn(1.0f, ag)), ag) : ga;
+    const long long gi = gcb + (long long)t * a.gc_t + (long long)(col + a.D + c) * a.gc_e;
+    const float dl = qz<S>(graw);
+    st<S>(a.grad_combined, gi, first ? dl : __fadd_rn(ld<S>(a.grad_combined, gi), dl));
+    bias_acc = __fadd_rn(bias_acc, graw);
+  }
+  __syncthreads();
+  if (active) gacc = __fmul_rn(gacc, __fsub_rn(1.0f, al));
+}
+
+template <typename S>
+__global__ void __launch_bounds__(1024) lookback_bwd_kernel(LbArgs a) {
+  extern __shared__ float sm[];
+  const int nth = blockDim.x;
+  float* red = sm;                       // [nth]
+  float* cp = red + nth;                 // [ncp][D]: state before each kLbBlock-th prefix token
+  float* blk = cp + (long long)a.ncp * a.D;  // [kLbBlock][D]: replayed states of one prefix block
+  const int b = blockIdx.x / a.H, h = blockIdx.x % a.H;
+  const int c = threadIdx.x;
+  const bool active = c < a.D;
+  const int cc = active ? c : 0;
+  int which, hloc, nheads;
+  split_head(h, a.NH, a.NKVH, which, hloc, nheads);
+  const long long cb = (long long)b * a.sc_b, gcb = (long long)b * a.gc_b;
+  const int col = h * (a.D + a.Da);
+  const int g = cc / a.r;
+  const long long* hs = a.hs[which];
+  const long long* gs = a.gs[which];
+  const long long hb = (long long)b * hs[0] + (long long)hloc * hs[1] + (long long)cc * hs[3];
+  const long long gb = (long long)b * gs[0] + (long long)hloc * gs[1] + (long long)cc * gs[3];
+  const float init = active ? ld<S>(a.inits, ((long long)b * a.H + h) * a.D + cc) : 0.f;
+  float ginit = 0.f;
+  float bias_acc = 0.f;  // threads c < Da: their group's bias gradient
+  int next_pref = a.T;   // t_pref of the next (later) chunk: tokens at or beyond it were reached already
+  for (int ci = a.nchunks - 1; ci >= 0; --ci) {
+    int t_start, t_end, t_pref;
+    chunk_bounds(a, ci, t_start, t_end, t_pref);
+    const int npre = t_start - t_pref;
+    // warm-up prefix replay with checkpoints (states before tokens t_pref + kLbBlock * j)
+    float s = init;
+    for (int i = 0; i < npre; ++i) {
+      if (active && i % kLbBlock == 0) cp[(long long)(i / kLbBlock) * a.D + c] = s;
+      if (active) s = lb_step(s, lb_alpha<S>(a, cb, t_pref + i, col, h, g),
+                              ld<S>(a.combined, cb + (long long)(t_pref + i) * a.sc_t + (long long)(col + c) * a.sc_e));
+    }
+    const float s_pre = qz<S>(s);  // the chunk's h_{t_start - 1}, rounded like a stored output
+    float gacc = 0.f;
+    // the chunk's own tokens: h_{t-1} is the saved output
+    for (int t = t_end - 1; t >= t_start; --t) {
+      float sprev = 0.f;
+      if (active) {
+        gacc = __fadd_rn(gacc, ld<S>(a.gh[which], gb + (long long)t * gs[2]));
+        sprev = t > t_start ? ld<S>(a.h[which], hb + (long long)(t - 1) * hs[2]) : s_pre;
+      }
+      lb_bwd_token<S>(a, red, cb, gcb, col, h, g, active, c, t, sprev, t < next_pref, gacc, bias_acc);
+    }
+    // the prefix, one replayed block at a time from the last
+    for (int j = (npre - 1) / kLbBlock; npre > 0 && j >= 0; --j) {
+      const int i0 = j * kLbBlock, n = min(kLbBlock, npre - i0);
+      if (active) {
+        float q = cp[(long long)j * a.D + c];
+        for (int i = 0; i < n; ++i) {
+          blk[(long long)i * a.D + c] = q;
+          q = lb_step(q, lb_alpha<S>(a, cb, t_pref + i0 + i, col, h, g),
+                      ld<S>(a.combined, cb + (long long)(t_pref + i0 + i) * a.sc_t + (long long)(col + c) * a.sc_e));
+        }
+      }
+      for (int i = n - 1; i >= 0; --i) {
+        const int t = t_pref + i0 + i;
+        const float sprev = active ? qz<S>(blk[(long long)i * a.D + c]) : 0.f;
+        lb_bwd_token<S>(a, red, cb, gcb, col, h, g, active, c, t, sprev, t < next_pref, gacc, bias_acc);
+      }
+    }
+    ginit = __fadd_rn(ginit, gacc);
+    next_pref = t_pref;
+  }
+  if (active) st<S>(a.grad_inits, ((long long)b * a.H + h) * a.D + c, ginit);
+  if (c < a.Da) a.bias_part[((long long)b * a.H + h) * a.Da + c] = bias_acc;
+}
+
+// grad_logit_bias[h, g] += sum over b (descending, the oracle's order) of per-(b, h) partials.
+__global__ void lookback_bias_reduce_kernel(const float* part, float* grad_bias, int B, int H, int Da) {
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= H * Da) return;
+  float sum = 0.f;
+  for (int b = B - 1; b >= 0; --b) sum = __fadd_rn(sum, part[(long long)b * H * Da + idx]);
+  grad_bias[idx] = __fadd_rn(grad_bias[idx], sum);
+}
+
+int lb_chunks(int T, long long P, long long Q) {
+  if ((long long)T <= P) return 1;
+  return (int)(1 + ((long long)T - P + Q - 1) / Q);
+}
+
+int lb_validate(int dtype, int B, int T, int NH, int NKVH, int Da, int r, long long P, long long Q, long long K) {
+  if (!ltvqkv_host::valid_dtype(dtype)) return LTVQKV_ERR_DTYPE;
+  if (B < 0 || T < 0 || NH < 0 || NKVH < 0 || Da < 1 || r < 1 || P < 1 || Q < 1 || K < 1) return LTVQKV_ERR_SHAPE;
+  if ((long long)Da * r > 1024) return LTVQKV_ERR_SHAPE;  // one thread per channel
+  return LTVQKV_OK;
+}
+
+int lb_threads(int D) { return (D + 31) / 32 * 32; }
+
+size_t lb_bwd_smem(int D, int T, long long K, int& ncp) {
+  const long long npre_max = std::min<long long>(K - 1, T);
+  ncp = (int)((npre_max + kLbBlock - 1) / kLbBlock);
+  return sizeof(float) * ((size_t)lb_threads(D) + (size_t)ncp * D + (size_t)kLbBlock * D);
+}
+
+}  // namespace
+}  // namespace ltvqkv
+
+using namespace ltvqkv;
+
+extern "C" size_t ltvqkv_lookback_workspace_bytes(int B, int NH, int NKVH, int Da) {
+  if (B < 0 || NH < 0 || NKVH < 0 || Da < 1) return 0;
+  return 256 + sizeof(float) * (size_t)B * (NH + 2 * NKVH) * Da;
+}
+
+extern "C" int ltvqkv_lookback_scan_fwd(int dtype, const void* combined, int64_t sc_b, int64_t sc_t, int64_t sc_e,
+                                        const void* inits, const float* logit_bias, void* out_q, void* out_k,
+                                        void* out_v, int B, int T, int NH, int NKVH, int Da, int r, int64_t P,
+                                        int64_t Q, int64_t K, int use_sigmoid, void* stream) {
+  int rc = lb_validate(dtype, B, T, NH, NKVH, Da, r, P, Q, K);
+  if (rc != LTVQKV_OK) return rc;
+  const int H = NH + 2 * NKVH;
+  if ((long long)B * H * T == 0) return LTVQKV_OK;
+  if (!combined || !inits || !logit_bias || (NH > 0 && !out_q) || (NKVH > 0 && (!out_k || !out_v)))
+    return LTVQKV_ERR_INVALID_ARG;
+  if (sc_b < 0 || sc_t < 0 || sc_e < 0) return LTVQKV_ERR_STRIDE;
+  LbArgs a = {};
+  a.combined = combined; a.sc_b = sc_b; a.sc_t = sc_t; a.sc_e = sc_e;
+  a.inits = inits; a.logit_bias = logit_bias;
+  a.out[0] = out_q; a.out[1] = out_k; a.out[2] = out_v;
+  a.B = B; a.T = T; a.NH = NH; a.NKVH = NKVH; a.Da = Da; a.r = r; a.D = Da * r; a.H = H;
+  a.use_sigmoid = use_sigmoid; a.P = P; a.Q = Q; a.K = K;
+  a.nchunks = lb_chunks(T, P, Q);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int threads = lb_threads(a.D);
+  if (dtype == LTVQKV_DTYPE_F32)
+    lookback_fwd_kernel<float><<<(unsigned int)(B * H), threads, 0, s>>>(a);
+  else
+    lookback_fwd_kernel<__nv_bfloat16><<<(unsigned int)(B * H), threads, 0, s>>>(a);
+  return ltvqkv_host::check_launch();
+}
+
+extern "C" int ltvqkv_lookback_scan_bwd(int dtype, const void* combined, int64_t sc_b, int64_t sc_t, int64_t sc_e,
+                                        const void* inits, const float* logit_bias, const void* hq,
+                                        const int64_t* hq_strides, const void* hk, const int64_t* hk_strides,
+                                        const void* hv, const int64_t* hv_strides, const void* grad_hq,
+                                        const int64_t* gq_strides, const void* grad_hk, const int64_t* gk_strides,
+                                        const void* grad_hv, const int64_t* gv_strides, void* grad_combined,
+                                        int64_t gc_b, int64_t gc_t, int64_t gc_e, void* grad_inits,
+                                        float* grad_logit_bias, int B, int T, int NH, int NKVH, int Da, int r,
+                                        int64_t P, int64_t Q, int64_t K, int use_sigmoid, void* workspace,
+                                        size_t workspace_bytes, void* stream) {
+  int rc = lb_validate(dtype, B, T, NH, NKVH, Da, r, P, Q, K);
+  if (rc != LTVQKV_OK) return rc;
+  const int H = NH + 2 * NKVH, D = Da * r;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if ((long long)B * H == 0) return LTVQKV_OK;
+  if (T == 0) {
+    // no tokens: d init = 0, d bias unchanged
+    if (!grad_inits) return LTVQKV_ERR_INVALID_ARG;
+    if (cudaMemsetAsync(grad_inits, 0, (size_t)B * H * D * (dtype == LTVQKV_DTYPE_F32 ? 4 : 2), s) != cudaSuccess)
+      return ltvqkv_host::check_launch();
+    return LTVQKV_OK;
+  }
+  const void* hp[3] = {hq, hk, hv};
+  const void* gp[3] = {grad_hq, grad_hk, grad_hv};
+  const int64_t* hst[3] = {hq_strides, hk_strides, hv_strides};
+  const int64_t* gst[3] = {gq_strides, gk_strides, gv_strides};
+  if (!combined || !inits || !logit_bias || !grad_combined || !grad_inits || !grad_logit_bias)
+    return LTVQKV_ERR_INVALID_ARG;
+  for (int w = 0; w < 3; ++w) {
+    const int n = w == 0 ? NH : NKVH;
+    if (n > 0 && (!hp[w] || !gp[w] || !hst[w] || !gst[w])) return LTVQKV_ERR_INVALID_ARG;
+  }
+  if (sc_b < 0 || sc_t < 0 || sc_e < 0 || gc_b < 0 || gc_t < 0 || gc_e < 0) return LTVQKV_ERR_STRIDE;
+  if (!workspace || workspace_bytes < ltvqkv_lookback_workspace_bytes(B, NH, NKVH, Da)) return LTVQKV_ERR_WORKSPACE;
+  LbArgs a = {};
+  a.combined = combined; a.sc_b = sc_b; a.sc_t = sc_t; a.sc_e = sc_e;
+  a.inits = inits; a.logit_bias = logit_bias;
+  for (int w = 0; w < 3; ++w) {
+    a.h[w] = hp[w];
+    a.gh[w] = gp[w];
+    for (int k = 0; k < 4; ++k) {
+      a.hs[w][k] = hst[w] ? hst[w][k] : 0;
+      a.gs[w][k] = gst[w] ? gst[w][k] : 0;
+    }
+  }
+  a.grad_combined = grad_combined; a.gc_b = gc_b; a.gc_t = gc_t; a.gc_e = gc_e;
+  a.grad_inits = grad_inits;
+  a.bias_part = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + 256);
+  a.B = B; a.T = T; a.NH = NH; a.NKVH = NKVH; a.Da = Da; a.r = r; a.D = D; a.H = H;
+  a.use_sigmoid = use_sigmoid; a.P = P; a.Q = Q; a.K = K;
+  a.nchunks = lb_chunks(T, P, Q);
+  const size_t smem = lb_bwd_smem(D, T, K, a.ncp);
+  if (smem > 220 * 1024) return LTVQKV_ERR_TOO_LARGE;  // warm-up prefix too long for the checkpoints
+  const int threads = lb_threads(D);
+  auto kern = dtype == LTVQKV_DTYPE_F32 ? lookback_bwd_kernel<float> : lookback_bwd_kernel<__nv_bfloat16>;
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return ltvqkv_host::check_launch();
+  kern<<<(unsigned int)(B * H), threads, smem, s>>>(a);
+  rc = ltvqkv_host::check_launch();
+  if (rc != LTVQKV_OK) return rc;
+  lookback_bias_reduce_kernel<<<(H * Da + 127) / 128, 128, 0, s>>>(a.bias_part, grad_logit_bias, B, H, Da);
+  return ltvqkv_host::check_launch();
+}

@@ -13,6 +13,12 @@ so code written against the reference's `torch.ops.nanochat_cuda.*` runs unchang
   fused_linear_transpose
   fused_linear_transpose_backward_kernel
 
+the look-back (chunk-restarting) scans of nanochat/ops/ltv_cuda_look_back_fused_concat_head_major_register_cast_
+{blelloch,sequential}_scan.py (schemas ltv_cuda_ops.py:172-240; both families share one implementation):
+
+  ltv_look_back_fused_concat_head_major_register_cast_{blelloch,sequential}_scan_cuda_op (autograd)
+  ..._forward_kernel, ..._backward_kernel
+
 plus ops the reference does not have: `ltv_decode_step` (one-launch decode update) and
 `ltv_proj_scan_cuda_op` / `ltv_proj_scan_forward_kernel` (projection and scan forward in one
 call, the composition the reference's filter runs as two ops; same outputs bit for bit).
@@ -73,6 +79,34 @@ lib.define(
     "Tensor x, Tensor weight, Tensor grad_out, Tensor(a!) grad_x, Tensor(b!) grad_weight"
     ") -> ()"
 )
+_LB = "ltv_look_back_fused_concat_head_major_register_cast_{}_scan_cuda_{}"
+_LB_TUNE_FWD = {"blelloch": "int scan_threads_forward, int r_threads_forward, int r_items_forward, ",
+                "sequential": "int r_threads_forward, int r_items_forward, "}
+_LB_TUNE_BWD = {"blelloch": "int scan_threads_backward, int r_threads_backward, int r_items_backward, ",
+                "sequential": "int r_threads_backward, int r_items_backward, "}
+for _kind in ("blelloch", "sequential"):
+    lib.define(
+        f"{_LB.format(_kind, 'op')}("
+        "Tensor combined, Tensor inits, Tensor logit_bias, int NH, int NKVH, int da, int r, int P, int Q, int K, "
+        f"{_LB_TUNE_FWD[_kind]}{_LB_TUNE_BWD[_kind]}bool use_sigmoid"
+        ") -> (Tensor, Tensor, Tensor)"
+    )
+    lib.define(
+        f"{_LB.format(_kind, 'forward_kernel')}("
+        "Tensor combined, Tensor inits, Tensor logit_bias, Tensor(a!) out_q, Tensor(b!) out_k, Tensor(c!) out_v, "
+        "int B, int T, int NH, int NKVH, int da, int r, int P, int Q, int K, "
+        f"{_LB_TUNE_FWD[_kind]}bool use_sigmoid"
+        ") -> ()"
+    )
+    lib.define(
+        f"{_LB.format(_kind, 'backward_kernel')}("
+        "Tensor combined, Tensor inits, Tensor logit_bias, Tensor hq, Tensor hk, Tensor hv, "
+        "Tensor grad_hq, Tensor grad_hk, Tensor grad_hv, "
+        "Tensor(a!) grad_combined, Tensor(b!) grad_inits, Tensor(c!) grad_logit_bias, "
+        "int NH, int NKVH, int da, int r, int P, int Q, int K, "
+        f"{_LB_TUNE_BWD[_kind]}bool use_sigmoid"
+        ") -> ()"
+    )
 lib.define(
     "ltv_proj_scan_forward_kernel("
     "Tensor x, Tensor weight, Tensor inits, Tensor logit_bias, Tensor(a!) combined, "
@@ -321,6 +355,118 @@ def _flt_bwd_fake(x, weight, grad_out, grad_x, grad_weight):
 
 
 # ------------------------------------------------------------------------------------------
+# Look-back scans (reference nanochat/ops/ltv_cuda_look_back_fused_concat_head_major_register_cast_
+# {blelloch,sequential}_scan.py: op, forward_kernel, backward_kernel, autograd _setup/backward)
+# ------------------------------------------------------------------------------------------
+def _check_pqk(P, Q, K):
+    if P < 1 or Q < 1 or K < 1:
+        raise RuntimeError(f"look-back chunking needs P, Q, K >= 1, got P={P}, Q={Q}, K={K}")
+
+
+def _lb_forward_kernel(combined, inits, logit_bias, out_q, out_k, out_v, B, T, NH, NKVH, da, r, P, Q, K,
+                       *tuning_and_flag):
+    use_sigmoid = tuning_and_flag[-1]
+    _check_scan_inputs(combined, inits, logit_bias, NH, NKVH, da, r)
+    _check_pqk(P, Q, K)
+    if combined.shape[0] != B or combined.shape[1] != T:
+        raise RuntimeError(f"B={B}, T={T} do not match combined {tuple(combined.shape)}")
+    for o in (out_q, out_k, out_v):
+        if not o.is_contiguous() or o.dtype != combined.dtype:
+            raise RuntimeError("out_q/out_k/out_v must be contiguous and share combined's dtype")
+    L = _lib.load()
+    inits = inits.contiguous()
+    logit_bias = logit_bias.contiguous()
+    sc = combined.stride()
+    rc = L.ltvqkv_lookback_scan_fwd(_lib.dtype_code(combined.dtype), combined.data_ptr(), sc[0], sc[1], sc[2],
+                                    inits.data_ptr(), logit_bias.data_ptr(), out_q.data_ptr(), out_k.data_ptr(),
+                                    out_v.data_ptr(), B, T, NH, NKVH, da, r, P, Q, K, int(bool(use_sigmoid)),
+                                    _lib.stream_handle(combined.device))
+    _lib.check(rc, "ltvqkv_lookback_scan_fwd")
+
+
+def _lb_op(combined, inits, logit_bias, NH, NKVH, da, r, P, Q, K, *tuning_and_flag):
+    B, T, _ = combined.shape
+    D = da * r
+    kw = dict(device=combined.device, dtype=combined.dtype, memory_format=torch.contiguous_format)
+    out_q = torch.empty((B, NH, T, D), **kw)
+    out_k = torch.empty((B, NKVH, T, D), **kw)
+    out_v = torch.empty((B, NKVH, T, D), **kw)
+    _lb_forward_kernel(combined, inits, logit_bias, out_q, out_k, out_v, B, T, NH, NKVH, da, r, P, Q, K,
+                       tuning_and_flag[-1])
+    return out_q, out_k, out_v
+
+
+def _lb_backward_kernel(combined, inits, logit_bias, hq, hk, hv, grad_hq, grad_hk, grad_hv, grad_combined,
+                        grad_inits, grad_logit_bias, NH, NKVH, da, r, P, Q, K, *tuning_and_flag):
+    use_sigmoid = tuning_and_flag[-1]
+    _check_scan_inputs(combined, inits, logit_bias, NH, NKVH, da, r)
+    _check_pqk(P, Q, K)
+    if not grad_inits.is_contiguous() or not grad_logit_bias.is_contiguous():
+        raise RuntimeError("grad_inits and grad_logit_bias must be contiguous")
+    if grad_combined.shape != combined.shape or grad_combined.dtype != combined.dtype:
+        raise RuntimeError("grad_combined must match combined's shape and dtype")
+    for t in (hq, hk, hv, grad_hq, grad_hk, grad_hv):
+        if t.dtype != combined.dtype:
+            raise RuntimeError("saved outputs and their gradients must share combined's dtype")
+    L = _lib.load()
+    B, T, _ = combined.shape
+    inits = inits.contiguous()
+    logit_bias = logit_bias.contiguous()
+    ws = _lib.workspace(combined.device, L.ltvqkv_lookback_workspace_bytes(B, NH, NKVH, da))
+    sc, gc = combined.stride(), grad_combined.stride()
+    S = _lib.strides
+    rc = L.ltvqkv_lookback_scan_bwd(
+        _lib.dtype_code(combined.dtype), combined.data_ptr(), sc[0], sc[1], sc[2], inits.data_ptr(),
+        logit_bias.data_ptr(),
+        hq.data_ptr(), S(hq.stride()), hk.data_ptr(), S(hk.stride()), hv.data_ptr(), S(hv.stride()),
+        grad_hq.data_ptr(), S(grad_hq.stride()), grad_hk.data_ptr(), S(grad_hk.stride()),
+        grad_hv.data_ptr(), S(grad_hv.stride()),
+        grad_combined.data_ptr(), gc[0], gc[1], gc[2], grad_inits.data_ptr(), grad_logit_bias.data_ptr(),
+        B, T, NH, NKVH, da, r, P, Q, K, int(bool(use_sigmoid)), ws.data_ptr(), ws.numel(),
+        _lib.stream_handle(combined.device))
+    _lib.check(rc, "ltvqkv_lookback_scan_bwd")
+
+
+def _lb_setup(ctx, inputs, output):
+    combined, inits, logit_bias, NH, NKVH, da, r, P, Q, K = inputs[:10]
+    ctx.save_for_backward(combined, inits, logit_bias, *output)
+    ctx.args = (NH, NKVH, da, r, P, Q, K)
+    ctx.tuning_bwd = tuple(inputs[10:-1])[len(inputs[10:-1]) // 2:]
+    ctx.use_sigmoid = inputs[-1]
+
+
+def _make_lb_backward(kind):
+    def _lb_backward(ctx, grad_hq, grad_hk, grad_hv):
+        combined, inits, logit_bias, hq, hk, hv = ctx.saved_tensors
+        grad_hq = torch.zeros_like(hq) if grad_hq is None else grad_hq
+        grad_hk = torch.zeros_like(hk) if grad_hk is None else grad_hk
+        grad_hv = torch.zeros_like(hv) if grad_hv is None else grad_hv
+        grad_combined = torch.empty_like(combined)
+        grad_inits = torch.empty_like(inits, memory_format=torch.contiguous_format)
+        grad_logit_bias = torch.zeros_like(logit_bias, memory_format=torch.contiguous_format)
+        getattr(torch.ops.nanochat_cuda, _LB.format(kind, "backward_kernel"))(
+            combined, inits, logit_bias, hq, hk, hv, grad_hq, grad_hk, grad_hv, grad_combined, grad_inits,
+            grad_logit_bias, *ctx.args, *ctx.tuning_bwd, ctx.use_sigmoid)
+        return (grad_combined, grad_inits, grad_logit_bias) + (None,) * (len(ctx.tuning_bwd) * 2 + 8)
+    return _lb_backward
+
+
+def _lb_op_fake(combined, inits, logit_bias, NH, NKVH, da, r, *rest):
+    B, T, _ = combined.shape
+    D = da * r
+    return (combined.new_empty((B, NH, T, D)), combined.new_empty((B, NKVH, T, D)),
+            combined.new_empty((B, NKVH, T, D)))
+
+
+for _kind in ("blelloch", "sequential"):
+    torch.library.register_autograd(f"nanochat_cuda::{_LB.format(_kind, 'op')}", _make_lb_backward(_kind),
+                                    setup_context=_lb_setup)
+    torch.library.register_fake(f"nanochat_cuda::{_LB.format(_kind, 'op')}", _lb_op_fake)
+    torch.library.register_fake(f"nanochat_cuda::{_LB.format(_kind, 'forward_kernel')}", lambda *args: None)
+    torch.library.register_fake(f"nanochat_cuda::{_LB.format(_kind, 'backward_kernel')}", lambda *args: None)
+
+
+# ------------------------------------------------------------------------------------------
 # Projection + scan forward in one call
 # ------------------------------------------------------------------------------------------
 def _proj_scan_forward_kernel(x, weight, inits, logit_bias, combined, out_q, out_k, out_v, NH, NKVH, da, r,
@@ -476,6 +622,10 @@ torch.library.impl("nanochat_cuda::fused_linear_transpose", "CUDA", _fused_linea
 torch.library.impl("nanochat_cuda::fused_linear_transpose_cuda_op", "CUDA", _fused_linear_transpose_op)
 torch.library.impl("nanochat_cuda::fused_linear_transpose_backward_kernel", "CUDA", _fused_linear_transpose_backward_kernel)
 torch.library.impl("nanochat_cuda::ltv_decode_step", "CUDA", _decode_step)
+for _kind in ("blelloch", "sequential"):
+    torch.library.impl(f"nanochat_cuda::{_LB.format(_kind, 'op')}", "CUDA", _lb_op)
+    torch.library.impl(f"nanochat_cuda::{_LB.format(_kind, 'forward_kernel')}", "CUDA", _lb_forward_kernel)
+    torch.library.impl(f"nanochat_cuda::{_LB.format(_kind, 'backward_kernel')}", "CUDA", _lb_backward_kernel)
 torch.library.impl("nanochat_cuda::ltv_proj_scan_forward_kernel", "CUDA", _proj_scan_forward_kernel)
 torch.library.impl("nanochat_cuda::ltv_proj_scan_cuda_op", "CUDA", _proj_scan_op)
 

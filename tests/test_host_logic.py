@@ -50,6 +50,44 @@ def test_fake_kernels_give_reference_shapes():
     assert sq.shape == (B, NH, D) and sk.shape == (B, NKVH, D)
 
 
+LB_OPS = [f"ltv_look_back_fused_concat_head_major_register_cast_{kind}_scan_cuda_{part}"
+          for kind in ("blelloch", "sequential") for part in ("op", "forward_kernel", "backward_kernel")]
+
+
+def test_lookback_operator_schemas_match_reference():
+    """The six look-back operators with the reference's argument lists (ltv_cuda_ops.py:172-240)."""
+    for n in LB_OPS:
+        assert hasattr(OPS, n), n
+    s = str(getattr(OPS, LB_OPS[0]).default._schema)
+    assert "int P, int Q, int K, int scan_threads_forward" in s and s.endswith("-> (Tensor, Tensor, Tensor)")
+    s = str(getattr(OPS, LB_OPS[1]).default._schema)
+    assert "Tensor(a!) out_q" in s and "int B, int T, int NH" in s
+    s = str(getattr(OPS, LB_OPS[3]).default._schema)
+    assert "int P, int Q, int K, int r_threads_forward, int r_items_forward, int r_threads_backward" in s
+    s = str(getattr(OPS, LB_OPS[5]).default._schema)
+    assert "Tensor(c!) grad_logit_bias" in s and "int r_threads_backward, int r_items_backward, bool use_sigmoid" in s
+
+
+def test_lookback_and_proj_scan_fake_shapes():
+    B, T, NH, NKVH, D = 2, 9, 1, 1, 32
+    comb = torch.empty(B, T, 3 * (D + 1), device="meta")
+    inits, bias = torch.empty(B, 3, D, device="meta"), torch.empty(3, 1, device="meta")
+    for kind, tune in (("blelloch", (8, 8, 4, 32, 2, 8)), ("sequential", (2, 4, 2, 8))):
+        out = getattr(OPS, f"ltv_look_back_fused_concat_head_major_register_cast_{kind}_scan_cuda_op")(
+            comb, inits, bias, NH, NKVH, 1, D, 4, 3, 2, *tune, True)
+        assert [tuple(t.shape) for t in out] == [(B, NH, T, D), (B, NKVH, T, D), (B, NKVH, T, D)]
+    x, w = torch.empty(B, T, 64, device="meta"), torch.empty(3 * (D + 1), 64, device="meta")
+    comb2, q, k, v = OPS.ltv_proj_scan_cuda_op(x, w, inits, bias, NH, NKVH, 1, D, True)
+    assert tuple(comb2.shape) == (B, 3 * (D + 1), T) and tuple(q.shape) == (B, NH, T, D)
+
+
+def test_lookback_no_cpu_fallback():
+    comb = torch.randn(1, 8, 3 * 3)
+    with pytest.raises(NotImplementedError):
+        OPS.ltv_look_back_fused_concat_head_major_register_cast_sequential_scan_cuda_op(
+            comb, torch.randn(1, 3, 2), torch.randn(3, 1), 1, 1, 1, 2, 4, 3, 2, 2, 4, 2, 8, True)
+
+
 def test_filter_on_meta_device_traces_shapes():
     f = nf.LtvCudaFusedConcatHeadMajorRegisterCastBlellochScanQkvFilter(6, 6, 128, 128).to("meta")
     x = torch.empty(2, 64, 768, device="meta")
