@@ -14,6 +14,16 @@ from .filters import (  # noqa: F401
     LtvCudaFusedConcatHeadMajorRegisterCastBlellochScanQkvFilter,
 )
 from .kv_cache import KVCache  # noqa: F401
+from .lookback import (  # noqa: F401
+    UNBOUNDED_LAYER_SPEC,
+    UNBOUNDED_P,
+    ChunksAndHistory,
+    LtvLookBackFusedConcatHeadMajorRegisterCastBlellochScanQkvFilter,
+    LtvLookBackFusedConcatHeadMajorRegisterCastSequentialScanQkvFilter,
+    LtvLookBackHeadMajorQkvFilter,
+    LtvLookBackQkvComputerModule,
+    advance_kv_cache,
+)
 from .module import LtvCombinedQkvComputerModule  # noqa: F401
 from .ops import (  # noqa: F401
     fused_linear_transpose,

@@ -152,3 +152,36 @@ def test_lookback_plain_equals_scan_op(cuda_device):
         tc, ti, tb, 2, 1, 1, 128, 8, 8, 4, 32, 2, 8, True)
     for a, b in ((q1, q2), (k1, k2), (v1, v2)):
         assert max_rel_err(_np(a), _np(b), FLOOR) <= 2e-2
+
+
+@pytest.mark.parametrize("variant", ["blelloch", "sequential"])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_lookback_filter_decode_equals_batch(cuda_device, variant, dtype):
+    """The look-back filter on the CUDA operators: token-by-token decode through the cache
+    (advance_kv_cache) equals the chunked batch forward (bf16: within the bf16 bound, since the
+    decode restarts from states stored in bf16)."""
+    import nanochat_filter_b200 as nf
+
+    spec = nf.ChunksAndHistory(p=16, q=12, k=5)
+    cls = (nf.LtvLookBackFusedConcatHeadMajorRegisterCastBlellochScanQkvFilter if variant == "blelloch"
+           else nf.LtvLookBackFusedConcatHeadMajorRegisterCastSequentialScanQkvFilter)
+    torch.manual_seed(0)
+    filt = cls(2, 1, 128, 128, spec).to(cuda_device)
+    filt.init_weights(2.0, 0.05, 0.5, 0.5)
+    x = torch.randn(2, 40, 256, device=cuda_device).to(dtype)
+    inits = filt.init_param.unsqueeze(0).expand(2, -1, -1)
+    # bf16 as in training: fp32 parameters under autocast (the sequential variant's nn.Linear
+    # projection then yields bf16)
+    with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16, enabled=dtype == torch.bfloat16):
+        batch = filt(x, inits, full_recurrence=False)
+        cache = nf.KVCache(2, 2, 1, 64, 128, num_layers=1, layer_specs=[spec])
+        steps = [nf.advance_kv_cache(x[:, t:t + 1], 0, filt, inits, cache) for t in range(40)]
+    for i in range(3):
+        dec = torch.cat([s[i] for s in steps], dim=1)
+        if dtype == torch.float32:
+            torch.testing.assert_close(dec, batch[i], rtol=1e-5, atol=1e-5)
+        else:
+            # every decode step restarts from a state stored in bf16, so rounding accumulates over
+            # the 40 steps: norm-wise bound, as for the whole bf16 layer
+            d, e = _np(dec), _np(batch[i])
+            assert np.abs(d - e).max() <= 2e-2 * np.abs(e).max()
