@@ -11,6 +11,8 @@
 // new state (which may alias the previous state).
 #include "ltvqkv_common.cuh"
 
+#include <mutex>
+
 namespace ltvqkv {
 
 constexpr int kDecSlice = 16;   // value channels per CTA
@@ -99,6 +101,136 @@ __global__ void __launch_bounds__(kDecThreads) decode_step_kernel(DecodeArgs a) 
   }
 }
 
+// bf16 path: per (head, 16-channel slice) CTA, the [tokens x projection rows] block is one small
+// GEMM on the tensor cores (mma.sync m16n8k16, fp32 accumulation) from shared-memory copies of the
+// slice's W rows and a 64-token tile of x, instead of one warp-wide dot product per (row, token).
+// The copies are 16-byte cp.async pieces issued by all threads at once (one wait for the whole
+// tile). 8 warps: warp w owns tokens 16 (w / 2) .. +15 and projection rows 16 (w % 2) .. +15. Rows
+// are padded to 32 (16 value rows + up to 16 logit rows of the slice's groups), tokens to 64, K to
+// a multiple of 16 (zeros); shared-memory rows are padded by 16 bytes so that ldmatrix is
+// conflict-free. A GEMM of 64 x 32 x C per CTA is too small for tcgen05's 128-row tiles.
+constexpr int kDmTok = 64;
+constexpr int kDmSlice = 16;
+constexpr int kDmRows = 32;
+constexpr int kDmNt = kDmRows / 8 / 2;  // n-tiles (8 rows) per warp
+
+// 16-byte global -> shared copy that bypasses registers (cp.async, L2 only), and the wait for all
+// of this thread's copies.
+LTVQKV_DEVICE void cp_async16(void* smem_dst, const void* gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
+}
+LTVQKV_DEVICE void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+LTVQKV_DEVICE void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+LTVQKV_DEVICE void ldsm_x2(uint32_t addr, uint32_t (&r)[2]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0, %1}, [%2];" : "=r"(r[0]), "=r"(r[1]) : "r"(addr));
+}
+LTVQKV_DEVICE void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
+__global__ void __launch_bounds__(kDecThreads) decode_step_mma_kernel(DecodeArgs a, int Cp) {
+  extern __shared__ __align__(16) unsigned char dm_smem[];
+  const int ld = Cp + 8;  // elements per shared row
+  __nv_bfloat16* sW = reinterpret_cast<__nv_bfloat16*>(dm_smem);
+  __nv_bfloat16* sX = sW + (size_t)kDmRows * ld;
+  float* res = reinterpret_cast<float*>(sX + (size_t)kDmTok * ld);  // [kDmTok][kDmRows]
+  const int h = blockIdx.x;
+  const int c0 = blockIdx.y * kDmSlice;
+  const int c1 = min(c0 + kDmSlice, a.D);
+  const int nv = c1 - c0;
+  const int g0 = c0 / a.r, g1 = (c1 - 1) / a.r;
+  const int rows = nv + g1 - g0 + 1;  // <= kDmRows (callers with r < 2 take the other kernel)
+  const int head_row = h * (a.D + a.Da);
+  const __nv_bfloat16* X = reinterpret_cast<const __nv_bfloat16*>(a.x);
+  const __nv_bfloat16* W = reinterpret_cast<const __nv_bfloat16*>(a.w);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const bool vec = (a.C % 8) == 0 && ((reinterpret_cast<uintptr_t>(X) | reinterpret_cast<uintptr_t>(W)) & 15) == 0;
+  int which, hloc;
+  dec_split_head(h, a.NH, a.NKVH, which, hloc);
+  // one warp per shared row, lanes along the row in 16-byte pieces (no index divisions)
+  auto stage_row = [&](__nv_bfloat16* dst, const __nv_bfloat16* src, bool live) {
+    for (int k = lane * 8; k < Cp; k += 256) {
+      if (live && k < a.C) {
+        if (vec) cp_async16(dst + k, src + k);
+        else
+          for (int e = 0; e < 8; ++e) dst[k + e] = k + e < a.C ? src[k + e] : __float2bfloat16_rn(0.f);
+      } else {
+        *reinterpret_cast<uint4*>(dst + k) = make_uint4(0, 0, 0, 0);
+      }
+    }
+  };
+  // the slice's projection rows: value rows c0 .. c1-1, then the logit rows of groups g0 .. g1
+  for (int row = warp; row < kDmRows; row += kDecThreads / 32) {
+    const int wrow = row < nv ? head_row + c0 + row : head_row + a.D + g0 + (row - nv);
+    stage_row(sW + (size_t)row * ld, W + (long long)(row < rows ? wrow : 0) * a.C, row < rows);
+  }
+  const int mt = warp / 2, nb0 = (warp % 2) * kDmNt;  // this warp's 16 tokens, kDmNt x 8 rows
+  const uint32_t sX_u = smem_u32(sX), sW_u = smem_u32(sW);
+  for (int b0 = 0; b0 < a.B; b0 += kDmTok) {
+    const int nb = min(kDmTok, a.B - b0);
+    for (int tk = warp; tk < kDmTok; tk += kDecThreads / 32)
+      stage_row(sX + (size_t)tk * ld, X + (long long)(b0 + min(tk, nb - 1)) * a.C, tk < nb);
+    cp_async_wait_all();
+    __syncthreads();
+    float acc[kDmNt][4] = {};
+    const uint32_t a_addr = sX_u + (uint32_t)(((16 * mt + (lane % 16)) * ld + (lane / 16) * 8) * 2);
+    uint32_t b_addr[kDmNt];
+#pragma unroll
+    for (int j = 0; j < kDmNt; ++j)
+      b_addr[j] = sW_u + (uint32_t)(((8 * (nb0 + j) + (lane % 8)) * ld + ((lane / 8) % 2) * 8) * 2);
+    for (int k = 0; k < Cp; k += 16) {
+      uint32_t af[4], bf[kDmNt][2];
+      ldsm_x4(a_addr + (uint32_t)(k * 2), af);
+#pragma unroll
+      for (int j = 0; j < kDmNt; ++j) ldsm_x2(b_addr[j] + (uint32_t)(k * 2), bf[j]);
+#pragma unroll
+      for (int j = 0; j < kDmNt; ++j) mma_bf16_16816(acc[j], af, bf[j]);
+    }
+    // fragment (token 16 mt + lane/4 (+8), row 8 n + 2 (lane % 4) (+1)) -> res[token][row]
+#pragma unroll
+    for (int j = 0; j < kDmNt; ++j) {
+      const int rr = 8 * (nb0 + j) + 2 * (lane % 4), tt = 16 * mt + lane / 4;
+      *reinterpret_cast<float2*>(&res[tt * kDmRows + rr]) = make_float2(acc[j][0], acc[j][1]);
+      *reinterpret_cast<float2*>(&res[(tt + 8) * kDmRows + rr]) = make_float2(acc[j][2], acc[j][3]);
+    }
+    __syncthreads();
+    // consecutive threads take consecutive channels of one token: the state reads and writes of
+    // a token's slice are one contiguous 32-byte piece
+    for (int i = threadIdx.x; i < nv * nb; i += kDecThreads) {
+      const int bb = i / nv, cc = i - (i / nv) * nv;
+      const int c = c0 + cc, b = b0 + bb;
+      const int g = c / a.r;
+      // projection values rounded to bf16, as the reference's projection buffer stores them
+      const float u = __bfloat162float(__float2bfloat16_rn(res[bb * kDmRows + cc]));
+      const float l = __fadd_rn(__bfloat162float(__float2bfloat16_rn(res[bb * kDmRows + nv + g - g0])),
+                                a.logit_bias[h * a.Da + g]);
+      const float al = a.use_sigmoid ? sigmoid_f32(l) : l;
+      float hp;
+      if (a.prev[0] != nullptr) {
+        const long long* ps = a.ps[which];
+        hp = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(a.prev[which])[b * ps[0] + hloc * ps[1] + c * ps[2]]);
+      } else {
+        hp = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(a.init_param)[(long long)h * a.D + c]);
+      }
+      const float hn = __fadd_rn(__fmul_rn(__fsub_rn(1.0f, al), hp), __fmul_rn(al, u));
+      const long long* os = a.os[which];
+      reinterpret_cast<__nv_bfloat16*>(a.out[which])[b * os[0] + hloc * os[1] + c * os[2]] = __float2bfloat16_rn(hn);
+    }
+    __syncthreads();
+  }
+}
+
+size_t decode_mma_smem(int Cp) { return (size_t)(kDmRows + kDmTok) * (Cp + 8) * 2 + (size_t)kDmRows * kDmTok * 4; }
+
 }  // namespace ltvqkv
 
 using namespace ltvqkv;
@@ -134,7 +266,29 @@ extern "C" int ltvqkv_decode_step(int dtype, const void* x, const void* weight, 
   a.H = NH + 2 * NKVH; a.use_sigmoid = use_sigmoid;
   dim3 grid(a.H, (a.D + kDecSlice - 1) / kDecSlice);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  if (dtype == LTVQKV_DTYPE_BF16) decode_step_kernel<__nv_bfloat16><<<grid, kDecThreads, 0, s>>>(a);
-  else decode_step_kernel<float><<<grid, kDecThreads, 0, s>>>(a);
+  const int Cp = (C + 15) / 16 * 16;
+  const size_t smem = decode_mma_smem(Cp);
+  // the tensor-core path holds a slice's logit rows next to its value rows: r >= 2 keeps them <= 16
+  if (dtype == LTVQKV_DTYPE_BF16 && smem <= 200 * 1024 && (kDmSlice + kDmSlice / r + 1) <= kDmRows) {
+    static std::mutex mu;
+    static bool done[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return ltvqkv_host::check_launch();
+    {
+      std::lock_guard<std::mutex> lock(mu);
+      if (!done[dev]) {
+        if (cudaFuncSetAttribute(decode_step_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) !=
+            cudaSuccess)
+          return ltvqkv_host::check_launch();
+        done[dev] = true;
+      }
+    }
+    dim3 grid_mma(a.H, (a.D + kDmSlice - 1) / kDmSlice);
+    decode_step_mma_kernel<<<grid_mma, kDecThreads, smem, s>>>(a, Cp);
+  } else if (dtype == LTVQKV_DTYPE_BF16) {
+    decode_step_kernel<__nv_bfloat16><<<grid, kDecThreads, 0, s>>>(a);
+  } else {
+    decode_step_kernel<float><<<grid, kDecThreads, 0, s>>>(a);
+  }
   return ltvqkv_host::check_launch();
 }

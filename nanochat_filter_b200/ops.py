@@ -119,6 +119,12 @@ lib.define(
     ") -> (Tensor, Tensor, Tensor, Tensor)"
 )
 lib.define(
+    "ltv_decode_step_("
+    "Tensor x, Tensor weight, Tensor logit_bias, Tensor(a!) state_q, Tensor(b!) state_k, Tensor(c!) state_v, "
+    "int NH, int NKVH, int da, int r, bool use_sigmoid"
+    ") -> ()"
+)
+lib.define(
     "ltv_decode_step("
     "Tensor x, Tensor weight, Tensor logit_bias, Tensor? prev_q, Tensor? prev_k, Tensor? prev_v, "
     "Tensor init_param, int NH, int NKVH, int da, int r, bool use_sigmoid"
@@ -605,6 +611,39 @@ def _decode_step(x, weight, logit_bias, prev_q, prev_k, prev_v, init_param, NH, 
     return oq, ok, ov
 
 
+def _decode_step_inplace(x, weight, logit_bias, state_q, state_k, state_v, NH, NKVH, da, r, use_sigmoid):
+    """ltv_decode_step writing the new states over the previous ones (a cache's states updated in
+    place: one launch per layer-step, no copies)."""
+    L = _lib.load()
+    if x.dim() == 3:
+        if x.shape[1] != 1:
+            raise RuntimeError("ltv_decode_step_ takes one token per sequence")
+        x = x.reshape(x.shape[0], x.shape[2])
+    x = x.contiguous()
+    B, C = x.shape
+    D = da * r
+    H = NH + 2 * NKVH
+    w = (weight if weight.dtype == x.dtype else weight.to(x.dtype)).contiguous()
+    if tuple(w.shape) != (H * (D + da), C):
+        raise RuntimeError(f"weight must be [{H * (D + da)}, {C}], got {tuple(w.shape)}")
+    for p, n in ((state_q, NH), (state_k, NKVH), (state_v, NKVH)):
+        if tuple(p.shape) != (B, n, D) or p.dtype != x.dtype:
+            raise RuntimeError("states must be [B, heads, D] in x's dtype")
+    logit_bias = logit_bias.contiguous()
+    S = _lib.strides
+    sq, sk, sv = S(state_q.stride()), S(state_k.stride()), S(state_v.stride())
+    rc = L.ltvqkv_decode_step(_lib.dtype_code(x.dtype), x.data_ptr(), w.data_ptr(), logit_bias.data_ptr(),
+                              state_q.data_ptr(), sq, state_k.data_ptr(), sk, state_v.data_ptr(), sv, None,
+                              state_q.data_ptr(), sq, state_k.data_ptr(), sk, state_v.data_ptr(), sv,
+                              B, C, NH, NKVH, da, r, int(bool(use_sigmoid)), _lib.stream_handle(x.device))
+    _lib.check(rc, "ltvqkv_decode_step")
+
+
+@torch.library.register_fake("nanochat_cuda::ltv_decode_step_")
+def _decode_step_inplace_fake(*args):
+    return None
+
+
 @torch.library.register_fake("nanochat_cuda::ltv_decode_step")
 def _decode_step_fake(x, weight, logit_bias, prev_q, prev_k, prev_v, init_param, NH, NKVH, da, r, use_sigmoid):
     B = x.shape[0]
@@ -622,6 +661,7 @@ torch.library.impl("nanochat_cuda::fused_linear_transpose", "CUDA", _fused_linea
 torch.library.impl("nanochat_cuda::fused_linear_transpose_cuda_op", "CUDA", _fused_linear_transpose_op)
 torch.library.impl("nanochat_cuda::fused_linear_transpose_backward_kernel", "CUDA", _fused_linear_transpose_backward_kernel)
 torch.library.impl("nanochat_cuda::ltv_decode_step", "CUDA", _decode_step)
+torch.library.impl("nanochat_cuda::ltv_decode_step_", "CUDA", _decode_step_inplace)
 for _kind in ("blelloch", "sequential"):
     torch.library.impl(f"nanochat_cuda::{_LB.format(_kind, 'op')}", "CUDA", _lb_op)
     torch.library.impl(f"nanochat_cuda::{_LB.format(_kind, 'forward_kernel')}", "CUDA", _lb_forward_kernel)

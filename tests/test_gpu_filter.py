@@ -153,3 +153,20 @@ def test_decode_kernel_vs_oracle(cuda_device, dtype, with_state):
     tol = 2e-2 if bf16 else 1e-5
     for a, e in ((q, eq[:, :, 0]), (k, ek[:, :, 0]), (v, ev[:, :, 0])):
         assert max_rel_err(_np(a), e, FLOOR) <= tol
+
+
+@pytest.mark.parametrize("B,C", [(64, 768), (70, 256), (3, 200)])
+def test_decode_step_inplace_equals_out_of_place(cuda_device, B, C):
+    """ltv_decode_step_ (states updated in place, as a cache update) equals ltv_decode_step."""
+    NH, NKVH, Da, r = 2, 1, 1, 128
+    H, D = NH + 2 * NKVH, Da * r
+    g = torch.Generator(device=cuda_device).manual_seed(B + C)
+    x = torch.randn(B, C, generator=g, device=cuda_device).to(torch.bfloat16)
+    w = (torch.randn(H * (D + Da), C, generator=g, device=cuda_device) * C ** -0.5).to(torch.bfloat16)
+    bias = torch.randn(H, Da, generator=g, device=cuda_device)
+    init = torch.zeros(H, D, device=cuda_device, dtype=torch.bfloat16)
+    st = [torch.randn(B, n, D, generator=g, device=cuda_device).to(torch.bfloat16) for n in (NH, NKVH, NKVH)]
+    ref = torch.ops.nanochat_cuda.ltv_decode_step(x, w, bias, *st, init, NH, NKVH, Da, r, True)
+    torch.ops.nanochat_cuda.ltv_decode_step_(x, w, bias, *st, NH, NKVH, Da, r, True)
+    for a, b in zip(st, ref):
+        assert torch.equal(a, b)
