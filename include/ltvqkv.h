@@ -171,6 +171,26 @@ LTVQKV_API int ltvqkv_lookback_scan_bwd(int dtype,
                     void* workspace, size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------------------------
+ * Consumer prologue of the filtered q and k: rotary embedding then QK RMS-norm, fused. Replaces
+ * the reference attention's apply_rotary_emb + norm on q and k (nanochat/gpt.py:96-111, 224-230;
+ * no reference C function). q [B, T, NH, D], k [B, T, NKVH, D], outputs and gradients with any
+ * element strides (4 per tensor: b, t, head, d); cos/sin [T, D/2] in q's dtype (2 strides: t, j);
+ * eps: F.rms_norm's default is the fp32 epsilon for bf16 and fp32 inputs (its compute type).
+ * Odd D: no rotation (as the reference). D <= 512.
+ * The backward takes the forward's inputs and the output gradients and writes dq, dk. */
+LTVQKV_API int ltvqkv_rotary_qk_norm_fwd(int dtype, const void* q, const int64_t* q_strides,
+                    const void* k, const int64_t* k_strides, const void* cos, const void* sin,
+                    const int64_t* cs_strides, void* out_q, const int64_t* oq_strides,
+                    void* out_k, const int64_t* ok_strides,
+                    int B, int T, int NH, int NKVH, int D, float eps, void* stream);
+LTVQKV_API int ltvqkv_rotary_qk_norm_bwd(int dtype, const void* q, const int64_t* q_strides,
+                    const void* k, const int64_t* k_strides, const void* cos, const void* sin,
+                    const int64_t* cs_strides, const void* grad_q, const int64_t* gq_strides,
+                    const void* grad_k, const int64_t* gk_strides, void* dq, const int64_t* dq_strides,
+                    void* dk, const int64_t* dk_strides,
+                    int B, int T, int NH, int NKVH, int D, float eps, void* stream);
+
+/* ------------------------------------------------------------------------------------------
  * Projection ("fused linear transpose"): replaces cpp_ewma_cuda.fused_linear_transpose
  * (reference cpp_ewma/src/fused_linear_transpose_forward.cu:23-58; called from
  * nanochat/ops/fused_linear_transpose.py:20-41).

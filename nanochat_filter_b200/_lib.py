@@ -39,6 +39,8 @@ EXPORTED_SYMBOLS = (
     "ltvqkv_lookback_workspace_bytes",
     "ltvqkv_lookback_scan_fwd",
     "ltvqkv_lookback_scan_bwd",
+    "ltvqkv_rotary_qk_norm_fwd",
+    "ltvqkv_rotary_qk_norm_bwd",
 )
 
 _lib: Optional[ctypes.CDLL] = None
@@ -81,6 +83,12 @@ def _declare(lib: ctypes.CDLL) -> None:
                                              _vp, _pi64, _vp, _pi64, _vp, _pi64,
                                              _vp, _i64, _i64, _i64, _vp, _pf,
                                              _i, _i, _i, _i, _i, _i, _i64, _i64, _i64, _i, _vp, _sz, _vp]
+    lib.ltvqkv_rotary_qk_norm_fwd.restype = _i
+    lib.ltvqkv_rotary_qk_norm_fwd.argtypes = [_i, _vp, _pi64, _vp, _pi64, _vp, _vp, _pi64, _vp, _pi64, _vp, _pi64,
+                                              _i, _i, _i, _i, _i, ctypes.c_float, _vp]
+    lib.ltvqkv_rotary_qk_norm_bwd.restype = _i
+    lib.ltvqkv_rotary_qk_norm_bwd.argtypes = [_i, _vp, _pi64, _vp, _pi64, _vp, _vp, _pi64, _vp, _pi64, _vp, _pi64,
+                                              _vp, _pi64, _vp, _pi64, _i, _i, _i, _i, _i, ctypes.c_float, _vp]
     lib.ltvqkv_gemm_workspace_bytes.restype = _sz
     lib.ltvqkv_gemm_workspace_bytes.argtypes = []
     lib.ltvqkv_gemm_fwd.restype = _i

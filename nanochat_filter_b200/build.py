@@ -18,7 +18,7 @@ INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 LIB_NAME = "libltvqkv.so"
 LIB_PATH = os.path.join(HERE, LIB_NAME)
 
-SOURCES = ["ltvqkv_abi.cu", "ltvqkv_scan.cu", "ltvqkv_gemm.cu", "ltvqkv_decode.cu", "ltvqkv_lookback.cu"]
+SOURCES = ["ltvqkv_abi.cu", "ltvqkv_scan.cu", "ltvqkv_gemm.cu", "ltvqkv_decode.cu", "ltvqkv_lookback.cu", "ltvqkv_rotary.cu"]
 HEADERS = sorted(f for f in os.listdir(CSRC) if f.endswith(".cuh"))
 
 NVCC_FLAGS = [

@@ -118,6 +118,11 @@ lib.define(
     "Tensor x, Tensor weight, Tensor inits, Tensor logit_bias, int NH, int NKVH, int da, int r, bool use_sigmoid"
     ") -> (Tensor, Tensor, Tensor, Tensor)"
 )
+lib.define("ltv_rotary_qk_norm(Tensor q, Tensor k, Tensor cos, Tensor sin) -> (Tensor, Tensor)")
+lib.define(
+    "ltv_rotary_qk_norm_backward(Tensor q, Tensor k, Tensor cos, Tensor sin, Tensor grad_q, Tensor grad_k) "
+    "-> (Tensor, Tensor)"
+)
 lib.define(
     "ltv_decode_step_("
     "Tensor x, Tensor weight, Tensor logit_bias, Tensor(a!) state_q, Tensor(b!) state_k, Tensor(c!) state_v, "
@@ -575,6 +580,96 @@ def _proj_scan_kernel_fake(*args):
 
 
 # ------------------------------------------------------------------------------------------
+# Rotary embedding + QK RMS-norm of the filtered q and k (the reference attention's prologue,
+# nanochat/gpt.py:96-111, 224-230), fused
+# ------------------------------------------------------------------------------------------
+# F.rms_norm's default eps for bf16 and fp32 inputs: the epsilon of its fp32 compute type
+_RMS_EPS = float(torch.finfo(torch.float32).eps)
+
+
+def _rot_cs(cos, sin, q):
+    if cos.dim() == 4:  # the model's [1, T, 1, D/2] rotary cache
+        cos, sin = cos[0, :, 0, :], sin[0, :, 0, :]
+    if cos.dtype != q.dtype:
+        cos, sin = cos.to(q.dtype), sin.to(q.dtype)
+    if cos.stride() != sin.stride():
+        cos, sin = cos.contiguous(), sin.contiguous()
+    return cos, sin
+
+
+def _rot_check(q, k, cos):
+    if q.dim() != 4 or k.dim() != 4 or q.shape[0] != k.shape[0] or q.shape[1] != k.shape[1] or \
+            q.shape[3] != k.shape[3] or q.dtype != k.dtype:
+        raise RuntimeError(f"q and k must be [B, T, heads, D] of one dtype, got {tuple(q.shape)}, {tuple(k.shape)}")
+    T, D = q.shape[1], q.shape[3]
+    if D % 2 == 0 and tuple(cos.shape) != (T, D // 2):
+        raise RuntimeError(f"cos/sin must hold [T, D/2] = {(T, D // 2)} values, got {tuple(cos.shape)}")
+
+
+def _head_major_like(x):
+    B, T, H, D = x.shape
+    return torch.empty((B, H, T, D), dtype=x.dtype, device=x.device).transpose(1, 2)
+
+
+def _rotary_qk_norm(q, k, cos, sin):
+    cos, sin = _rot_cs(cos, sin, q)
+    _rot_check(q, k, cos)
+    L = _lib.load()
+    oq, ok = _head_major_like(q), _head_major_like(k)
+    S = _lib.strides
+    B, T, NH, D = q.shape
+    rc = L.ltvqkv_rotary_qk_norm_fwd(_lib.dtype_code(q.dtype), q.data_ptr(), S(q.stride()), k.data_ptr(),
+                                     S(k.stride()), cos.data_ptr(), sin.data_ptr(), S(cos.stride()), oq.data_ptr(),
+                                     S(oq.stride()), ok.data_ptr(), S(ok.stride()), B, T, NH, k.shape[2], D,
+                                     _RMS_EPS, _lib.stream_handle(q.device))
+    _lib.check(rc, "ltvqkv_rotary_qk_norm_fwd")
+    return oq, ok
+
+
+def _rotary_qk_norm_backward_kernel(q, k, cos, sin, grad_q, grad_k):
+    cos, sin = _rot_cs(cos, sin, q)
+    _rot_check(q, k, cos)
+    L = _lib.load()
+    dq, dk = torch.empty_like(q), torch.empty_like(k)
+    grad_q, grad_k = grad_q.to(q.dtype), grad_k.to(k.dtype)
+    S = _lib.strides
+    B, T, NH, D = q.shape
+    rc = L.ltvqkv_rotary_qk_norm_bwd(_lib.dtype_code(q.dtype), q.data_ptr(), S(q.stride()), k.data_ptr(),
+                                     S(k.stride()), cos.data_ptr(), sin.data_ptr(), S(cos.stride()),
+                                     grad_q.data_ptr(), S(grad_q.stride()), grad_k.data_ptr(), S(grad_k.stride()),
+                                     dq.data_ptr(), S(dq.stride()), dk.data_ptr(), S(dk.stride()), B, T, NH,
+                                     k.shape[2], D, _RMS_EPS, _lib.stream_handle(q.device))
+    _lib.check(rc, "ltvqkv_rotary_qk_norm_bwd")
+    return dq, dk
+
+
+def _rot_setup(ctx, inputs, output):
+    q, k, cos, sin = inputs
+    ctx.save_for_backward(q, k, cos, sin)
+
+
+def _rot_backward(ctx, grad_oq, grad_ok):
+    q, k, cos, sin = ctx.saved_tensors
+    grad_oq = torch.zeros_like(q) if grad_oq is None else grad_oq
+    grad_ok = torch.zeros_like(k) if grad_ok is None else grad_ok
+    dq, dk = torch.ops.nanochat_cuda.ltv_rotary_qk_norm_backward(q, k, cos, sin, grad_oq, grad_ok)
+    return dq, dk, None, None
+
+
+torch.library.register_autograd("nanochat_cuda::ltv_rotary_qk_norm", _rot_backward, setup_context=_rot_setup)
+
+
+@torch.library.register_fake("nanochat_cuda::ltv_rotary_qk_norm")
+def _rot_fake(q, k, cos, sin):
+    return _head_major_like(q), _head_major_like(k)
+
+
+@torch.library.register_fake("nanochat_cuda::ltv_rotary_qk_norm_backward")
+def _rot_bwd_fake(q, k, cos, sin, grad_q, grad_k):
+    return torch.empty_like(q), torch.empty_like(k)
+
+
+# ------------------------------------------------------------------------------------------
 # Decode step
 # ------------------------------------------------------------------------------------------
 def _decode_step(x, weight, logit_bias, prev_q, prev_k, prev_v, init_param, NH, NKVH, da, r, use_sigmoid):
@@ -662,6 +757,8 @@ torch.library.impl("nanochat_cuda::fused_linear_transpose_cuda_op", "CUDA", _fus
 torch.library.impl("nanochat_cuda::fused_linear_transpose_backward_kernel", "CUDA", _fused_linear_transpose_backward_kernel)
 torch.library.impl("nanochat_cuda::ltv_decode_step", "CUDA", _decode_step)
 torch.library.impl("nanochat_cuda::ltv_decode_step_", "CUDA", _decode_step_inplace)
+torch.library.impl("nanochat_cuda::ltv_rotary_qk_norm", "CUDA", _rotary_qk_norm)
+torch.library.impl("nanochat_cuda::ltv_rotary_qk_norm_backward", "CUDA", _rotary_qk_norm_backward_kernel)
 for _kind in ("blelloch", "sequential"):
     torch.library.impl(f"nanochat_cuda::{_LB.format(_kind, 'op')}", "CUDA", _lb_op)
     torch.library.impl(f"nanochat_cuda::{_LB.format(_kind, 'forward_kernel')}", "CUDA", _lb_forward_kernel)
@@ -700,3 +797,10 @@ def ltv_proj_scan(x: torch.Tensor, weight: torch.Tensor, inits: torch.Tensor, lo
                   NKVH: int, da: int, r: int, use_sigmoid: bool = True):
     """Projection and scan forward in one call; returns (combined [B, F, T], q, k, v [B, heads, T, D])."""
     return torch.ops.nanochat_cuda.ltv_proj_scan_cuda_op(x, weight, inits, logit_bias, NH, NKVH, da, r, use_sigmoid)
+
+
+def rotary_qk_norm(q: torch.Tensor, k: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor):
+    """apply_rotary_emb then norm on q and k (nanochat/gpt.py:224-230) in one pass each way;
+    q, k [B, T, heads, D] -> [B, T, heads, D] views of head-major storage (the attention's
+    transpose(1, 2) is then contiguous)."""
+    return torch.ops.nanochat_cuda.ltv_rotary_qk_norm(q, k, cos, sin)

@@ -88,6 +88,17 @@ def test_lookback_no_cpu_fallback():
             comb, torch.randn(1, 3, 2), torch.randn(3, 1), 1, 1, 1, 2, 4, 3, 2, 2, 4, 2, 8, True)
 
 
+def test_rotary_qk_norm_op_schema_and_fake():
+    s = str(OPS.ltv_rotary_qk_norm.default._schema)
+    assert s.startswith("nanochat_cuda::ltv_rotary_qk_norm(Tensor q, Tensor k, Tensor cos, Tensor sin)")
+    q = torch.empty(2, 5, 3, 8, device="meta")
+    k = torch.empty(2, 5, 1, 8, device="meta")
+    oq, ok = OPS.ltv_rotary_qk_norm(q, k, torch.empty(1, 5, 1, 4, device="meta"), torch.empty(1, 5, 1, 4, device="meta"))
+    assert tuple(oq.shape) == (2, 5, 3, 8) and oq.transpose(1, 2).is_contiguous()
+    with pytest.raises(NotImplementedError):
+        OPS.ltv_rotary_qk_norm(torch.randn(1, 2, 1, 4), torch.randn(1, 2, 1, 4), torch.randn(2, 2), torch.randn(2, 2))
+
+
 def test_filter_on_meta_device_traces_shapes():
     f = nf.LtvCudaFusedConcatHeadMajorRegisterCastBlellochScanQkvFilter(6, 6, 128, 128).to("meta")
     x = torch.empty(2, 64, 768, device="meta")
