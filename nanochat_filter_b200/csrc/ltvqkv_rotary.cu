@@ -13,6 +13,8 @@
 // elementwise ops round; the norm computes in fp32 and rounds once.
 #include "ltvqkv_common.cuh"
 
+#include <algorithm>
+
 namespace ltvqkv {
 namespace {
 
@@ -28,6 +30,7 @@ struct RotArgs {
   long long gs[2][4];
   int B, T, NH, NKVH, D;
   float eps;
+  int vec;  // pairs of adjacent elements load and store as one (D % 4 == 0, d stride 1, even strides)
 };
 
 template <typename S>
@@ -41,23 +44,30 @@ LTVQKV_DEVICE void rst(void* p, long long i, float v) {
   else reinterpret_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
 }
 template <typename S>
+LTVQKV_DEVICE float2 rld2(const void* p, long long i) {
+  if constexpr (sizeof(S) == 4) return *reinterpret_cast<const float2*>(reinterpret_cast<const float*>(p) + i);
+  else return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(reinterpret_cast<const __nv_bfloat16*>(p) + i));
+}
+template <typename S>
+LTVQKV_DEVICE void rst2(void* p, long long i, float x, float y) {
+  if constexpr (sizeof(S) == 4) *reinterpret_cast<float2*>(reinterpret_cast<float*>(p) + i) = make_float2(x, y);
+  else *reinterpret_cast<__nv_bfloat162*>(reinterpret_cast<__nv_bfloat16*>(p) + i) = __floats2bfloat162_rn(x, y);
+}
+template <typename S>
 LTVQKV_DEVICE float rq(float v) {  // rounding to the storage dtype
   if constexpr (sizeof(S) == 4) return v;
   else return __bfloat162float(__float2bfloat16_rn(v));
 }
 
-// Row index -> (tensor, b, t, head); one warp per row, q rows first.
-LTVQKV_DEVICE bool rot_row(const RotArgs& a, long long row, int& w, int& b, int& t, int& hh) {
-  const long long nq = (long long)a.B * a.T * a.NH, nk = (long long)a.B * a.T * a.NKVH;
-  if (row >= nq + nk) return false;
-  w = row < nq ? 0 : 1;
-  long long r = row < nq ? row : row - nq;
+// CTA row y -> (tensor, b, head): q heads first. Each warp then walks tokens (one row per token),
+// so consecutive warps stream consecutive rows of the filter's head-major storage.
+LTVQKV_DEVICE void rot_head(const RotArgs& a, int y, int& w, int& b, int& hh) {
+  const int nq = a.B * a.NH;
+  w = y < nq ? 0 : 1;
+  const int r = y < nq ? y : y - nq;
   const int nh = w == 0 ? a.NH : a.NKVH;
-  hh = (int)(r % nh);
-  r /= nh;
-  t = (int)(r % a.T);
-  b = (int)(r / a.T);
-  return true;
+  hh = r % nh;
+  b = r / nh;
 }
 
 // The rotated row element pair (j, j + d) in the storage dtype's rounding.
@@ -70,17 +80,47 @@ LTVQKV_DEVICE void rotate(float x1, float x2, float c, float s, float& y1, float
 constexpr int kRotMaxPer = 8;  // elements per lane and half (D <= 512; odd D <= 256)
 
 template <typename S>
-__global__ void __launch_bounds__(256) rotary_norm_fwd_kernel(RotArgs a) {
-  const long long row = (long long)blockIdx.x * 8 + threadIdx.x / 32;
+__global__ void __launch_bounds__(256, 4) rotary_norm_fwd_kernel(RotArgs a) {
   const int lane = threadIdx.x % 32;
-  int w, b, t, hh;
-  if (!rot_row(a, row, w, b, t, hh)) return;
+  int w, b, hh;
+  rot_head(a, blockIdx.y, w, b, hh);
+  for (int t = blockIdx.x * 8 + threadIdx.x / 32; t < a.T; t += gridDim.x * 8) {
   const long long* xs = a.xs[w];
   const long long xb = b * xs[0] + t * xs[1] + hh * xs[2];
   const long long* os = a.os[w];
   const long long ob = b * os[0] + t * os[1] + hh * os[2];
   const bool rot = (a.D & 1) == 0;
   const int d = a.D / 2;
+  if (a.vec) {
+    // lane holds element pairs (2p, 2p + 1), p = lane + 32 n, of both halves
+    float y[4][kRotMaxPer / 2];
+    float ss = 0.f;
+#pragma unroll
+    for (int n = 0; n < kRotMaxPer / 2; ++n) {
+      const int j = 2 * (lane + 32 * n);
+      y[0][n] = y[1][n] = y[2][n] = y[3][n] = 0.f;
+      if (j < d) {
+        const float2 c = rld2<S>(a.cos, t * a.cs[0] + j), sn = rld2<S>(a.sin, t * a.cs[0] + j);
+        const float2 x1 = rld2<S>(a.x[w], xb + j), x2 = rld2<S>(a.x[w], xb + j + d);
+        rotate<S>(x1.x, x2.x, c.x, sn.x, y[0][n], y[2][n]);
+        rotate<S>(x1.y, x2.y, c.y, sn.y, y[1][n], y[3][n]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) ss = __fmaf_rn(y[e][n], y[e][n], ss);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float inv = rsqrtf(ss / (float)a.D + a.eps);
+#pragma unroll
+    for (int n = 0; n < kRotMaxPer / 2; ++n) {
+      const int j = 2 * (lane + 32 * n);
+      if (j < d) {
+        rst2<S>(a.out[w], ob + j, y[0][n] * inv, y[1][n] * inv);
+        rst2<S>(a.out[w], ob + j + d, y[2][n] * inv, y[3][n] * inv);
+      }
+    }
+    continue;
+  }
   // lane holds elements j = lane + 32 n of both halves (rotation) or of the whole row (odd D)
   const int half = rot ? d : a.D;
   float y1[kRotMaxPer], y2[kRotMaxPer];
@@ -110,16 +150,17 @@ __global__ void __launch_bounds__(256) rotary_norm_fwd_kernel(RotArgs a) {
       if (rot) rst<S>(a.out[w], ob + (j + d) * os[3], y2[n] * inv);
     }
   }
+  }
 }
 
 // Backward: z = y r, r = (mean(y^2) + eps)^(-1/2):  dy = r g - y r^3 (sum g y) / D;
 // rotation transposed: dx1 = dy1 cos - dy2 sin,  dx2 = dy1 sin + dy2 cos.
 template <typename S>
-__global__ void __launch_bounds__(256) rotary_norm_bwd_kernel(RotArgs a) {
-  const long long row = (long long)blockIdx.x * 8 + threadIdx.x / 32;
+__global__ void __launch_bounds__(256, 3) rotary_norm_bwd_kernel(RotArgs a) {
   const int lane = threadIdx.x % 32;
-  int w, b, t, hh;
-  if (!rot_row(a, row, w, b, t, hh)) return;
+  int w, b, hh;
+  rot_head(a, blockIdx.y, w, b, hh);
+  for (int t = blockIdx.x * 8 + threadIdx.x / 32; t < a.T; t += gridDim.x * 8) {
   const long long* xs = a.xs[w];
   const long long xb = b * xs[0] + t * xs[1] + hh * xs[2];
   const long long* gs = a.gs[w];
@@ -128,6 +169,55 @@ __global__ void __launch_bounds__(256) rotary_norm_bwd_kernel(RotArgs a) {
   const long long ob = b * os[0] + t * os[1] + hh * os[2];
   const bool rot = (a.D & 1) == 0;
   const int d = a.D / 2;
+  if (a.vec) {
+    constexpr int NP = kRotMaxPer / 2;
+    float y[4][NP], g[4][NP], c2[2][NP], s2[2][NP];
+    float ss = 0.f, gy = 0.f;
+#pragma unroll
+    for (int n = 0; n < NP; ++n) {
+      const int j = 2 * (lane + 32 * n);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) y[e][n] = g[e][n] = 0.f;
+      c2[0][n] = c2[1][n] = s2[0][n] = s2[1][n] = 0.f;
+      if (j < d) {
+        const float2 c = rld2<S>(a.cos, t * a.cs[0] + j), sn = rld2<S>(a.sin, t * a.cs[0] + j);
+        c2[0][n] = c.x; c2[1][n] = c.y; s2[0][n] = sn.x; s2[1][n] = sn.y;
+        const float2 x1 = rld2<S>(a.x[w], xb + j), x2 = rld2<S>(a.x[w], xb + j + d);
+        rotate<S>(x1.x, x2.x, c.x, sn.x, y[0][n], y[2][n]);
+        rotate<S>(x1.y, x2.y, c.y, sn.y, y[1][n], y[3][n]);
+        const float2 ga = rld2<S>(a.g[w], gb + j), gbb = rld2<S>(a.g[w], gb + j + d);
+        g[0][n] = ga.x; g[1][n] = ga.y; g[2][n] = gbb.x; g[3][n] = gbb.y;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          ss = __fmaf_rn(y[e][n], y[e][n], ss);
+          gy = __fmaf_rn(g[e][n], y[e][n], gy);
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      gy += __shfl_xor_sync(0xffffffffu, gy, o);
+    }
+    const float r = rsqrtf(ss / (float)a.D + a.eps);
+    const float k3 = r * r * r * gy / (float)a.D;
+#pragma unroll
+    for (int n = 0; n < NP; ++n) {
+      const int j = 2 * (lane + 32 * n);
+      if (j < d) {
+        float dx1[2], dx2[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const float dy1 = r * g[e][n] - y[e][n] * k3, dy2 = r * g[2 + e][n] - y[2 + e][n] * k3;
+          dx1[e] = dy1 * c2[e][n] - dy2 * s2[e][n];
+          dx2[e] = dy1 * s2[e][n] + dy2 * c2[e][n];
+        }
+        rst2<S>(a.out[w], ob + j, dx1[0], dx1[1]);
+        rst2<S>(a.out[w], ob + j + d, dx2[0], dx2[1]);
+      }
+    }
+    continue;
+  }
   const int half = rot ? d : a.D;
   float y1[kRotMaxPer], y2[kRotMaxPer], g1[kRotMaxPer], g2[kRotMaxPer], cs_[kRotMaxPer], sn_[kRotMaxPer];
   float ss = 0.f, gy = 0.f;
@@ -170,6 +260,7 @@ __global__ void __launch_bounds__(256) rotary_norm_bwd_kernel(RotArgs a) {
       }
     }
   }
+  }
 }
 
 int rot_setup(RotArgs& a, int dtype, const void* q, const int64_t* qs, const void* k, const int64_t* ks,
@@ -189,6 +280,15 @@ int rot_setup(RotArgs& a, int dtype, const void* q, const int64_t* qs, const voi
   }
   a.cos = cos; a.sin = sin; a.cs[0] = css[0]; a.cs[1] = css[1];
   a.B = B; a.T = T; a.NH = NH; a.NKVH = NKVH; a.D = D; a.eps = eps;
+  // paired accesses: D % 4 == 0, unit d stride and even other strides, pointers aligned to a pair
+  const size_t pair = dtype == LTVQKV_DTYPE_F32 ? 8 : 4;
+  auto ok4 = [&](const void* p, const long long* st) {
+    return p == nullptr || ((reinterpret_cast<uintptr_t>(p) % pair) == 0 && st[3] == 1 && st[0] % 2 == 0 &&
+                            st[1] % 2 == 0 && st[2] % 2 == 0);
+  };
+  a.vec = D % 4 == 0 && css[1] == 1 && css[0] % 2 == 0 && reinterpret_cast<uintptr_t>(cos) % pair == 0 &&
+          reinterpret_cast<uintptr_t>(sin) % pair == 0 && ok4(q, a.xs[0]) && ok4(k, a.xs[1]) && ok4(oq, a.os[0]) &&
+          ok4(ok, a.os[1]);
   return LTVQKV_OK;
 }
 
@@ -209,7 +309,9 @@ extern "C" int ltvqkv_rotary_qk_norm_fwd(int dtype, const void* q, const int64_t
   const long long rows = (long long)B * T * (NH + NKVH);
   if (rows == 0) return LTVQKV_OK;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  const unsigned int grid = (unsigned int)((rows + 7) / 8);
+  // x: token tiles (each warp walks tokens w, w + 8 gridDim.x, ...), y: the q and k head rows
+  const dim3 grid((unsigned int)std::min(64, (T + 63) / 64), (unsigned int)(B * (NH + NKVH)));
+  if (B * (NH + NKVH) > 65535) return LTVQKV_ERR_SHAPE;
   if (dtype == LTVQKV_DTYPE_F32) rotary_norm_fwd_kernel<float><<<grid, 256, 0, s>>>(a);
   else rotary_norm_fwd_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(a);
   return ltvqkv_host::check_launch();
@@ -231,10 +333,17 @@ extern "C" int ltvqkv_rotary_qk_norm_bwd(int dtype, const void* q, const int64_t
     a.gs[0][i] = gq_strides ? gq_strides[i] : 0;
     a.gs[1][i] = gk_strides ? gk_strides[i] : 0;
   }
+  const size_t pair = dtype == LTVQKV_DTYPE_F32 ? 8 : 4;
+  for (int w = 0; w < 2; ++w)
+    if (a.g[w] && ((reinterpret_cast<uintptr_t>(a.g[w]) % pair) != 0 || a.gs[w][3] != 1 || a.gs[w][0] % 2 ||
+                   a.gs[w][1] % 2 || a.gs[w][2] % 2))
+      a.vec = 0;
   const long long rows = (long long)B * T * (NH + NKVH);
   if (rows == 0) return LTVQKV_OK;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  const unsigned int grid = (unsigned int)((rows + 7) / 8);
+  // x: token tiles (each warp walks tokens w, w + 8 gridDim.x, ...), y: the q and k head rows
+  const dim3 grid((unsigned int)std::min(64, (T + 63) / 64), (unsigned int)(B * (NH + NKVH)));
+  if (B * (NH + NKVH) > 65535) return LTVQKV_ERR_SHAPE;
   if (dtype == LTVQKV_DTYPE_F32) rotary_norm_bwd_kernel<float><<<grid, 256, 0, s>>>(a);
   else rotary_norm_bwd_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(a);
   return ltvqkv_host::check_launch();
