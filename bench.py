@@ -33,7 +33,7 @@ METRIC = "filtered-QKV fwd+bwd tokens/s"
 UNIT = "tokens/s"
 
 CONFIGS = {
-    # BASELINE configs 1-3 mapped onto the reference parameterisation (head_dim 128, r = 128 ->
+    # Benchmark configs 1-3 mapped onto the reference parameterisation (head_dim 128, r = 128 ->
     # one decay logit per head per token; F = (NH + 2 NKVH) * 129).
     "config2": dict(B=32, T=1024, C=768, NH=6, NKVH=6, D=128, r=128, dtype="bf16", bias=0.0,
                     desc="d=12 training shape: B=32/rank, T=1024, C=768, 6+6+6 heads x 128, r=128, bf16"),
@@ -553,7 +553,7 @@ def run_reference(args, cfg):
 
 
 def run_decode(args):
-    """BASELINE config 4, kernel level: the filter-state decode update of a d=12 model (12 layers,
+    """Benchmark config 4, kernel level: the filter-state decode update of a d=12 model (12 layers,
     C=768, 6+6+6 heads x 128, batch 64, bf16) for 256 token steps — one `ltv_decode_step` launch
     per layer-step (projection of the new token, gate, recurrence step), replayed as a CUDA graph
     per token step, updating the cache's states in place. Attention, MLP and the prompt prefill

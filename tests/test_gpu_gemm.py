@@ -3,7 +3,7 @@
 Ports the reference's GEMM test (tests/test_fused_linear_transpose.py:32-86): shapes
 (1,16,32,128), (4,128,128,256), (4,1024,1024,3096), (2,31,63,127); tolerance 1e-4 (fp32) and
 5e-2 (bf16) for out, grad_x and grad_weight. The small shapes compare with the reference's golden
-vectors; the large ones (incl. the BASELINE d=12 training shape) with an fp32 contraction of the
+vectors; the large ones (incl. the d=12 training shape of config 2) with an fp32 contraction of the
 same bf16 values. Both grad_out layouts the reference accepts are exercised, and fp32 master
 weights with bf16 activations (grad_weight in fp32).
 """

@@ -4,7 +4,7 @@ Ports the reference's kernel tests (tests/test_ltv_cuda_fused_concat_head_major_
 patterned integer inputs, seq_len 1, 2, 3, 31, 32, 33, every divisor r of head dim 2, every dense
 stride layout of `combined` (with and without gaps), all-ones upstream gradients, tolerance
 exact without sigmoid and atol = rtol = 0.025 with sigmoid (tests/ltv_scan_test_utils.py:134-140).
-Beyond that: production head dim 128 with several look-back chunks, the BASELINE shapes at full
+Beyond that: production head dim 128 with several look-back chunks, the benchmark shapes at full
 size against the CPU oracle (max relative error with an absolute floor: <= 1e-5 fp32,
 <= 2e-2 bf16), transposed q/k gradient layouts, and the bounded-wait failure path.
 """
