@@ -418,7 +418,8 @@ def run_ours(args, cfg):
     step_bytes = float(B * T * (6 * C + 6 * H * D) * esz + F * C * esz)
     t_tc = step_flops / (tc_peak * 1e12)
     t_hbm = step_bytes / (peaks["hbm_gbs"] * 1e9)
-    step_frac = max(t_tc, t_hbm) / (ms_per_step / 1e3) if world == 1 else None
+    # per rank (weak scaling: every rank's step does the same work)
+    step_frac = max(t_tc, t_hbm) / (ms_per_step / 1e3)
 
     result = {
         "metric": METRIC,
