@@ -450,7 +450,7 @@ def run_ours(args, cfg):
                 "path": "LtvCudaFusedConcatHeadMajorRegisterCastBlellochScanQkvFilter forward + autograd backward",
                 "h2d": "pinned host -> device on a copy stream, one step ahead (overlaps the previous step's "
                        "compute; every step's copy is inside the timed region)"},
-        "gpu_launches": 5 * K,
+        "gpu_launches": 4 * K,  # logit pre-pass, projection+scan, scan backward, projection backward
         "roofline": {"bound": "tensor", "kernel": "gemm_pair_kernel (projection backward: dW + dx, CTA pairs)",
                      "achieved": round(achieved, 1), "peak": tc_peak, "unit": "TFLOP/s",
                      "frac": round(achieved / tc_peak, 4),

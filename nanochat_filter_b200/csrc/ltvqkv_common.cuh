@@ -57,6 +57,21 @@ LTVQKV_DEVICE unsigned int draw_ticket(WorkspaceHeader* ws) { return atomicAdd(&
 // Called once per CTA by one thread after the CTA has drawn its last ticket and finished
 // every global write whose ordering matters. The last CTA resets the counters and bumps the
 // epoch for the next launch on this workspace.
+// As finish_launch; returns true in the CTA that finished last (whose thread then sees every other
+// CTA's writes that preceded their finish_launch, through L2).
+LTVQKV_DEVICE bool finish_launch_last(WorkspaceHeader* ws, unsigned int num_ctas) {
+  __threadfence();
+  unsigned int done = atomicAdd(&ws->exit_counter, 1u);
+  if (done == num_ctas - 1) {
+    atomicExch(&ws->tile_counter, 0u);
+    atomicExch(&ws->exit_counter, 0u);
+    atomicAdd(&ws->epoch, 1u);
+    __threadfence();
+    return true;
+  }
+  return false;
+}
+
 LTVQKV_DEVICE void finish_launch(WorkspaceHeader* ws, unsigned int num_ctas) {
   __threadfence();
   unsigned int done = atomicAdd(&ws->exit_counter, 1u);

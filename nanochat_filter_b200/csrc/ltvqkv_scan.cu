@@ -801,6 +801,7 @@ int try_row_bwd(bool& used, int dtype, const void* combined, int64_t sc_b, int64
   f.grad_combined = reinterpret_cast<__nv_bfloat16*>(grad_combined);
   f.grad_inits = reinterpret_cast<__nv_bfloat16*>(grad_inits);
   f.bias_part = reinterpret_cast<float*>(ws + wx.bias_part);
+  f.grad_bias = grad_logit_bias;
   f.B = B; f.T = T; f.NH = NH; f.NKVH = NKVH; f.Da = Da; f.r = r; f.D = D; f.H = H; f.F = Fh;
   f.nchunks = (T + rtt - 1) / rtt; f.nrows = B * H; f.use_sigmoid = use_sigmoid; f.stages = rst;
   f.ws = reinterpret_cast<WorkspaceHeader*>(ws);
@@ -810,10 +811,7 @@ int try_row_bwd(bool& used, int dtype, const void* combined, int64_t sc_b, int64
     return ltvqkv_host::check_launch();
   const int grid = persistent_grid((const void*)kern, threads, tsm, f.nrows);
   kern<<<grid, threads, tsm, s>>>(tm_u, tm_l, tm_du, tm_g[0], tm_g[1], tm_g[2], tm_h[0], tm_h[1], tm_h[2], f);
-  int rc = ltvqkv_host::check_launch();
-  if (rc != LTVQKV_OK) return rc;
-  bias_reduce_kernel<<<H * Da, kBiasReduceThreads, 0, s>>>(f.bias_part, grad_logit_bias, B, 1, H, Da);
-  return ltvqkv_host::check_launch();
+  return ltvqkv_host::check_launch();  // the kernel's last CTA also reduces the bias partials
 }
 
 }  // namespace

@@ -44,6 +44,7 @@ struct TmaBwdArgs {
   __nv_bfloat16* grad_combined;
   __nv_bfloat16* grad_inits;
   float* bias_part;  // [B][H][Da]: one partial per row
+  float* grad_bias;  // backward: [H][Da], the partials' sums are added here by the last CTA
   int B, T, NH, NKVH, Da, r, D, H, F, nchunks, nrows, use_sigmoid;
   int stages;  // shared-memory ring depth (2..kRowMaxStages)
   WorkspaceHeader* ws;
@@ -496,7 +497,18 @@ __global__ void __launch_bounds__(kD / 2 + 32, row_bwd_min_blocks(kD, kTT))
     if (tid == 0) tma_store_wait0();
   }
   __syncthreads();
-  if (tid == 0) finish_launch(a.ws, gridDim.x);
+  // the CTA that finishes last adds the per-row logit-bias partials, batch by batch in order
+  __shared__ int last_cta;
+  if (tid == 0) last_cta = finish_launch_last(a.ws, gridDim.x) ? 1 : 0;
+  __syncthreads();
+  if (last_cta) {
+    const int n = a.H * Da;
+    for (int idx = tid; idx < n; idx += blockDim.x) {
+      float sum = 0.f;
+      for (int b = 0; b < a.B; ++b) sum += __ldcg(a.bias_part + (long long)b * n + idx);
+      a.grad_bias[idx] += sum;
+    }
+  }
 }
 
 }  // namespace ltvqkv
