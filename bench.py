@@ -213,8 +213,9 @@ def run_ours(args, cfg):
         if record is not None:
             record[0].record()
         # projection + scan forward in one call (equal to fused_linear_transpose_cuda_op followed
-        # by the scan op on comb^T, the filter's composition)
-        comb, q, k, v = ops.ltv_proj_scan_cuda_op(d["x"], w_c, inits, bias, *scan_args, True)   # comb [B, F, T]
+        # by the scan op on comb^T, the filter's composition); ckpt: the scan states at the 32-token
+        # chunk starts, from which the scan backward replays q/k/v instead of reading them
+        comb, q, k, v, ckpt = ops.ltv_proj_scan_cuda_op(d["x"], w_c, inits, bias, *scan_args, True)  # comb [B, F, T]
         if record is not None:
             record[1].record()
             record[2].record()
@@ -224,8 +225,12 @@ def run_ours(args, cfg):
         gb = torch.zeros_like(bias)
         if record is not None:
             record[3].record()
-        ops.ltv_fused_concat_head_major_register_cast_blelloch_scan_cuda_backward_kernel(
-            combined, inits, bias, q, k, v, d["gq"], d["gk"], d["gv"], gc, gi, gb, *scan_args, 32, 2, 8, True)
+        if ckpt.numel():
+            ops.ltv_scan_ckpt_backward_kernel(combined, inits, bias, ckpt, d["gq"], d["gk"], d["gv"], gc, gi, gb,
+                                              *scan_args, True)
+        else:
+            ops.ltv_fused_concat_head_major_register_cast_blelloch_scan_cuda_backward_kernel(
+                combined, inits, bias, q, k, v, d["gq"], d["gk"], d["gv"], gc, gi, gb, *scan_args, 32, 2, 8, True)
         if record is not None:
             record[4].record()
         gx = torch.empty_like(d["x"])

@@ -136,6 +136,24 @@ LTVQKV_API int ltvqkv_scan_bwd(int dtype,
                     int B, int T, int NH, int NKVH, int Da, int r, int use_sigmoid,
                     void* workspace, size_t workspace_bytes, void* stream);
 
+/* Scan backward from state checkpoints: ltvqkv_scan_bwd without the forward's outputs hq/hk/hv.
+ * ckpt is what ltvqkv_proj_scan_fwd_ckpt wrote for the same combined, inits and logit_bias; the
+ * kernel replays each 32-token chunk's outputs from it (the forward's own arithmetic, so results
+ * equal ltvqkv_scan_bwd's bit for bit) and reads 8 KB less per chunk of D = 128. Taken by bf16,
+ * D = 128, T % 32 == 0, B * H >= 2 * (SM count) and the production layouts ltvqkv_scan_bwd's
+ * row-streaming kernel needs; other requests return LTVQKV_ERR_UNSUPPORTED before anything is
+ * launched. No reference function corresponds (the reference always reads the outputs). */
+LTVQKV_API int ltvqkv_scan_bwd_ckpt(int dtype,
+                    const void* combined, int64_t sc_b, int64_t sc_t, int64_t sc_e,
+                    const void* inits, const float* logit_bias, const float* ckpt,
+                    const void* grad_hq, const int64_t* gq_strides,
+                    const void* grad_hk, const int64_t* gk_strides,
+                    const void* grad_hv, const int64_t* gv_strides,
+                    void* grad_combined, int64_t gc_b, int64_t gc_t, int64_t gc_e,
+                    void* grad_inits, float* grad_logit_bias,
+                    int B, int T, int NH, int NKVH, int Da, int r, int use_sigmoid,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------------------------------------------------
  * Look-back scan: replaces cpp_ewma_cuda.ltv_look_back_fused_concat_head_major_register_cast_
  * {blelloch,sequential}_scan_cuda_{forward,backward} (reference cpp_ewma/src/ltv_look_back_*.cu;
@@ -217,6 +235,16 @@ LTVQKV_API int ltvqkv_gemm_fwd(int dtype, const void* x, const void* weight, voi
  * is the scan's (ltvqkv_scan_workspace_bytes). */
 LTVQKV_API int ltvqkv_proj_scan_fwd(int dtype, const void* x, const void* weight, const void* inits,
                     const float* logit_bias, void* combined, void* out_q, void* out_k, void* out_v,
+                    int B, int T, int C, int NH, int NKVH, int Da, int r, int use_sigmoid,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
+/* As ltvqkv_proj_scan_fwd, and also writes the scan's fp32 state entering every 32-token chunk
+ * but the first: ckpt [B, H, T / 32, D] fp32 (16-byte aligned; entry [b, h, j] is the state after
+ * token 32 * j + 31, the last one is not written), for ltvqkv_scan_bwd_ckpt. Only the fused kernel
+ * writes checkpoints: where ltvqkv_proj_scan_fwd would run the two entry points in sequence, this
+ * returns LTVQKV_ERR_UNSUPPORTED before anything is launched (call ltvqkv_proj_scan_fwd instead). */
+LTVQKV_API int ltvqkv_proj_scan_fwd_ckpt(int dtype, const void* x, const void* weight, const void* inits,
+                    const float* logit_bias, void* combined, void* out_q, void* out_k, void* out_v, float* ckpt,
                     int B, int T, int C, int NH, int NKVH, int Da, int r, int use_sigmoid,
                     void* workspace, size_t workspace_bytes, void* stream);
 

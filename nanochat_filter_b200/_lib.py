@@ -20,6 +20,7 @@ LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libltvqkv.s
 
 DTYPE_F32 = 0
 DTYPE_BF16 = 1
+ERR_UNSUPPORTED = 9  # LTVQKV_ERR_UNSUPPORTED: a valid request this entry point does not take
 
 EXPORTED_SYMBOLS = (
     "ltvqkv_abi_version",
@@ -28,6 +29,7 @@ EXPORTED_SYMBOLS = (
     "ltvqkv_scan_workspace_bytes",
     "ltvqkv_scan_fwd",
     "ltvqkv_scan_bwd",
+    "ltvqkv_scan_bwd_ckpt",
     "ltvqkv_gemm_workspace_bytes",
     "ltvqkv_gemm_fwd",
     "ltvqkv_gemm_bwd",
@@ -36,6 +38,7 @@ EXPORTED_SYMBOLS = (
     "ltvqkv_debug_wait_timeout",
     "ltvqkv_scan_fwd_noalloc",
     "ltvqkv_proj_scan_fwd",
+    "ltvqkv_proj_scan_fwd_ckpt",
     "ltvqkv_lookback_workspace_bytes",
     "ltvqkv_lookback_scan_fwd",
     "ltvqkv_lookback_scan_bwd",
@@ -72,6 +75,11 @@ def _declare(lib: ctypes.CDLL) -> None:
                                     _vp, _pi64, _vp, _pi64, _vp, _pi64,
                                     _vp, _i64, _i64, _i64, _vp, _pf,
                                     _i, _i, _i, _i, _i, _i, _i, _vp, _sz, _vp]
+    lib.ltvqkv_scan_bwd_ckpt.restype = _i
+    lib.ltvqkv_scan_bwd_ckpt.argtypes = [_i, _vp, _i64, _i64, _i64, _vp, _pf, _pf,
+                                         _vp, _pi64, _vp, _pi64, _vp, _pi64,
+                                         _vp, _i64, _i64, _i64, _vp, _pf,
+                                         _i, _i, _i, _i, _i, _i, _i, _vp, _sz, _vp]
     lib.ltvqkv_lookback_workspace_bytes.restype = _sz
     lib.ltvqkv_lookback_workspace_bytes.argtypes = [_i, _i, _i, _i]
     lib.ltvqkv_lookback_scan_fwd.restype = _i
@@ -96,6 +104,9 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.ltvqkv_proj_scan_fwd.restype = _i
     lib.ltvqkv_proj_scan_fwd.argtypes = [_i, _vp, _vp, _vp, _pf, _vp, _vp, _vp, _vp,
                                          _i, _i, _i, _i, _i, _i, _i, _i, _vp, _sz, _vp]
+    lib.ltvqkv_proj_scan_fwd_ckpt.restype = _i
+    lib.ltvqkv_proj_scan_fwd_ckpt.argtypes = [_i, _vp, _vp, _vp, _pf, _vp, _vp, _vp, _vp, _pf,
+                                              _i, _i, _i, _i, _i, _i, _i, _i, _vp, _sz, _vp]
     lib.ltvqkv_gemm_bwd.restype = _i
     lib.ltvqkv_gemm_bwd.argtypes = [_i, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _vp, _i,
                                     _i, _i, _i, _i, _vp, _sz, _vp]

@@ -57,6 +57,7 @@ struct PsParams {
   const __nv_bfloat16* inits;     // [B][H][128]
   const float* logit_bias;        // [H]
   __nv_bfloat16* out[3];          // [B][heads][T][128]
+  float* ckpt;                    // optional [B][H][T / 32][128]: the fp32 state after every 32nd token
   WorkspaceHeader* ws;
 };
 
@@ -335,6 +336,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPsThreads, 1)
             E = __fmaf_rn(g.z, E, __fmul_rn(g.w, u1));
             op[(2 * j + 1) * kPsD] = __float2bfloat16_rn(E);
           }
+          // the state entering the next 32 tokens: the backward replays each 32-token chunk from
+          // it instead of re-reading the chunk's outputs (a warp writes 128 contiguous bytes)
+          if (prm.ckpt != nullptr && c0 + 32 < prm.T)
+            prm.ckpt[(((long long)b * prm.H + hh) * (prm.T / 32) + c0 / 32) * kPsD + c] = E;
         }
         // all TMEM reads of this accumulator are complete (tcgen05.wait::ld above)
         tc_fence_before();

@@ -684,8 +684,10 @@ template <int kTT>
 decltype(&scan_fwd_rows_kernel<128, 32>) row_fwd_kernel(int D) {
   return D == 64 ? scan_fwd_rows_kernel<64, kTT> : (D == 128 ? scan_fwd_rows_kernel<128, kTT> : scan_fwd_rows_kernel<256, kTT>);
 }
-decltype(&scan_bwd_rows_kernel<128, 32>) row_bwd_kernel(int D) {
-  return D == 64 ? scan_bwd_rows_kernel<64, 32> : (D == 128 ? scan_bwd_rows_kernel<128, 32> : scan_bwd_rows_kernel<256, 32>);
+decltype(&scan_bwd_rows_kernel<128, 32, false>) row_bwd_kernel(int D, bool ckpt) {
+  if (ckpt) return scan_bwd_rows_kernel<128, 32, true>;  // checkpoints come from the D = 128 fused forward
+  return D == 64 ? scan_bwd_rows_kernel<64, 32, false>
+                 : (D == 128 ? scan_bwd_rows_kernel<128, 32, false> : scan_bwd_rows_kernel<256, 32, false>);
 }
 // Chunk lengths and ring depths of the row kernels, measured on B200 at config 2 (576 rows, head
 // dim 128). Forward: 64-token chunks (128-byte value-tile rows; 32 when a decay group is narrower
@@ -756,11 +758,13 @@ int try_row_bwd(bool& used, int dtype, const void* combined, int64_t sc_b, int64
                 const int64_t* gq_strides, const void* grad_hk, const int64_t* gk_strides, const void* grad_hv,
                 const int64_t* gv_strides, void* grad_combined, int64_t gc_b, int64_t gc_t, int64_t gc_e,
                 void* grad_inits, float* grad_logit_bias, int B, int T, int NH, int NKVH, int Da, int r,
-                int use_sigmoid, char* ws, size_t workspace_bytes, cudaStream_t s) {
+                int use_sigmoid, char* ws, size_t workspace_bytes, cudaStream_t s, const float* ckpt = nullptr) {
   used = false;
   auto rows_ok = [&](const void* p, const int64_t* st) {
     return p == nullptr || (aligned16p(p) && st[3] == 1 && st[0] % 8 == 0 && st[1] % 8 == 0 && st[2] % 8 == 0);
   };
+  // with checkpoints the outputs are not read (their maps are never used)
+  auto h_ok = [&](const void* p, const int64_t* st) { return ckpt != nullptr || rows_ok(p, st); };
   const int H = NH + 2 * NKVH, D = Da * r;
   const int tpg = r / 32;
   const bool r_ok = r % 32 == 0 && tpg >= 1 && (tpg & (tpg - 1)) == 0;
@@ -772,9 +776,10 @@ int try_row_bwd(bool& used, int dtype, const void* combined, int64_t sc_b, int64
         H * Da <= kRowMaxBias && fast_shape_ok(T, Da, r) && tsm <= kMaxDynSmem &&
         (long long)B * H >= 2LL * ltvqkv_host::num_sms() && production_layout(combined, sc_b, sc_t, sc_e, T, Fh) &&
         production_layout(grad_combined, gc_b, gc_t, gc_e, T, Fh) && aligned16p(inits) &&
-        rows_ok(hq, hq_strides) && rows_ok(grad_hq, gq_strides) &&
-        (NKVH == 0 || (rows_ok(hk, hk_strides) && rows_ok(hv, hv_strides) && rows_ok(grad_hk, gk_strides) &&
-                       rows_ok(grad_hv, gv_strides)))))
+        h_ok(hq, hq_strides) && rows_ok(grad_hq, gq_strides) &&
+        (NKVH == 0 || (h_ok(hk, hk_strides) && h_ok(hv, hv_strides) && rows_ok(grad_hk, gk_strides) &&
+                       rows_ok(grad_hv, gv_strides))) &&
+        (ckpt == nullptr || (D == 128 && T % rtt == 0 && aligned16p(ckpt)))))
     return LTVQKV_OK;
   used = true;
   CUtensorMap tm_u, tm_du, tm_l, tm_g[3], tm_h[3];
@@ -790,8 +795,9 @@ int try_row_bwd(bool& used, int dtype, const void* combined, int64_t sc_b, int64
   const int heads[3] = {NH, NKVH, NKVH};
   for (int i = 0; i < 3 && ok; ++i) {
     const int src = heads[i] > 0 ? i : 0;  // unused groups reuse the q maps
-    ok = bf16_map_rows(&tm_g[i], gg[src], gst[src], B, heads[src], T, D, rtt) &&
-         bf16_map_rows(&tm_h[i], hh[src], hst[src], B, heads[src], T, D, rtt);
+    ok = bf16_map_rows(&tm_g[i], gg[src], gst[src], B, heads[src], T, D, rtt);
+    if (ckpt == nullptr) ok = ok && bf16_map_rows(&tm_h[i], hh[src], hst[src], B, heads[src], T, D, rtt);
+    else tm_h[i] = tm_g[i];  // not read
   }
   if (!ok) return LTVQKV_ERR_LAUNCH;
   const ScanWorkspaceLayout wx = scan_ws_layout(fast_geometry(B, T, NH, NKVH, Da, r));
@@ -802,11 +808,12 @@ int try_row_bwd(bool& used, int dtype, const void* combined, int64_t sc_b, int64
   f.grad_inits = reinterpret_cast<__nv_bfloat16*>(grad_inits);
   f.bias_part = reinterpret_cast<float*>(ws + wx.bias_part);
   f.grad_bias = grad_logit_bias;
+  f.ckpt = ckpt;
   f.B = B; f.T = T; f.NH = NH; f.NKVH = NKVH; f.Da = Da; f.r = r; f.D = D; f.H = H; f.F = Fh;
   f.nchunks = (T + rtt - 1) / rtt; f.nrows = B * H; f.use_sigmoid = use_sigmoid; f.stages = rst;
   f.ws = reinterpret_cast<WorkspaceHeader*>(ws);
-  const int threads = D / 2 + 32;  // consumers own channel pairs, plus the producer warp
-  auto kern = row_bwd_kernel(D);  // 32-token chunks
+  const int threads = D / 2 + (ckpt != nullptr ? 64 : 32);  // consumers own channel pairs, producer (+ replay) warp
+  auto kern = row_bwd_kernel(D, ckpt != nullptr);  // 32-token chunks
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tsm) != cudaSuccess)
     return ltvqkv_host::check_launch();
   const int grid = persistent_grid((const void*)kern, threads, tsm, f.nrows);
@@ -1041,6 +1048,35 @@ extern "C" int ltvqkv_scan_bwd(int dtype, const void* combined, int64_t sc_b, in
   return ltvqkv_host::check_launch();
 }
 
+// Scan backward from the forward's state checkpoints (ltvqkv_proj_scan_fwd_ckpt) instead of its
+// outputs: the row-streaming kernel replays each 32-token chunk's outputs from the stored fp32 state.
+// Results equal ltvqkv_scan_bwd's bit for bit; shapes or layouts that kernel does not take return
+// LTVQKV_ERR_UNSUPPORTED before anything is launched.
+extern "C" int ltvqkv_scan_bwd_ckpt(int dtype, const void* combined, int64_t sc_b, int64_t sc_t, int64_t sc_e,
+                                    const void* inits, const float* logit_bias, const float* ckpt,
+                                    const void* grad_hq, const int64_t* gq_strides, const void* grad_hk,
+                                    const int64_t* gk_strides, const void* grad_hv, const int64_t* gv_strides,
+                                    void* grad_combined, int64_t gc_b, int64_t gc_t, int64_t gc_e, void* grad_inits,
+                                    float* grad_logit_bias, int B, int T, int NH, int NKVH, int Da, int r,
+                                    int use_sigmoid, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!ltvqkv_host::valid_dtype(dtype)) return LTVQKV_ERR_DTYPE;
+  int st = validate_scan_shape(B, T, NH, NKVH, Da, r);
+  if (st != LTVQKV_OK) return st;
+  if (!combined || !inits || !logit_bias || !ckpt || !grad_combined || !grad_inits || !grad_logit_bias)
+    return LTVQKV_ERR_INVALID_ARG;
+  if ((NH > 0 && (!grad_hq || !gq_strides)) || (NKVH > 0 && (!grad_hk || !grad_hv || !gk_strides || !gv_strides)))
+    return LTVQKV_ERR_INVALID_ARG;
+  if (B == 0 || T == 0) return LTVQKV_ERR_UNSUPPORTED;
+  if (!workspace) return LTVQKV_ERR_WORKSPACE;
+  static const int64_t kNone[4] = {0, 0, 0, 1};
+  bool used = false;
+  const int rc = try_row_bwd(used, dtype, combined, sc_b, sc_t, sc_e, inits, logit_bias, nullptr, kNone, nullptr,
+                             kNone, nullptr, kNone, grad_hq, gq_strides, grad_hk, gk_strides, grad_hv, gv_strides,
+                             grad_combined, gc_b, gc_t, gc_e, grad_inits, grad_logit_bias, B, T, NH, NKVH, Da, r,
+                             use_sigmoid, reinterpret_cast<char*>(workspace), workspace_bytes,
+                             reinterpret_cast<cudaStream_t>(stream), ckpt);
+  return used ? rc : LTVQKV_ERR_UNSUPPORTED;
+}
 
 // ------------------------------------------------------------------------------------------
 // Allocation-free forward scan.

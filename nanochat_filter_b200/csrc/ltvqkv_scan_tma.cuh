@@ -45,6 +45,7 @@ struct TmaBwdArgs {
   __nv_bfloat16* grad_inits;
   float* bias_part;  // [B][H][Da]: one partial per row
   float* grad_bias;  // backward: [H][Da], the partials' sums are added here by the last CTA
+  const float* ckpt; // backward from checkpoints: [B][H][nchunks][D], the fp32 state entering chunk j + 1
   int B, T, NH, NKVH, Da, r, D, H, F, nchunks, nrows, use_sigmoid;
   int stages;  // shared-memory ring depth (2..kRowMaxStages)
   WorkspaceHeader* ws;
@@ -86,7 +87,7 @@ inline size_t row_fwd_smem_bytes(int D, int Da, int H, int tt, int stages) {
 inline size_t row_bwd_smem_bytes(int D, int Da, int H, int tt, int stages) {
   return 1024 + (size_t)stages * row_bwd_stage_bytes(D, Da, tt) + (size_t)row_align(H * Da, 4) * 4 +
          (size_t)16 * Da * tt + (size_t)4 * (D / 32) * tt + (size_t)4 * Da * tt + sizeof(RowTile) * stages + 16 +
-         16 * stages + 64;
+         24 * stages + 64;
 }
 
 
@@ -101,13 +102,19 @@ constexpr int row_min_blocks(int smem, int threads, int regs) {
 constexpr int row_fwd_min_blocks(int D, int tt) {
   return row_min_blocks(4 * row_fwd_stage_bytes(D, 1, tt) + 3072, D + 32, 64);
 }
-constexpr int row_bwd_min_blocks(int D, int tt) {
-  return row_min_blocks(2 * row_bwd_stage_bytes(D, 1, tt) + 3072, D / 2 + 32, 128);
+constexpr int row_bwd_min_blocks(int D, int tt, bool ckpt) {
+  return row_min_blocks(2 * row_bwd_stage_bytes(D, 1, tt) + 3072, D / 2 + (ckpt ? 64 : 32), 128);
 }
 
 
 // 16-byte chunk k of row `row` in a tile of kTT bf16 per row, as TMA writes it with the 128-byte
 // (kTT = 64) or 64-byte (kTT = 32) swizzle.
+// Two floats rounded to bf16 and packed (lo in the low half), as one 32-bit shared-memory word.
+LTVQKV_DEVICE uint32_t pack_bf16x2(float lo, float hi) {
+  const __nv_bfloat162 p = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&p);
+}
+
 template <int kTT>
 LTVQKV_DEVICE const uint4* swz_chunk(const uint8_t* tile, int row, int k) {
   if constexpr (kTT == 64) {
@@ -255,8 +262,13 @@ __global__ void __launch_bounds__(kD + 32, row_fwd_min_blocks(kD, kTT))
 // ------------------------------------------------------------------------------------------
 // Backward
 // ------------------------------------------------------------------------------------------
-template <int kD, int kTT>
-__global__ void __launch_bounds__(kD / 2 + 32, row_bwd_min_blocks(kD, kTT))
+// kCkpt: h_{t-1} is not read from the forward's outputs but replayed per chunk from the fp32 state
+// the forward stored at the chunk's start (its recurrence step for step, so the replayed outputs are
+// the forward's bit for bit); the chunk's 8 KB output tile becomes a 512-byte state read. A fourth
+// warp replays each chunk while the consumers walk the previous one, so the consumers' per-chunk
+// path is unchanged.
+template <int kD, int kTT, bool kCkpt>
+__global__ void __launch_bounds__(kD / 2 + (kCkpt ? 64 : 32), row_bwd_min_blocks(kD, kTT, kCkpt))
     scan_bwd_rows_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_constant__ CUtensorMap tm_l,
                          const __grid_constant__ CUtensorMap tm_du,
                          const __grid_constant__ CUtensorMap tm_gq, const __grid_constant__ CUtensorMap tm_gk,
@@ -281,6 +293,7 @@ __global__ void __launch_bounds__(kD / 2 + 32, row_bwd_min_blocks(kD, kTT))
   RowTile* info = reinterpret_cast<RowTile*>(bsum + Da * kTT);               // [S]
   uint64_t* full = smem_align<uint64_t>(info + S, 16);
   uint64_t* empty = full + S;
+  uint64_t* hfull = empty + S;  // kCkpt: the stage's replayed outputs are in place (32 replay lanes)
   __shared__ volatile int abort_flag;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -288,6 +301,7 @@ __global__ void __launch_bounds__(kD / 2 + 32, row_bwd_min_blocks(kD, kTT))
     for (int i = 0; i < S; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], ncons / 32);
+      if (kCkpt) mbar_init(&hfull[i], 32);
     }
     abort_flag = 0;
     fence_mbar_init();
@@ -328,15 +342,82 @@ __global__ void __launch_bounds__(kD / 2 + 32, row_bwd_min_blocks(kD, kTT))
           ti.b = b; ti.h = h; ti.j = j; ti.t0 = t0; ti.tlen = min(kTT, a.T - t0);
           ti.which = which; ti.hloc = hloc; ti.nheads = nheads;
           uint8_t* sb = stages + st * sbytes;
-          const uint32_t bytes = (uint32_t)(D * kTT * 2 + Da * LB * 2 + 2 * kTT * D * 2 + (q == 0 ? D * 2 : 0));
+          const uint32_t hbytes = kCkpt ? (j > 0 ? D * 4 : 0) : kTT * D * 2;
+          const uint32_t bytes = (uint32_t)(D * kTT * 2 + Da * LB * 2 + kTT * D * 2 + hbytes + (q == 0 ? D * 2 : 0));
           mbar_arrive_expect_tx(&full[st], bytes);
           tma_load_2d(sb, &tm_u, &full[st], t0, frow);
           tma_load_2d(sb + loff, &tm_l, &full[st], t0, frow + D);
           tma_load_4d(sb + goff, mg, &full[st], 0, t0, hloc, b);
-          tma_load_4d(sb + hoff, mh, &full[st], 0, t0 - 1, hloc, b);
+          if (!kCkpt)
+            tma_load_4d(sb + hoff, mh, &full[st], 0, t0 - 1, hloc, b);
+          else if (j > 0)
+            bulk_load(sb + hoff, a.ckpt + (((long long)b * a.H + h) * a.nchunks + (j - 1)) * D, D * 4, &full[st]);
           if (q == 0) bulk_load(sb + ioff, a.inits + ((long long)b * a.H + h) * D, D * 2, &full[st]);
         }
       }
+    }
+    __syncwarp();
+  } else if (kCkpt && warp == ncons / 32 + 1) {
+    // ---------------- replay (kCkpt): H32 row t = h_{t0 + t - 1}, from the chunk's entering state ----------------
+    // Lane l does the work of consumers l and l + 32 (channel pairs (2l, 2l + 1) and (2l + 64,
+    // 2l + 65)) with their conflict-free read order, one chunk ahead of them. The forward's
+    // arithmetic step for step: alpha = sigmoid(logit + bias), E = fma(1 - alpha, E, alpha * u), h = bf16(E).
+    static_assert(!kCkpt || kD == 128, "checkpoints come from the head-dim-128 fused forward");
+    const int sw = (lane >> 2) & 1;
+    uint32_t initA = 0, initB = 0;  // h_{-1} of the two channel pairs
+    for (int i = 0;; ++i) {
+      const int st = i % S;
+      const uint32_t ph = (uint32_t)(i / S) & 1u;
+      if (!mbar_wait(&full[st], ph, &abort_flag, a.ws, 0x7203)) break;
+      const RowTile ti = info[st];
+      if (ti.row < 0) break;
+      uint8_t* sb = stages + st * sbytes;
+      if (ti.j == a.nchunks - 1) {
+        initA = reinterpret_cast<const uint32_t*>(sb + ioff)[lane];
+        initB = reinterpret_cast<const uint32_t*>(sb + ioff)[lane + 32];
+      }
+      // alpha of token t0 + lane (one decay group; the chunk is whole: T % 32 == 0)
+      const float lg = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(sb + loff)[lane]) + lb_s[ti.h];
+      const float al_l = a.use_sigmoid ? sigmoid_f32(lg) : lg;
+      float E0, E1, E2, E3;
+      if (ti.j == 0) {
+        E0 = __uint_as_float(initA << 16); E1 = __uint_as_float(initA & 0xffff0000u);
+        E2 = __uint_as_float(initB << 16); E3 = __uint_as_float(initB & 0xffff0000u);
+      } else {
+        const float2 ea = reinterpret_cast<const float2*>(sb + hoff)[lane];
+        const float2 eb = reinterpret_cast<const float2*>(sb + hoff)[lane + 32];
+        E0 = ea.x; E1 = ea.y; E2 = eb.x; E3 = eb.y;
+      }
+      __syncwarp();  // every lane has its state before row 0 is written over the stored states
+      uint32_t* H32 = reinterpret_cast<uint32_t*>(sb + hoff);
+      H32[lane] = pack_bf16x2(E0, E1);
+      H32[lane + 32] = pack_bf16x2(E2, E3);
+#pragma unroll
+      for (int k = 0; k < kTT / 8; ++k) {
+        const int ra = 2 * lane, rb = 2 * lane + 64;
+        const uint4 a0 = *swz_chunk<kTT>(sb, ra + sw, k), a1 = *swz_chunk<kTT>(sb, ra + 1 - sw, k);
+        const uint4 b0 = *swz_chunk<kTT>(sb, rb + sw, k), b1 = *swz_chunk<kTT>(sb, rb + 1 - sw, k);
+        float fa0[8], fa1[8], fb0[8], fb1[8];
+        unpack8(sw ? a1 : a0, fa0);
+        unpack8(sw ? a0 : a1, fa1);
+        unpack8(sw ? b1 : b0, fb0);
+        unpack8(sw ? b0 : b1, fb1);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int t = 8 * k + e;
+          if (t + 1 < kTT) {
+            const float al = __shfl_sync(0xffffffffu, al_l, t);
+            const float om = 1.0f - al;
+            E0 = __fmaf_rn(om, E0, __fmul_rn(al, fa0[e]));
+            E1 = __fmaf_rn(om, E1, __fmul_rn(al, fa1[e]));
+            E2 = __fmaf_rn(om, E2, __fmul_rn(al, fb0[e]));
+            E3 = __fmaf_rn(om, E3, __fmul_rn(al, fb1[e]));
+            H32[(t + 1) * (D / 2) + lane] = pack_bf16x2(E0, E1);
+            H32[(t + 1) * (D / 2) + lane + 32] = pack_bf16x2(E2, E3);
+          }
+        }
+      }
+      mbar_arrive(&hfull[st]);  // release: this lane's H32 writes are visible to the consumers' wait
     }
     __syncwarp();
   } else {
@@ -377,7 +458,7 @@ __global__ void __launch_bounds__(kD / 2 + 32, row_bwd_min_blocks(kD, kTT))
       const uint32_t* G32 = reinterpret_cast<const uint32_t*>(sb + goff);
       uint32_t* H32 = reinterpret_cast<uint32_t*>(sb + hoff);
       // h_{t-1} of the row's first token is the initial state (the tile's row -1 was filled with 0)
-      if (ti.t0 == 0) H32[tid] = init2;
+      if (!kCkpt && ti.t0 == 0) H32[tid] = init2;
       for (int q = tid; q < Da * kTT; q += ncons) {
         const int g = q / kTT, t = q % kTT;
         const float lb = lb_s[ti.h * Da + g];
@@ -394,8 +475,10 @@ __global__ void __launch_bounds__(kD / 2 + 32, row_bwd_min_blocks(kD, kTT))
       }
       named_barrier(1, ncons);  // gates ready
 
-      // reverse walk: adjoint carries, du, and the per-token dalpha terms of both channels
       const float4* grow = gates + gi * kTT;
+      if (kCkpt && !mbar_wait(&hfull[st], ph, &abort_flag, a.ws, 0x7204)) break;  // replayed outputs in place
+
+      // reverse walk: adjoint carries, du, and the per-token dalpha terms of both channels
       // one 8-token block per iteration: unrolling across blocks would let every block's loads be
       // hoisted to the top and spill
 #pragma unroll 1

@@ -116,7 +116,14 @@ lib.define(
 lib.define(
     "ltv_proj_scan_cuda_op("
     "Tensor x, Tensor weight, Tensor inits, Tensor logit_bias, int NH, int NKVH, int da, int r, bool use_sigmoid"
-    ") -> (Tensor, Tensor, Tensor, Tensor)"
+    ") -> (Tensor, Tensor, Tensor, Tensor, Tensor)"
+)
+lib.define(
+    "ltv_scan_ckpt_backward_kernel("
+    "Tensor combined, Tensor inits, Tensor logit_bias, Tensor ckpt, Tensor grad_hq, Tensor grad_hk, Tensor grad_hv, "
+    "Tensor(a!) grad_combined, Tensor(b!) grad_inits, Tensor(c!) grad_logit_bias, int NH, int NKVH, int da, int r, "
+    "bool use_sigmoid"
+    ") -> ()"
 )
 lib.define("ltv_rotary_qk_norm(Tensor q, Tensor k, Tensor cos, Tensor sin) -> (Tensor, Tensor)")
 lib.define(
@@ -481,12 +488,14 @@ for _kind in ("blelloch", "sequential"):
 # Projection + scan forward in one call
 # ------------------------------------------------------------------------------------------
 def _proj_scan_forward_kernel(x, weight, inits, logit_bias, combined, out_q, out_k, out_v, NH, NKVH, da, r,
-                              use_sigmoid):
+                              use_sigmoid, ckpt=None):
     """fused_linear_transpose(x, weight) -> combined [B, F, T], then the scan over combined^T.
 
     Equals `fused_linear_transpose` followed by the scan forward kernel on `combined.transpose(1, 2)`
     (the reference filter's composition,
     nanochat/ltv_cuda_fused_concat_head_major_register_cast_blelloch_scan_qkv_filter.py:24-73).
+    With `ckpt` ([B, H, T / 32, D] fp32) the scan states at the 32-token chunk starts are written
+    too; returns False (and writes nothing) where the one-kernel form that writes them does not apply.
     """
     if not x.is_contiguous() or x.dim() != 3:
         raise RuntimeError("ltv_proj_scan requires a contiguous [B, T, C] x")
@@ -508,11 +517,34 @@ def _proj_scan_forward_kernel(x, weight, inits, logit_bias, combined, out_q, out
             raise RuntimeError("out_q/out_k/out_v must be contiguous [B, heads, T, D] of x's dtype")
     nbytes = max(L.ltvqkv_scan_workspace_bytes(B, T, NH, NKVH, da, r), L.ltvqkv_gemm_workspace_bytes())
     ws = _lib.workspace(x.device, nbytes)
-    rc = L.ltvqkv_proj_scan_fwd(_lib.dtype_code(x.dtype), x.data_ptr(), w.data_ptr(), inits.data_ptr(),
-                                logit_bias.data_ptr(), combined.data_ptr(), out_q.data_ptr(), out_k.data_ptr(),
-                                out_v.data_ptr(), B, T, C, NH, NKVH, da, r, int(bool(use_sigmoid)), ws.data_ptr(),
-                                ws.numel(), _lib.stream_handle(x.device))
+    args = (_lib.dtype_code(x.dtype), x.data_ptr(), w.data_ptr(), inits.data_ptr(), logit_bias.data_ptr(),
+            combined.data_ptr(), out_q.data_ptr(), out_k.data_ptr(), out_v.data_ptr())
+    rest = (B, T, C, NH, NKVH, da, r, int(bool(use_sigmoid)), ws.data_ptr(), ws.numel(), _lib.stream_handle(x.device))
+    if ckpt is not None:
+        if tuple(ckpt.shape) != (B, H, T // 32, D) or ckpt.dtype != torch.float32 or not ckpt.is_contiguous():
+            raise RuntimeError("ckpt must be a contiguous [B, H, T / 32, D] float32 tensor")
+        rc = L.ltvqkv_proj_scan_fwd_ckpt(*args, ckpt.data_ptr(), *rest)
+        if rc == _lib.ERR_UNSUPPORTED:
+            return False
+        _lib.check(rc, "ltvqkv_proj_scan_fwd_ckpt")
+        return True
+    rc = L.ltvqkv_proj_scan_fwd(*args, *rest)
     _lib.check(rc, "ltvqkv_proj_scan_fwd")
+    return False
+
+
+def _ckpt_shape(x, NH, NKVH, da, r):
+    """Shape of the state checkpoints the one-kernel forward writes for these sizes, or (0,) where it
+    does not apply (bf16, head dim 128 in one decay group, T % 32 == 0, and at least two
+    (batch, head) rows per SM)."""
+    B, T, _ = x.shape
+    H, D = NH + 2 * NKVH, da * r
+    if x.dtype != torch.bfloat16 or D != 128 or da != 1 or T % 32 != 0 or T == 0 or not 1 <= H <= 128:
+        return (0,)
+    dev = x.device if x.device.type == "cuda" else None
+    sms = (torch.cuda.get_device_properties(dev if dev is not None else torch.cuda.current_device())
+           .multi_processor_count if torch.cuda.is_available() else 148)
+    return (B, H, T // 32, D) if B * H >= 2 * sms else (0,)
 
 
 def _proj_scan_op(x, weight, inits, logit_bias, NH, NKVH, da, r, use_sigmoid):
@@ -524,25 +556,79 @@ def _proj_scan_op(x, weight, inits, logit_bias, NH, NKVH, da, r, use_sigmoid):
     out_q = torch.empty((B, NH, T, D), **kw)
     out_k = torch.empty((B, NKVH, T, D), **kw)
     out_v = torch.empty((B, NKVH, T, D), **kw)
-    _proj_scan_forward_kernel(x, weight, inits, logit_bias, combined, out_q, out_k, out_v, NH, NKVH, da, r,
-                              use_sigmoid)
-    return combined, out_q, out_k, out_v
+    shape = _ckpt_shape(x, NH, NKVH, da, r)
+    ckpt = torch.empty(shape, device=x.device, dtype=torch.float32)
+    written = _proj_scan_forward_kernel(x, weight, inits, logit_bias, combined, out_q, out_k, out_v, NH, NKVH, da,
+                                        r, use_sigmoid, ckpt if ckpt.numel() else None)
+    if ckpt.numel() and not written:
+        raise RuntimeError("ltvqkv_proj_scan_fwd_ckpt did not take a shape the checkpoint rule admits")
+    return combined, out_q, out_k, out_v, ckpt
+
+
+def _rows_ok(t):
+    """The row-streaming backward's layout for an upstream gradient: unit channel stride, 16-byte
+    aligned rows."""
+    st = t.stride()
+    return st[3] == 1 and all(s_ % 8 == 0 for s_ in st[:3]) and t.data_ptr() % 16 == 0
+
+
+def _scan_ckpt_backward(combined, inits, logit_bias, ckpt, grad_hq, grad_hk, grad_hv, grad_combined, grad_inits,
+                        grad_logit_bias, NH, NKVH, da, r, use_sigmoid):
+    """ltvqkv_scan_bwd_ckpt; returns its status (ERR_UNSUPPORTED: nothing was launched)."""
+    _check_scan_inputs(combined, inits, logit_bias, NH, NKVH, da, r)
+    L = _lib.load()
+    B, T, _ = combined.shape
+    inits = inits.contiguous()
+    logit_bias = logit_bias.contiguous()
+    if not grad_inits.is_contiguous() or not grad_logit_bias.is_contiguous():
+        raise RuntimeError("grad_inits and grad_logit_bias must be contiguous")
+    if grad_combined.shape != combined.shape or grad_combined.dtype != combined.dtype:
+        raise RuntimeError("grad_combined must match combined's shape and dtype")
+    if ckpt.dtype != torch.float32 or not ckpt.is_contiguous():
+        raise RuntimeError("ckpt must be a contiguous float32 tensor")
+    for t in (grad_hq, grad_hk, grad_hv):
+        if t.dtype != combined.dtype:
+            raise RuntimeError("output gradients must share combined's dtype")
+    nbytes = L.ltvqkv_scan_workspace_bytes(B, T, NH, NKVH, da, r)
+    ws = _lib.workspace(combined.device, nbytes)
+    sc, gc = combined.stride(), grad_combined.stride()
+    S = _lib.strides
+    return L.ltvqkv_scan_bwd_ckpt(
+        _lib.dtype_code(combined.dtype), combined.data_ptr(), sc[0], sc[1], sc[2], inits.data_ptr(),
+        logit_bias.data_ptr(), ckpt.data_ptr(),
+        grad_hq.data_ptr(), S(grad_hq.stride()), grad_hk.data_ptr(), S(grad_hk.stride()),
+        grad_hv.data_ptr(), S(grad_hv.stride()),
+        grad_combined.data_ptr(), gc[0], gc[1], gc[2], grad_inits.data_ptr(), grad_logit_bias.data_ptr(),
+        B, T, NH, NKVH, da, r, int(bool(use_sigmoid)), ws.data_ptr(), ws.numel(),
+        _lib.stream_handle(combined.device))
+
+
+def _scan_ckpt_backward_kernel(combined, inits, logit_bias, ckpt, grad_hq, grad_hk, grad_hv, grad_combined,
+                               grad_inits, grad_logit_bias, NH, NKVH, da, r, use_sigmoid):
+    """The scan backward kernel from the forward's state checkpoints (ltv_proj_scan_cuda_op's fifth
+    output) instead of its outputs; results equal the backward kernel's bit for bit."""
+    rc = _scan_ckpt_backward(combined, inits, logit_bias, ckpt, grad_hq, grad_hk, grad_hv, grad_combined, grad_inits,
+                             grad_logit_bias, NH, NKVH, da, r, use_sigmoid)
+    _lib.check(rc, "ltvqkv_scan_bwd_ckpt")
 
 
 def _ps_setup(ctx, inputs, output):
     x, weight, inits, logit_bias, NH, NKVH, da, r, use_sigmoid = inputs
-    combined, hq, hk, hv = output
+    combined, hq, hk, hv, ckpt = output
     # `combined` is usually not used downstream: keep its gradient None instead of a zero tensor
     ctx.set_materialize_grads(False)
-    ctx.save_for_backward(x, weight, combined, inits, logit_bias, hq, hk, hv)
+    ctx.mark_non_differentiable(ckpt)
+    ctx.save_for_backward(x, weight, combined, inits, logit_bias, hq, hk, hv, ckpt)
     ctx.args = (NH, NKVH, da, r)
     ctx.use_sigmoid = use_sigmoid
 
 
-def _ps_backward(ctx, grad_comb, grad_hq, grad_hk, grad_hv):
+def _ps_backward(ctx, grad_comb, grad_hq, grad_hk, grad_hv, _grad_ckpt):
     # the two reference backward kernels in sequence: scan backward into grad_combined (whose
-    # [B, F, T] memory is the projection's grad_out), then the projection backward
-    x, weight, comb, inits, logit_bias, hq, hk, hv = ctx.saved_tensors
+    # [B, F, T] memory is the projection's grad_out), then the projection backward. Where the
+    # forward wrote state checkpoints the scan backward replays its outputs from them (equal results,
+    # less memory traffic) instead of reading them.
+    x, weight, comb, inits, logit_bias, hq, hk, hv, ckpt = ctx.saved_tensors
     combined = comb.transpose(1, 2)
     grad_hq = torch.zeros_like(hq) if grad_hq is None else grad_hq
     grad_hk = torch.zeros_like(hk) if grad_hk is None else grad_hk
@@ -550,9 +636,17 @@ def _ps_backward(ctx, grad_comb, grad_hq, grad_hk, grad_hv):
     grad_combined = torch.empty_like(combined)
     grad_inits = torch.empty_like(inits, memory_format=torch.contiguous_format)
     grad_logit_bias = torch.zeros_like(logit_bias, memory_format=torch.contiguous_format)
-    torch.ops.nanochat_cuda.ltv_fused_concat_head_major_register_cast_blelloch_scan_cuda_backward_kernel(
-        combined, inits, logit_bias, hq, hk, hv, grad_hq, grad_hk, grad_hv, grad_combined, grad_inits,
-        grad_logit_bias, *ctx.args, 32, 2, 8, ctx.use_sigmoid)
+    rc = _lib.ERR_UNSUPPORTED
+    if ckpt.numel():
+        gq, gk, gv = (g if _rows_ok(g) else g.contiguous() for g in (grad_hq, grad_hk, grad_hv))
+        rc = _scan_ckpt_backward(combined, inits, logit_bias, ckpt, gq, gk, gv, grad_combined, grad_inits,
+                                 grad_logit_bias, *ctx.args, ctx.use_sigmoid)
+    if rc == _lib.ERR_UNSUPPORTED:
+        torch.ops.nanochat_cuda.ltv_fused_concat_head_major_register_cast_blelloch_scan_cuda_backward_kernel(
+            combined, inits, logit_bias, hq, hk, hv, grad_hq, grad_hk, grad_hv, grad_combined, grad_inits,
+            grad_logit_bias, *ctx.args, 32, 2, 8, ctx.use_sigmoid)
+    else:
+        _lib.check(rc, "ltvqkv_scan_bwd_ckpt")
     grad_out = grad_combined.transpose(1, 2)
     if grad_comb is not None:
         grad_out = grad_out + grad_comb
@@ -571,7 +665,12 @@ def _proj_scan_fake(x, weight, inits, logit_bias, NH, NKVH, da, r, use_sigmoid):
     D = da * r
     F = (NH + 2 * NKVH) * (D + da)
     return (x.new_empty((B, F, T)), x.new_empty((B, NH, T, D)), x.new_empty((B, NKVH, T, D)),
-            x.new_empty((B, NKVH, T, D)))
+            x.new_empty((B, NKVH, T, D)), x.new_empty(_ckpt_shape(x, NH, NKVH, da, r), dtype=torch.float32))
+
+
+@torch.library.register_fake("nanochat_cuda::ltv_scan_ckpt_backward_kernel")
+def _scan_ckpt_backward_fake(*args):
+    return None
 
 
 @torch.library.register_fake("nanochat_cuda::ltv_proj_scan_forward_kernel")
@@ -765,6 +864,7 @@ for _kind in ("blelloch", "sequential"):
     torch.library.impl(f"nanochat_cuda::{_LB.format(_kind, 'backward_kernel')}", "CUDA", _lb_backward_kernel)
 torch.library.impl("nanochat_cuda::ltv_proj_scan_forward_kernel", "CUDA", _proj_scan_forward_kernel)
 torch.library.impl("nanochat_cuda::ltv_proj_scan_cuda_op", "CUDA", _proj_scan_op)
+torch.library.impl("nanochat_cuda::ltv_scan_ckpt_backward_kernel", "CUDA", _scan_ckpt_backward_kernel)
 
 
 
@@ -796,7 +896,8 @@ def ltv_decode_step(x: torch.Tensor, weight: torch.Tensor, logit_bias: torch.Ten
 def ltv_proj_scan(x: torch.Tensor, weight: torch.Tensor, inits: torch.Tensor, logit_bias: torch.Tensor, NH: int,
                   NKVH: int, da: int, r: int, use_sigmoid: bool = True):
     """Projection and scan forward in one call; returns (combined [B, F, T], q, k, v [B, heads, T, D])."""
-    return torch.ops.nanochat_cuda.ltv_proj_scan_cuda_op(x, weight, inits, logit_bias, NH, NKVH, da, r, use_sigmoid)
+    return torch.ops.nanochat_cuda.ltv_proj_scan_cuda_op(x, weight, inits, logit_bias, NH, NKVH, da, r,
+                                                         use_sigmoid)[:4]
 
 
 def rotary_qk_norm(q: torch.Tensor, k: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor):

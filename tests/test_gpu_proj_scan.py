@@ -75,6 +75,14 @@ def test_proj_scan_equals_two_ops(cuda_device, B, T, C, NH, NKVH, Da, r, use_sig
     for a, b, n in zip(got, ref, ("combined", "q", "k", "v")):
         assert a.shape == b.shape, n
         assert torch.equal(a, b), f"{n}: {(a.float() - b.float()).abs().max().item()}"
+    ckpt = got[4]
+    if ckpt.numel():
+        # entry j is the fp32 state after token 32 j + 31, whose bf16 rounding is that token's output
+        H = NH + 2 * NKVH
+        assert tuple(ckpt.shape) == (B, H, T // 32, 128)
+        outs = torch.cat([o for o, n in zip(got[1:4], (NH, NKVH, NKVH)) if n], dim=1)
+        last = outs[:, :, 31::32][:, :, :-1]
+        assert torch.equal(ckpt[:, :, :-1].to(torch.bfloat16), last)
 
 
 def test_proj_scan_fp32_fallback(cuda_device):
@@ -89,7 +97,7 @@ def test_proj_scan_against_oracle(cuda_device):
     """The fused path against the CPU restatement of the scan on the kernel's own `combined`."""
     B, T, C, NH, NKVH, Da, r = 300, 64, 192, 1, 0, 1, 128   # 300 rows: the fused kernel
     x, w, inits, bias = _inputs(cuda_device, B, T, C, NH, NKVH, Da, r, torch.bfloat16, 99)
-    comb, q, k, v = OPS.ltv_proj_scan_cuda_op(x, w, inits, bias, NH, NKVH, Da, r, True)
+    comb, q, k, v, _ = OPS.ltv_proj_scan_cuda_op(x, w, inits, bias, NH, NKVH, Da, r, True)
     # projection: fp32 contraction of the same bf16 values, rounded once
     ref_comb = torch.matmul(w.float(), x.float().transpose(1, 2))
     np.testing.assert_allclose(comb.float().cpu().numpy(), ref_comb.cpu().numpy(), rtol=1e-2, atol=1e-2)
@@ -116,7 +124,7 @@ def test_proj_scan_autograd_equals_two_ops(cuda_device):
         ii = inits.clone().requires_grad_(True)
         bb = bias.clone().requires_grad_(True)
         if fused:
-            _, q, k, v = OPS.ltv_proj_scan_cuda_op(xx, ww, ii, bb, NH, NKVH, Da, r, True)
+            _, q, k, v, _ = OPS.ltv_proj_scan_cuda_op(xx, ww, ii, bb, NH, NKVH, Da, r, True)
         else:
             comb = OPS.fused_linear_transpose_cuda_op(xx, ww)  # fp32 master weight, as the filter passes it
             q, k, v = OPS.ltv_fused_concat_head_major_register_cast_blelloch_scan_cuda_op(
@@ -143,3 +151,53 @@ def test_filter_module_fused_forward(cuda_device):
     _, rq, rk, rv = _two_ops(x, f.c.weight.to(torch.bfloat16), inits, f.logit_bias.detach(), 6, 6, 1, 128, True)
     for a, b in ((q, rq), (k, rk), (v, rv)):
         assert torch.equal(a, b.transpose(1, 2))
+
+
+@pytest.mark.parametrize("B,T,C,NH,NKVH,layout", [
+    (32, 1024, 768, 6, 6, "contiguous"),   # config 2
+    (100, 288, 192, 2, 1, "transposed"),   # upstream grads as [B, T, heads, D] storage
+    (300, 64, 128, 1, 0, "contiguous"),    # Q-only, two chunks per row
+])
+def test_scan_ckpt_backward_equals_backward_kernel(cuda_device, B, T, C, NH, NKVH, layout):
+    """The scan backward from the forward's state checkpoints equals the backward kernel that reads
+    the forward's outputs, bit for bit (grad_combined, grad_inits, grad_logit_bias)."""
+    x, w, inits, bias = _inputs(cuda_device, B, T, C, NH, NKVH, 1, 128, torch.bfloat16, B + T)
+    comb, q, k, v, ckpt = OPS.ltv_proj_scan_cuda_op(x, w, inits, bias, NH, NKVH, 1, 128, True)
+    assert ckpt.numel() > 0
+    gen = torch.Generator(device=cuda_device).manual_seed(B)
+
+    def grad(n):
+        g = torch.randn((B, n, T, 128), generator=gen, device=cuda_device).to(torch.bfloat16)
+        return g.transpose(1, 2).contiguous().transpose(1, 2) if layout == "transposed" else g
+
+    gq, gk, gv = grad(NH), grad(NKVH), grad(NKVH)
+    combined = comb.transpose(1, 2)
+    res = []
+    for use_ckpt in (True, False):
+        gc = torch.full_like(combined, float("nan"))
+        gi = torch.full_like(inits, float("nan"))
+        gb = torch.zeros_like(bias)
+        if use_ckpt:
+            OPS.ltv_scan_ckpt_backward_kernel(combined, inits, bias, ckpt, gq, gk, gv, gc, gi, gb, NH, NKVH, 1, 128,
+                                              True)
+        else:
+            OPS.ltv_fused_concat_head_major_register_cast_blelloch_scan_cuda_backward_kernel(
+                combined, inits, bias, q, k, v, gq, gk, gv, gc, gi, gb, NH, NKVH, 1, 128, 32, 2, 8, True)
+        res.append((gc, gi, gb))
+    torch.cuda.synchronize()
+    for a, b, n in zip(res[0], res[1], ("grad_combined", "grad_inits", "grad_logit_bias")):
+        assert torch.equal(a, b), n
+
+
+def test_scan_ckpt_backward_unsupported_shape(cuda_device):
+    """Shapes the row-streaming kernel does not take raise instead of running something else."""
+    B, T, NH, NKVH = 2, 64, 1, 0   # 2 rows
+    combined = torch.randn(B, T, 129, device=cuda_device).to(torch.bfloat16)
+    inits = torch.zeros(B, 1, 128, device=cuda_device, dtype=torch.bfloat16)
+    bias = torch.zeros(1, 1, device=cuda_device)
+    ckpt = torch.zeros(B, 1, 2, 128, device=cuda_device)
+    g = torch.zeros(B, 1, T, 128, device=cuda_device, dtype=torch.bfloat16)
+    e = torch.zeros(B, 0, T, 128, device=cuda_device, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="not implement|unsupported|Unsupported"):
+        OPS.ltv_scan_ckpt_backward_kernel(combined, inits, bias, ckpt, g, e, e, torch.empty_like(combined),
+                                          torch.empty_like(inits), torch.zeros_like(bias), NH, NKVH, 1, 128, True)

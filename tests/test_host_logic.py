@@ -77,8 +77,14 @@ def test_lookback_and_proj_scan_fake_shapes():
             comb, inits, bias, NH, NKVH, 1, D, 4, 3, 2, *tune, True)
         assert [tuple(t.shape) for t in out] == [(B, NH, T, D), (B, NKVH, T, D), (B, NKVH, T, D)]
     x, w = torch.empty(B, T, 64, device="meta"), torch.empty(3 * (D + 1), 64, device="meta")
-    comb2, q, k, v = OPS.ltv_proj_scan_cuda_op(x, w, inits, bias, NH, NKVH, 1, D, True)
+    comb2, q, k, v, ckpt = OPS.ltv_proj_scan_cuda_op(x, w, inits, bias, NH, NKVH, 1, D, True)
     assert tuple(comb2.shape) == (B, 3 * (D + 1), T) and tuple(q.shape) == (B, NH, T, D)
+    assert tuple(ckpt.shape) == (0,) and ckpt.dtype == torch.float32  # fp32 and D = 32: no checkpoints
+    xb = torch.empty(300, 64, 64, device="meta", dtype=torch.bfloat16)
+    wb = torch.empty(129, 64, device="meta", dtype=torch.bfloat16)
+    ib, bb = torch.empty(300, 1, 128, device="meta", dtype=torch.bfloat16), torch.empty(1, 1, device="meta")
+    ckpt = OPS.ltv_proj_scan_cuda_op(xb, wb, ib, bb, 1, 0, 1, 128, True)[4]
+    assert tuple(ckpt.shape) == (300, 1, 2, 128)  # 300 rows of 64 tokens: states at the 32-token chunk starts
 
 
 def test_lookback_no_cpu_fallback():
