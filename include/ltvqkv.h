@@ -142,10 +142,14 @@ LTVQKV_API int ltvqkv_scan_bwd(int dtype,
  * equal ltvqkv_scan_bwd's bit for bit) and reads 8 KB less per chunk of D = 128. Taken by bf16,
  * D = 128, T % 32 == 0, B * H >= 2 * (SM count) and the production layouts ltvqkv_scan_bwd's
  * row-streaming kernel needs; other requests return LTVQKV_ERR_UNSUPPORTED before anything is
- * launched. No reference function corresponds (the reference always reads the outputs). */
+ * launched. No reference function corresponds (the reference always reads the outputs).
+ * Differences from ltvqkv_scan_bwd: grad_logit_bias is overwritten (not added to); inits_bs is the
+ * element distance between the sequences' initial states, H * D (inits [B, H, D]) or 0 (one state
+ * [H, D] for every sequence, the training case), and with 0 grad_inits is fp32 [H, D]: the
+ * per-sequence gradients, each rounded to dtype, summed in batch order. */
 LTVQKV_API int ltvqkv_scan_bwd_ckpt(int dtype,
                     const void* combined, int64_t sc_b, int64_t sc_t, int64_t sc_e,
-                    const void* inits, const float* logit_bias, const float* ckpt,
+                    const void* inits, int64_t inits_bs, const float* logit_bias, const float* ckpt,
                     const void* grad_hq, const int64_t* gq_strides,
                     const void* grad_hk, const int64_t* gk_strides,
                     const void* grad_hv, const int64_t* gv_strides,
@@ -240,11 +244,14 @@ LTVQKV_API int ltvqkv_proj_scan_fwd(int dtype, const void* x, const void* weight
 
 /* As ltvqkv_proj_scan_fwd, and also writes the scan's fp32 state entering every 32-token chunk
  * but the first: ckpt [B, H, T / 32, D] fp32 (16-byte aligned; entry [b, h, j] is the state after
- * token 32 * j + 31, the last one is not written), for ltvqkv_scan_bwd_ckpt. Only the fused kernel
- * writes checkpoints: where ltvqkv_proj_scan_fwd would run the two entry points in sequence, this
- * returns LTVQKV_ERR_UNSUPPORTED before anything is launched (call ltvqkv_proj_scan_fwd instead). */
+ * token 32 * j + 31, the last one is not written), for ltvqkv_scan_bwd_ckpt. inits_bs: element
+ * distance between the sequences' initial states, H * D, or 0 for one state [H, D] shared by every
+ * sequence. Only the fused kernel writes checkpoints: where ltvqkv_proj_scan_fwd would run the two
+ * entry points in sequence, this returns LTVQKV_ERR_UNSUPPORTED before anything is launched (call
+ * ltvqkv_proj_scan_fwd instead). */
 LTVQKV_API int ltvqkv_proj_scan_fwd_ckpt(int dtype, const void* x, const void* weight, const void* inits,
-                    const float* logit_bias, void* combined, void* out_q, void* out_k, void* out_v, float* ckpt,
+                    int64_t inits_bs, const float* logit_bias, void* combined, void* out_q, void* out_k,
+                    void* out_v, float* ckpt,
                     int B, int T, int C, int NH, int NKVH, int Da, int r, int use_sigmoid,
                     void* workspace, size_t workspace_bytes, void* stream);
 

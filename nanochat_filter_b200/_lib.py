@@ -76,7 +76,7 @@ def _declare(lib: ctypes.CDLL) -> None:
                                     _vp, _i64, _i64, _i64, _vp, _pf,
                                     _i, _i, _i, _i, _i, _i, _i, _vp, _sz, _vp]
     lib.ltvqkv_scan_bwd_ckpt.restype = _i
-    lib.ltvqkv_scan_bwd_ckpt.argtypes = [_i, _vp, _i64, _i64, _i64, _vp, _pf, _pf,
+    lib.ltvqkv_scan_bwd_ckpt.argtypes = [_i, _vp, _i64, _i64, _i64, _vp, _i64, _pf, _pf,
                                          _vp, _pi64, _vp, _pi64, _vp, _pi64,
                                          _vp, _i64, _i64, _i64, _vp, _pf,
                                          _i, _i, _i, _i, _i, _i, _i, _vp, _sz, _vp]
@@ -105,7 +105,7 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.ltvqkv_proj_scan_fwd.argtypes = [_i, _vp, _vp, _vp, _pf, _vp, _vp, _vp, _vp,
                                          _i, _i, _i, _i, _i, _i, _i, _i, _vp, _sz, _vp]
     lib.ltvqkv_proj_scan_fwd_ckpt.restype = _i
-    lib.ltvqkv_proj_scan_fwd_ckpt.argtypes = [_i, _vp, _vp, _vp, _pf, _vp, _vp, _vp, _vp, _pf,
+    lib.ltvqkv_proj_scan_fwd_ckpt.argtypes = [_i, _vp, _vp, _vp, _i64, _pf, _vp, _vp, _vp, _vp, _pf,
                                               _i, _i, _i, _i, _i, _i, _i, _i, _vp, _sz, _vp]
     lib.ltvqkv_gemm_bwd.restype = _i
     lib.ltvqkv_gemm_bwd.argtypes = [_i, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _vp, _i,

@@ -264,35 +264,38 @@ extern "C" int ltvqkv_gemm_fwd(int dtype, const void* x, const void* weight, voi
 }
 
 namespace {
-int proj_scan_fwd_impl(int dtype, const void* x, const void* weight, const void* inits, const float* logit_bias,
-                       void* combined, void* out_q, void* out_k, void* out_v, float* ckpt, int B, int T, int C, int NH,
-                       int NKVH, int Da, int r, int use_sigmoid, void* workspace, size_t workspace_bytes,
-                       void* stream);
+int proj_scan_fwd_impl(int dtype, const void* x, const void* weight, const void* inits, int64_t inits_bs,
+                       const float* logit_bias, void* combined, void* out_q, void* out_k, void* out_v, float* ckpt,
+                       int B, int T, int C, int NH, int NKVH, int Da, int r, int use_sigmoid, void* workspace,
+                       size_t workspace_bytes, void* stream);
 }  // namespace
 
 extern "C" int ltvqkv_proj_scan_fwd(int dtype, const void* x, const void* weight, const void* inits,
                                     const float* logit_bias, void* combined, void* out_q, void* out_k, void* out_v,
                                     int B, int T, int C, int NH, int NKVH, int Da, int r, int use_sigmoid,
                                     void* workspace, size_t workspace_bytes, void* stream) {
-  return proj_scan_fwd_impl(dtype, x, weight, inits, logit_bias, combined, out_q, out_k, out_v, nullptr, B, T, C, NH,
-                            NKVH, Da, r, use_sigmoid, workspace, workspace_bytes, stream);
+  return proj_scan_fwd_impl(dtype, x, weight, inits, -1, logit_bias, combined, out_q, out_k, out_v, nullptr, B, T, C,
+                            NH, NKVH, Da, r, use_sigmoid, workspace, workspace_bytes, stream);
 }
 
 extern "C" int ltvqkv_proj_scan_fwd_ckpt(int dtype, const void* x, const void* weight, const void* inits,
-                                         const float* logit_bias, void* combined, void* out_q, void* out_k,
-                                         void* out_v, float* ckpt, int B, int T, int C, int NH, int NKVH, int Da,
-                                         int r, int use_sigmoid, void* workspace, size_t workspace_bytes,
-                                         void* stream) {
+                                         int64_t inits_bs, const float* logit_bias, void* combined, void* out_q,
+                                         void* out_k, void* out_v, float* ckpt, int B, int T, int C, int NH,
+                                         int NKVH, int Da, int r, int use_sigmoid, void* workspace,
+                                         size_t workspace_bytes, void* stream) {
   if (!ckpt || (reinterpret_cast<uintptr_t>(ckpt) & 15u) != 0) return LTVQKV_ERR_INVALID_ARG;
-  return proj_scan_fwd_impl(dtype, x, weight, inits, logit_bias, combined, out_q, out_k, out_v, ckpt, B, T, C, NH,
-                            NKVH, Da, r, use_sigmoid, workspace, workspace_bytes, stream);
+  if (inits_bs != 0 && inits_bs != (int64_t)(NH + 2 * NKVH) * Da * r) return LTVQKV_ERR_STRIDE;
+  return proj_scan_fwd_impl(dtype, x, weight, inits, inits_bs, logit_bias, combined, out_q, out_k, out_v, ckpt, B, T,
+                            C, NH, NKVH, Da, r, use_sigmoid, workspace, workspace_bytes, stream);
 }
 
 namespace {
-int proj_scan_fwd_impl(int dtype, const void* x, const void* weight, const void* inits, const float* logit_bias,
-                       void* combined, void* out_q, void* out_k, void* out_v, float* ckpt, int B, int T, int C, int NH,
-                       int NKVH, int Da, int r, int use_sigmoid, void* workspace, size_t workspace_bytes,
-                       void* stream) {
+// inits_bs: elements between the sequences' initial states (0: one state for every sequence, fused
+// kernel only; < 0: contiguous [B][H][D]).
+int proj_scan_fwd_impl(int dtype, const void* x, const void* weight, const void* inits, int64_t inits_bs,
+                       const float* logit_bias, void* combined, void* out_q, void* out_k, void* out_v, float* ckpt,
+                       int B, int T, int C, int NH, int NKVH, int Da, int r, int use_sigmoid, void* workspace,
+                       size_t workspace_bytes, void* stream) {
   if (!ltvqkv_host::valid_dtype(dtype)) return LTVQKV_ERR_DTYPE;
   if (B < 0 || T < 0 || C < 0 || NH < 0 || NKVH < 0 || Da < 1 || r < 1) return LTVQKV_ERR_SHAPE;
   const int H = NH + 2 * NKVH, D = Da * r, F = H * (D + Da);
@@ -305,7 +308,9 @@ int proj_scan_fwd_impl(int dtype, const void* x, const void* weight, const void*
                      combined && aligned16(x) && aligned16(weight) && aligned16(combined) &&
                      (NH == 0 || (out_q && aligned16(out_q))) &&
                      (NKVH == 0 || (out_k && out_v && aligned16(out_k) && aligned16(out_v)));
-  if (!fused && ckpt != nullptr) return LTVQKV_ERR_UNSUPPORTED;  // checkpoints come from the fused kernel only
+  // checkpoints and a shared initial state come from the fused kernel only
+  if (!fused && (ckpt != nullptr || inits_bs == 0)) return LTVQKV_ERR_UNSUPPORTED;
+  if (inits_bs < 0) inits_bs = (int64_t)H * D;
   if (!fused) {
     // the two operators in sequence: projection into `combined`, then the scan reading it
     int rc = ltvqkv_gemm_fwd(dtype, x, weight, combined, B, T, C, F, workspace, workspace_bytes, stream);
@@ -349,6 +354,7 @@ int proj_scan_fwd_impl(int dtype, const void* x, const void* weight, const void*
   pp.out[1] = reinterpret_cast<__nv_bfloat16*>(out_k);
   pp.out[2] = reinterpret_cast<__nv_bfloat16*>(out_v);
   pp.ckpt = ckpt;
+  pp.inits_bs = inits_bs;
   pp.ws = ws;
   CUtensorMap tmW, tmXh;
   if (!make_map(&tmW, false, weight, C, F, 1, (uint64_t)C * 2, (uint64_t)C * F * 2, 64, 128) ||

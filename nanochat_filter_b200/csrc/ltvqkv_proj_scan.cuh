@@ -54,7 +54,8 @@ struct PsParams {
   int npairs;                // B * ceil(H / 2)
   int use_sigmoid;
   __nv_bfloat16* combined;        // [B][F][T]: logit rows written by the pre-pass, value rows here
-  const __nv_bfloat16* inits;     // [B][H][128]
+  const __nv_bfloat16* inits;     // [B][H][128], sequences inits_bs elements apart (0: shared)
+  long long inits_bs;
   const float* logit_bias;        // [H]
   __nv_bfloat16* out[3];          // [B][heads][T][128]
   float* ckpt;                    // optional [B][H][T / 32][128]: the fp32 state after every 32nd token
@@ -269,7 +270,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPsThreads, 1)
       const long long vrow0 = (long long)b * prm.F + hh * (kPsD + 1) + q * 32;  // the warp's first value row
       const __nv_bfloat16* lrow = prm.combined + ((long long)b * prm.F + hh * (kPsD + 1) + kPsD) * prm.T;
       const float lb = prm.logit_bias[hh];
-      float E = __bfloat162float(prm.inits[((long long)b * prm.H + hh) * kPsD + c]);
+      float E = __bfloat162float(prm.inits[(long long)b * prm.inits_bs + (long long)hh * kPsD + c]);
       uint4 lg = live ? ps_load_logits(lrow, lane * 8, prm.T) : make_uint4(0, 0, 0, 0);
       bool ok = true;
       for (int nt = 0; nt < prm.n_tiles; ++nt) {

@@ -66,7 +66,7 @@ constexpr int kFwdBudget = 8192;
 constexpr int kBwdBudget = 4096;
 
 struct ScanWorkspaceLayout {
-  size_t flags, aggA, aggX, inclX, bias_part, total;
+  size_t flags, aggA, aggX, inclX, bias_part, init_part, init_cnt, total;
 };
 
 inline ScanWorkspaceLayout scan_ws_layout(const ScanGeometry& g) {
@@ -79,6 +79,8 @@ inline ScanWorkspaceLayout scan_ws_layout(const ScanGeometry& g) {
   L.aggX = off;  off = align_up(off + tiles * g.D * 4, 256);
   L.inclX = off; off = align_up(off + tiles * g.D * 4, 256);
   L.bias_part = off; off = align_up(off + (size_t)g.B * g.nchunks * g.H * g.Da * 4, 256);
+  L.init_part = off; off = align_up(off + (size_t)g.B * g.H * g.D * 4, 256);  // shared initial state
+  L.init_cnt = off;  off = align_up(off + (size_t)g.H * 4, 256);
   L.total = off;
   return L;
 }
@@ -758,7 +760,8 @@ int try_row_bwd(bool& used, int dtype, const void* combined, int64_t sc_b, int64
                 const int64_t* gq_strides, const void* grad_hk, const int64_t* gk_strides, const void* grad_hv,
                 const int64_t* gv_strides, void* grad_combined, int64_t gc_b, int64_t gc_t, int64_t gc_e,
                 void* grad_inits, float* grad_logit_bias, int B, int T, int NH, int NKVH, int Da, int r,
-                int use_sigmoid, char* ws, size_t workspace_bytes, cudaStream_t s, const float* ckpt = nullptr) {
+                int use_sigmoid, char* ws, size_t workspace_bytes, cudaStream_t s, const float* ckpt = nullptr,
+                bool shared_init = false, float* grad_init_sum = nullptr, bool bias_overwrite = false) {
   used = false;
   auto rows_ok = [&](const void* p, const int64_t* st) {
     return p == nullptr || (aligned16p(p) && st[3] == 1 && st[0] % 8 == 0 && st[1] % 8 == 0 && st[2] % 8 == 0);
@@ -809,6 +812,13 @@ int try_row_bwd(bool& used, int dtype, const void* combined, int64_t sc_b, int64
   f.bias_part = reinterpret_cast<float*>(ws + wx.bias_part);
   f.grad_bias = grad_logit_bias;
   f.ckpt = ckpt;
+  f.inits_bs = shared_init ? 0 : (long long)H * D;
+  f.init_part = shared_init ? reinterpret_cast<float*>(ws + wx.init_part) : nullptr;
+  f.init_cnt = reinterpret_cast<unsigned int*>(ws + wx.init_cnt);
+  f.grad_init_sum = grad_init_sum;
+  f.bias_overwrite = bias_overwrite ? 1 : 0;
+  if (shared_init && cudaMemsetAsync(f.init_cnt, 0, (size_t)H * 4, s) != cudaSuccess)
+    return ltvqkv_host::check_launch();
   f.B = B; f.T = T; f.NH = NH; f.NKVH = NKVH; f.Da = Da; f.r = r; f.D = D; f.H = H; f.F = Fh;
   f.nchunks = (T + rtt - 1) / rtt; f.nrows = B * H; f.use_sigmoid = use_sigmoid; f.stages = rst;
   f.ws = reinterpret_cast<WorkspaceHeader*>(ws);
@@ -1050,10 +1060,11 @@ extern "C" int ltvqkv_scan_bwd(int dtype, const void* combined, int64_t sc_b, in
 
 // Scan backward from the forward's state checkpoints (ltvqkv_proj_scan_fwd_ckpt) instead of its
 // outputs: the row-streaming kernel replays each 32-token chunk's outputs from the stored fp32 state.
-// Results equal ltvqkv_scan_bwd's bit for bit; shapes or layouts that kernel does not take return
-// LTVQKV_ERR_UNSUPPORTED before anything is launched.
+// Results equal ltvqkv_scan_bwd's bit for bit (grad_logit_bias overwritten, not added to; with a
+// shared initial state the per-sequence initial-state gradients summed in batch order); shapes or
+// layouts that kernel does not take return LTVQKV_ERR_UNSUPPORTED before anything is launched.
 extern "C" int ltvqkv_scan_bwd_ckpt(int dtype, const void* combined, int64_t sc_b, int64_t sc_t, int64_t sc_e,
-                                    const void* inits, const float* logit_bias, const float* ckpt,
+                                    const void* inits, int64_t inits_bs, const float* logit_bias, const float* ckpt,
                                     const void* grad_hq, const int64_t* gq_strides, const void* grad_hk,
                                     const int64_t* gk_strides, const void* grad_hv, const int64_t* gv_strides,
                                     void* grad_combined, int64_t gc_b, int64_t gc_t, int64_t gc_e, void* grad_inits,
@@ -1068,13 +1079,17 @@ extern "C" int ltvqkv_scan_bwd_ckpt(int dtype, const void* combined, int64_t sc_
     return LTVQKV_ERR_INVALID_ARG;
   if (B == 0 || T == 0) return LTVQKV_ERR_UNSUPPORTED;
   if (!workspace) return LTVQKV_ERR_WORKSPACE;
+  const int64_t HD = (int64_t)(NH + 2 * NKVH) * Da * r;
+  if (inits_bs != 0 && inits_bs != HD) return LTVQKV_ERR_STRIDE;
+  const bool shared = inits_bs == 0;
   static const int64_t kNone[4] = {0, 0, 0, 1};
   bool used = false;
   const int rc = try_row_bwd(used, dtype, combined, sc_b, sc_t, sc_e, inits, logit_bias, nullptr, kNone, nullptr,
                              kNone, nullptr, kNone, grad_hq, gq_strides, grad_hk, gk_strides, grad_hv, gv_strides,
-                             grad_combined, gc_b, gc_t, gc_e, grad_inits, grad_logit_bias, B, T, NH, NKVH, Da, r,
-                             use_sigmoid, reinterpret_cast<char*>(workspace), workspace_bytes,
-                             reinterpret_cast<cudaStream_t>(stream), ckpt);
+                             grad_combined, gc_b, gc_t, gc_e, shared ? nullptr : grad_inits, grad_logit_bias, B, T,
+                             NH, NKVH, Da, r, use_sigmoid, reinterpret_cast<char*>(workspace), workspace_bytes,
+                             reinterpret_cast<cudaStream_t>(stream), ckpt, shared,
+                             shared ? reinterpret_cast<float*>(grad_inits) : nullptr, true);
   return used ? rc : LTVQKV_ERR_UNSUPPORTED;
 }
 

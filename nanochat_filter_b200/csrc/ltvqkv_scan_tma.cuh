@@ -46,6 +46,13 @@ struct TmaBwdArgs {
   float* bias_part;  // [B][H][Da]: one partial per row
   float* grad_bias;  // backward: [H][Da], the partials' sums are added here by the last CTA
   const float* ckpt; // backward from checkpoints: [B][H][nchunks][D], the fp32 state entering chunk j + 1
+  long long inits_bs;    // elements between sequences' initial states (0: one state shared by the batch)
+  // shared initial state: per-row gradients (each rounded to bf16) go to init_part [B][H][D], and
+  // the row that completes a head's batch sums them in batch order into grad_init_sum [H][D] (fp32)
+  float* init_part;
+  unsigned int* init_cnt;  // [H] rows of each head done (zero at launch)
+  float* grad_init_sum;
+  int bias_overwrite;      // grad_bias = sum (1) or grad_bias += sum (0)
   int B, T, NH, NKVH, Da, r, D, H, F, nchunks, nrows, use_sigmoid;
   int stages;  // shared-memory ring depth (2..kRowMaxStages)
   WorkspaceHeader* ws;
@@ -295,6 +302,7 @@ __global__ void __launch_bounds__(kD / 2 + (kCkpt ? 64 : 32), row_bwd_min_blocks
   uint64_t* empty = full + S;
   uint64_t* hfull = empty + S;  // kCkpt: the stage's replayed outputs are in place (32 replay lanes)
   __shared__ volatile int abort_flag;
+  __shared__ int init_last;  // this row completed its head's batch (shared initial state)
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
@@ -352,7 +360,7 @@ __global__ void __launch_bounds__(kD / 2 + (kCkpt ? 64 : 32), row_bwd_min_blocks
             tma_load_4d(sb + hoff, mh, &full[st], 0, t0 - 1, hloc, b);
           else if (j > 0)
             bulk_load(sb + hoff, a.ckpt + (((long long)b * a.H + h) * a.nchunks + (j - 1)) * D, D * 4, &full[st]);
-          if (q == 0) bulk_load(sb + ioff, a.inits + ((long long)b * a.H + h) * D, D * 2, &full[st]);
+          if (q == 0) bulk_load(sb + ioff, a.inits + (long long)b * a.inits_bs + (long long)h * D, D * 2, &full[st]);
         }
       }
     }
@@ -534,7 +542,11 @@ __global__ void __launch_bounds__(kD / 2 + (kCkpt ? 64 : 32), row_bwd_min_blocks
       if (ti.t0 == 0) {
         const __nv_bfloat162 gi2 =
             __floats2bfloat162_rn(carry0 * (1.0f - grow[0].y), carry1 * (1.0f - grow[0].y));
-        reinterpret_cast<__nv_bfloat162*>(a.grad_inits + rowbase * D)[tid] = gi2;
+        if (a.init_part == nullptr)
+          reinterpret_cast<__nv_bfloat162*>(a.grad_inits + rowbase * D)[tid] = gi2;
+        else
+          reinterpret_cast<float2*>(a.init_part + rowbase * D)[tid] =
+              make_float2(__low2float(gi2), __high2float(gi2));
       }
       fence_proxy_async_smem();
       named_barrier(1, ncons);  // the du tile and the segment sums are complete
@@ -574,7 +586,26 @@ __global__ void __launch_bounds__(kD / 2 + (kCkpt ? 64 : 32), row_bwd_min_blocks
           for (int j = 0; j < kTT; ++j) t += bsum[tid * kTT + j];
           a.bias_part[rowbase * Da + tid] = t;
         }
-        named_barrier(1, ncons);  // bsum is free again
+        if (a.init_part != nullptr) {
+          // shared initial state: the row that completes its head's batch sums the head's per-row
+          // gradients in batch order (each thread its two channels)
+          __threadfence();
+          named_barrier(1, ncons);
+          if (tid == 0) init_last = atomicAdd(&a.init_cnt[ti.h], 1u) == (unsigned int)(a.B - 1) ? 1 : 0;
+          named_barrier(1, ncons);
+          if (init_last) {
+            __threadfence();
+            float s0 = 0.f, s1 = 0.f;
+#pragma unroll 8
+            for (int bb = 0; bb < a.B; ++bb) {
+              const float2 v = __ldcg(reinterpret_cast<const float2*>(a.init_part + ((long long)bb * a.H + ti.h) * D) + tid);
+              s0 += v.x;
+              s1 += v.y;
+            }
+            reinterpret_cast<float2*>(a.grad_init_sum + (long long)ti.h * D)[tid] = make_float2(s0, s1);
+          }
+        }
+        named_barrier(1, ncons);  // bsum (and init_last) are free again
       }
     }
     if (tid == 0) tma_store_wait0();
@@ -589,7 +620,8 @@ __global__ void __launch_bounds__(kD / 2 + (kCkpt ? 64 : 32), row_bwd_min_blocks
     for (int idx = tid; idx < n; idx += blockDim.x) {
       float sum = 0.f;
       for (int b = 0; b < a.B; ++b) sum += __ldcg(a.bias_part + (long long)b * n + idx);
-      a.grad_bias[idx] += sum;
+      if (a.bias_overwrite) a.grad_bias[idx] = sum;
+      else a.grad_bias[idx] += sum;
     }
   }
 }

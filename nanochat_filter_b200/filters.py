@@ -127,7 +127,12 @@ class LtvCudaFusedConcatHeadMajorRegisterCastBlellochScanQkvFilter(LtvCombinedHe
         if not run_ltv_in_fp32:
             # projection + scan in one call (tensor-core accumulator straight into the recurrence);
             # outputs and gradients equal the two-op composition below bit for bit
-            inits = resolve_inits_original_dtype(B, self.init_param, previous_values).to(dtype=x.dtype).contiguous()
+            if previous_values.q is None:
+                # training: one initial state [H, D] for every sequence (its gradient is summed over
+                # the batch inside the scan backward instead of by an expand's backward)
+                inits = self.init_param
+            else:
+                inits = resolve_inits_original_dtype(B, self.init_param, previous_values).to(dtype=x.dtype).contiguous()
             _, hq, hk, hv = _ops.ltv_proj_scan(x.contiguous(), self.c.weight, inits, self.logit_bias.contiguous(),
                                                self.n_head, self.n_kv_head, self.num_alpha_groups, self.r, True)
             return hq.transpose(1, 2), hk.transpose(1, 2), hv.transpose(1, 2)

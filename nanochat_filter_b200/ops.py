@@ -495,7 +495,8 @@ def _proj_scan_forward_kernel(x, weight, inits, logit_bias, combined, out_q, out
     (the reference filter's composition,
     nanochat/ltv_cuda_fused_concat_head_major_register_cast_blelloch_scan_qkv_filter.py:24-73).
     With `ckpt` ([B, H, T / 32, D] fp32) the scan states at the 32-token chunk starts are written
-    too; returns False (and writes nothing) where the one-kernel form that writes them does not apply.
+    too, and `inits` may be one state [H, D] for every sequence instead of [B, H, D]; returns False
+    (and writes nothing) where the one-kernel form that does both does not apply.
     """
     if not x.is_contiguous() or x.dim() != 3:
         raise RuntimeError("ltv_proj_scan requires a contiguous [B, T, C] x")
@@ -509,7 +510,11 @@ def _proj_scan_forward_kernel(x, weight, inits, logit_bias, combined, out_q, out
         raise RuntimeError(f"weight must be [{F}, {C}], got {tuple(w.shape)}")
     if tuple(combined.shape) != (B, F, T) or not combined.is_contiguous() or combined.dtype != x.dtype:
         raise RuntimeError("combined must be a contiguous [B, F, T] tensor of x's dtype")
-    _check_scan_inputs(combined.transpose(1, 2), inits, logit_bias, NH, NKVH, da, r)
+    shared = inits.dim() == 2
+    if shared and ckpt is None:
+        raise RuntimeError("a shared [H, D] initial state is taken with the checkpoint output only")
+    _check_scan_inputs(combined.transpose(1, 2), inits.unsqueeze(0).expand(B, -1, -1) if shared else inits,
+                       logit_bias, NH, NKVH, da, r)
     inits = inits.contiguous()
     logit_bias = logit_bias.contiguous()
     for o, n in ((out_q, NH), (out_k, NKVH), (out_v, NKVH)):
@@ -517,18 +522,18 @@ def _proj_scan_forward_kernel(x, weight, inits, logit_bias, combined, out_q, out
             raise RuntimeError("out_q/out_k/out_v must be contiguous [B, heads, T, D] of x's dtype")
     nbytes = max(L.ltvqkv_scan_workspace_bytes(B, T, NH, NKVH, da, r), L.ltvqkv_gemm_workspace_bytes())
     ws = _lib.workspace(x.device, nbytes)
-    args = (_lib.dtype_code(x.dtype), x.data_ptr(), w.data_ptr(), inits.data_ptr(), logit_bias.data_ptr(),
-            combined.data_ptr(), out_q.data_ptr(), out_k.data_ptr(), out_v.data_ptr())
+    head = (_lib.dtype_code(x.dtype), x.data_ptr(), w.data_ptr(), inits.data_ptr())
+    outs = (logit_bias.data_ptr(), combined.data_ptr(), out_q.data_ptr(), out_k.data_ptr(), out_v.data_ptr())
     rest = (B, T, C, NH, NKVH, da, r, int(bool(use_sigmoid)), ws.data_ptr(), ws.numel(), _lib.stream_handle(x.device))
     if ckpt is not None:
         if tuple(ckpt.shape) != (B, H, T // 32, D) or ckpt.dtype != torch.float32 or not ckpt.is_contiguous():
             raise RuntimeError("ckpt must be a contiguous [B, H, T / 32, D] float32 tensor")
-        rc = L.ltvqkv_proj_scan_fwd_ckpt(*args, ckpt.data_ptr(), *rest)
+        rc = L.ltvqkv_proj_scan_fwd_ckpt(*head, 0 if shared else H * D, *outs, ckpt.data_ptr(), *rest)
         if rc == _lib.ERR_UNSUPPORTED:
             return False
         _lib.check(rc, "ltvqkv_proj_scan_fwd_ckpt")
         return True
-    rc = L.ltvqkv_proj_scan_fwd(*args, *rest)
+    rc = L.ltvqkv_proj_scan_fwd(*head, *outs, *rest)
     _lib.check(rc, "ltvqkv_proj_scan_fwd")
     return False
 
@@ -556,13 +561,17 @@ def _proj_scan_op(x, weight, inits, logit_bias, NH, NKVH, da, r, use_sigmoid):
     out_q = torch.empty((B, NH, T, D), **kw)
     out_k = torch.empty((B, NKVH, T, D), **kw)
     out_v = torch.empty((B, NKVH, T, D), **kw)
-    shape = _ckpt_shape(x, NH, NKVH, da, r)
-    ckpt = torch.empty(shape, device=x.device, dtype=torch.float32)
-    written = _proj_scan_forward_kernel(x, weight, inits, logit_bias, combined, out_q, out_k, out_v, NH, NKVH, da,
-                                        r, use_sigmoid, ckpt if ckpt.numel() else None)
-    if ckpt.numel() and not written:
-        raise RuntimeError("ltvqkv_proj_scan_fwd_ckpt did not take a shape the checkpoint rule admits")
-    return combined, out_q, out_k, out_v, ckpt
+    shared = inits.dim() == 2
+    inits_k = inits.to(x.dtype) if shared else inits  # the state starts from its value in x's dtype
+    ckpt = torch.empty(_ckpt_shape(x, NH, NKVH, da, r), device=x.device, dtype=torch.float32)
+    if ckpt.numel() and _proj_scan_forward_kernel(x, weight, inits_k, logit_bias, combined, out_q, out_k, out_v, NH,
+                                                  NKVH, da, r, use_sigmoid, ckpt):
+        return combined, out_q, out_k, out_v, ckpt
+    if shared:
+        inits_k = inits_k.unsqueeze(0).expand(B, -1, -1).contiguous()
+    _proj_scan_forward_kernel(x, weight, inits_k, logit_bias, combined, out_q, out_k, out_v, NH, NKVH, da, r,
+                              use_sigmoid)
+    return combined, out_q, out_k, out_v, ckpt.new_empty((0,))
 
 
 def _rows_ok(t):
@@ -575,13 +584,19 @@ def _rows_ok(t):
 def _scan_ckpt_backward(combined, inits, logit_bias, ckpt, grad_hq, grad_hk, grad_hv, grad_combined, grad_inits,
                         grad_logit_bias, NH, NKVH, da, r, use_sigmoid):
     """ltvqkv_scan_bwd_ckpt; returns its status (ERR_UNSUPPORTED: nothing was launched)."""
-    _check_scan_inputs(combined, inits, logit_bias, NH, NKVH, da, r)
     L = _lib.load()
     B, T, _ = combined.shape
+    H, D = NH + 2 * NKVH, da * r
+    shared = inits.dim() == 2
+    _check_scan_inputs(combined, inits.unsqueeze(0).expand(B, -1, -1) if shared else inits, logit_bias, NH, NKVH,
+                       da, r)
     inits = inits.contiguous()
     logit_bias = logit_bias.contiguous()
     if not grad_inits.is_contiguous() or not grad_logit_bias.is_contiguous():
         raise RuntimeError("grad_inits and grad_logit_bias must be contiguous")
+    if shared and (tuple(grad_inits.shape) != (H, D) or grad_inits.dtype != torch.float32):
+        raise RuntimeError("with one initial state [H, D] for every sequence, grad_inits is its float32 [H, D] "
+                           "gradient (summed over the batch)")
     if grad_combined.shape != combined.shape or grad_combined.dtype != combined.dtype:
         raise RuntimeError("grad_combined must match combined's shape and dtype")
     if ckpt.dtype != torch.float32 or not ckpt.is_contiguous():
@@ -595,7 +610,7 @@ def _scan_ckpt_backward(combined, inits, logit_bias, ckpt, grad_hq, grad_hk, gra
     S = _lib.strides
     return L.ltvqkv_scan_bwd_ckpt(
         _lib.dtype_code(combined.dtype), combined.data_ptr(), sc[0], sc[1], sc[2], inits.data_ptr(),
-        logit_bias.data_ptr(), ckpt.data_ptr(),
+        0 if shared else H * D, logit_bias.data_ptr(), ckpt.data_ptr(),
         grad_hq.data_ptr(), S(grad_hq.stride()), grad_hk.data_ptr(), S(grad_hk.stride()),
         grad_hv.data_ptr(), S(grad_hv.stride()),
         grad_combined.data_ptr(), gc[0], gc[1], gc[2], grad_inits.data_ptr(), grad_logit_bias.data_ptr(),
@@ -606,7 +621,10 @@ def _scan_ckpt_backward(combined, inits, logit_bias, ckpt, grad_hq, grad_hk, gra
 def _scan_ckpt_backward_kernel(combined, inits, logit_bias, ckpt, grad_hq, grad_hk, grad_hv, grad_combined,
                                grad_inits, grad_logit_bias, NH, NKVH, da, r, use_sigmoid):
     """The scan backward kernel from the forward's state checkpoints (ltv_proj_scan_cuda_op's fifth
-    output) instead of its outputs; results equal the backward kernel's bit for bit."""
+    output) instead of its outputs; results equal the backward kernel's bit for bit, except that
+    grad_logit_bias is overwritten (not added to), and that with one initial state [H, D] for every
+    sequence grad_inits is its float32 [H, D] gradient (each sequence's term rounded to combined's
+    dtype, summed in batch order)."""
     rc = _scan_ckpt_backward(combined, inits, logit_bias, ckpt, grad_hq, grad_hk, grad_hv, grad_combined, grad_inits,
                              grad_logit_bias, NH, NKVH, da, r, use_sigmoid)
     _lib.check(rc, "ltvqkv_scan_bwd_ckpt")
@@ -629,24 +647,36 @@ def _ps_backward(ctx, grad_comb, grad_hq, grad_hk, grad_hv, _grad_ckpt):
     # forward wrote state checkpoints the scan backward replays its outputs from them (equal results,
     # less memory traffic) instead of reading them.
     x, weight, comb, inits, logit_bias, hq, hk, hv, ckpt = ctx.saved_tensors
+    NH, NKVH, da, r = ctx.args
+    B = x.shape[0]
+    shared = inits.dim() == 2
+    inits_k = inits.to(x.dtype) if shared else inits
     combined = comb.transpose(1, 2)
     grad_hq = torch.zeros_like(hq) if grad_hq is None else grad_hq
     grad_hk = torch.zeros_like(hk) if grad_hk is None else grad_hk
     grad_hv = torch.zeros_like(hv) if grad_hv is None else grad_hv
     grad_combined = torch.empty_like(combined)
-    grad_inits = torch.empty_like(inits, memory_format=torch.contiguous_format)
-    grad_logit_bias = torch.zeros_like(logit_bias, memory_format=torch.contiguous_format)
     rc = _lib.ERR_UNSUPPORTED
     if ckpt.numel():
         gq, gk, gv = (g if _rows_ok(g) else g.contiguous() for g in (grad_hq, grad_hk, grad_hv))
-        rc = _scan_ckpt_backward(combined, inits, logit_bias, ckpt, gq, gk, gv, grad_combined, grad_inits,
-                                 grad_logit_bias, *ctx.args, ctx.use_sigmoid)
+        grad_inits = (torch.empty(inits_k.shape, device=x.device, dtype=torch.float32) if shared
+                      else torch.empty_like(inits_k, memory_format=torch.contiguous_format))
+        grad_logit_bias = torch.empty_like(logit_bias, memory_format=torch.contiguous_format)
+        rc = _scan_ckpt_backward(combined, inits_k, logit_bias, ckpt, gq, gk, gv, grad_combined, grad_inits,
+                                 grad_logit_bias, NH, NKVH, da, r, ctx.use_sigmoid)
     if rc == _lib.ERR_UNSUPPORTED:
+        ib = inits_k.unsqueeze(0).expand(B, -1, -1).contiguous() if shared else inits_k
+        grad_inits = torch.empty_like(ib, memory_format=torch.contiguous_format)
+        grad_logit_bias = torch.zeros_like(logit_bias, memory_format=torch.contiguous_format)
         torch.ops.nanochat_cuda.ltv_fused_concat_head_major_register_cast_blelloch_scan_cuda_backward_kernel(
-            combined, inits, logit_bias, hq, hk, hv, grad_hq, grad_hk, grad_hv, grad_combined, grad_inits,
-            grad_logit_bias, *ctx.args, 32, 2, 8, ctx.use_sigmoid)
+            combined, ib, logit_bias, hq, hk, hv, grad_hq, grad_hk, grad_hv, grad_combined, grad_inits,
+            grad_logit_bias, NH, NKVH, da, r, 32, 2, 8, ctx.use_sigmoid)
+        if shared:
+            grad_inits = grad_inits.float().sum(0)
     else:
         _lib.check(rc, "ltvqkv_scan_bwd_ckpt")
+    if shared:
+        grad_inits = grad_inits.to(inits.dtype)
     grad_out = grad_combined.transpose(1, 2)
     if grad_comb is not None:
         grad_out = grad_out + grad_comb
@@ -895,7 +925,9 @@ def ltv_decode_step(x: torch.Tensor, weight: torch.Tensor, logit_bias: torch.Ten
 
 def ltv_proj_scan(x: torch.Tensor, weight: torch.Tensor, inits: torch.Tensor, logit_bias: torch.Tensor, NH: int,
                   NKVH: int, da: int, r: int, use_sigmoid: bool = True):
-    """Projection and scan forward in one call; returns (combined [B, F, T], q, k, v [B, heads, T, D])."""
+    """Projection and scan forward in one call; returns (combined [B, F, T], q, k, v [B, heads, T, D]).
+    `inits`: the initial state of every sequence [B, H, D] (x's dtype), or one state [H, D] shared by
+    the batch (any float dtype; its gradient is summed over the batch in the kernel)."""
     return torch.ops.nanochat_cuda.ltv_proj_scan_cuda_op(x, weight, inits, logit_bias, NH, NKVH, da, r,
                                                          use_sigmoid)[:4]
 

@@ -201,3 +201,66 @@ def test_scan_ckpt_backward_unsupported_shape(cuda_device):
     with pytest.raises(RuntimeError, match="not implement|unsupported|Unsupported"):
         OPS.ltv_scan_ckpt_backward_kernel(combined, inits, bias, ckpt, g, e, e, torch.empty_like(combined),
                                           torch.empty_like(inits), torch.zeros_like(bias), NH, NKVH, 1, 128, True)
+
+
+@pytest.mark.parametrize("B,T,C,NH,NKVH", [(32, 1024, 768, 6, 6), (300, 64, 128, 1, 0)])
+def test_shared_initial_state(cuda_device, B, T, C, NH, NKVH):
+    """One initial state [H, D] for every sequence (the training case): outputs equal those of the
+    same state expanded over the batch bit for bit; the checkpoint backward's grad_combined and
+    grad_logit_bias equal the per-sequence form's bit for bit, and its [H, D] float32 initial-state
+    gradient is the per-sequence bf16 gradients summed over the batch (fp32; summation order only)."""
+    H = NH + 2 * NKVH
+    x, w, _, bias = _inputs(cuda_device, B, T, C, NH, NKVH, 1, 128, torch.bfloat16, B * 7 + T)
+    gen = torch.Generator(device=cuda_device).manual_seed(11)
+    init = ((torch.rand((H, 128), generator=gen, device=cuda_device) * 2 - 1) * 0.5).to(torch.bfloat16)
+    expanded = init.unsqueeze(0).expand(B, -1, -1).contiguous()
+    shared = OPS.ltv_proj_scan_cuda_op(x, w, init, bias, NH, NKVH, 1, 128, True)
+    per_seq = OPS.ltv_proj_scan_cuda_op(x, w, expanded, bias, NH, NKVH, 1, 128, True)
+    assert shared[4].numel() > 0
+    for a, b, n in zip(shared, per_seq, ("combined", "q", "k", "v")):
+        assert torch.equal(a, b), n
+    assert torch.equal(shared[4][:, :, :-1], per_seq[4][:, :, :-1])  # the last entry is not written
+    comb, q, k, v, ckpt = shared
+    combined = comb.transpose(1, 2)
+    grads = [torch.randn((B, n, T, 128), generator=gen, device=cuda_device).to(torch.bfloat16)
+             for n in (NH, NKVH, NKVH)]
+    gc1, gi1 = torch.empty_like(combined), torch.full((H, 128), float("nan"), device=cuda_device)
+    gb1 = torch.full_like(bias, float("nan"))  # overwritten, not added to
+    OPS.ltv_scan_ckpt_backward_kernel(combined, init, bias, ckpt, *grads, gc1, gi1, gb1, NH, NKVH, 1, 128, True)
+    gc2, gi2, gb2 = torch.empty_like(combined), torch.empty_like(expanded), torch.zeros_like(bias)
+    OPS.ltv_scan_ckpt_backward_kernel(combined, expanded, bias, ckpt, *grads, gc2, gi2, gb2, NH, NKVH, 1, 128, True)
+    torch.cuda.synchronize()
+    assert torch.equal(gc1, gc2) and torch.equal(gb1, gb2)
+    want = gi2.float().sum(0)
+    torch.testing.assert_close(gi1, want, rtol=1e-5, atol=1e-5 * want.abs().max().item())
+
+
+def test_shared_initial_state_autograd(cuda_device):
+    """ltv_proj_scan_cuda_op with the fp32 [H, D] parameter as the initial state: gradients equal the
+    expanded-state composition's bit for bit, except the [H, D] one, which the composition's expand
+    backward sums as a bf16 tensor (one bf16 rounding of the batch sum, <= 2^-9 relative) while the
+    shared form keeps the fp32 sum."""
+    B, T, C, NH, NKVH = 100, 288, 192, 2, 1
+    H = NH + 2 * NKVH
+    x, w, _, bias = _inputs(cuda_device, B, T, C, NH, NKVH, 1, 128, torch.bfloat16, 21)
+    gen = torch.Generator(device=cuda_device).manual_seed(4)
+    init = (torch.rand((H, 128), generator=gen, device=cuda_device) * 2 - 1) * 0.5
+    grads = [torch.randn((B, n, T, 128), generator=gen, device=cuda_device).to(torch.bfloat16)
+             for n in (NH, NKVH, NKVH)]
+
+    def run(shared):
+        xx = x.clone().requires_grad_(True)
+        ww = w.float().clone().requires_grad_(True)
+        ii = init.clone().requires_grad_(True)
+        bb = bias.clone().requires_grad_(True)
+        inits = ii if shared else ii.to(torch.bfloat16).unsqueeze(0).expand(B, -1, -1)
+        _, q, k, v, ckpt = OPS.ltv_proj_scan_cuda_op(xx, ww, inits, bb, NH, NKVH, 1, 128, True)
+        assert ckpt.numel() > 0
+        torch.autograd.backward((q, k, v), grads)
+        return (q, k, v, xx.grad, ww.grad, bb.grad), ii.grad
+
+    (got, gi_got), (ref, gi_ref) = run(True), run(False)
+    for a, b, n in zip(got, ref, ("q", "k", "v", "grad_x", "grad_w", "grad_bias")):
+        assert a.dtype == b.dtype and torch.equal(a, b), n
+    assert gi_got.dtype == torch.float32
+    torch.testing.assert_close(gi_got, gi_ref, rtol=2 ** -8, atol=1e-5 * gi_ref.abs().max().item())
