@@ -328,6 +328,13 @@ LTVQKV_DEVICE void st_cluster_u32(uint32_t cluster_addr, uint32_t v) {
 LTVQKV_DEVICE void mbar_arrive_cluster(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
+// Relaxed remote arrive, for barriers that only hand back tensor memory: the arriving warp's TMEM
+// reads are complete (tcgen05.wait::ld, then tcgen05.fence::before_thread_sync) and it publishes no
+// memory writes through the barrier, so the release ordering of its preceding global stores (which
+// waits for them to be acknowledged) is not needed.
+LTVQKV_DEVICE void mbar_arrive_cluster_relaxed(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
 // Wait on a local mbarrier whose phase completes through arrivals from the peer CTA (acquire at
 // cluster scope, so the peer's writes made before its arrive are visible).
 LTVQKV_DEVICE bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {

@@ -342,7 +342,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
       __syncwarp();
       if (lane == 0) {
         if (leader) mbar_arrive(&tempty_bar[acc]);
-        else mbar_arrive_cluster(tempty_leader0 + (uint32_t)(acc * 8));
+        else mbar_arrive_cluster_relaxed(tempty_leader0 + (uint32_t)(acc * 8));
       }
       if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
     }

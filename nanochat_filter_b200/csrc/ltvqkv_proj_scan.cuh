@@ -345,7 +345,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPsThreads, 1)
         // all TMEM reads of this accumulator are complete (tcgen05.wait::ld above)
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive_cluster(tempty_leader);
+        if (lane == 0) mbar_arrive_cluster_relaxed(tempty_leader);
         acc_phase ^= 1u;
       }
       if (!ok) break;
