@@ -184,8 +184,9 @@ __global__ void __launch_bounds__(512) scan_fwd_fast_kernel(FastFwdArgs a) {
       if (s == 1) {
         a.aggX[tile_idx * D + c] = tileX;
         if (c % a.r == 0) a.aggA[tile_idx * Da + c / a.r] = tileA;
-        __threadfence();
       }
+      // the barrier orders every thread's payload stores before thread 0's release store of the
+      // flag, which publishes them at GPU scope (release is cumulative): no per-thread fence
       __syncthreads();
       if (tid == 0) st_release_u32(&a.flags[tile_idx], (epoch << 2) | kFlagAgg);
     }
@@ -200,11 +201,8 @@ __global__ void __launch_bounds__(512) scan_fwd_fast_kernel(FastFwdArgs a) {
                           : compose_carry(a.inclX, a.aggA, a.aggX, BH, bh, a.nchunks, m, j, false, D, Da, c, c / a.r);
   }
   if (is_anchor) {
-    if (s == 1) {
-      a.inclX[tile_idx * D + c] = tileA * shE[c] + tileX;
-      __threadfence();
-    }
-    __syncthreads();
+    if (s == 1) a.inclX[tile_idx * D + c] = tileA * shE[c] + tileX;
+    __syncthreads();  // as above: thread 0's release store publishes the block's payload
     if (tid == 0) st_release_u32(&a.flags[tile_idx], (epoch << 2) | kFlagIncl);
   }
   __syncthreads();
@@ -236,13 +234,13 @@ __global__ void __launch_bounds__(512) scan_fwd_fast_kernel(FastFwdArgs a) {
 // ------------------------------------------------------------------------------------------
 // Backward
 // ------------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(512) scan_bwd_fast_kernel(FastBwdArgs a) {
+__global__ void __launch_bounds__(512, 2) scan_bwd_fast_kernel(FastBwdArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int D = a.D, Da = a.Da;
   __nv_bfloat16* G_s = reinterpret_cast<__nv_bfloat16*>(smem_raw);                        // [64][D] upstream grad
   __nv_bfloat16* H_s = G_s + kFastTT * D;                                                 // [64][D] h_{t-1}
-  float* red = reinterpret_cast<float*>(H_s + kFastTT * D);                               // [64][D] dlogit terms
-  float* alpha_s = red + kFastTT * D;                                                     // [Da][65]
+  float* part = reinterpret_cast<float*>(H_s + kFastTT * D);                              // [D/16][64] warp sums
+  float* alpha_s = part + (D / 16) * kFastTT;                                             // [Da][65]
   float* dlog_s = alpha_s + Da * (kFastTT + 1);                                           // [Da][64]
   float* shE = dlog_s + Da * kFastTT;                                                     // [D]
   __shared__ unsigned int sh_tile, sh_epoch;
@@ -301,11 +299,12 @@ __global__ void __launch_bounds__(512) scan_bwd_fast_kernel(FastBwdArgs a) {
       Hv[i] = hv;
     }
   }
-  uint4 uv[4];
   const __nv_bfloat16* urow = cb + (long long)(head_col + c) * a.sc_e + t0 + s * kFastSeg;
-#pragma unroll
-  for (int k = 0; k < 4; ++k)
-    uv[k] = (s * kFastSeg + 8 * k < tlen) ? __ldg(reinterpret_cast<const uint4*>(urow + 8 * k)) : make_uint4(0, 0, 0, 0);
+  auto load_u = [&](int k) {  // the value row's 8 tokens of block k of this thread's segment
+    return (s * kFastSeg + 8 * k < tlen) ? __ldg(reinterpret_cast<const uint4*>(urow + 8 * k))
+                                         : make_uint4(0, 0, 0, 0);
+  };
+  uint4 uv_next = load_u(3);  // in flight during the local scan and the look-back
   __syncthreads();
 
   const int gi = c / a.r;
@@ -333,9 +332,8 @@ __global__ void __launch_bounds__(512) scan_bwd_fast_kernel(FastBwdArgs a) {
       if (s == 0) {
         a.aggX[tile_idx * D + c] = tileX;
         if (c % a.r == 0) a.aggA[tile_idx * Da + gi] = tileA;
-        __threadfence();
       }
-      __syncthreads();
+      __syncthreads();  // thread 0's release store of the flag publishes the block's payload
       if (tid == 0) st_release_u32(&a.flags[tile_idx], (epoch << 2) | kFlagAgg);
     }
     const int mr = (rj - 1) / kAnchorStride * kAnchorStride;
@@ -349,25 +347,26 @@ __global__ void __launch_bounds__(512) scan_bwd_fast_kernel(FastBwdArgs a) {
                           : compose_carry(a.inclX, a.aggA, a.aggX, BH, bh, a.nchunks, mr, rj, true, D, Da, c, gi);
   }
   if (is_anchor) {
-    if (s == 0) {
-      a.inclX[tile_idx * D + c] = tileA * shE[c] + tileX;
-      __threadfence();
-    }
-    __syncthreads();
+    if (s == 0) a.inclX[tile_idx * D + c] = tileA * shE[c] + tileX;
+    __syncthreads();  // thread 0's release store of the flag publishes the block's payload
     if (tid == 0) st_release_u32(&a.flags[tile_idx], (epoch << 2) | kFlagIncl);
   }
   __syncthreads();
 
   // final reverse walk fused with the elementwise part: g^_t, du (t-contiguous row of
-  // grad_combined) and the dlogit terms, one token at a time from the end of the segment
+  // grad_combined) and the dlogit terms, one 8-token block at a time from the end of the segment
   {
     __nv_bfloat16* grow =
         a.grad_combined + (long long)b * a.gc_b + (long long)(head_col + c) * a.gc_e + t0 + s * kFastSeg;
     float carry = (s == 1) ? shE[c] : a1 * shE[c] + x1;
-#pragma unroll
+    const int wq = tid >> 5;  // this warp's 16 channels
+    // after the butterfly, lane l holds the warp's sum of token (l >> 2) & 7 of the block
+    const int tloc = ((lane & 16) ? 4 : 0) + ((lane & 8) ? 2 : 0) + ((lane & 4) ? 1 : 0);
+#pragma unroll 1
     for (int k = 3; k >= 0; --k) {
-      float f[8], du[8];
-      unpack8(uv[k], f);
+      float f[8], du[8], ds[8];
+      unpack8(uv_next, f);
+      if (k > 0) uv_next = load_u(k - 1);  // the next block's row, in flight during this block
 #pragma unroll
       for (int e = 7; e >= 0; --e) {
         const int t = 8 * k + e;
@@ -377,40 +376,49 @@ __global__ void __launch_bounds__(512) scan_bwd_fast_kernel(FastBwdArgs a) {
         du[e] = al * carry;
         const float hp = __bfloat162float(H_s[tl * D + c]);
         const float dalpha = (f[e] - hp) * carry;
-        red[tl * D + c] = a.use_sigmoid ? dalpha * (al * (1.0f - al)) : dalpha;
+        ds[e] = a.use_sigmoid ? dalpha * (al * (1.0f - al)) : dalpha;
       }
       if (s * kFastSeg + 8 * k < tlen) *reinterpret_cast<uint4*>(grow + 8 * k) = pack8(du);
+      // the block's 8 dlogit terms summed over the warp's 16 channels of this segment (lanes of
+      // equal bit 0): halving rounds over lane bits 4, 3, 2 keep the upper half of the values in
+      // the lanes with the bit set, then a plain round over bit 1
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) {
+        const bool up = (lane & 16) != 0;
+        const float send = up ? ds[jj] : ds[jj + 4];
+        const float keep = up ? ds[jj + 4] : ds[jj];
+        ds[jj] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+      }
+#pragma unroll
+      for (int jj = 0; jj < 2; ++jj) {
+        const bool up = (lane & 8) != 0;
+        const float send = up ? ds[jj] : ds[jj + 2];
+        const float keep = up ? ds[jj + 2] : ds[jj];
+        ds[jj] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+      }
+      {
+        const bool up = (lane & 4) != 0;
+        const float send = up ? ds[0] : ds[1];
+        const float keep = up ? ds[1] : ds[0];
+        ds[0] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+      }
+      ds[0] += __shfl_xor_sync(0xffffffffu, ds[0], 2);
+      if ((lane & 2) == 0) part[wq * kFastTT + s * kFastSeg + 8 * k + tloc] = ds[0];
     }
     if (t0 == 0 && s == 0)
       a.grad_inits[((long long)b * a.H + h) * D + c] = __float2bfloat16_rn(carry * (1.0f - al_row[0]));
   }
   __syncthreads();
 
-  // group sums over the r channels of each (token, group): tpg = r / 32 threads per pair, each
-  // summing 32 channels in a lane-rotated order (conflict-free), then a fixed shuffle tree.
-  {
-    const int tpg = a.r / 32;
-    const int npairs = Da * kFastTT;
-    for (int base = 0; base < npairs * tpg; base += blockDim.x) {
-      const int w = base + tid;
-      const int pair = w / tpg, part = w % tpg;
-      float sum = 0.f;
-      if (pair < npairs) {
-        const int g = pair / kFastTT, t = pair % kFastTT;
-        const float* row = red + t * D + g * a.r + part * 32;
-        const int rot = (t + part * (32 / tpg)) & 31;  // distinct banks across the warp
-#pragma unroll 8
-        for (int i = 0; i < 32; ++i) sum += row[(i + rot) & 31];
-      }
-      for (int o = tpg >> 1; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-      if (pair < npairs && part == 0) {
-        const int g = pair / kFastTT, t = pair % kFastTT;
-        dlog_s[g * kFastTT + t] = sum;
-        if (t < tlen)
-          a.grad_combined[(long long)b * a.gc_b + (long long)(head_col + D + g) * a.gc_e + t0 + t] =
-              __float2bfloat16_rn(sum);
-      }
-    }
+  // dlogit of each (group, token): the group's r / 16 warp sums in a fixed order
+  for (int q = tid; q < Da * kFastTT; q += blockDim.x) {
+    const int g = q / kFastTT, t = q % kFastTT;
+    const int wpg = a.r / 16;
+    float sum = 0.f;
+    for (int w = 0; w < wpg; ++w) sum += part[(g * wpg + w) * kFastTT + t];
+    dlog_s[g * kFastTT + t] = sum;
+    if (t < tlen)
+      a.grad_combined[(long long)b * a.gc_b + (long long)(head_col + D + g) * a.gc_e + t0 + t] = __float2bfloat16_rn(sum);
   }
   __syncthreads();
   // per-tile bias partial: warp g sums the tile's dlogit of group g in a fixed tree order
@@ -432,7 +440,7 @@ inline size_t fast_fwd_smem_bytes(int D, int Da) {
   return (size_t)kFastTT * D * 2 + sizeof(float) * ((size_t)Da * kFastTT + D);
 }
 inline size_t fast_bwd_smem_bytes(int D, int Da) {
-  return (size_t)kFastTT * D * 2 * 2 + sizeof(float) * ((size_t)kFastTT * D + (size_t)Da * (kFastTT + 1) +
+  return (size_t)kFastTT * D * 2 * 2 + sizeof(float) * ((size_t)(D / 16) * kFastTT + (size_t)Da * (kFastTT + 1) +
                                                          (size_t)Da * kFastTT + D);
 }
 
