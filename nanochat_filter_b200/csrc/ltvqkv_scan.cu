@@ -902,8 +902,10 @@ extern "C" int ltvqkv_scan_fwd(int dtype, const void* combined, int64_t sc_b, in
     f.aggX = reinterpret_cast<float*>(ws + wx.aggX);
     f.inclX = reinterpret_cast<float*>(ws + wx.inclX);
     const size_t fsm = fast_fwd_smem_bytes(gx.D, Da);
-    cudaFuncSetAttribute(scan_fwd_fast_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fsm);
-    scan_fwd_fast_kernel<<<(unsigned int)((long long)B * gx.H * gx.nchunks), 2 * gx.D, fsm, s>>>(f);
+    // head dims up to 128 (256 threads) take a register cap that fits more CTAs per SM
+    auto kern = gx.D <= 128 ? scan_fwd_fast_kernel<256, kFastFwdMinBlocks256> : scan_fwd_fast_kernel<512, 2>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fsm);
+    kern<<<(unsigned int)((long long)B * gx.H * gx.nchunks), 2 * gx.D, fsm, s>>>(f);
     return ltvqkv_host::check_launch();
   }
   size_t smem = fwd_smem_bytes(g);
@@ -1035,8 +1037,9 @@ extern "C" int ltvqkv_scan_bwd(int dtype, const void* combined, int64_t sc_b, in
       f.aggX = reinterpret_cast<float*>(ws + wx.aggX);
       f.inclX = reinterpret_cast<float*>(ws + wx.inclX);
       const size_t fsm = fast_bwd_smem_bytes(gx.D, Da);
-      cudaFuncSetAttribute(scan_bwd_fast_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fsm);
-      scan_bwd_fast_kernel<<<(unsigned int)((long long)B * gx.H * gx.nchunks), 2 * gx.D, fsm, s>>>(f);
+      auto kern = gx.D <= 128 ? scan_bwd_fast_kernel<256, kFastBwdMinBlocks256> : scan_bwd_fast_kernel<512, 2>;
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fsm);
+      kern<<<(unsigned int)((long long)B * gx.H * gx.nchunks), 2 * gx.D, fsm, s>>>(f);
       int rc = ltvqkv_host::check_launch();
       if (rc != LTVQKV_OK) return rc;
       bias_reduce_kernel<<<H * Da, kBiasReduceThreads, 0, s>>>(f.bias_part, grad_logit_bias, B, gx.nchunks, H, Da);

@@ -17,6 +17,10 @@ namespace ltvqkv {
 constexpr int kFastTT = 64;   // tokens per tile
 constexpr int kFastSeg = 32;  // tokens per thread
 constexpr int kFastMaxDa = 8;
+// CTAs per SM targeted for 256-thread tiles (head dim <= 128) by the register cap: the backward
+// fits 6 without spills (40 registers), the forward 4 (62; lower caps spill)
+constexpr int kFastFwdMinBlocks256 = 4;
+constexpr int kFastBwdMinBlocks256 = 6;
 
 LTVQKV_DEVICE void unpack8(const uint4& v, float (&f)[8]) {
   const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&v);
@@ -113,7 +117,8 @@ LTVQKV_DEVICE float compose_carry(const float* inclX, const float* aggA, const f
 // ------------------------------------------------------------------------------------------
 // Forward
 // ------------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(512) scan_fwd_fast_kernel(FastFwdArgs a) {
+template <int kThreads, int kMinBlocks>
+__global__ void __launch_bounds__(kThreads, kMinBlocks) scan_fwd_fast_kernel(FastFwdArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int D = a.D, Da = a.Da;
   __nv_bfloat16* out_s = reinterpret_cast<__nv_bfloat16*>(smem_raw);                 // [64][D]
@@ -234,7 +239,8 @@ __global__ void __launch_bounds__(512) scan_fwd_fast_kernel(FastFwdArgs a) {
 // ------------------------------------------------------------------------------------------
 // Backward
 // ------------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(512, 2) scan_bwd_fast_kernel(FastBwdArgs a) {
+template <int kThreads, int kMinBlocks>
+__global__ void __launch_bounds__(kThreads, kMinBlocks) scan_bwd_fast_kernel(FastBwdArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int D = a.D, Da = a.Da;
   __nv_bfloat16* G_s = reinterpret_cast<__nv_bfloat16*>(smem_raw);                        // [64][D] upstream grad
