@@ -72,8 +72,10 @@ LTVQKV_DEVICE bool finish_launch_last(WorkspaceHeader* ws, unsigned int num_ctas
   return false;
 }
 
+// No fence before the count: nothing in the launch reads what a CTA wrote because of it (the next
+// launch on the workspace is ordered after this one by the stream), so the CTA need not wait for
+// its stores to be acknowledged before it exits.
 LTVQKV_DEVICE void finish_launch(WorkspaceHeader* ws, unsigned int num_ctas) {
-  __threadfence();
   unsigned int done = atomicAdd(&ws->exit_counter, 1u);
   if (done == num_ctas - 1) {
     atomicExch(&ws->tile_counter, 0u);
