@@ -901,11 +901,21 @@ extern "C" int ltvqkv_scan_fwd(int dtype, const void* combined, int64_t sc_b, in
     f.aggA = reinterpret_cast<float*>(ws + wx.aggA);
     f.aggX = reinterpret_cast<float*>(ws + wx.aggX);
     f.inclX = reinterpret_cast<float*>(ws + wx.inclX);
+    // three passes: tile aggregates, carries per (row, channel), tiles from their carries
+    const unsigned int tiles = (unsigned int)((long long)B * gx.H * gx.nchunks);
+    const bool small = gx.D <= 128;  // 256 threads: a register cap that fits more CTAs per SM
+    auto agg = small ? scan_fwd_agg_kernel<256, kFastFwdMinBlocks256> : scan_fwd_agg_kernel<512, 2>;
+    agg<<<tiles, 2 * gx.D, 0, s>>>(f);
+    int rc = ltvqkv_host::check_launch();
+    if (rc != LTVQKV_OK) return rc;
+    const long long nthreads = (long long)B * gx.H * gx.D;
+    scan_fwd_carry_kernel<<<(unsigned int)((nthreads + 255) / 256), 256, 0, s>>>(f);
+    rc = ltvqkv_host::check_launch();
+    if (rc != LTVQKV_OK) return rc;
     const size_t fsm = fast_fwd_smem_bytes(gx.D, Da);
-    // head dims up to 128 (256 threads) take a register cap that fits more CTAs per SM
-    auto kern = gx.D <= 128 ? scan_fwd_fast_kernel<256, kFastFwdMinBlocks256> : scan_fwd_fast_kernel<512, 2>;
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fsm);
-    kern<<<(unsigned int)((long long)B * gx.H * gx.nchunks), 2 * gx.D, fsm, s>>>(f);
+    auto apply = small ? scan_fwd_apply_kernel<256, kFastFwdMinBlocks256> : scan_fwd_apply_kernel<512, 2>;
+    cudaFuncSetAttribute(apply, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fsm);
+    apply<<<tiles, 2 * gx.D, fsm, s>>>(f);
     return ltvqkv_host::check_launch();
   }
   size_t smem = fwd_smem_bytes(g);

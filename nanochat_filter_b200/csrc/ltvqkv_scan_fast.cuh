@@ -8,8 +8,10 @@
 // and tokens [32 s, 32 s + 32) of the chunk. t-contiguous rows are read and written straight
 // from/to registers with 16-byte vector accesses (4 per thread); d-contiguous tiles pass through
 // shared memory ([64][D] bf16, one contiguous 16 KB block per tile in global memory). The two
-// 32-token segments of a channel are adjacent lanes and combine with one shuffle. Chunk carries
-// use the anchored look-back of the generic kernels (fixed association: deterministic).
+// 32-token segments of a channel are adjacent lanes and combine with one shuffle. Chunk carries:
+// the forward composes them in a separate pass between two tile passes (no waits between CTAs);
+// the backward uses the anchored look-back of the generic kernels. Both associations are fixed,
+// so results are deterministic.
 #pragma once
 
 namespace ltvqkv {
@@ -115,55 +117,55 @@ LTVQKV_DEVICE float compose_carry(const float* inclX, const float* aggA, const f
 }
 
 // ------------------------------------------------------------------------------------------
-// Forward
+// Forward: three passes, no look-back. (1) every tile's aggregates (the decay product of each
+// group and the zero-carry scan end of each channel), all tiles in parallel; (2) per (row,
+// channel), the carries entering every tile, composed in tile order; (3) every tile again from its
+// carry, writing the outputs. Nothing waits on another CTA; the value rows are read twice (the
+// second time mostly from L2) instead of once, which costs less than the look-back chain did.
 // ------------------------------------------------------------------------------------------
-template <int kThreads, int kMinBlocks>
-__global__ void __launch_bounds__(kThreads, kMinBlocks) scan_fwd_fast_kernel(FastFwdArgs a) {
-  extern __shared__ __align__(16) unsigned char smem_raw[];
-  const int D = a.D, Da = a.Da;
-  __nv_bfloat16* out_s = reinterpret_cast<__nv_bfloat16*>(smem_raw);                 // [64][D]
-  float* alpha_s = reinterpret_cast<float*>(smem_raw + (size_t)kFastTT * D * 2);      // [Da][64]
-  float* shE = alpha_s + Da * kFastTT;                                                // [D]
-  __shared__ unsigned int sh_tile, sh_epoch;
-  __shared__ int sh_timeout;
 
-  const int tid = threadIdx.x, lane = tid & 31;
-  const int c = tid >> 1, s = tid & 1;
-  if (tid == 0) {
-    sh_tile = draw_ticket(a.ws);
-    sh_epoch = *((volatile unsigned int*)&a.ws->epoch) & 0x3FFFFFFFu;
-  }
-  __syncthreads();
-  const unsigned int epoch = sh_epoch;
+// Tile geometry shared by passes 1 and 3 (tile = blockIdx.x = chunk * B * H + row).
+struct FastTile {
+  int j, bh, b, h, t0, tlen, head_col;
+};
+LTVQKV_DEVICE FastTile fast_tile(const FastFwdArgs& a) {
+  FastTile t;
   const int BH = a.B * a.H;
-  const int j = (int)(sh_tile / BH);
-  const int bh = (int)(sh_tile % BH);
-  const int b = bh / a.H, h = bh % a.H;
-  const int t0 = j * kFastTT;
-  const int tlen = min(kFastTT, a.T - t0);
-  const __nv_bfloat16* cb = a.combined + (long long)b * a.sc_b;
-  const int head_col = h * (D + Da);
+  t.j = (int)(blockIdx.x / BH);
+  t.bh = (int)(blockIdx.x % BH);
+  t.b = t.bh / a.H;
+  t.h = t.bh % a.H;
+  t.t0 = t.j * kFastTT;
+  t.tlen = min(kFastTT, a.T - t.t0);
+  t.head_col = t.h * (a.D + a.Da);
+  return t;
+}
 
-  for (int i = tid; i < Da * kFastTT; i += blockDim.x) {
-    const int gi = i / kFastTT, t = i % kFastTT;
-    float al = 0.f;  // tokens beyond T: identity steps
-    if (t < tlen) {
-      const float l = __bfloat162float(cb[(long long)(head_col + D + gi) * a.sc_e + t0 + t]) + a.logit_bias[h * Da + gi];
+// Gates of the tile (identity beyond T) into alpha_s [Da][64], and this thread's value-row segment.
+LTVQKV_DEVICE void fast_fwd_load(const FastFwdArgs& a, const FastTile& t, float* alpha_s, int c, int s,
+                                 uint4 (&uv)[4]) {
+  const __nv_bfloat16* cb = a.combined + (long long)t.b * a.sc_b;
+  for (int i = threadIdx.x; i < a.Da * kFastTT; i += blockDim.x) {
+    const int gi = i / kFastTT, tt = i % kFastTT;
+    float al = 0.f;
+    if (tt < t.tlen) {
+      const float l = __bfloat162float(cb[(long long)(t.head_col + a.D + gi) * a.sc_e + t.t0 + tt]) +
+                      a.logit_bias[t.h * a.Da + gi];
       al = a.use_sigmoid ? sigmoid_f32(l) : l;
     }
     alpha_s[i] = al;
   }
-  uint4 uv[4];
-  {
-    const __nv_bfloat16* urow = cb + (long long)(head_col + c) * a.sc_e + t0 + s * kFastSeg;
+  const __nv_bfloat16* urow = cb + (long long)(t.head_col + c) * a.sc_e + t.t0 + s * kFastSeg;
 #pragma unroll
-    for (int k = 0; k < 4; ++k)
-      uv[k] = (s * kFastSeg + 8 * k < tlen) ? __ldg(reinterpret_cast<const uint4*>(urow + 8 * k)) : make_uint4(0, 0, 0, 0);
-  }
-  __syncthreads();
-  const float* al_row = alpha_s + (c / a.r) * kFastTT + s * kFastSeg;
+  for (int k = 0; k < 4; ++k)
+    uv[k] = (s * kFastSeg + 8 * k < t.tlen) ? __ldg(reinterpret_cast<const uint4*>(urow + 8 * k))
+                                            : make_uint4(0, 0, 0, 0);
+}
 
-  float sa = 1.f, sx = 0.f;
+// Zero-carry scan of this thread's segment: sa = product of (1 - alpha), sx = end state.
+LTVQKV_DEVICE void fast_fwd_local(const float* al_row, const uint4 (&uv)[4], float& sa, float& sx) {
+  sa = 1.f;
+  sx = 0.f;
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
     float f[8];
@@ -175,44 +177,77 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks) scan_fwd_fast_kernel(Fas
       sa *= (1.0f - al);
     }
   }
+}
+
+template <int kThreads, int kMinBlocks>
+__global__ void __launch_bounds__(kThreads, kMinBlocks) scan_fwd_agg_kernel(FastFwdArgs a) {
+  __shared__ float alpha_s[kFastMaxDa * kFastTT];
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int c = tid >> 1, s = tid & 1;
+  const FastTile t = fast_tile(a);
+  uint4 uv[4];
+  fast_fwd_load(a, t, alpha_s, c, s, uv);
+  __syncthreads();
+  float sa, sx;
+  fast_fwd_local(alpha_s + (c / a.r) * kFastTT + s * kFastSeg, uv, sa, sx);
   // segment 0 lives in the even lane of each pair
   const float a0 = __shfl_sync(0xffffffffu, sa, lane & ~1);
   const float x0 = __shfl_sync(0xffffffffu, sx, lane & ~1);
-  const float tileA = a0 * sa, tileX = sa * x0 + sx;  // meaningful on s == 1
+  if (s == 1) {
+    a.aggX[(long long)blockIdx.x * a.D + c] = sa * x0 + sx;
+    if (c % a.r == 0) a.aggA[(long long)blockIdx.x * a.Da + c / a.r] = a0 * sa;
+  }
+}
 
-  const long long tile_idx = (long long)j * BH + bh;
-  const bool is_anchor = (j % kAnchorStride) == 0;
-  if (j == 0) {
-    if (s == 1) shE[c] = __bfloat162float(a.inits[((long long)b * a.H + h) * D + c]);
-  } else {
-    if (!is_anchor) {
-      if (s == 1) {
-        a.aggX[tile_idx * D + c] = tileX;
-        if (c % a.r == 0) a.aggA[tile_idx * Da + c / a.r] = tileA;
+// One thread per (row, channel): the state entering each tile of the row, from the initial state
+// and the tiles' aggregates in tile order (16 tiles' aggregates in flight at a time).
+__global__ void __launch_bounds__(256) scan_fwd_carry_kernel(FastFwdArgs a) {
+  const int BH = a.B * a.H;
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long long)BH * a.D) return;
+  const int bh = (int)(i / a.D), c = (int)(i % a.D), gi = c / a.r;
+  float E = __bfloat162float(a.inits[(long long)bh * a.D + c]);
+  for (int j0 = 0; j0 < a.nchunks; j0 += 16) {
+    float A[16], X[16];
+#pragma unroll
+    for (int q = 0; q < 16; ++q) {
+      const long long tile = (long long)(j0 + q) * BH + bh;
+      A[q] = 1.f;
+      X[q] = 0.f;
+      if (j0 + q < a.nchunks) {
+        A[q] = ld_cg_f32(&a.aggA[tile * a.Da + gi]);
+        X[q] = ld_cg_f32(&a.aggX[tile * a.D + c]);
       }
-      // the barrier orders every thread's payload stores before thread 0's release store of the
-      // flag, which publishes them at GPU scope (release is cumulative): no per-thread fence
-      __syncthreads();
-      if (tid == 0) st_release_u32(&a.flags[tile_idx], (epoch << 2) | kFlagAgg);
     }
-    const int m = (j - 1) / kAnchorStride * kAnchorStride;
-    if (tid < 32) {
-      const bool to = warp_wait_flags(a.flags, BH, bh, a.nchunks, m, j, false, epoch, a.ws, lane);
-      if (tid == 0) sh_timeout = to;
+#pragma unroll
+    for (int q = 0; q < 16; ++q) {
+      if (j0 + q < a.nchunks) {
+        a.inclX[((long long)(j0 + q) * BH + bh) * a.D + c] = E;  // carry into tile j0 + q
+        E = A[q] * E + X[q];
+      }
     }
-    __syncthreads();
-    if (s == 1)
-      shE[c] = sh_timeout ? 0.f
-                          : compose_carry(a.inclX, a.aggA, a.aggX, BH, bh, a.nchunks, m, j, false, D, Da, c, c / a.r);
   }
-  if (is_anchor) {
-    if (s == 1) a.inclX[tile_idx * D + c] = tileA * shE[c] + tileX;
-    __syncthreads();  // as above: thread 0's release store publishes the block's payload
-    if (tid == 0) st_release_u32(&a.flags[tile_idx], (epoch << 2) | kFlagIncl);
-  }
-  __syncthreads();
+}
 
-  float carry = (s == 0) ? shE[c] : a0 * shE[c] + x0;
+template <int kThreads, int kMinBlocks>
+__global__ void __launch_bounds__(kThreads, kMinBlocks) scan_fwd_apply_kernel(FastFwdArgs a) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int D = a.D;
+  __nv_bfloat16* out_s = reinterpret_cast<__nv_bfloat16*>(smem_raw);                 // [64][D]
+  float* alpha_s = reinterpret_cast<float*>(smem_raw + (size_t)kFastTT * D * 2);      // [Da][64]
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int c = tid >> 1, s = tid & 1;
+  const FastTile t = fast_tile(a);
+  uint4 uv[4];
+  fast_fwd_load(a, t, alpha_s, c, s, uv);
+  const float E_in = a.inclX[(long long)blockIdx.x * D + c];
+  __syncthreads();
+  const float* al_row = alpha_s + (c / a.r) * kFastTT + s * kFastSeg;
+  float sa, sx;
+  fast_fwd_local(al_row, uv, sa, sx);
+  const float a0 = __shfl_sync(0xffffffffu, sa, lane & ~1);
+  const float x0 = __shfl_sync(0xffffffffu, sx, lane & ~1);
+  float carry = (s == 0) ? E_in : a0 * E_in + x0;
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
     float f[8];
@@ -227,13 +262,11 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks) scan_fwd_fast_kernel(Fas
   __syncthreads();
 
   int which, hloc, nheads;
-  split_head(h, a.NH, a.NKVH, which, hloc, nheads);
-  uint4* go = reinterpret_cast<uint4*>(a.out[which] + (((long long)b * nheads + hloc) * a.T + t0) * D);
+  split_head(t.h, a.NH, a.NKVH, which, hloc, nheads);
+  uint4* go = reinterpret_cast<uint4*>(a.out[which] + (((long long)t.b * nheads + hloc) * a.T + t.t0) * D);
   const uint4* so = reinterpret_cast<const uint4*>(out_s);
-  const int n16 = tlen * D / 8;
+  const int n16 = t.tlen * D / 8;
   for (int i = tid; i < n16; i += blockDim.x) go[i] = so[i];
-
-  if (tid == 0) finish_launch(a.ws, gridDim.x);
 }
 
 // ------------------------------------------------------------------------------------------
@@ -443,7 +476,7 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks) scan_bwd_fast_kernel(Fas
 }
 
 inline size_t fast_fwd_smem_bytes(int D, int Da) {
-  return (size_t)kFastTT * D * 2 + sizeof(float) * ((size_t)Da * kFastTT + D);
+  return (size_t)kFastTT * D * 2 + sizeof(float) * (size_t)Da * kFastTT;
 }
 inline size_t fast_bwd_smem_bytes(int D, int Da) {
   return (size_t)kFastTT * D * 2 * 2 + sizeof(float) * ((size_t)(D / 16) * kFastTT + (size_t)Da * (kFastTT + 1) +
