@@ -904,7 +904,7 @@ extern "C" int ltvqkv_scan_fwd(int dtype, const void* combined, int64_t sc_b, in
     // three passes: tile aggregates, carries per (row, channel), tiles from their carries
     const unsigned int tiles = (unsigned int)((long long)B * gx.H * gx.nchunks);
     const bool small = gx.D <= 128;  // 256 threads: a register cap that fits more CTAs per SM
-    auto agg = small ? scan_fwd_agg_kernel<256, kFastFwdMinBlocks256> : scan_fwd_agg_kernel<512, 2>;
+    auto agg = small ? scan_fwd_agg_kernel<256, kFastFwdAggMinBlocks256> : scan_fwd_agg_kernel<512, 2>;
     agg<<<tiles, 2 * gx.D, 0, s>>>(f);
     int rc = ltvqkv_host::check_launch();
     if (rc != LTVQKV_OK) return rc;

@@ -20,8 +20,10 @@ constexpr int kFastTT = 64;   // tokens per tile
 constexpr int kFastSeg = 32;  // tokens per thread
 constexpr int kFastMaxDa = 8;
 // CTAs per SM targeted for 256-thread tiles (head dim <= 128) by the register cap: the backward
-// fits 6 without spills (40 registers), the forward 4 (62; lower caps spill)
-constexpr int kFastFwdMinBlocks256 = 4;
+// and the forward's aggregate pass fit 6 without spills (40 and 38 registers), the forward's
+// apply pass 5 (48 registers, one 4-byte spill)
+constexpr int kFastFwdAggMinBlocks256 = 6;
+constexpr int kFastFwdMinBlocks256 = 5;
 constexpr int kFastBwdMinBlocks256 = 6;
 
 LTVQKV_DEVICE void unpack8(const uint4& v, float (&f)[8]) {
