@@ -896,8 +896,6 @@ extern "C" int ltvqkv_scan_fwd(int dtype, const void* combined, int64_t sc_b, in
     f.out[2] = reinterpret_cast<__nv_bfloat16*>(out_v);
     f.B = B; f.T = T; f.NH = NH; f.NKVH = NKVH; f.Da = Da; f.r = r; f.D = gx.D; f.H = gx.H;
     f.nchunks = gx.nchunks; f.use_sigmoid = use_sigmoid;
-    f.ws = reinterpret_cast<WorkspaceHeader*>(ws);
-    f.flags = reinterpret_cast<unsigned int*>(ws + wx.flags);
     f.aggA = reinterpret_cast<float*>(ws + wx.aggA);
     f.aggX = reinterpret_cast<float*>(ws + wx.aggX);
     f.inclX = reinterpret_cast<float*>(ws + wx.inclX);

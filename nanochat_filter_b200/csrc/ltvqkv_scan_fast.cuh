@@ -51,11 +51,9 @@ struct FastFwdArgs {
   const float* logit_bias;
   __nv_bfloat16* out[3];
   int B, T, NH, NKVH, Da, r, D, H, nchunks, use_sigmoid;
-  WorkspaceHeader* ws;
-  unsigned int* flags;
-  float* aggA;
-  float* aggX;
-  float* inclX;
+  float* aggA;   // [tiles][Da] decay product of each tile
+  float* aggX;   // [tiles][D] zero-carry scan end of each tile
+  float* inclX;  // [tiles][D] state entering each tile (written by the carry pass)
 };
 
 struct FastBwdArgs {
