@@ -95,7 +95,8 @@ LTVQKV_API int ltvqkv_scan_fwd(int dtype,
  * that cannot allocate device memory or hand out a workspace on the call path — plugin hosts
  * and serving runtimes that own all device memory under a fixed plan, or foreign-language
  * callers without an allocator. Same arguments and results as ltvqkv_scan_fwd minus the
- * workspace: the look-back scratch is a fixed 32 MiB file-scope device array in the library
+ * workspace: the scan's scratch (chunk aggregates, carries, look-back flags) is a fixed 32 MiB
+ * file-scope device array in the library
  * (held on every GPU that loads the library until exit). Shapes whose forward scratch exceeds
  * it return LTVQKV_ERR_TOO_LARGE (D = 128, r = 128: about 1 KiB per (batch, head, 64-token
  * chunk) tile, so up to about 32 k tiles; B=4, T=16384, 8+8+8 heads needs 24 576 and fits). Calls no cudaMalloc/cudaFree.
