@@ -76,6 +76,19 @@ def test_argument_validation_without_device():
                                   None, None, None, None, 0, 8, 1, 1, 1, 1, 1, None) == 0
     assert lib.ltvqkv_decode_step(1, None, None, None, None, None, None, None, None, None, None, None, None,
                                   None, None, None, None, 2, 8, 1, 1, 1, 1, 1, None) == 1
+    # checkpoint forms: a missing or misaligned checkpoint buffer, or an initial-state stride other
+    # than H * D or 0, is rejected before any device work
+    assert lib.ltvqkv_proj_scan_fwd_ckpt(1, fake, fake, fake, 0, fake, fake, fake, fake, fake, None, 2, 64, 64, 1, 1,
+                                         1, 128, 1, fake, 4096, None) == 1
+    assert lib.ltvqkv_proj_scan_fwd_ckpt(1, fake, fake, fake, 0, fake, fake, fake, fake, fake,
+                                         ctypes.c_void_p(0x10004), 2, 64, 64, 1, 1, 1, 128, 1, fake, 4096, None) == 1
+    assert lib.ltvqkv_proj_scan_fwd_ckpt(1, fake, fake, fake, 5, fake, fake, fake, fake, fake, fake, 2, 64, 64, 1, 1,
+                                         1, 128, 1, fake, 4096, None) == 3
+    st = _lib.strides([0, 0, 0, 1])
+    assert lib.ltvqkv_scan_bwd_ckpt(1, fake, 0, 1, 64, fake, 0, fake, None, fake, st, fake, st, fake, st,
+                                    fake, 0, 1, 64, fake, fake, 2, 64, 1, 1, 1, 128, 1, fake, 4096, None) == 1
+    assert lib.ltvqkv_scan_bwd_ckpt(1, fake, 0, 1, 64, fake, 7, fake, fake, fake, st, fake, st, fake, st,
+                                    fake, 0, 1, 64, fake, fake, 2, 64, 1, 1, 1, 128, 1, fake, 4096, None) == 3
 
 
 def test_check_raises_runtime_error():
