@@ -19,9 +19,12 @@ the look-back (chunk-restarting) scans of nanochat/ops/ltv_cuda_look_back_fused_
   ltv_look_back_fused_concat_head_major_register_cast_{blelloch,sequential}_scan_cuda_op (autograd)
   ..._forward_kernel, ..._backward_kernel
 
-plus ops the reference does not have: `ltv_decode_step` (one-launch decode update) and
+plus ops the reference does not have: `ltv_decode_step` (one-launch decode update),
 `ltv_proj_scan_cuda_op` / `ltv_proj_scan_forward_kernel` (projection and scan forward in one
-call, the composition the reference's filter runs as two ops; same outputs bit for bit).
+call, the composition the reference's filter runs as two ops; same outputs bit for bit; its fifth
+output holds the scan state at every 32-token chunk start) and `ltv_scan_ckpt_backward_kernel`
+(the scan backward replaying the outputs from those states instead of reading them; same
+gradients bit for bit), and the rotary + QK-norm consumer ops.
 
 The CUDA implementations call libltvqkv.so through its C ABI; only "CUDA" and "Meta"
 dispatch keys are registered, so CPU tensors raise NotImplementedError from the dispatcher —
