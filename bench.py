@@ -10,7 +10,8 @@ scan backward, projection backward (dx and dW), [all-reduce of dW, d logit_bias,
 `value`: device-resident inputs, timed with CUDA events, max over ranks.
 `e2e`: the same step through the public module API (filter forward + autograd backward),
 with the step's inputs (x and the upstream q/k/v gradients) copied from pinned host memory
-and the step's result (the logit-bias gradient) read back, inside the timed region.
+and the step's result (the layer's parameter gradients: dW, d logit_bias, d init) read back,
+inside the timed region.
 Prints one JSON line (rank 0).
 """
 
@@ -37,7 +38,9 @@ CONFIGS = {
     # one decay logit per head per token; F = (NH + 2 NKVH) * 129).
     "config2": dict(B=32, T=1024, C=768, NH=6, NKVH=6, D=128, r=128, dtype="bf16", bias=0.0,
                     desc="d=12 training shape: B=32/rank, T=1024, C=768, 6+6+6 heads x 128, r=128, bf16"),
-    "config3": dict(B=4, T=16384, C=1024, NH=8, NKVH=8, D=128, r=128, dtype="bf16", bias=-3.0,
+    # config 3's decay a = 1 - alpha ~ 0.95 (reference gate alpha = sigmoid(logit)): the decay
+    # pre-activation ~ N(3, 1) as logit rows ~ N(0, 1/sqrt(C)) (pre-activation std 1) and bias -3
+    "config3": dict(B=4, T=16384, C=1024, NH=8, NKVH=8, D=128, r=128, dtype="bf16", bias=-3.0, logit_std="1/sqrt(C)",
                     desc="long sequence: B=4/rank, T=16384, C=1024, 8+8+8 heads x 128, r=128, bf16, a~0.95"),
     "config1": dict(B=2, T=256, C=768, NH=6, NKVH=6, D=128, r=128, dtype="f32", bias=0.0,
                     desc="CPU-runnable shape in fp32: B=2/rank, T=256, C=768, 6+6+6 heads x 128"),
@@ -146,6 +149,10 @@ def gpu_id_for(dev_index: int) -> str:
 # ------------------------------------------------------------------------------------------
 # Workload
 # ------------------------------------------------------------------------------------------
+def _logit_std(cfg):
+    return 1.0 / math.sqrt(cfg["C"]) if cfg.get("logit_std") == "1/sqrt(C)" else 0.02
+
+
 def make_inputs(cfg, device, seed):
     import torch
 
@@ -156,7 +163,7 @@ def make_inputs(cfg, device, seed):
     dt = torch.bfloat16 if cfg["dtype"] == "bf16" else torch.float32
     x = torch.randn(B, T, C, generator=g).to(dt)
     wv = torch.randn(H, D, C, generator=g) / math.sqrt(C)      # value rows ~ N(0, 1/sqrt(C))
-    wl = torch.randn(H, Da, C, generator=g) * 0.02            # decay-logit rows ~ N(0, 0.02)
+    wl = torch.randn(H, Da, C, generator=g) * _logit_std(cfg)  # decay-logit rows ~ N(0, 0.02) (config 3: 1/sqrt(C))
     W = torch.cat([wv, wl], dim=1).reshape(F, C)              # head-major interleaved, fp32 master
     bias = torch.full((H, Da), float(cfg["bias"]))
     init = torch.zeros(H, D)
@@ -368,9 +375,12 @@ def run_ours(args, cfg):
     copy_stream = torch.cuda.Stream(device)
     copied = [torch.cuda.Event() for _ in range(2)]     # slot's inputs are on the device
     consumed = [torch.cuda.Event() for _ in range(2)]   # slot's previous step is done with them
-    out_host = torch.empty((H, Da), dtype=torch.float32).pin_memory()
+    # the step's result read back: the layer's parameter gradients (dW fp32 [F, C], d logit_bias,
+    # d init_param), what an optimizer step consumes; dx stays on the device for the layer below
+    out_host = [torch.empty(p.shape, dtype=torch.float32).pin_memory()
+                for p in (filt.c.weight, filt.logit_bias, filt.init_param)]
     h2d_bytes = sum(t.numel() * t.element_size() for t in pin.values())
-    d2h_bytes = out_host.numel() * out_host.element_size()
+    d2h_bytes = sum(t.numel() * t.element_size() for t in out_host)
 
     def issue_copy(slot):
         copy_stream.wait_event(consumed[slot])
@@ -392,7 +402,8 @@ def run_ours(args, cfg):
                                             dv["gv"].transpose(1, 2)])
         if e2e_bucket is not None:
             e2e_bucket.reduce()
-        out_host.copy_(filt.logit_bias.grad, non_blocking=True)  # the step's result, read back
+        for dst, p in zip(out_host, (filt.c.weight, filt.logit_bias, filt.init_param)):
+            dst.copy_(p.grad, non_blocking=True)  # the step's result, read back
         consumed[slot].record(torch.cuda.current_stream(device))
 
     def e2e_run(n):
@@ -500,7 +511,7 @@ def _oracle_sample(cfg, seqs, seed=7):
     H, Da = NH + 2 * NKVH, D // r
     F = H * (D + Da)
     x = rng.standard_normal((seqs, T, C)).astype(np.float32)
-    w = np.concatenate([rng.standard_normal((H, D, C)) / np.sqrt(C), rng.standard_normal((H, Da, C)) * 0.02],
+    w = np.concatenate([rng.standard_normal((H, D, C)) / np.sqrt(C), rng.standard_normal((H, Da, C)) * _logit_std(cfg)],
                        axis=1).reshape(F, C).astype(np.float32)
     init = np.zeros((seqs, H, D), np.float32)
     bias = np.full((H, Da), float(cfg["bias"]), np.float32)
@@ -528,8 +539,8 @@ def cpu_baseline(cfg, seconds=10.0, seqs=1):
         times.append(time.perf_counter() - t0)
     med = statistics.median(times)
     return {"value": round(seqs * cfg["T"] / med, 2), "unit": UNIT, "cores": cores, "kind": "port",
-            "sample": f"{seqs} sequence(s) x {cfg['T']} tokens of {cfg['desc']}; oracle/ltv_oracle.c "
-                      f"(C restatement of the reference's CPU oracle, double-accumulated GEMMs), "
+            "sample": f"{seqs} sequence(s) x {cfg['T']} tokens of {cfg['desc']}; oracle port of the "
+                      f"reference's CPU algorithm (oracle/ltv_oracle.c scan, float64 BLAS GEMMs), "
                       f"median of {len(times)} runs"}
 
 
@@ -553,8 +564,9 @@ def run_reference(args, cfg):
     total = sum(times)
     value = args.steps * cfg["T"] / total
     n = int(os.environ.get("WORLD_SIZE", "1"))
-    sample_desc = (f"1 sequence x {cfg['T']} tokens per step of {cfg['desc']}; oracle port "
-                   "(the reference's CPU path is a torch Python oracle that cannot run on the GPU box)")
+    sample_desc = (f"1 sequence x {cfg['T']} tokens per step of {cfg['desc']}; oracle port: "
+                   "the reference's CPU path is Python source (its torch oracle) that is not shipped to "
+                   "the GPU box, so its algorithm runs as the port (C scan, float64 BLAS GEMMs)")
     print(json.dumps({
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": n, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(1e3 * total / args.steps, 3), "higher_is_better": True,

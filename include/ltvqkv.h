@@ -102,13 +102,21 @@ LTVQKV_API int ltvqkv_scan_fwd(int dtype,
  * chunk) tile, so up to about 32 k tiles; B=4, T=16384, 8+8+8 heads needs 24 576 and fits). Calls no cudaMalloc/cudaFree.
  * The first call on a device looks up the array's address (may load the library's device code
  * there) and should come before any stream capture. All calls share the array and each clears
- * its counters and flags on `stream`: calls that overlap on the GPU race. */
+ * its counters and flags on `stream`: calls that overlap on the GPU race. A bounded device-side
+ * wait that gives up inside a call records LTVQKV_ERR_TIMEOUT in the array's error word, which
+ * later calls leave set: read it with ltvqkv_scan_noalloc_error. */
 LTVQKV_API int ltvqkv_scan_fwd_noalloc(int dtype,
                     const void* combined, int64_t sc_b, int64_t sc_t, int64_t sc_e,
                     const void* inits, const float* logit_bias,
                     void* out_q, void* out_k, void* out_v,
                     int B, int T, int NH, int NKVH, int Da, int r, int use_sigmoid,
                     void* stream);
+
+/* Reads and clears the error word of ltvqkv_scan_fwd_noalloc's array on the current device
+ * (synchronises `stream`): *err_out receives LTVQKV_OK, or LTVQKV_ERR_TIMEOUT when a bounded
+ * device-side wait of an earlier allocation-free call gave up (its outputs are then incomplete).
+ * No reference counterpart: the allocation-free entry point has none. Allocates nothing. */
+LTVQKV_API int ltvqkv_scan_noalloc_error(void* stream, uint32_t* err_out);
 
 /* Scan backward: replaces cpp_ewma_cuda.ltv_fused_concat_head_major_register_cast_blelloch_scan_cuda_backward
  * (reference cpp_ewma/src/ltv_fused_concat_head_major_register_cast_blelloch_scan_cuda_backward.cu:882-976;
@@ -302,7 +310,9 @@ LTVQKV_API int ltvqkv_workspace_error(void* workspace, void* stream, uint32_t* e
 /* Failure-path check (no reference counterpart): launches one thread that waits on a
  * workspace word nothing sets, gives up after limit_ns (at most 5 s), records
  * LTVQKV_ERR_TIMEOUT in the workspace and returns; read it with ltvqkv_workspace_error.
- * This is the bounded-wait path of every inter-CTA wait in the library. */
+ * This is the bounded-wait path of every inter-CTA wait in the library. With workspace NULL the
+ * wait records into ltvqkv_scan_fwd_noalloc's array on the current device instead (read it with
+ * ltvqkv_scan_noalloc_error). */
 LTVQKV_API int ltvqkv_debug_wait_timeout(void* workspace, uint64_t limit_ns, void* stream);
 
 #ifdef __cplusplus

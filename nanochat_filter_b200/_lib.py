@@ -37,6 +37,7 @@ EXPORTED_SYMBOLS = (
     "ltvqkv_workspace_error",
     "ltvqkv_debug_wait_timeout",
     "ltvqkv_scan_fwd_noalloc",
+    "ltvqkv_scan_noalloc_error",
     "ltvqkv_proj_scan_fwd",
     "ltvqkv_proj_scan_fwd_ckpt",
     "ltvqkv_lookback_workspace_bytes",
@@ -120,6 +121,8 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.ltvqkv_scan_fwd_noalloc.restype = _i
     lib.ltvqkv_scan_fwd_noalloc.argtypes = [_i, _vp, _i64, _i64, _i64, _vp, _pf, _vp, _vp, _vp,
                                             _i, _i, _i, _i, _i, _i, _i, _vp]
+    lib.ltvqkv_scan_noalloc_error.restype = _i
+    lib.ltvqkv_scan_noalloc_error.argtypes = [_vp, ctypes.POINTER(ctypes.c_uint32)]
     lib.ltvqkv_debug_wait_timeout.restype = _i
     lib.ltvqkv_debug_wait_timeout.argtypes = [_vp, ctypes.c_uint64, _vp]
 
@@ -206,6 +209,16 @@ def workspace_error(ws: torch.Tensor) -> int:
     err = ctypes.c_uint32(0)
     check(lib.ltvqkv_workspace_error(ws.data_ptr(), stream_handle(ws.device), ctypes.byref(err)),
           "ltvqkv_workspace_error")
+    return int(err.value)
+
+
+def noalloc_error(device: torch.device) -> int:
+    """Reads and clears the error word of ltvqkv_scan_fwd_noalloc's array on `device` (synchronises
+    the device's current stream)."""
+    lib = load()
+    err = ctypes.c_uint32(0)
+    with torch.cuda.device(device):
+        check(lib.ltvqkv_scan_noalloc_error(stream_handle(device), ctypes.byref(err)), "ltvqkv_scan_noalloc_error")
     return int(err.value)
 
 

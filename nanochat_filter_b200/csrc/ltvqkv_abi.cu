@@ -146,8 +146,12 @@ __global__ void wait_never_set_kernel(ltvqkv::WorkspaceHeader* ws, unsigned long
 }  // namespace
 
 extern "C" int ltvqkv_debug_wait_timeout(void* workspace, uint64_t limit_ns, void* stream) {
-  if (!workspace) return LTVQKV_ERR_WORKSPACE;
   if (limit_ns > 5000000000ull) return LTVQKV_ERR_INVALID_ARG;
+  if (!workspace) {
+    // no workspace: the wait records into the allocation-free entry point's array on this device
+    const int st = ltvqkv_host::noalloc_scratch(&workspace);
+    if (st != LTVQKV_OK) return st;
+  }
   wait_never_set_kernel<<<1, 1, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<ltvqkv::WorkspaceHeader*>(workspace), (unsigned long long)limit_ns);
   return ltvqkv_host::check_launch();

@@ -453,6 +453,8 @@ bool encode_tiled_map(CUtensorMap* map, CUtensorMapDataType dtype, int rank, con
 int num_sms();
 void set_last_cuda_error(cudaError_t e);
 int check_launch();  // returns LTVQKV_OK or LTVQKV_ERR_LAUNCH (and records the CUDA error text)
+// Device address of ltvqkv_scan_fwd_noalloc's fixed array on the current device (ltvqkv_scan.cu).
+int noalloc_scratch(void** out);
 inline bool valid_dtype(int dtype) { return dtype == LTVQKV_DTYPE_F32 || dtype == LTVQKV_DTYPE_BF16; }
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 }  // namespace ltvqkv_host

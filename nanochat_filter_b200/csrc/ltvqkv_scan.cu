@@ -21,6 +21,7 @@
 // do not depend on timing). Tiles are drawn from a ticket counter in chunk-major order, so every
 // tile waited on was scheduled earlier (no deadlock); each spin is bounded.
 #include <algorithm>
+#include <cstddef>
 #include <mutex>
 
 #include "ltvqkv_common.cuh"
@@ -1132,6 +1133,32 @@ std::mutex g_noalloc_mu;
 void* g_noalloc_ptr[kNoAllocMaxDevices] = {};
 }  // namespace
 
+namespace ltvqkv_host {
+// Device address of the allocation-free array on the current device, looked up once per device with
+// cudaGetSymbolAddress (the host-side name of a __device__ array is not a device address).
+int noalloc_scratch(void** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e);
+    return LTVQKV_ERR_LAUNCH;
+  }
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return LTVQKV_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  void* ptr = g_noalloc_ptr[dev];
+  if (ptr == nullptr) {
+    e = cudaGetSymbolAddress(&ptr, g_scan_noalloc_scratch);
+    if (e != cudaSuccess || ptr == nullptr) {
+      set_last_cuda_error(e);
+      return LTVQKV_ERR_LAUNCH;
+    }
+    g_noalloc_ptr[dev] = ptr;
+  }
+  *out = ptr;
+  return LTVQKV_OK;
+}
+}  // namespace ltvqkv_host
+
 extern "C" int ltvqkv_scan_fwd_noalloc(int dtype, const void* combined, int64_t sc_b, int64_t sc_t, int64_t sc_e,
                                        const void* inits, const float* logit_bias, void* out_q, void* out_k,
                                        void* out_v, int B, int T, int NH, int NKVH, int Da, int r, int use_sigmoid,
@@ -1143,32 +1170,32 @@ extern "C" int ltvqkv_scan_fwd_noalloc(int dtype, const void* combined, int64_t 
   const ScanWorkspaceLayout wl = scan_ws_layout(make_geometry(B, T, NH, NKVH, Da, r, kFwdBudget));
   const ScanWorkspaceLayout wx = scan_ws_layout(fast_geometry(B, T, NH, NKVH, Da, r));
   if (std::max(wl.total, wx.total) > kNoAllocScratchBytes) return LTVQKV_ERR_TOO_LARGE;
-  int dev = -1;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) {
-    ltvqkv_host::set_last_cuda_error(e);
-    return LTVQKV_ERR_LAUNCH;
-  }
-  if (dev < 0 || dev >= kNoAllocMaxDevices) return LTVQKV_ERR_UNSUPPORTED;
   void* ptr = nullptr;
-  {
-    std::lock_guard<std::mutex> lock(g_noalloc_mu);
-    ptr = g_noalloc_ptr[dev];
-    if (ptr == nullptr) {
-      e = cudaGetSymbolAddress(&ptr, g_scan_noalloc_scratch);
-      if (e != cudaSuccess || ptr == nullptr) {
-        ltvqkv_host::set_last_cuda_error(e);
-        return LTVQKV_ERR_LAUNCH;
-      }
-      g_noalloc_ptr[dev] = ptr;
-    }
-  }
-  // Header (ticket/exit counters, epoch) and the look-back flags must start at zero.
-  e = cudaMemsetAsync(ptr, 0, std::max(wl.aggA, wx.aggA), reinterpret_cast<cudaStream_t>(stream));
+  st = ltvqkv_host::noalloc_scratch(&ptr);
+  if (st != LTVQKV_OK) return st;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  // The ticket/exit counters and the epoch (the header's first 12 bytes) and the look-back flags must
+  // start at zero. The header's error words are left alone: a timed-out wait of an earlier call stays
+  // recorded until ltvqkv_scan_noalloc_error reads it.
+  static_assert(offsetof(WorkspaceHeader, error) == 12, "counters and epoch precede the error word");
+  cudaError_t e = cudaMemsetAsync(ptr, 0, offsetof(WorkspaceHeader, error), s);
+  const size_t flags_end = std::max(wl.aggA, wx.aggA);
+  if (e == cudaSuccess)
+    e = cudaMemsetAsync(static_cast<char*>(ptr) + sizeof(WorkspaceHeader), 0, flags_end - sizeof(WorkspaceHeader), s);
   if (e != cudaSuccess) {
     ltvqkv_host::set_last_cuda_error(e);
     return LTVQKV_ERR_LAUNCH;
   }
   return ltvqkv_scan_fwd(dtype, combined, sc_b, sc_t, sc_e, inits, logit_bias, out_q, out_k, out_v, B, T, NH, NKVH,
                          Da, r, use_sigmoid, ptr, kNoAllocScratchBytes, stream);
+}
+
+// Error word of the allocation-free array: a bounded device-side wait inside ltvqkv_scan_fwd_noalloc
+// that gave up records LTVQKV_ERR_TIMEOUT there; this reads and clears it like ltvqkv_workspace_error.
+extern "C" int ltvqkv_scan_noalloc_error(void* stream, uint32_t* err_out) {
+  if (!err_out) return LTVQKV_ERR_INVALID_ARG;
+  void* ptr = nullptr;
+  const int st = ltvqkv_host::noalloc_scratch(&ptr);
+  if (st != LTVQKV_OK) return st;
+  return ltvqkv_workspace_error(ptr, stream, err_out);
 }

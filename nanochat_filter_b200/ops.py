@@ -543,11 +543,14 @@ def _proj_scan_forward_kernel(x, weight, inits, logit_bias, combined, out_q, out
 
 def _ckpt_shape(x, NH, NKVH, da, r):
     """Shape of the state checkpoints the one-kernel forward writes for these sizes, or (0,) where it
-    does not apply (bf16, head dim 128 in one decay group, T % 32 == 0, and at least two
-    (batch, head) rows per SM)."""
-    B, T, _ = x.shape
+    does not apply. Mirrors the library's condition for that kernel (ltvqkv_proj_scan_fwd_ckpt): bf16,
+    head dim 128 in one decay group, T % 32 == 0, C % 8 == 0, at most 128 heads and at least two
+    (batch, head) rows per SM; its 16-byte alignment condition holds because _proj_scan_op hands
+    the kernel aligned x and weight (copies where the caller's are not)."""
+    B, T, C = x.shape
     H, D = NH + 2 * NKVH, da * r
-    if x.dtype != torch.bfloat16 or D != 128 or da != 1 or T % 32 != 0 or T == 0 or not 1 <= H <= 128:
+    if (x.dtype != torch.bfloat16 or D != 128 or da != 1 or T % 32 != 0 or T == 0 or C % 8 != 0 or C == 0
+            or not 1 <= H <= 128):
         return (0,)
     dev = x.device if x.device.type == "cuda" else None
     sms = (torch.cuda.get_device_properties(dev if dev is not None else torch.cuda.current_device())
@@ -567,6 +570,13 @@ def _proj_scan_op(x, weight, inits, logit_bias, NH, NKVH, da, r, use_sigmoid):
     shared = inits.dim() == 2
     inits_k = inits.to(x.dtype) if shared else inits  # the state starts from its value in x's dtype
     ckpt = torch.empty(_ckpt_shape(x, NH, NKVH, da, r), device=x.device, dtype=torch.float32)
+    if ckpt.numel():
+        # the one-kernel form reads x and W with TMA (16-byte aligned bases): realign offset views so
+        # that the checkpoint output the fake kernel promises is always written
+        if x.data_ptr() % 16:
+            x = x.clone()
+        if weight.dtype == x.dtype and weight.is_contiguous() and weight.data_ptr() % 16:
+            weight = weight.clone()
     if ckpt.numel() and _proj_scan_forward_kernel(x, weight, inits_k, logit_bias, combined, out_q, out_k, out_v, NH,
                                                   NKVH, da, r, use_sigmoid, ckpt):
         return combined, out_q, out_k, out_v, ckpt
@@ -594,7 +604,11 @@ def _scan_ckpt_backward(combined, inits, logit_bias, ckpt, grad_hq, grad_hk, gra
     _check_scan_inputs(combined, inits.unsqueeze(0).expand(B, -1, -1) if shared else inits, logit_bias, NH, NKVH,
                        da, r)
     inits = inits.contiguous()
+    if inits.data_ptr() % 16:  # the kernel loads initial states with 16-byte bulk copies
+        inits = inits.clone()
     logit_bias = logit_bias.contiguous()
+    # the row-streaming kernel's layout for the upstream gradients (unit channel stride, 16-byte rows)
+    grad_hq, grad_hk, grad_hv = (g if _rows_ok(g) else g.contiguous() for g in (grad_hq, grad_hk, grad_hv))
     if not grad_inits.is_contiguous() or not grad_logit_bias.is_contiguous():
         raise RuntimeError("grad_inits and grad_logit_bias must be contiguous")
     if shared and (tuple(grad_inits.shape) != (H, D) or grad_inits.dtype != torch.float32):
@@ -649,6 +663,9 @@ def _ps_backward(ctx, grad_comb, grad_hq, grad_hk, grad_hv, _grad_ckpt):
     # [B, F, T] memory is the projection's grad_out), then the projection backward. Where the
     # forward wrote state checkpoints the scan backward replays its outputs from them (equal results,
     # less memory traffic) instead of reading them.
+    # Only operators here (no library calls, no pointer checks): under torch.compile AOTAutograd
+    # traces this function with fake tensors. The checkpoints are non-empty exactly where the
+    # one-kernel forward ran, and that kernel's shapes are ones the checkpoint backward takes.
     x, weight, comb, inits, logit_bias, hq, hk, hv, ckpt = ctx.saved_tensors
     NH, NKVH, da, r = ctx.args
     B = x.shape[0]
@@ -659,15 +676,14 @@ def _ps_backward(ctx, grad_comb, grad_hq, grad_hk, grad_hv, _grad_ckpt):
     grad_hk = torch.zeros_like(hk) if grad_hk is None else grad_hk
     grad_hv = torch.zeros_like(hv) if grad_hv is None else grad_hv
     grad_combined = torch.empty_like(combined)
-    rc = _lib.ERR_UNSUPPORTED
     if ckpt.numel():
-        gq, gk, gv = (g if _rows_ok(g) else g.contiguous() for g in (grad_hq, grad_hk, grad_hv))
         grad_inits = (torch.empty(inits_k.shape, device=x.device, dtype=torch.float32) if shared
                       else torch.empty_like(inits_k, memory_format=torch.contiguous_format))
         grad_logit_bias = torch.empty_like(logit_bias, memory_format=torch.contiguous_format)
-        rc = _scan_ckpt_backward(combined, inits_k, logit_bias, ckpt, gq, gk, gv, grad_combined, grad_inits,
-                                 grad_logit_bias, NH, NKVH, da, r, ctx.use_sigmoid)
-    if rc == _lib.ERR_UNSUPPORTED:
+        torch.ops.nanochat_cuda.ltv_scan_ckpt_backward_kernel(combined, inits_k, logit_bias, ckpt, grad_hq, grad_hk,
+                                                              grad_hv, grad_combined, grad_inits, grad_logit_bias, NH,
+                                                              NKVH, da, r, ctx.use_sigmoid)
+    else:
         ib = inits_k.unsqueeze(0).expand(B, -1, -1).contiguous() if shared else inits_k
         grad_inits = torch.empty_like(ib, memory_format=torch.contiguous_format)
         grad_logit_bias = torch.zeros_like(logit_bias, memory_format=torch.contiguous_format)
@@ -676,8 +692,6 @@ def _ps_backward(ctx, grad_comb, grad_hq, grad_hk, grad_hv, _grad_ckpt):
             grad_logit_bias, NH, NKVH, da, r, 32, 2, 8, ctx.use_sigmoid)
         if shared:
             grad_inits = grad_inits.float().sum(0)
-    else:
-        _lib.check(rc, "ltvqkv_scan_bwd_ckpt")
     if shared:
         grad_inits = grad_inits.to(inits.dtype)
     grad_out = grad_combined.transpose(1, 2)

@@ -110,8 +110,42 @@ def scan_bwd(combined, inits, logit_bias, gq, gk, gv, NH, NKVH, Da, r, use_sigmo
     return gc, gi, gb
 
 
+def _qz(a, bf16):
+    return round_bf16(a) if bf16 else _f32(a)
+
+
 def gemm_fwd(x, w, bf16):
-    """out[b,f,t] = sum_k x[b,t,k] w[f,k] (double accumulation, rounded to dtype)."""
+    """out[b,f,t] = sum_k x[b,t,k] w[f,k] (double accumulation, rounded to dtype): the reference's
+    fused_linear_transpose_reference (ltv_reference_ops.py:299-308, matmul(x, W^T).transpose(1, 2)),
+    contracted in float64 by numpy's BLAS one sequence at a time, then rounded once."""
+    x, w = _f32(x), _f32(w)
+    B, T, K = x.shape
+    F = w.shape[0]
+    out = np.empty((B, F, T), np.float32)
+    w64 = w.astype(np.float64)
+    for b in range(B):
+        out[b] = _qz(w64 @ x[b].astype(np.float64).T, bf16)
+    return out
+
+
+def gemm_bwd(x, w, g, bf16_x, bf16_w):
+    """g [B,F,T] -> (grad_x [B,T,K] = sum_f g w, grad_w [F,K] = sum_b sum_t g x), the gradients of
+    gemm_fwd, contracted in float64 (numpy BLAS) and rounded once to their dtypes."""
+    x, w, g = _f32(x), _f32(w), _f32(g)
+    B, T, K = x.shape
+    F = w.shape[0]
+    gx = np.empty((B, T, K), np.float32)
+    gw = np.zeros((F, K), np.float64)
+    w64 = w.astype(np.float64)
+    for b in range(B):
+        gb = g[b].astype(np.float64)
+        gx[b] = _qz(gb.T @ w64, bf16_x)
+        gw += gb @ x[b].astype(np.float64)
+    return gx, _qz(gw, bf16_w)
+
+
+def gemm_fwd_c(x, w, bf16):
+    """gemm_fwd by ltv_oracle.c's loops (double accumulation; the pinned C restatement)."""
     x, w = _f32(x), _f32(w)
     B, T, K = x.shape
     F = w.shape[0]
@@ -120,8 +154,8 @@ def gemm_fwd(x, w, bf16):
     return out
 
 
-def gemm_bwd(x, w, g, bf16_x, bf16_w):
-    """g [B,F,T] -> (grad_x [B,T,K], grad_w [F,K])."""
+def gemm_bwd_c(x, w, g, bf16_x, bf16_w):
+    """gemm_bwd by ltv_oracle.c's loops."""
     x, w, g = _f32(x), _f32(w), _f32(g)
     B, T, K = x.shape
     F = w.shape[0]

@@ -264,3 +264,27 @@ def test_shared_initial_state_autograd(cuda_device):
         assert a.dtype == b.dtype and torch.equal(a, b), n
     assert gi_got.dtype == torch.float32
     torch.testing.assert_close(gi_got, gi_ref, rtol=2 ** -8, atol=1e-5 * gi_ref.abs().max().item())
+
+
+@pytest.mark.parametrize("C,offset", [(124, 0), (128, 0), (128, 8)])
+def test_proj_scan_fake_and_real_checkpoint_shapes_agree(cuda_device, C, offset):
+    """The fake kernel's checkpoint shape equals the real op's: C % 8 != 0 (no one-kernel form, empty
+    checkpoint), and x at an 8-element (16-byte) offset and at a 2-element (4-byte) one (the op
+    realigns it, so the checkpoints the fake promises are written)."""
+    B, T, NH, NKVH = 32, 64, 6, 6
+    H, F = NH + 2 * NKVH, (NH + 2 * NKVH) * 129
+    gen = torch.Generator(device=cuda_device).manual_seed(C + offset)
+    for off in (offset, 2):
+        buf = torch.randn(B * T * C + off, generator=gen, device=cuda_device).to(torch.bfloat16)
+        x = buf[off:].view(B, T, C)
+        w = (torch.randn(F, C, generator=gen, device=cuda_device) / C ** 0.5).to(torch.bfloat16)
+        init = torch.zeros(H, 128, device=cuda_device)
+        bias = torch.zeros(H, 1, device=cuda_device)
+        real = OPS.ltv_proj_scan_cuda_op(x, w, init, bias, NH, NKVH, 1, 128, True)
+        with torch.device("meta"):
+            fake = OPS.ltv_proj_scan_cuda_op(torch.empty(B, T, C, dtype=torch.bfloat16),
+                                             torch.empty(F, C, dtype=torch.bfloat16), torch.empty(H, 128),
+                                             torch.empty(H, 1), NH, NKVH, 1, 128, True)
+        for a, b in zip(real, fake):
+            assert tuple(a.shape) == tuple(b.shape) and a.dtype == b.dtype
+        assert (real[4].numel() > 0) == (C % 8 == 0)

@@ -112,6 +112,42 @@ def test_filter_on_meta_device_traces_shapes():
     assert q.shape == (2, 64, 6, 128) and k.shape == (2, 64, 6, 128) and v.shape == (2, 64, 6, 128)
 
 
+@pytest.mark.parametrize("B,T,C", [(32, 64, 128), (2, 96, 256)])
+def test_filter_compiles_fullgraph_on_meta(B, T, C):
+    """Dynamo traces the filter's forward with fullgraph=True (a graph break raises) through the fake
+    kernels, and AOTAutograd traces the backward formula (operators only, no library calls), on the
+    one-kernel shape (B * heads >= 2 * SMs: checkpoints, shared initial state) and on the two-op one."""
+    NH, NKVH, D, r = 6, 6, 128, 128
+    torch._dynamo.reset()
+    with torch.device("meta"):
+        f = nf.LtvCudaFusedConcatHeadMajorRegisterCastBlellochScanQkvFilter(NH, NKVH, D, r)
+        f.c = torch.nn.Linear(C, f.c.out_features, bias=False)
+        x = torch.empty(B, T, C, dtype=torch.bfloat16).requires_grad_(True)
+        grads = [torch.empty(B, T, n, D, dtype=torch.bfloat16) for n in (NH, NKVH, NKVH)]
+    cf = torch.compile(f, fullgraph=True, backend="aot_eager")
+    q, k, v = cf(x, nf.LtvInitValues())
+    assert q.shape == (B, T, NH, D) and k.shape == (B, T, NKVH, D) and v.shape == (B, T, NKVH, D)
+    torch.autograd.backward([q, k, v], grads)
+    assert x.grad.shape == x.shape and f.c.weight.grad.shape == f.c.weight.shape
+    assert f.init_param.grad.shape == (NH + 2 * NKVH, D) and f.logit_bias.grad.shape == (NH + 2 * NKVH, 1)
+
+
+def test_ckpt_fake_shape_mirrors_the_kernel_condition():
+    """The fake kernel promises checkpoints only where the one-kernel forward runs: C % 8 != 0, a
+    head dim other than 128, fp32 or T % 32 != 0 give the empty checkpoint."""
+    from nanochat_filter_b200 import ops
+
+    def shape(B, T, C, dtype=torch.bfloat16, NH=6, NKVH=6, da=1, r=128):
+        return ops._ckpt_shape(torch.empty(B, T, C, device="meta", dtype=dtype), NH, NKVH, da, r)
+
+    assert shape(32, 64, 128) == (32, 18, 2, 128)
+    assert shape(32, 64, 124) == (0,)                       # C % 8 != 0
+    assert shape(32, 64, 128, dtype=torch.float32) == (0,)
+    assert shape(32, 48, 128) == (0,)                       # T % 32 != 0
+    assert shape(32, 64, 128, da=2, r=64) == (0,)           # two decay groups per head
+    assert shape(2, 64, 128) == (0,)                        # fewer than two rows per SM
+
+
 def test_no_cpu_fallback():
     x = torch.randn(1, 8, 16)
     w = torch.randn(24, 16)
