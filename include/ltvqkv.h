@@ -272,6 +272,11 @@ LTVQKV_API int ltvqkv_proj_scan_fwd_ckpt(int dtype, const void* x, const void* w
  * grad_out [B, F, T] with strides (go_b, go_f, go_t): contiguous (F*T, T, 1) or the
  * transposed view (F*T, 1, F). x, weight, grad_x use `dtype`; grad_weight uses
  * grad_weight_dtype (fp32 master weights under autocast). One launch computes both.
+ * An fp32 grad_weight over an even number of batches is reduced as two batch halves whose
+ * partial sums the kernel combines in place (no zero fill, no floating-point atomics;
+ * deterministic) through counters kept in the workspace after its header: use a workspace of
+ * ltvqkv_gemm_workspace_bytes() that no scan entry point shares (their look-back flags stay
+ * set between calls), zero-filled once.
  */
 LTVQKV_API int ltvqkv_gemm_bwd(int dtype, const void* x, const void* weight,
                     const void* grad_out, int64_t go_b, int64_t go_f, int64_t go_t,

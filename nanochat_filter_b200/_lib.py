@@ -189,9 +189,12 @@ _ws_lock = threading.Lock()
 _workspaces: dict = {}
 
 
-def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+def workspace(device: torch.device, nbytes: int, kind: str = "shared") -> torch.Tensor:
+    """The zero-initialised workspace of (device, current stream, kind). ltvqkv_gemm_bwd keeps counters
+    after the header that must read zero at each launch, so it takes kind="gemm_bwd" (a buffer the
+    scan entry points, whose look-back flags stay set between calls, never use)."""
     dev = torch.device(device)
-    key = (dev.index if dev.index is not None else torch.cuda.current_device(), stream_handle(dev))
+    key = (dev.index if dev.index is not None else torch.cuda.current_device(), stream_handle(dev), kind)
     with _ws_lock:
         ws = _workspaces.get(key)
         if ws is None or ws.numel() < nbytes:

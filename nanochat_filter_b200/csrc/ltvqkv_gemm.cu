@@ -6,9 +6,9 @@
 //   backward (reference cpp_ewma/src/fused_linear_transpose_backward.cu:22-132, which issues
 //   2*B serial cuBLAS calls): in ONE launch
 //     dW[f, k]    = sum_b sum_t g[b, f, t] x[b, t, k]   tiles: M = k, N = f, K = t over the batches;
-//                   the batches are split in two halves whose fp32 tiles are added into a zeroed
-//                   dW with red.global.add (two addends onto 0.0: order-independent, so the result
-//                   is the same on every run)
+//                   fp32 dW takes the batches in two halves: the half that finishes first stores
+//                   its tile, the other adds its own to it (two addends, so the result is the same
+//                   on every run; no zero fill, no floating-point atomics)
 //     dx[b, t, k] = sum_f g[b, f, t] W[f, k]           tiles: M = t, N = k, K = f
 // The backward's tensor-core kernel (CTA pairs, tcgen05 cta_group::2) is in ltvqkv_gemm_pair.cuh.
 #include <algorithm>
@@ -106,6 +106,20 @@ using namespace ltvqkv;
 // Host side
 // ------------------------------------------------------------------------------------------
 namespace {
+
+// MN-major operand of the pair GEMM as one 16 KB box: element (mn, k, batch) of a tensor whose mn
+// index is contiguous (extent mn_ext, a multiple of 64), k rows `k_pitch` bytes apart and batches
+// `b_pitch` bytes apart, viewed as 4-D {64 mn_lo, k, mn_ext / 64 mn_hi, batch}; box {64, 64, 2, 1}
+// fills shared memory as [mn_hi][k][mn_lo] with the 128-byte swizzle, the canonical MN-major layout
+// of two 64-wide blocks that two separate 3-D boxes would write.
+bool make_mn_blk_map(CUtensorMap* m, const void* base, uint64_t mn_ext, uint64_t k_ext, uint64_t batches,
+                     uint64_t k_pitch, uint64_t b_pitch) {
+  const uint64_t dims[4] = {64, k_ext, mn_ext / 64, batches};
+  const uint64_t strides[3] = {k_pitch, 128, b_pitch};
+  const uint32_t box[4] = {64, 64, 2, 1};
+  return ltvqkv_host::encode_tiled_map(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, base, dims, strides, box,
+                                       CU_TENSOR_MAP_SWIZZLE_128B);
+}
 
 // 3-D tiled map: dims (d0 innermost, d1, d2), byte strides of d1 and d2, box (box0, box1, 1).
 bool make_map(CUtensorMap* m, bool f32, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1,
@@ -227,7 +241,10 @@ __global__ void zero_fill_kernel(void* p, long long nbytes) {
 
 }  // namespace
 
-extern "C" size_t ltvqkv_gemm_workspace_bytes(void) { return 256; }
+// Header, then the per-(output tile, CTA, warp) counters of the projection backward's two-split fp32
+// dW (kOutColsF32Pair): enough for 2048 dW tiles of 256 x 256 (larger problems take one split).
+constexpr size_t kGemmCombineWords = 2048 * 8;
+extern "C" size_t ltvqkv_gemm_workspace_bytes(void) { return 256 + kGemmCombineWords * 4; }
 
 extern "C" int ltvqkv_gemm_fwd(int dtype, const void* x, const void* weight, void* out, int B, int T, int K, int F,
                                void* workspace, size_t workspace_bytes, void* stream) {
@@ -423,13 +440,17 @@ extern "C" int ltvqkv_gemm_bwd(int dtype, const void* x, const void* weight, con
   prm.ws = reinterpret_cast<WorkspaceHeader*>(workspace);
   CUtensorMap maps[4];
   // Problem 0: dW tiles. M = k (lanes), N = f, reduction over the B batches x T tokens; fp32 dW
-  // takes the batches in two halves added into the zeroed output.
+  // takes the batches in two halves (two tiles per output tile, so the long dW tiles balance the dx
+  // tiles across the clusters), combined by the epilogues: the first half to finish stores, the
+  // second adds (no zero fill, no floating-point atomics).
   PairProblem& w = prm.p[0];
-  const int splits = (gw_f32 && B % 2 == 0) ? 2 : 1;
+  const long long dw_tiles = (long long)((K + 255) / 256) * ((F + kPairBN - 1) / kPairBN);
+  const int splits = (gw_f32 && B % 2 == 0 && dw_tiles * 8 <= (long long)kGemmCombineWords) ? 2 : 1;
   w.M = K; w.N = F; w.out_batches = 1; w.splits = splits; w.red_batches = B / splits;
   w.a_mn = 1; w.b_mn = go_contig ? 0 : 1; w.a_bmode = 2; w.b_bmode = 2;
-  w.out_mode = splits == 2 ? kOutColsF32Add : (gw_f32 ? kOutColsF32 : kOutColsBf16);
+  w.out_mode = splits == 2 ? kOutColsF32Pair : (gw_f32 ? kOutColsF32 : kOutColsBf16);
   w.out = grad_weight; w.out_ld = K; w.out_bs = 0;  // dW [F][K]
+  w.combine = reinterpret_cast<unsigned int*>(reinterpret_cast<char*>(workspace) + 256);
   finalize_pair(w, T);
   // Problem 1: dx tiles. M = t (lanes), N = k, reduction over F.
   PairProblem& d = prm.p[1];
@@ -438,21 +459,28 @@ extern "C" int ltvqkv_gemm_bwd(int dtype, const void* x, const void* weight, con
   d.out = grad_x; d.out_ld = K; d.out_bs = (long long)T * K;  // dx [B][T][K]
   finalize_pair(d, F);
   bool ok = true;
+  // MN-major operands whose contiguous extent is a multiple of 64 load as one 4-D box per stage
+  w.a_blk = K % 64 == 0;
+  w.b_blk = !go_contig && F % 64 == 0;
+  d.a_blk = go_contig && T % 64 == 0;
+  d.b_blk = K % 64 == 0;
   // x as [B][T][K]: MN-major A operand of dW (m = k, k = t).
-  ok = ok && make_map(&maps[0], false, x, K, T, B, (uint64_t)K * 2, (uint64_t)T * K * 2, 64, 64);
+  ok = ok && (w.a_blk ? make_mn_blk_map(&maps[0], x, K, T, B, (uint64_t)K * 2, (uint64_t)T * K * 2)
+                      : make_map(&maps[0], false, x, K, T, B, (uint64_t)K * 2, (uint64_t)T * K * 2, 64, 64));
   if (go_contig) {
     // g as [B][F][T]: K-major B of dW (n = f, k = t), MN-major A of dx (m = t, k = f).
     ok = ok && make_map(&maps[1], false, grad_out, T, F, B, (uint64_t)T * 2, (uint64_t)go_b * 2, 64, 128);
-    ok = ok && make_map(&maps[2], false, grad_out, T, F, B, (uint64_t)T * 2, (uint64_t)go_b * 2, 64, 64);
+    ok = ok && (d.a_blk ? make_mn_blk_map(&maps[2], grad_out, T, F, B, (uint64_t)T * 2, (uint64_t)go_b * 2)
+                        : make_map(&maps[2], false, grad_out, T, F, B, (uint64_t)T * 2, (uint64_t)go_b * 2, 64, 64));
   } else {
     // g as [B][T][F]: MN-major B of dW (n = f, k = t), K-major A of dx (m = t, k = f).
-    ok = ok && make_map(&maps[1], false, grad_out, F, T, B, (uint64_t)F * 2, (uint64_t)go_b * 2, 64, 64);
+    ok = ok && (w.b_blk ? make_mn_blk_map(&maps[1], grad_out, F, T, B, (uint64_t)F * 2, (uint64_t)go_b * 2)
+                        : make_map(&maps[1], false, grad_out, F, T, B, (uint64_t)F * 2, (uint64_t)go_b * 2, 64, 64));
     ok = ok && make_map(&maps[2], false, grad_out, F, T, B, (uint64_t)F * 2, (uint64_t)go_b * 2, 64, 128);
   }
   // W as [F][K]: MN-major B operand of dx (n = k, k = f).
-  ok = ok && make_map(&maps[3], false, weight, K, F, 1, (uint64_t)K * 2, (uint64_t)K * F * 2, 64, 64);
+  ok = ok && (d.b_blk ? make_mn_blk_map(&maps[3], weight, K, F, 1, (uint64_t)K * 2, (uint64_t)K * F * 2)
+                      : make_map(&maps[3], false, weight, K, F, 1, (uint64_t)K * 2, (uint64_t)K * F * 2, 64, 64));
   if (!ok) return LTVQKV_ERR_LAUNCH;
-  if (splits == 2 && cudaMemsetAsync(grad_weight, 0, (size_t)F * K * 4, s) != cudaSuccess)
-    return ltvqkv_host::check_launch();
   return launch_pair(prm, maps, s);
 }

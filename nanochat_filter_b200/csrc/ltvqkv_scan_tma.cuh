@@ -2,7 +2,8 @@
 // ltvqkv_scan.cu): combined / grad_combined are the transposed view of a contiguous [B, F, T]
 // buffer, so one 2-D tensor map [B*F rows, T columns] addresses every head's value and logit rows.
 //
-// A persistent CTA owns whole (batch, head) rows, drawn from a ticket counter, and walks each row
+// A persistent CTA owns whole (batch, head) rows (the forward draws them from a ticket counter, the
+// backward takes rows blockIdx.x, blockIdx.x + gridDim.x, ...: rows cost the same), and walks each row
 // chunk by chunk (kTT = 32 or 64 tokens; forward in time order, backward in reverse). Consumer
 // thread c owns channel c and walks all kTT tokens of a chunk, so the carry never leaves its
 // register: no look-back, no inter-CTA communication, results fixed by construction. One producer
@@ -318,19 +319,24 @@ __global__ void __launch_bounds__(kD / 2 + (kCkpt ? 64 : 32), row_bwd_min_blocks
   __syncthreads();
 
   if (warp == ncons / 32) {
-    // ---------------- producer: rows from the ticket counter, chunks in reverse time order ----------------
-    if (lane == 0) {
-      tma_prefetch_desc(&tm_u);
-      tma_prefetch_desc(&tm_l);
+    // ---------------- producers: rows blockIdx.x, + gridDim.x, ...; chunks in reverse time order ----------------
+    // Lanes 0-3 walk the same chunk sequence and each issues one of a chunk's copies (lane 0: the
+    // value tile, with the stage's bookkeeping; 1: the logit rows; 2: the gradient tile; 3: the
+    // state tile or checkpoint, and the initial state): one thread issues about one bulk-tensor copy
+    // per few hundred cycles, so the four land together instead of one after another.
+    if (lane < 4) {
+      if (lane == 0) {
+        tma_prefetch_desc(&tm_u);
+        tma_prefetch_desc(&tm_l);
+      }
       int i = 0;
       bool ok = true;
-      while (ok) {
-        int row = (int)draw_ticket(a.ws);
-        if (row >= a.nrows) row = -1;
-        const int nch = row < 0 ? 1 : a.nchunks;
-        const int b = row < 0 ? 0 : row / a.H, h = row < 0 ? 0 : row % a.H;
+      for (int row = (int)blockIdx.x; ok; row += (int)gridDim.x) {
+        const bool end = row >= a.nrows;
+        const int nch = end ? 1 : a.nchunks;
+        const int b = end ? 0 : row / a.H, h = end ? 0 : row % a.H;
         int which = 0, hloc = 0, nheads = 0;
-        if (row >= 0) split_head(h, a.NH, a.NKVH, which, hloc, nheads);
+        if (!end) split_head(h, a.NH, a.NKVH, which, hloc, nheads);
         const int frow = b * a.F + h * (D + Da);
         const CUtensorMap* mg = which == 0 ? &tm_gq : (which == 1 ? &tm_gk : &tm_gv);
         const CUtensorMap* mh = which == 0 ? &tm_hq : (which == 1 ? &tm_hk : &tm_hv);
@@ -338,29 +344,37 @@ __global__ void __launch_bounds__(kD / 2 + (kCkpt ? 64 : 32), row_bwd_min_blocks
           const int st = i % S;
           const uint32_t ph = (uint32_t)(i / S) & 1u;
           if (!mbar_wait(&empty[st], ph ^ 1u, &abort_flag, a.ws, 0x7201)) { ok = false; break; }
-          RowTile& ti = info[st];
-          ti.row = row;
-          if (row < 0) {
-            mbar_arrive(&full[st]);
+          if (end) {
+            if (lane == 0) {
+              info[st].row = -1;
+              mbar_arrive(&full[st]);
+            }
             ok = false;
             break;
           }
           const int j = a.nchunks - 1 - q;
           const int t0 = j * kTT;
-          ti.b = b; ti.h = h; ti.j = j; ti.t0 = t0; ti.tlen = min(kTT, a.T - t0);
-          ti.which = which; ti.hloc = hloc; ti.nheads = nheads;
           uint8_t* sb = stages + st * sbytes;
-          const uint32_t hbytes = kCkpt ? (j > 0 ? D * 4 : 0) : kTT * D * 2;
-          const uint32_t bytes = (uint32_t)(D * kTT * 2 + Da * LB * 2 + kTT * D * 2 + hbytes + (q == 0 ? D * 2 : 0));
-          mbar_arrive_expect_tx(&full[st], bytes);
-          tma_load_2d(sb, &tm_u, &full[st], t0, frow);
-          tma_load_2d(sb + loff, &tm_l, &full[st], t0, frow + D);
-          tma_load_4d(sb + goff, mg, &full[st], 0, t0, hloc, b);
-          if (!kCkpt)
-            tma_load_4d(sb + hoff, mh, &full[st], 0, t0 - 1, hloc, b);
-          else if (j > 0)
-            bulk_load(sb + hoff, a.ckpt + (((long long)b * a.H + h) * a.nchunks + (j - 1)) * D, D * 4, &full[st]);
-          if (q == 0) bulk_load(sb + ioff, a.inits + (long long)b * a.inits_bs + (long long)h * D, D * 2, &full[st]);
+          if (lane == 0) {
+            RowTile& ti = info[st];
+            ti.row = row;
+            ti.b = b; ti.h = h; ti.j = j; ti.t0 = t0; ti.tlen = min(kTT, a.T - t0);
+            ti.which = which; ti.hloc = hloc; ti.nheads = nheads;
+            const uint32_t hbytes = kCkpt ? (j > 0 ? D * 4 : 0) : kTT * D * 2;
+            const uint32_t bytes = (uint32_t)(D * kTT * 2 + Da * LB * 2 + kTT * D * 2 + hbytes + (q == 0 ? D * 2 : 0));
+            mbar_arrive_expect_tx(&full[st], bytes);
+            tma_load_2d(sb, &tm_u, &full[st], t0, frow);
+          } else if (lane == 1) {
+            tma_load_2d(sb + loff, &tm_l, &full[st], t0, frow + D);
+          } else if (lane == 2) {
+            tma_load_4d(sb + goff, mg, &full[st], 0, t0, hloc, b);
+          } else {
+            if (!kCkpt)
+              tma_load_4d(sb + hoff, mh, &full[st], 0, t0 - 1, hloc, b);
+            else if (j > 0)
+              bulk_load(sb + hoff, a.ckpt + (((long long)b * a.H + h) * a.nchunks + (j - 1)) * D, D * 4, &full[st]);
+            if (q == 0) bulk_load(sb + ioff, a.inits + (long long)b * a.inits_bs + (long long)h * D, D * 2, &full[st]);
+          }
         }
       }
     }

@@ -325,7 +325,7 @@ def _fused_linear_transpose_backward_kernel(x, weight, grad_out, grad_x, grad_we
         (B, T, K), dtype=grad_out.dtype, device=x.device)
     if not grad_weight.is_contiguous():
         raise RuntimeError("grad_weight must be contiguous")
-    ws = _lib.workspace(x.device, L.ltvqkv_gemm_workspace_bytes())
+    ws = _lib.workspace(x.device, L.ltvqkv_gemm_workspace_bytes(), kind="gemm_bwd")
     gs = grad_out.stride()
     rc = L.ltvqkv_gemm_bwd(_lib.dtype_code(grad_out.dtype), xx.data_ptr(), w.data_ptr(), grad_out.data_ptr(),
                            gs[0], gs[1], gs[2], gx.data_ptr(), grad_weight.data_ptr(),

@@ -114,33 +114,34 @@ def _qz(a, bf16):
     return round_bf16(a) if bf16 else _f32(a)
 
 
-def gemm_fwd(x, w, bf16):
-    """out[b,f,t] = sum_k x[b,t,k] w[f,k] (double accumulation, rounded to dtype): the reference's
+def gemm_fwd(x, w, bf16, acc=np.float64):
+    """out[b,f,t] = sum_k x[b,t,k] w[f,k] (accumulated in `acc`, rounded to dtype): the reference's
     fused_linear_transpose_reference (ltv_reference_ops.py:299-308, matmul(x, W^T).transpose(1, 2)),
-    contracted in float64 by numpy's BLAS one sequence at a time, then rounded once."""
+    contracted by numpy's BLAS one sequence at a time, then rounded once. acc=np.float64 is the
+    oracle; acc=np.float32 is the reference's own arithmetic (torch / cuBLAS accumulate in fp32)."""
     x, w = _f32(x), _f32(w)
     B, T, K = x.shape
     F = w.shape[0]
     out = np.empty((B, F, T), np.float32)
-    w64 = w.astype(np.float64)
+    wa = w.astype(acc)
     for b in range(B):
-        out[b] = _qz(w64 @ x[b].astype(np.float64).T, bf16)
+        out[b] = _qz(wa @ x[b].astype(acc).T, bf16)
     return out
 
 
-def gemm_bwd(x, w, g, bf16_x, bf16_w):
+def gemm_bwd(x, w, g, bf16_x, bf16_w, acc=np.float64):
     """g [B,F,T] -> (grad_x [B,T,K] = sum_f g w, grad_w [F,K] = sum_b sum_t g x), the gradients of
-    gemm_fwd, contracted in float64 (numpy BLAS) and rounded once to their dtypes."""
+    gemm_fwd, contracted in `acc` (numpy BLAS) and rounded once to their dtypes."""
     x, w, g = _f32(x), _f32(w), _f32(g)
     B, T, K = x.shape
     F = w.shape[0]
     gx = np.empty((B, T, K), np.float32)
-    gw = np.zeros((F, K), np.float64)
-    w64 = w.astype(np.float64)
+    gw = np.zeros((F, K), acc)
+    wa = w.astype(acc)
     for b in range(B):
-        gb = g[b].astype(np.float64)
-        gx[b] = _qz(gb.T @ w64, bf16_x)
-        gw += gb @ x[b].astype(np.float64)
+        gb = g[b].astype(acc)
+        gx[b] = _qz(gb.T @ wa, bf16_x)
+        gw += gb @ x[b].astype(acc)
     return gx, _qz(gw, bf16_w)
 
 
@@ -165,14 +166,15 @@ def gemm_bwd_c(x, w, g, bf16_x, bf16_w):
     return gx, gw
 
 
-def layer_fwd_bwd(x, w, inits, logit_bias, gq, gk, gv, NH, NKVH, Da, r, bf16, use_sigmoid=True):
+def layer_fwd_bwd(x, w, inits, logit_bias, gq, gk, gv, NH, NKVH, Da, r, bf16, use_sigmoid=True, acc=np.float64):
     """Whole filtered-QKV layer, forward and backward, as the reference composes it:
     combined = W x^T (rounded to dtype), scan, then the scan backward and the projection
-    backward. Returns a dict of every output and gradient."""
-    comb = gemm_fwd(x, w, bf16)                       # [B, F, T]
+    backward. Returns a dict of every output and gradient. `acc`: the GEMMs' accumulation type
+    (float64: the oracle; float32: the reference's own fp32-accumulated arithmetic)."""
+    comb = gemm_fwd(x, w, bf16, acc)                  # [B, F, T]
     comb_btf = np.ascontiguousarray(comb.transpose(0, 2, 1))
     hq, hk, hv = scan_fwd(comb_btf, inits, logit_bias, NH, NKVH, Da, r, use_sigmoid, bf16)
     gc, gi, gb = scan_bwd(comb_btf, inits, logit_bias, gq, gk, gv, NH, NKVH, Da, r, use_sigmoid, bf16)
-    gx, gw = gemm_bwd(x, w, np.ascontiguousarray(gc.transpose(0, 2, 1)), bf16, False)
+    gx, gw = gemm_bwd(x, w, np.ascontiguousarray(gc.transpose(0, 2, 1)), bf16, False, acc)
     return dict(combined=comb, hq=hq, hk=hk, hv=hv, grad_combined=gc, grad_inits=gi, grad_logit_bias=gb,
                 grad_x=gx, grad_w=gw)

@@ -86,6 +86,23 @@ def max_rel_err(actual, expected, floor_frac=1e-3) -> float:
     return float((np.abs(a - e) / den).max())
 
 
+def max_rel_err_rms(actual, expected) -> float:
+    """max |a - e| / max(|e|, rms(e)): relative error with the absolute floor at the tensor's RMS
+    (the form of the reference's own kernel tests, |a - e| <= atol + rtol |e| with atol = rtol on
+    unit-scale data). A bf16 value that rounds to the neighbouring value in one implementation and
+    not in the other (fp32 vs float64 accumulation of a GEMM) moves every later state of the scan by
+    a fraction of that value's ulp; relative to entries far below the tensor's scale that is not
+    small, so the floor sits at the scale of the data."""
+    a = np.asarray(actual, dtype=np.float64)
+    e = np.asarray(expected, dtype=np.float64)
+    if e.size == 0:
+        return 0.0
+    rms = float(np.sqrt(np.mean(e * e)))
+    if rms == 0:
+        return float(np.abs(a).max())
+    return float((np.abs(a - e) / np.maximum(np.abs(e), rms)).max())
+
+
 def assert_allclose_np(actual, expected, rtol, atol, label=""):
     a = np.asarray(actual, dtype=np.float32)
     e = np.asarray(expected, dtype=np.float32)

@@ -14,10 +14,27 @@ gradient). Inputs follow benchmark configs 2 and 3:
   and logit_bias = -3;
 * the initial state: the filter's init_param, uniform(-0.5, 0.5), shared by the batch.
 
-Every output and gradient (q, k, v, dx, dW, d logit_bias, d init_param) is compared with
-oracle.layer_fwd_bwd (the reference's CPU algorithm, float64 GEMMs) elementwise:
-max |a - e| / max(|e|, 1e-2 * max|e|) <= 2e-2, the bf16 bound. The measured errors are printed
-(run with -s to see them).
+Two checks against the oracle (the reference's CPU algorithm, oracle.layer_fwd_bwd):
+
+1. Stage by stage, elementwise:
+   * the projection output `combined` (bf16) is within one bf16 ulp of the float64-accumulated
+     projection everywhere (or, for entries far below the data's scale, within 1e-4 of its RMS: the
+     fp32 accumulation error of C terms), and differs from it in at most 1e-3 of the entries;
+   * q, k, v, d logit_bias and d init_param are within 2e-2 of the oracle run from this build's own
+     `combined` (the scan forward and backward given the same projection output), with the floor of
+     the relative error at 1% of max|e|; dx and dW too, with their floor at the tensor's RMS: each
+     of their entries sums thousands of bf16 entries of the scan backward's output, whose rounding
+     flips (fp32 vs float64 order) add up in entries far below the data's scale.
+2. End to end against the float64 oracle, elementwise with the floor at the tensor's RMS
+   (err = max |a - e| / max(|e|, rms(e)); the reference's own tests bound |a - e| by atol + rtol |e|
+   with atol = rtol). The bound is 2e-2, or three times the error of the reference's own arithmetic
+   where that is larger: the same layer computed by oracle.layer_fwd_bwd with fp32-accumulated GEMMs
+   (the accumulation of the reference's cuBLAS and torch paths). The projection's rounding flips of
+   check 1 are the difference: a flipped decay logit moves all 128 channels of its head for the
+   next ~1 / alpha tokens, so in the slow-memory regime (config 3) fp32 accumulation alone reaches
+   about 2e-2 at the tail, and the tensor cores' accumulation flips about four times as many
+   entries as numpy's sgemm (both flip rates are printed). Every measured error is printed (run
+   with -s).
 """
 
 from __future__ import annotations
@@ -28,7 +45,7 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import max_rel_err
+from conftest import max_rel_err, max_rel_err_rms
 from nanochat_filter_b200 import LtvCudaFusedConcatHeadMajorRegisterCastBlellochScanQkvFilter, LtvInitValues
 from nanochat_filter_b200 import ops as nf_ops
 from oracle import oracle as O
@@ -37,6 +54,7 @@ pytestmark = pytest.mark.gpu
 
 TOL = 2e-2
 FLOOR = 1e-2
+MAX_FLIP_FRACTION = 1e-3
 
 CONFIGS = {
     "config2": dict(B=32, T=1024, C=768, NH=6, NKVH=6, D=128, r=128, logit_std=0.02, bias=0.0),
@@ -66,6 +84,21 @@ def _np(t):
     return t.detach().float().cpu().numpy()
 
 
+def _bf16_ulp(e):
+    """The spacing of bfloat16 values at |e| (8 significant bits)."""
+    a = np.maximum(np.abs(e), np.float32(2.0 ** -126))
+    return np.exp2(np.floor(np.log2(a)) - 7.0)
+
+
+def _fmt(d):
+    return ", ".join(f"{n} {e:.2e}" for n, e in d.items())
+
+
+def _layer_dict(res):
+    return {"q": res["hq"], "k": res["hk"], "v": res["hv"], "dx": res["grad_x"], "dW": res["grad_w"],
+            "dbias": res["grad_logit_bias"], "dinit": res["grad_inits"].astype(np.float64).sum(0)}
+
+
 @pytest.mark.parametrize("name", ["config2", "config3"])
 def test_production_layer_at_benchmark_config_vs_oracle(cuda_device, name):
     cfg = CONFIGS[name]
@@ -85,27 +118,65 @@ def test_production_layer_at_benchmark_config_vs_oracle(cuda_device, name):
     q, k, v = f(x, LtvInitValues())
     torch.autograd.backward([q, k, v], [gq_h.to(dev).transpose(1, 2), gk_h.to(dev).transpose(1, 2),
                                         gv_h.to(dev).transpose(1, 2)])
+    # the projection output of the same forward: the operator the module calls, once more without
+    # autograd (same kernels, so q, k, v equal the module's bit for bit)
+    with torch.no_grad():
+        comb, q2, k2, v2, _ = torch.ops.nanochat_cuda.ltv_proj_scan_cuda_op(
+            x.detach(), f.c.weight, f.init_param, f.logit_bias, NH, NKVH, Da, r, True)
     torch.cuda.synchronize()
+    for a, b in ((q.transpose(1, 2), q2), (k.transpose(1, 2), k2), (v.transpose(1, 2), v2)):
+        assert torch.equal(a, b)
     got = {
         "q": _np(q.transpose(1, 2)), "k": _np(k.transpose(1, 2)), "v": _np(v.transpose(1, 2)),
         "dx": _np(x.grad), "dW": _np(f.c.weight.grad), "dbias": _np(f.logit_bias.grad),
         "dinit": _np(f.init_param.grad),
     }
-    del q, k, v, x, f
+    comb_gpu = _np(comb)  # [B, F, T]
+    del q, k, v, q2, k2, v2, comb, x, f
     torch.cuda.empty_cache()
 
-    # the oracle sees what the module computes from: bf16 x, the weight and the initial state cast
-    # to bf16 (the autocast casts), the fp32 bias; dW accumulated in double and rounded to fp32
+    # what the module computes from: bf16 x, the weight and the initial state cast to bf16 (the
+    # autocast casts), the fp32 bias; dW accumulated and rounded to fp32
+    xf = x_h.float().numpy()
     W_b = O.round_bf16(W_h.numpy())
     inits = np.repeat(O.round_bf16(init_h.numpy())[None], B, axis=0)
-    ref = O.layer_fwd_bwd(x_h.float().numpy(), W_b, inits, bias_h.numpy(), gq_h.float().numpy(),
-                          gk_h.float().numpy(), gv_h.float().numpy(), NH, NKVH, Da, r, bf16=True)
-    exp = {
-        "q": ref["hq"], "k": ref["hk"], "v": ref["hv"], "dx": ref["grad_x"], "dW": ref["grad_w"],
-        "dbias": ref["grad_logit_bias"], "dinit": ref["grad_inits"].astype(np.float64).sum(0),
-    }
-    errs = {n: max_rel_err(got[n], exp[n], FLOOR) for n in got}
-    print(f"\n{name}: max relative error per output (floor {FLOOR} of max|e|): "
-          + ", ".join(f"{n} {e:.2e}" for n, e in errs.items()))
-    bad = {n: e for n, e in errs.items() if e > TOL}
-    assert not bad, f"{name}: above {TOL}: {bad} (all {errs})"
+    bias = bias_h.numpy()
+    gq, gk, gv = gq_h.float().numpy(), gk_h.float().numpy(), gv_h.float().numpy()
+
+    # ---- 1. stage by stage ----
+    comb64 = O.gemm_fwd(xf, W_b, True)
+    diff = np.abs(comb_gpu - comb64)
+    flips = float((diff > 0).mean())
+    # one bf16 ulp, or (entries far below the data's scale, where the fp32 accumulation error of C
+    # terms is larger than their ulp) 1e-4 of the tensor's RMS
+    rms = float(np.sqrt(np.mean(comb64.astype(np.float64) ** 2)))
+    within = (diff <= _bf16_ulp(comb64) * 1.0001) | (diff <= 1e-4 * rms)
+    assert within.all(), (f"projection output beyond one bf16 ulp (or 1e-4 rms) of float64 at "
+                          f"{int((~within).sum())} entries, max |diff| {float(diff[~within].max()):.3e}")
+    assert flips <= MAX_FLIP_FRACTION, f"projection rounding flips in {flips:.2e} of the entries"
+    comb_btf = np.ascontiguousarray(comb_gpu.transpose(0, 2, 1))
+    hq, hk, hv = O.scan_fwd(comb_btf, inits, bias, NH, NKVH, Da, r, True, True)
+    gc, gi, gb = O.scan_bwd(comb_btf, inits, bias, gq, gk, gv, NH, NKVH, Da, r, True, True)
+    gx, gw = O.gemm_bwd(xf, W_b, np.ascontiguousarray(gc.transpose(0, 2, 1)), True, False)
+    stage = _layer_dict(dict(hq=hq, hk=hk, hv=hv, grad_x=gx, grad_w=gw, grad_logit_bias=gb, grad_inits=gi))
+    errs_stage = {n: (max_rel_err_rms(got[n], stage[n]) if n in ("dx", "dW") else max_rel_err(got[n], stage[n], FLOOR))
+                  for n in got}
+
+    # ---- 2. end to end ----
+    exp = _layer_dict(O.layer_fwd_bwd(xf, W_b, inits, bias, gq, gk, gv, NH, NKVH, Da, r, bf16=True))
+    r32 = O.layer_fwd_bwd(xf, W_b, inits, bias, gq, gk, gv, NH, NKVH, Da, r, bf16=True, acc=np.float32)
+    flips32 = float((r32["combined"] != comb64).mean())
+    ref32 = _layer_dict(r32)
+    errs = {n: max_rel_err_rms(got[n], exp[n]) for n in got}
+    errs32 = {n: max_rel_err_rms(ref32[n], exp[n]) for n in got}
+    print(f"\n{name}: projection rounding flips vs float64: {flips:.2e} of the entries (fp32-accumulated "
+          f"reference arithmetic: {flips32:.2e})"
+          f"\n{name}: stage by stage (oracle from this build's projection), floor 1% of max|e| (dx, dW: "
+          f"rms(e)): {_fmt(errs_stage)}"
+          f"\n{name}: end to end vs the float64 oracle, floor rms(e): {_fmt(errs)}"
+          f"\n{name}: fp32-accumulated reference arithmetic vs the float64 oracle, floor rms(e): {_fmt(errs32)}")
+    bad = {n: e for n, e in errs_stage.items() if e > TOL}
+    assert not bad, f"{name}: stage-by-stage errors above {TOL}: {bad}"
+    bound = {n: max(TOL, 3.0 * errs32[n]) for n in got}
+    bad = {n: (e, bound[n]) for n, e in errs.items() if e > bound[n]}
+    assert not bad, f"{name}: end-to-end (error, bound) above the bound: {bad}"

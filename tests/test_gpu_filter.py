@@ -13,7 +13,7 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import max_rel_err
+from conftest import max_rel_err, max_rel_err_rms
 from nanochat_filter_b200 import (
     KVCache,
     LtvCombinedQkvComputerModule,
@@ -66,20 +66,23 @@ def test_filter_forward_backward_vs_oracle(cuda_device, dtype):
                           _np(gq.transpose(1, 2)), _np(gk.transpose(1, 2)), _np(gv.transpose(1, 2)),
                           NH, NKVH, D // r, r, bf16=bf16)
     # fp32: elementwise relative error (floor 1% of the tensor's max) <= 1e-5.
-    # bf16: the layer rounds three times in sequence (projection buffer, scan output, gradient
-    # buffer) and a one-ulp flip at any of them moves its dependents, so the composed layer is
-    # compared norm-wise: max|a - e| <= 2e-2 * max|e|. Each stage alone is held to the
-    # elementwise bound in test_gpu_scan.py / test_gpu_gemm.py.
+    # bf16: elementwise relative error with the floor at the tensor's RMS <= 2e-2: the layer rounds
+    # three times in sequence (projection buffer, scan output, gradient buffer) and a one-ulp flip at
+    # any of them (fp32 vs float64 accumulation) moves its dependents by a fraction of that ulp, which
+    # is not small next to entries far below the data's scale (test_gpu_configs.py measures it).
     tol = 2e-2 if bf16 else 1e-5
-    floor = 1.0 if bf16 else FLOOR
+
+    def err(a, e):
+        return max_rel_err_rms(a, e) if bf16 else max_rel_err(a, e, FLOOR)
+
     errs = {
-        "q": max_rel_err(_np(q.transpose(1, 2)), ref["hq"], floor),
-        "k": max_rel_err(_np(k.transpose(1, 2)), ref["hk"], floor),
-        "v": max_rel_err(_np(v.transpose(1, 2)), ref["hv"], floor),
-        "dx": max_rel_err(_np(x.grad), ref["grad_x"], floor),
-        "dW": max_rel_err(_np(f.c.weight.grad), ref["grad_w"], floor),
-        "dbias": max_rel_err(_np(f.logit_bias.grad), ref["grad_logit_bias"], floor),
-        "dinit": max_rel_err(_np(f.init_param.grad), ref["grad_inits"].sum(0), floor),
+        "q": err(_np(q.transpose(1, 2)), ref["hq"]),
+        "k": err(_np(k.transpose(1, 2)), ref["hk"]),
+        "v": err(_np(v.transpose(1, 2)), ref["hv"]),
+        "dx": err(_np(x.grad), ref["grad_x"]),
+        "dW": err(_np(f.c.weight.grad), ref["grad_w"]),
+        "dbias": err(_np(f.logit_bias.grad), ref["grad_logit_bias"]),
+        "dinit": err(_np(f.init_param.grad), ref["grad_inits"].sum(0)),
     }
     bad = {k2: e for k2, e in errs.items() if e > tol}
     assert not bad, f"above {tol}: {bad} (all {errs})"
