@@ -181,7 +181,7 @@ def run_ours(args, cfg):
 
     import nanochat_filter_b200 as nf
     from nanochat_filter_b200 import _lib
-    from nanochat_filter_b200.dist import GradBucket
+    from nanochat_filter_b200.dist import GradBucket, LayerGradSync
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -366,7 +366,9 @@ def run_ours(args, cfg):
         filt.c.weight.copy_(W)
         filt.logit_bias.copy_(bias)
         filt.init_param.copy_(init)
-    e2e_bucket = GradBucket([filt.c.weight, filt.logit_bias, filt.init_param]) if world > 1 else None
+    # the model-side exchange: the layer's all_reduce is started by its parameters' post-accumulate-grad
+    # hooks inside the backward (LayerGradSync) and waited for at the end of the step
+    e2e_sync = LayerGradSync([filt]) if world > 1 else None
     pin = {k: host[k].pin_memory() for k in ("x", "gq", "gk", "gv")}
     # two device copies of the step's inputs: the host->device copy of step i+1 (its own stream)
     # overlaps the compute of step i, as a prefetching data loader does; every step's copy is
@@ -400,8 +402,8 @@ def run_ours(args, cfg):
         q, k, v = filt(xin, nf.LtvInitValues())
         torch.autograd.backward([q, k, v], [dv["gq"].transpose(1, 2), dv["gk"].transpose(1, 2),
                                             dv["gv"].transpose(1, 2)])
-        if e2e_bucket is not None:
-            e2e_bucket.reduce()
+        if e2e_sync is not None:
+            e2e_sync.wait()
         for dst, p in zip(out_host, (filt.c.weight, filt.logit_bias, filt.init_param)):
             dst.copy_(p.grad, non_blocking=True)  # the step's result, read back
         consumed[slot].record(torch.cuda.current_stream(device))

@@ -94,7 +94,7 @@ inline size_t row_fwd_smem_bytes(int D, int Da, int H, int tt, int stages) {
 }
 inline size_t row_bwd_smem_bytes(int D, int Da, int H, int tt, int stages) {
   return 1024 + (size_t)stages * row_bwd_stage_bytes(D, Da, tt) + (size_t)row_align(H * Da, 4) * 4 +
-         (size_t)16 * Da * tt + (size_t)4 * (D / 32) * tt + (size_t)4 * Da * tt + sizeof(RowTile) * stages + 16 +
+         (size_t)16 * Da * tt * stages + (size_t)4 * (D / 32) * tt + (size_t)4 * Da * tt + sizeof(RowTile) * stages + 16 +
          24 * stages + 64;
 }
 
@@ -294,9 +294,11 @@ __global__ void __launch_bounds__(kD / 2 + (kCkpt ? 64 : 32), row_bwd_min_blocks
   const int nlb = a.H * Da;
   uint8_t* stages = base;
   float* lb_s = reinterpret_cast<float*>(stages + S * sbytes);               // [H][Da]
-  float4* gates = reinterpret_cast<float4*>(lb_s + row_align(nlb, 4));       // [Da][kTT]
+  // per stage: (1 - alpha_{t+1}, alpha_t, alpha_t (1 - alpha_t)) of the chunk's tokens, written by the
+  // consumers, or with checkpoints by the replay warp one chunk ahead of them
+  float4* gates = reinterpret_cast<float4*>(lb_s + row_align(nlb, 4));       // [S][Da][kTT]
   // dalpha partial sums per lane segment (see below) and per-row logit-bias sums
-  float* part = reinterpret_cast<float*>(gates + Da * kTT);                  // [D / 32][kTT]
+  float* part = reinterpret_cast<float*>(gates + S * Da * kTT);              // [D / 32][kTT]
   float* bsum = part + (D / 32) * kTT;                                        // [Da][kTT]
   RowTile* info = reinterpret_cast<RowTile*>(bsum + Da * kTT);               // [S]
   uint64_t* full = smem_align<uint64_t>(info + S, 16);
@@ -399,8 +401,22 @@ __global__ void __launch_bounds__(kD / 2 + (kCkpt ? 64 : 32), row_bwd_min_blocks
         initB = reinterpret_cast<const uint32_t*>(sb + ioff)[lane + 32];
       }
       // alpha of token t0 + lane (one decay group; the chunk is whole: T % 32 == 0)
-      const float lg = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(sb + loff)[lane]) + lb_s[ti.h];
+      const __nv_bfloat16* L_s = reinterpret_cast<const __nv_bfloat16*>(sb + loff);
+      const float lg = __bfloat162float(L_s[lane]) + lb_s[ti.h];
       const float al_l = a.use_sigmoid ? sigmoid_f32(lg) : lg;
+      {
+        // the consumers' gates of this chunk: alpha_{t+1} from the next lane, or for the last token
+        // the next chunk's first (identity beyond T), with the consumers' own arithmetic
+        float an = __shfl_down_sync(0xffffffffu, al_l, 1);
+        if (lane == kTT - 1) {
+          an = 0.f;
+          if (ti.t0 + kTT < a.T) {
+            const float ln = __bfloat162float(L_s[kTT]) + lb_s[ti.h];
+            an = a.use_sigmoid ? sigmoid_f32(ln) : ln;
+          }
+        }
+        gates[st * kTT + lane] = make_float4(1.0f - an, al_l, a.use_sigmoid ? al_l * (1.0f - al_l) : 1.0f, 0.f);
+      }
       float E0, E1, E2, E3;
       if (ti.j == 0) {
         E0 = __uint_as_float(initA << 16); E1 = __uint_as_float(initA & 0xffff0000u);
@@ -439,7 +455,7 @@ __global__ void __launch_bounds__(kD / 2 + (kCkpt ? 64 : 32), row_bwd_min_blocks
           }
         }
       }
-      mbar_arrive(&hfull[st]);  // release: this lane's H32 writes are visible to the consumers' wait
+      mbar_arrive(&hfull[st]);  // release: this lane's H32 and gate writes are visible to the consumers' wait
     }
     __syncwarp();
   } else {
@@ -481,7 +497,8 @@ __global__ void __launch_bounds__(kD / 2 + (kCkpt ? 64 : 32), row_bwd_min_blocks
       uint32_t* H32 = reinterpret_cast<uint32_t*>(sb + hoff);
       // h_{t-1} of the row's first token is the initial state (the tile's row -1 was filled with 0)
       if (!kCkpt && ti.t0 == 0) H32[tid] = init2;
-      for (int q = tid; q < Da * kTT; q += ncons) {
+      float4* gst = gates + st * Da * kTT;
+      for (int q = tid; !kCkpt && q < Da * kTT; q += ncons) {
         const int g = q / kTT, t = q % kTT;
         const float lb = lb_s[ti.h * Da + g];
         float al = 0.f, an = 0.f;  // alpha_t and alpha_{t+1}; identity steps beyond T
@@ -493,11 +510,11 @@ __global__ void __launch_bounds__(kD / 2 + (kCkpt ? 64 : 32), row_bwd_min_blocks
           const float l = __bfloat162float(L_s[g * LB + t + 1]) + lb;
           an = a.use_sigmoid ? sigmoid_f32(l) : l;
         }
-        gates[q] = make_float4(1.0f - an, al, a.use_sigmoid ? al * (1.0f - al) : 1.0f, 0.f);
+        gst[q] = make_float4(1.0f - an, al, a.use_sigmoid ? al * (1.0f - al) : 1.0f, 0.f);
       }
-      named_barrier(1, ncons);  // gates ready
+      if (!kCkpt) named_barrier(1, ncons);  // gates ready (with checkpoints: the replay warp's, below)
 
-      const float4* grow = gates + gi * kTT;
+      const float4* grow = gst + gi * kTT;
       if (kCkpt && !mbar_wait(&hfull[st], ph, &abort_flag, a.ws, 0x7204)) break;  // replayed outputs in place
 
       // reverse walk: adjoint carries, du, and the per-token dalpha terms of both channels

@@ -4,8 +4,10 @@ Training shards the batch across ranks (one process per GPU); the scan and the p
 no communication. The one exchange step is the gradient reduction of the parameters the path
 touches — c.weight, logit_bias and init_param of every filtered layer — which the reference
 performs inside DistMuonAdamW (nanochat/optim.py:367-403: all_reduce for small tensors,
-reduce_scatter for the stacked matrices). Here those gradients are flattened into one bucket
-(grouped by dtype) and reduced with a single all_reduce, over NCCL/NVLink on GPUs (gloo on CPU).
+reduce_scatter for the stacked matrices). Here those gradients are flattened into buckets
+(grouped by dtype) and reduced with all_reduce, over NCCL/NVLink on GPUs (gloo on CPU): one bucket
+for all layers (GradBucket, sync_filter_grads), or one per layer started from backward hooks as soon
+as the layer's gradients are final (LayerGradSync), overlapping the rest of the backward.
 """
 
 from __future__ import annotations
@@ -104,6 +106,93 @@ class GradBucket:
 
     def reduce(self, group: Optional[dist.ProcessGroup] = None, average: bool = True) -> None:
         self.start(group, average).wait(copy_back=True)
+
+
+def filter_modules(modules: Iterable[torch.nn.Module]) -> List[torch.nn.Module]:
+    """The filters (modules holding c.weight, logit_bias and init_param) found in `modules`, in order."""
+    out: List[torch.nn.Module] = []
+    seen = set()
+    for m in modules:
+        for sub in m.modules():
+            if hasattr(sub, "num_alpha_groups") and isinstance(getattr(sub, "logit_bias", None), torch.nn.Parameter) \
+                    and id(sub) not in seen:
+                seen.add(id(sub))
+                out.append(sub)
+    return out
+
+
+class LayerGradSync:
+    """One gradient bucket per filter layer, reduced as soon as that layer's gradients are final.
+
+    The reference reduces every filter gradient in its optimizer step, after the whole backward
+    (nanochat/optim.py:367-403). Here each layer's c.weight, logit_bias and init_param get a
+    post-accumulate-grad hook; when the last of a layer's parameters has its gradient for this
+    backward, the layer's bucket starts its all_reduce asynchronously, so the exchange of the later
+    layers (whose backward runs first) overlaps the backward of the earlier ones. `wait()` ends the
+    step: every started reduction is waited for and the averaged gradients are written back into the
+    parameters' .grad. Layers whose gradients never arrived (unused in this step) are reduced in
+    `wait()` with zero gradients, so every rank issues the same collectives in the same order.
+
+    Gradient accumulation: with `sync = False` (e.g. inside `no_sync()`) the hooks do nothing and
+    gradients accumulate locally; the backward of the step's last micro-batch runs with
+    sync = True. Call `remove()` to detach the hooks.
+    """
+
+    def __init__(self, modules: Iterable[torch.nn.Module], group: Optional[dist.ProcessGroup] = None,
+                 average: bool = True):
+        self.group, self.average = group, average
+        self.layers = [filter_parameters([m]) for m in filter_modules(modules)]
+        self.buckets = [GradBucket(ps) for ps in self.layers]
+        self.pending: List[Optional[PendingReduce]] = [None] * len(self.layers)
+        self.arrived = [set() for _ in self.layers]
+        self.started_order: List[int] = []  # layer indices in the order their reductions started
+        self.sync = True
+        self.handles = []
+        for li, ps in enumerate(self.layers):
+            for p in ps:
+                self.handles.append(p.register_post_accumulate_grad_hook(self._hook(li)))
+
+    def _hook(self, li: int):
+        def hook(p: torch.nn.Parameter) -> None:
+            if not self.sync or self.pending[li] is not None:
+                return
+            self.arrived[li].add(id(p))
+            if len(self.arrived[li]) == len(self.layers[li]):
+                self.pending[li] = self.buckets[li].start(self.group, self.average)
+                self.started_order.append(li)
+        return hook
+
+    class _NoSync:
+        def __init__(self, owner):
+            self.owner = owner
+
+        def __enter__(self):
+            self.prev, self.owner.sync = self.owner.sync, False
+            return self.owner
+
+        def __exit__(self, *exc):
+            self.owner.sync = self.prev
+            return False
+
+    def no_sync(self):
+        """Context manager: backward passes inside it accumulate gradients without reducing them."""
+        return LayerGradSync._NoSync(self)
+
+    def wait(self) -> None:
+        # in layer order on every rank: reductions not started by hooks are started here
+        for li in range(len(self.layers)):
+            if self.pending[li] is None:
+                self.pending[li] = self.buckets[li].start(self.group, self.average)
+                self.started_order.append(li)
+        for li in range(len(self.layers)):
+            self.pending[li].wait(copy_back=True)
+            self.pending[li] = None
+            self.arrived[li].clear()
+
+    def remove(self) -> None:
+        for h in self.handles:
+            h.remove()
+        self.handles = []
 
 
 def sync_filter_grads(modules: Iterable[torch.nn.Module], group: Optional[dist.ProcessGroup] = None,

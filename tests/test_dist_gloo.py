@@ -147,3 +147,88 @@ def test_two_rank_overlapped_reductions_keep_their_own_gradients():
         np.testing.assert_allclose(rw, gw, rtol=1e-5, atol=1e-6)   # average of 2x the shard sums
         np.testing.assert_allclose(rb, gb, rtol=1e-5, atol=1e-6)
         np.testing.assert_allclose(ri, gi, rtol=1e-5, atol=1e-6)
+
+
+class _CpuFilter(torch.nn.Module):
+    """A CPU stand-in with a filter's parameters (c.weight, logit_bias, init_param) and a plain
+    differentiable forward, so the hook-driven exchange can be exercised on gloo ranks."""
+
+    def __init__(self, C, H, D, seed):
+        super().__init__()
+        g = torch.Generator().manual_seed(seed)
+        self.num_alpha_groups = 1
+        self.c = torch.nn.Linear(C, H * (D + 1), bias=False)
+        with torch.no_grad():
+            self.c.weight.copy_(torch.randn(H * (D + 1), C, generator=g) / C ** 0.5)
+        self.logit_bias = torch.nn.Parameter(torch.randn(H, 1, generator=g))
+        self.init_param = torch.nn.Parameter(torch.randn(H, D, generator=g))
+        self.H, self.D, self.C = H, D, C
+
+    def forward(self, x):
+        y = torch.tanh(x @ self.c.weight.t())[..., : self.C]
+        return y + (self.logit_bias.sum() + self.init_param.mean()) * 0.1
+
+
+def _layered_grads(model, x):
+    model.zero_grad(set_to_none=True)
+    h = x
+    for layer in model:
+        h = layer(h)
+    (h * h).sum().backward()
+    return [[p.grad.detach().clone() for p in (l.c.weight, l.logit_bias, l.init_param)] for l in model]
+
+
+def _worker_layers(rank, world, port, out_q):
+    import sys
+    sys.path.insert(0, ROOT)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from nanochat_filter_b200.dist import LayerGradSync
+
+        model = torch.nn.ModuleList([_CpuFilter(8, 2, 4, seed=10 + i) for i in range(3)])
+        x = torch.randn(4, 5, 8, generator=torch.Generator().manual_seed(7))
+        shard = x[rank * 2:(rank + 1) * 2]
+        sync = LayerGradSync(model)
+        # two micro-batches of the shard: the first accumulates locally, the second reduces
+        with sync.no_sync():
+            _layered_grads(model, shard[:1])
+        started_no_sync = list(sync.started_order)
+        h = shard[1:]
+        for layer in model:
+            h = layer(h)
+        (h * h).sum().backward()
+        started_in_backward = list(sync.started_order)
+        sync.wait()
+        out_q.put((rank, started_no_sync, started_in_backward,
+                   [[p.grad.numpy().copy() for p in (l.c.weight, l.logit_bias, l.init_param)] for l in model]))
+        sync.remove()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_layer_buckets_reduced_from_backward_hooks():
+    """LayerGradSync: each layer's reduction starts from its parameters' post-accumulate-grad hooks
+    during the backward (last layer first), nothing is reduced inside no_sync, and after wait() every
+    rank holds the average over ranks of its accumulated gradients."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_layers, args=(r, 2, port, q)) for r in range(2)]
+    for pr in procs:
+        pr.start()
+    results = [q.get(timeout=240) for _ in range(2)]
+    for pr in procs:
+        pr.join(timeout=60)
+        assert pr.exitcode == 0
+    model = torch.nn.ModuleList([_CpuFilter(8, 2, 4, seed=10 + i) for i in range(3)])
+    x = torch.randn(4, 5, 8, generator=torch.Generator().manual_seed(7))
+    per_micro = [_layered_grads(model, x[i:i + 1]) for i in range(4)]
+    expect = [[sum(per_micro[i][li][pi] for i in range(4)).numpy() / 2 for pi in range(3)] for li in range(3)]
+    for _, started_no_sync, started_in_backward, grads in results:
+        assert started_no_sync == []
+        assert started_in_backward == [2, 1, 0]  # started by hooks during the backward, last layer first
+        for li in range(3):
+            for pi in range(3):
+                np.testing.assert_allclose(grads[li][pi], expect[li][pi], rtol=1e-5, atol=1e-6)
