@@ -4,6 +4,7 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <map>
 #include <mutex>
 
 #include "ltvqkv_common.cuh"
@@ -26,10 +27,71 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   });
   return fn;
 }
+
+PFN_cuTensorMapReplaceAddress_v12000 replace_fn() {
+  static PFN_cuTensorMapReplaceAddress_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, []() {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapReplaceAddress", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapReplaceAddress_v12000>(p);
+  });
+  return fn;
+}
+
+// Encoded maps by everything but the base address: a call with a known geometry copies the cached
+// map and swaps the address in (cuTensorMapReplaceAddress), a fraction of an encode's host time.
+struct MapKey {
+  int dtype, rank, swizzle;
+  uint64_t dims[5], strides[4];
+  uint32_t box[5];
+  bool operator<(const MapKey& o) const { return memcmp(this, &o, sizeof(MapKey)) < 0; }
+};
+std::mutex g_map_mu;
+std::map<MapKey, CUtensorMap>* g_maps = nullptr;
+
+bool encode_tiled_map_uncached(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base,
+                               const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
+                               CUtensorMapSwizzle swizzle);
 }  // namespace
 
 bool encode_tiled_map(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base, const uint64_t* dims,
                       const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swizzle) {
+  if (rank < 1 || rank > 5) return false;
+  MapKey k;
+  memset(&k, 0, sizeof(k));
+  k.dtype = (int)dtype; k.rank = rank; k.swizzle = (int)swizzle;
+  for (int i = 0; i < rank; ++i) {
+    k.dims[i] = dims[i];
+    k.box[i] = box[i];
+    if (i > 0) k.strides[i - 1] = strides_bytes[i - 1];
+  }
+  auto rep = replace_fn();
+  if (rep != nullptr && (reinterpret_cast<uintptr_t>(base) & 15) == 0) {
+    std::lock_guard<std::mutex> lock(g_map_mu);
+    if (g_maps == nullptr) g_maps = new std::map<MapKey, CUtensorMap>();
+    auto it = g_maps->find(k);
+    if (it != g_maps->end()) {
+      *map = it->second;
+      if (rep(map, const_cast<void*>(base)) == CUDA_SUCCESS) return true;
+    }
+  }
+  if (!encode_tiled_map_uncached(map, dtype, rank, base, dims, strides_bytes, box, swizzle)) return false;
+  if (rep != nullptr) {
+    std::lock_guard<std::mutex> lock(g_map_mu);
+    if (g_maps == nullptr) g_maps = new std::map<MapKey, CUtensorMap>();
+    if (g_maps->size() > 4096) g_maps->clear();  // bounded: geometries, not addresses, are the keys
+    (*g_maps)[k] = *map;
+  }
+  return true;
+}
+
+namespace {
+bool encode_tiled_map_uncached(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base,
+                               const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
+                               CUtensorMapSwizzle swizzle) {
   auto enc = encode_fn();
   if (!enc || rank < 1 || rank > 5) return false;
   cuuint64_t d[5];
@@ -61,6 +123,7 @@ bool encode_tiled_map(CUtensorMap* map, CUtensorMapDataType dtype, int rank, con
   }
   return r == CUDA_SUCCESS;
 }
+}  // namespace
 
 int num_sms() {
   int dev = 0, n = 0;

@@ -231,6 +231,161 @@ __global__ void __launch_bounds__(kDecThreads) decode_step_mma_kernel(DecodeArgs
 
 size_t decode_mma_smem(int Cp) { return (size_t)(kDmRows + kDmTok) * (Cp + 8) * 2 + (size_t)kDmRows * kDmTok * 4; }
 
+// bf16 path for C % 64 == 0 (the model widths): the same (head, 16-channel slice) CTAs, with
+//   * the operands staged by three bulk tensor copies issued from three warps at once: the 64-token
+//     tile of x as one 128-byte-swizzled box [C/64][64 tokens][64], the slice's value rows
+//     [C/64][16][64] and its logit rows [C/64][ngb][64] (cp.async from every thread reached about
+//     17 bytes per clock per SM, half the time of the step);
+//   * the previous state of the thread's outputs loaded into registers while the copies land;
+//   * the K range split between two warp halves: warp w multiplies tokens 16 (w % 4) .. +15 by all
+//     24 rows (3 independent accumulator chains) over half of C, and the halves are added in fixed
+//     order (first + second), so a warp's chain is 24 k-steps instead of 48.
+// The projection values and logits are rounded to bf16 exactly as the reference's projection
+// buffer stores them, then the gate and the recurrence step as in the other paths.
+constexpr int kDtTok = 64;      // tokens per tile (one box)
+constexpr int kDtRows = 24;     // 16 value rows + up to 8 logit rows (r >= 2)
+constexpr int kDtRegion = 1024; // swizzle atoms start on 1 KB boundaries
+
+struct DecodeTmaLayout {
+  size_t x, wv, wl, red, bar, total;
+};
+__host__ __device__ inline DecodeTmaLayout decode_tma_layout(int nkb) {
+  DecodeTmaLayout L;
+  size_t off = 0;
+  L.x = off; off += (size_t)nkb * kDtTok * 128;
+  L.wv = off; off += (size_t)nkb * 16 * 128;
+  L.wl = off; off += ((size_t)nkb * 8 * 128 + kDtRegion - 1) / kDtRegion * kDtRegion;
+  L.red = off; off += (size_t)kDtTok * kDtRows * 4;
+  L.bar = off; off += 64;
+  L.total = off + kDtRegion;  // alignment slack of the dynamic shared memory base
+  return L;
+}
+
+// Byte offset of the 16-byte piece `chunk` of 128-byte row `row` in a 128B-swizzled region.
+LTVQKV_DEVICE uint32_t swz128(int row, int chunk) { return (uint32_t)(row * 128 + ((chunk ^ (row & 7)) << 4)); }
+
+__global__ void __launch_bounds__(kDecThreads, 1)
+    decode_step_tma_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
+                           const __grid_constant__ CUtensorMap tmWl, DecodeArgs a, int nkb, int ngb) {
+  extern __shared__ __align__(16) unsigned char dt_raw[];
+  unsigned char* smem = smem_align<unsigned char>(dt_raw, kDtRegion);
+  const DecodeTmaLayout L = decode_tma_layout(nkb);
+  unsigned char* sX = smem + L.x;
+  unsigned char* sWv = smem + L.wv;
+  unsigned char* sWl = smem + L.wl;
+  float* red = reinterpret_cast<float*>(smem + L.red);  // [kDtTok][kDtRows]
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L.bar);
+  __shared__ volatile int abort_flag;
+  const int h = blockIdx.x;
+  const int c0 = blockIdx.y * kDmSlice;
+  const int nv = min(kDmSlice, a.D - c0);
+  const int g0 = c0 / a.r;
+  const int head_row = h * (a.D + a.Da);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  int which, hloc;
+  dec_split_head(h, a.NH, a.NKVH, which, hloc);
+  if (threadIdx.x == 0) {
+    mbar_init(bar, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const int mt = warp % 4, kh = warp / 4;
+  const int kb_half = (nkb + 1) / 2;
+  const int kb_beg = kh * kb_half, kb_end = min(nkb, kb_beg + kb_half);
+  const uint32_t sX_u = smem_u32(sX), sWv_u = smem_u32(sWv), sWl_u = smem_u32(sWl);
+  uint32_t phase = 0;
+  for (int b0 = 0; b0 < a.B; b0 += kDtTok, phase ^= 1u) {
+    const int nb = min(kDtTok, a.B - b0);
+    const bool first = b0 == 0;
+    // the copies (x every tile; the W rows once), each issued by its own warp
+    if (threadIdx.x == 0) {
+      const uint32_t bytes = (uint32_t)nkb * 128u * (kDtTok + (first ? 16u + (uint32_t)ngb : 0u));
+      mbar_arrive_expect_tx(bar, bytes);
+      tma_load_3d(sX, &tmX, bar, 0, b0, 0);
+    } else if (first && threadIdx.x == 32) {
+      tma_load_3d(sWv, &tmW, bar, 0, head_row + c0, 0);
+    } else if (first && threadIdx.x == 64) {
+      tma_load_3d(sWl, &tmWl, bar, 0, head_row + a.D + g0, 0);
+    }
+    // this thread's previous states, while the copies land
+    float hp[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int i = threadIdx.x + j * kDecThreads;
+      hp[j] = 0.f;
+      if (i < nv * nb) {
+        const int bb = i / nv, c = c0 + (i - bb * nv), b = b0 + bb;
+        if (a.prev[0] != nullptr) {
+          const long long* ps = a.ps[which];
+          hp[j] = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(a.prev[which])[b * ps[0] + hloc * ps[1] + c * ps[2]]);
+        } else {
+          hp[j] = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(a.init_param)[(long long)h * a.D + c]);
+        }
+      }
+    }
+    if (!mbar_wait(bar, phase, &abort_flag, nullptr, 0x7e01)) break;
+    // tokens 16 mt .. +15 x rows 0..23 over k-blocks kb_beg .. kb_end-1
+    float acc[3][4] = {};
+    const int arow = 16 * mt + (lane % 16);
+    const int brow = lane % 8;
+    const int lrow = brow < ngb ? brow : 0;  // logit rows beyond the slice's groups: any row (unused columns)
+    for (int kb = kb_beg; kb < kb_end; ++kb) {
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        uint32_t af[4], b0f[2], b1f[2], blf[2];
+        ldsm_x4(sX_u + (uint32_t)kb * (kDtTok * 128) + swz128(arow, kk * 2 + lane / 16), af);
+        const int bc = kk * 2 + (lane / 8) % 2;
+        ldsm_x2(sWv_u + (uint32_t)kb * (16 * 128) + swz128(brow, bc), b0f);
+        ldsm_x2(sWv_u + (uint32_t)kb * (16 * 128) + swz128(8 + brow, bc), b1f);
+        ldsm_x2(sWl_u + swz128(kb * ngb + lrow, bc), blf);
+        mma_bf16_16816(acc[0], af, b0f);
+        mma_bf16_16816(acc[1], af, b1f);
+        mma_bf16_16816(acc[2], af, blf);
+      }
+    }
+    // the two K halves, added in fixed order: red = half 0 + half 1
+    const int tt = 16 * mt + lane / 4, rr = 2 * (lane % 4);
+    if (kh == 1) {
+#pragma unroll
+      for (int j = 0; j < 3; ++j) {
+        *reinterpret_cast<float2*>(&red[tt * kDtRows + 8 * j + rr]) = make_float2(acc[j][0], acc[j][1]);
+        *reinterpret_cast<float2*>(&red[(tt + 8) * kDtRows + 8 * j + rr]) = make_float2(acc[j][2], acc[j][3]);
+      }
+    }
+    __syncthreads();
+    if (kh == 0) {
+#pragma unroll
+      for (int j = 0; j < 3; ++j) {
+        float2* p0 = reinterpret_cast<float2*>(&red[tt * kDtRows + 8 * j + rr]);
+        float2* p1 = reinterpret_cast<float2*>(&red[(tt + 8) * kDtRows + 8 * j + rr]);
+        const float2 q0 = *p0, q1 = *p1;
+        *p0 = make_float2(acc[j][0] + q0.x, acc[j][1] + q0.y);
+        *p1 = make_float2(acc[j][2] + q1.x, acc[j][3] + q1.y);
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int i = threadIdx.x + j * kDecThreads;
+      if (i < nv * nb) {
+        const int bb = i / nv, cc = i - bb * nv;
+        const int c = c0 + cc, b = b0 + bb;
+        const int g = c / a.r;
+        // projection values rounded to bf16, as the reference's projection buffer stores them
+        const float u = __bfloat162float(__float2bfloat16_rn(red[bb * kDtRows + cc]));
+        const float l = __fadd_rn(__bfloat162float(__float2bfloat16_rn(red[bb * kDtRows + 16 + g - g0])),
+                                  a.logit_bias[h * a.Da + g]);
+        const float al = a.use_sigmoid ? sigmoid_f32(l) : l;
+        const float hn = __fadd_rn(__fmul_rn(__fsub_rn(1.0f, al), hp[j]), __fmul_rn(al, u));
+        const long long* os = a.os[which];
+        reinterpret_cast<__nv_bfloat16*>(a.out[which])[b * os[0] + hloc * os[1] + c * os[2]] = __float2bfloat16_rn(hn);
+      }
+    }
+    __syncthreads();  // red and sX are free for the next token tile
+  }
+}
+
 }  // namespace ltvqkv
 
 using namespace ltvqkv;
@@ -268,8 +423,45 @@ extern "C" int ltvqkv_decode_step(int dtype, const void* x, const void* weight, 
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const int Cp = (C + 15) / 16 * 16;
   const size_t smem = decode_mma_smem(Cp);
-  // the tensor-core path holds a slice's logit rows next to its value rows: r >= 2 keeps them <= 16
-  if (dtype == LTVQKV_DTYPE_BF16 && smem <= 200 * 1024 && (kDmSlice + kDmSlice / r + 1) <= kDmRows) {
+  // the tensor-core paths hold a slice's logit rows next to its value rows: r >= 2 keeps them <= 16
+  const bool rows_fit = (kDmSlice + kDmSlice / r + 1) <= kDmRows;
+  const int nkb = C / 64;
+  // a 16-channel slice (starting at a multiple of 16) covers one decay group when 16 divides r, and
+  // 16 / r whole groups when r divides 16; other r take the paths below
+  const bool slice_groups = (r % kDmSlice == 0) || (kDmSlice % r == 0 && r >= 2);
+  const int ngb = r >= kDmSlice ? 1 : kDmSlice / r;  // logit rows of a slice (<= 8)
+  const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(weight)) & 15) == 0;
+  if (dtype == LTVQKV_DTYPE_BF16 && slice_groups && C % 64 == 0 && nkb >= 1 && nkb <= 256 && aligned &&
+      decode_tma_layout(nkb).total <= 220 * 1024) {
+    const int F = a.H * (a.D + Da);
+    const uint64_t dx[3] = {64, (uint64_t)B, (uint64_t)nkb}, sx[2] = {(uint64_t)C * 2, 128};
+    const uint64_t dw[3] = {64, (uint64_t)F, (uint64_t)nkb}, sw[2] = {(uint64_t)C * 2, 128};
+    const uint32_t bx[3] = {64, (uint32_t)kDtTok, (uint32_t)nkb}, bw[3] = {64, 16, (uint32_t)nkb},
+                   bl[3] = {64, (uint32_t)ngb, (uint32_t)nkb};
+    CUtensorMap tmX, tmW, tmWl;
+    if (!ltvqkv_host::encode_tiled_map(&tmX, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, x, dx, sx, bx, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !ltvqkv_host::encode_tiled_map(&tmW, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, weight, dw, sw, bw,
+                                       CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !ltvqkv_host::encode_tiled_map(&tmWl, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, weight, dw, sw, bl,
+                                       CU_TENSOR_MAP_SWIZZLE_128B))
+      return LTVQKV_ERR_LAUNCH;
+    const size_t tsm = decode_tma_layout(nkb).total;
+    static std::mutex mu3;
+    static size_t opted3[64] = {};  // dynamic shared memory this kernel is opted into, per device
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return ltvqkv_host::check_launch();
+    {
+      std::lock_guard<std::mutex> lock(mu3);
+      if (opted3[dev] < tsm) {
+        if (cudaFuncSetAttribute(decode_step_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tsm) !=
+            cudaSuccess)
+          return ltvqkv_host::check_launch();
+        opted3[dev] = tsm;
+      }
+    }
+    dim3 grid_tma(a.H, (a.D + kDmSlice - 1) / kDmSlice);
+    decode_step_tma_kernel<<<grid_tma, kDecThreads, tsm, s>>>(tmX, tmW, tmWl, a, nkb, ngb);
+  } else if (dtype == LTVQKV_DTYPE_BF16 && smem <= 200 * 1024 && rows_fit) {
     static std::mutex mu;
     static bool done[64] = {};
     int dev = 0;

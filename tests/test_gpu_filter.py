@@ -153,9 +153,12 @@ def test_decode_kernel_vs_oracle(cuda_device, dtype, with_state):
         pq, pk, pv = tp[:, :NH], tp[:, NH:NH + NKVH], tp[:, NH + NKVH:]
     q, k, v = torch.ops.nanochat_cuda.ltv_decode_step(T(x), T(w), torch.from_numpy(bias).to(dev), pq, pk, pv,
                                                       T(init), NH, NKVH, Da, r, True)
+    # fp32: elementwise, floor 1% of max|e|. bf16: elementwise with the floor at the tensor's RMS (a
+    # projection value that rounds to the neighbouring bf16 value under a different fp32 summation
+    # order moves its output by alpha * ulp(u), not small next to near-zero states)
     tol = 2e-2 if bf16 else 1e-5
     for a, e in ((q, eq[:, :, 0]), (k, ek[:, :, 0]), (v, ev[:, :, 0])):
-        assert max_rel_err(_np(a), e, FLOOR) <= tol
+        assert (max_rel_err_rms(_np(a), e) if bf16 else max_rel_err(_np(a), e, FLOOR)) <= tol
 
 
 @pytest.mark.parametrize("B,C", [(64, 768), (70, 256), (3, 200)])
