@@ -503,13 +503,18 @@ def run_ours(args, cfg):
 
 
 # ------------------------------------------------------------------------------------------
-# CPU baseline / reference arm: the oracle port of the reference's CPU algorithm
+# CPU baseline / reference arm: the reference's own CPU code for the path when its offline install
+# (baseline/_ref) is present, else the oracle port of the same algorithm
 # ------------------------------------------------------------------------------------------
-def _oracle_sample(cfg, seqs, seed=7):
+REF_OPS = os.path.join(ROOT, "baseline", "_ref", "nanochat", "ops", "ltv_reference_ops.py")
+
+
+def _oracle_sample(cfg, seqs, seed=7, T=None):
     import numpy as np
 
     rng = np.random.default_rng(seed)
-    T, C, NH, NKVH, D, r = (cfg[k] for k in ("T", "C", "NH", "NKVH", "D", "r"))
+    C, NH, NKVH, D, r = (cfg[k] for k in ("C", "NH", "NKVH", "D", "r"))
+    T = cfg["T"] if T is None else T
     H, Da = NH + 2 * NKVH, D // r
     F = H * (D + Da)
     x = rng.standard_normal((seqs, T, C)).astype(np.float32)
@@ -523,9 +528,81 @@ def _oracle_sample(cfg, seqs, seed=7):
     return x, w, init, bias, gq, gk, gv, NH, NKVH, Da, r
 
 
-def cpu_baseline(cfg, seconds=10.0, seqs=1):
-    """Times the oracle port (C, OpenMP over all host cores) on `seqs` sequences of the workload,
-    repeating until `seconds` of work (at most 8 repeats)."""
+def _reference_ops():
+    """The reference's CPU implementation of the path, `nanochat/ops/ltv_reference_ops.py` of the
+    offline install in baseline/_ref (it imports only torch), loaded by file path so that the
+    package's other modules (GPU extensions, Metal, Triton) are not imported. None when absent."""
+    if not os.path.exists(REF_OPS):
+        return None
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location("_nanochat_ltv_reference_ops", REF_OPS)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+class _RefLayer:
+    """One layer step through the reference's own CPU code: `fused_linear_transpose_reference`
+    (x @ W^T -> [B, F, T]), `ltv_fused_concat_head_major_register_cast_blelloch_scan_reference` on
+    its [B, T, F] view (the per-token QuantizedStateUpdate loop), then autograd back to x, the fp32
+    master W, logit_bias and the initial state — the composition the reference filter runs
+    (nanochat/ltv_cuda_fused_concat_head_major_register_cast_blelloch_scan_qkv_filter.py:24-73)."""
+
+    def __init__(self, R, cfg, tokens):
+        import torch
+
+        self.R, self.torch = R, torch
+        x, w, init, bias, gq, gk, gv, NH, NKVH, Da, r = _oracle_sample(cfg, 1, T=tokens)
+        dt = torch.bfloat16 if cfg["dtype"] == "bf16" else torch.float32
+        self.dt, self.meta = dt, (NH, NKVH, Da, r)
+        self.x = torch.from_numpy(x).to(dt)
+        self.w = torch.from_numpy(w)
+        self.init, self.bias = torch.from_numpy(init), torch.from_numpy(bias)
+        self.grads = [torch.from_numpy(g).to(dt) for g in (gq, gk, gv)]
+        self.tokens = tokens
+
+    def step(self):
+        torch, R = self.torch, self.R
+        NH, NKVH, Da, r = self.meta
+        x = self.x.detach().requires_grad_()
+        w = self.w.detach().requires_grad_()
+        init = self.init.detach().requires_grad_()
+        bias = self.bias.detach().requires_grad_()
+        combined = R.fused_linear_transpose_reference(x, w.to(self.dt))
+        q, k, v = R.ltv_fused_concat_head_major_register_cast_blelloch_scan_reference(
+            combined.transpose(1, 2), init.to(self.dt), bias, NH, NKVH, Da, r, 8, 8, 4, 32, 2, 8, True)
+        torch.autograd.backward([q, k, v], self.grads)
+        return w.grad
+
+
+def _ref_tokens_for(R, cfg, seconds_per_step):
+    """Tokens of one sequence per step so that a step of the reference's code takes at most about
+    `seconds_per_step`: from 64 tokens, doubled while the next size's estimated time fits (at most
+    the config's T). Its backward costs more per token as the sequence grows (each token's output
+    is an in-place slice write whose backward passes the whole gradient buffer), so the estimate
+    for the next size is 2.6x the measured time and a shorter sample favours the reference."""
+    tokens = 64
+    layer = _RefLayer(R, cfg, tokens)
+    layer.step()  # first call: allocator and thread-pool warm-up
+    while True:
+        t0 = time.perf_counter()
+        layer.step()
+        dt = time.perf_counter() - t0
+        if 2 * tokens > cfg["T"] or 2.6 * dt > seconds_per_step:
+            return tokens
+        tokens *= 2
+        layer = _RefLayer(R, cfg, tokens)
+
+
+def _ref_sample_desc(tokens, cfg, runs):
+    return (f"1 sequence x {tokens} tokens per run of {cfg['desc']}; the reference's own CPU code: "
+            "nanochat/ops/ltv_reference_ops.py from the offline install in baseline/_ref "
+            "(fused_linear_transpose_reference, the blelloch_scan_reference token loop, autograd "
+            f"backward through QuantizedStateUpdate), median of {runs} runs")
+
+
+def _port_seconds(cfg, seqs, runs_max, seconds):
     from oracle import oracle as O
 
     O.build()
@@ -535,47 +612,93 @@ def cpu_baseline(cfg, seconds=10.0, seqs=1):
     O.layer_fwd_bwd(*sample, bf16=bf16)  # warm-up (thread pool, page faults)
     times = []
     t_all = time.perf_counter()
-    while len(times) < 8 and (time.perf_counter() - t_all < seconds or len(times) < 1):
+    while len(times) < runs_max and (time.perf_counter() - t_all < seconds or len(times) < 1):
         t0 = time.perf_counter()
         O.layer_fwd_bwd(*sample, bf16=bf16)
         times.append(time.perf_counter() - t0)
-    med = statistics.median(times)
-    return {"value": round(seqs * cfg["T"] / med, 2), "unit": UNIT, "cores": cores, "kind": "port",
-            "sample": f"{seqs} sequence(s) x {cfg['T']} tokens of {cfg['desc']}; oracle port of the "
-                      f"reference's CPU algorithm (oracle/ltv_oracle.c scan, float64 BLAS GEMMs), "
-                      f"median of {len(times)} runs"}
+    return times, cores
+
+
+def cpu_baseline(cfg, seconds=10.0, seqs=1):
+    """The path on the host cores, over a bounded sample: the reference's own CPU code when
+    baseline/_ref holds it (kind "reference"), else the oracle port (C, OpenMP over all host
+    cores; kind "port"). The port's rate is reported beside the reference's as `port_value`."""
+    times, cores = _port_seconds(cfg, seqs, 8, seconds)
+    port_value = round(seqs * cfg["T"] / statistics.median(times), 2)
+    port_desc = (f"{seqs} sequence(s) x {cfg['T']} tokens of {cfg['desc']}; oracle port of the "
+                 f"reference's CPU algorithm (oracle/ltv_oracle.c scan, float64 BLAS GEMMs), "
+                 f"median of {len(times)} runs")
+    R = _reference_ops()
+    if R is None:
+        return {"value": port_value, "unit": UNIT, "cores": cores, "kind": "port", "sample": port_desc}
+    import torch
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    tokens = _ref_tokens_for(R, cfg, seconds / 3)
+    layer = _RefLayer(R, cfg, tokens)
+    rt = []
+    for _ in range(3):
+        t0 = time.perf_counter()
+        layer.step()
+        rt.append(time.perf_counter() - t0)
+    return {"value": round(tokens / statistics.median(rt), 2), "unit": UNIT, "cores": torch.get_num_threads(),
+            "kind": "reference", "sample": _ref_sample_desc(tokens, cfg, len(rt)),
+            "port_value": port_value, "port_sample": port_desc}
 
 
 def run_reference(args, cfg):
+    """`--impl reference`: the reference's own CPU code for the path (baseline/_ref), each step one
+    sequence of a bounded token count, so that K steps end within a few minutes; rank 0 only.
+    Without the install, the oracle port of the same algorithm, one full sequence per step."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    from oracle import oracle as O
-
-    O.build()
-    cores = O.set_threads(os.cpu_count() or 1)  # all host threads (torchrun sets OMP_NUM_THREADS=1)
-    sample = _oracle_sample(cfg, 1)
-    bf16 = cfg["dtype"] == "bf16"
-    for _ in range(max(1, min(args.warmup, 2))):
-        O.layer_fwd_bwd(*sample, bf16=bf16)
-    times = []
-    for _ in range(args.steps):
-        t0 = time.perf_counter()
-        O.layer_fwd_bwd(*sample, bf16=bf16)
-        times.append(time.perf_counter() - t0)
-    total = sum(times)
-    value = args.steps * cfg["T"] / total
     n = int(os.environ.get("WORLD_SIZE", "1"))
-    sample_desc = (f"1 sequence x {cfg['T']} tokens per step of {cfg['desc']}; oracle port: "
-                   "the reference's CPU path is Python source (its torch oracle) that is not shipped to "
-                   "the GPU box, so its algorithm runs as the port (C scan, float64 BLAS GEMMs)")
+    R = _reference_ops()
+    if R is not None:
+        import torch
+
+        torch.set_num_threads(os.cpu_count() or 1)  # all host threads (torchrun sets OMP_NUM_THREADS=1)
+        cores = torch.get_num_threads()
+        tokens = _ref_tokens_for(R, cfg, min(6.0, 120.0 / max(1, args.steps)))
+        layer = _RefLayer(R, cfg, tokens)
+        for _ in range(max(1, min(args.warmup, 1))):
+            layer.step()
+        times = []
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            layer.step()
+            times.append(time.perf_counter() - t0)
+        kind, sample_desc = "reference", _ref_sample_desc(tokens, cfg, args.steps).replace(
+            f", median of {args.steps} runs", f", {args.steps} timed steps")
+    else:
+        from oracle import oracle as O
+
+        O.build()
+        cores = O.set_threads(os.cpu_count() or 1)
+        tokens = cfg["T"]
+        sample = _oracle_sample(cfg, 1)
+        bf16 = cfg["dtype"] == "bf16"
+        for _ in range(max(1, min(args.warmup, 2))):
+            O.layer_fwd_bwd(*sample, bf16=bf16)
+        times = []
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            O.layer_fwd_bwd(*sample, bf16=bf16)
+            times.append(time.perf_counter() - t0)
+        kind = "port"
+        sample_desc = (f"1 sequence x {tokens} tokens per step of {cfg['desc']}; oracle port of the "
+                       "reference's CPU algorithm (C scan, float64 BLAS GEMMs): the reference's install "
+                       "(baseline/_ref) is absent")
+    total = sum(times)
+    value = args.steps * tokens / total
     print(json.dumps({
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": n, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(1e3 * total / args.steps, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": cfg["dtype"], "data": "synthetic",
-        "config": {"workload": f"{args.config}: {cfg['desc']}", "tokens_per_step": cfg["T"]},
+        "config": {"workload": f"{args.config}: {cfg['desc']}", "tokens_per_step": tokens},
         "impl": "reference",
-        "cpu_baseline": {"value": round(value, 2), "unit": UNIT, "cores": cores, "kind": "port",
+        "cpu_baseline": {"value": round(value, 2), "unit": UNIT, "cores": cores, "kind": kind,
                          "sample": sample_desc},
         "e2e": {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
