@@ -264,6 +264,34 @@ LTVQKV_API int ltvqkv_proj_scan_fwd_ckpt(int dtype, const void* x, const void* w
                     int B, int T, int C, int NH, int NKVH, int Da, int r, int use_sigmoid,
                     void* workspace, size_t workspace_bytes, void* stream);
 
+/* As ltvqkv_proj_scan_fwd_ckpt, with the attention's prologue on q and k folded into the scan's
+ * epilogue (reference nanochat/gpt.py:96-111, 224-230: apply_rotary_emb then F.rms_norm over the
+ * head dim; no reference C function corresponds): out_q / out_k receive the rotated, RMS-normalised
+ * rows instead of the raw filter outputs (v unchanged), equal bit for bit to ltvqkv_proj_scan_fwd_ckpt
+ * followed by ltvqkv_rotary_qk_norm_fwd. rope_cos / rope_sin: bf16 tables of D / 2 values per token
+ * (rows rope_stride elements apart, 4-byte aligned, even stride; the model's cos / sin buffers for
+ * the sequence's positions); eps: the norm's epsilon (F.rms_norm's default: FLT_EPSILON). The raw
+ * outputs are not stored: ltvqkv_rotary_qk_norm_bwd_ckpt replays them. */
+LTVQKV_API int ltvqkv_proj_scan_fwd_ckpt_rope(int dtype, const void* x, const void* weight, const void* inits,
+                    int64_t inits_bs, const float* logit_bias, void* combined, void* out_q, void* out_k,
+                    void* out_v, float* ckpt, const void* rope_cos, const void* rope_sin,
+                    int64_t rope_stride, float eps,
+                    int B, int T, int C, int NH, int NKVH, int Da, int r, int use_sigmoid,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
+/* Backward of that prologue: dq / dk (the gradients of the raw filter outputs, bf16 [B, heads, T, D]
+ * with any pair-aligned strides) from grad_q / grad_k (those of the rotated, normalised rows), with
+ * the raw outputs replayed from ckpt — ltvqkv_proj_scan_fwd_ckpt_rope does not store them. Equal bit
+ * for bit to ltvqkv_rotary_qk_norm_bwd on the raw outputs ltvqkv_proj_scan_fwd_ckpt would have
+ * stored; dq / dk then feed ltvqkv_scan_bwd_ckpt as grad_hq / grad_hk. combined, inits (inits_bs as
+ * for the forward), logit_bias and ckpt are the forward's; bf16, D = 128, Da = 1, T % 32 == 0. */
+LTVQKV_API int ltvqkv_rotary_qk_norm_bwd_ckpt(int dtype, const void* combined, const void* inits,
+                    int64_t inits_bs, const float* logit_bias, const float* ckpt,
+                    const void* rope_cos, const void* rope_sin, int64_t rope_stride, float eps,
+                    const void* grad_q, const int64_t* gq_strides, const void* grad_k, const int64_t* gk_strides,
+                    void* dq, const int64_t* dq_strides, void* dk, const int64_t* dk_strides,
+                    int B, int T, int NH, int NKVH, int Da, int r, int use_sigmoid, void* stream);
+
 /* Projection backward: replaces cpp_ewma_cuda.fused_linear_transpose_backward
  * (reference cpp_ewma/src/fused_linear_transpose_backward.cu:22-132; called from
  * nanochat/ops/fused_linear_transpose.py:84-101).

@@ -40,11 +40,13 @@ EXPORTED_SYMBOLS = (
     "ltvqkv_scan_noalloc_error",
     "ltvqkv_proj_scan_fwd",
     "ltvqkv_proj_scan_fwd_ckpt",
+    "ltvqkv_proj_scan_fwd_ckpt_rope",
     "ltvqkv_lookback_workspace_bytes",
     "ltvqkv_lookback_scan_fwd",
     "ltvqkv_lookback_scan_bwd",
     "ltvqkv_rotary_qk_norm_fwd",
     "ltvqkv_rotary_qk_norm_bwd",
+    "ltvqkv_rotary_qk_norm_bwd_ckpt",
 )
 
 _lib: Optional[ctypes.CDLL] = None
@@ -81,6 +83,10 @@ def _declare(lib: ctypes.CDLL) -> None:
                                          _vp, _pi64, _vp, _pi64, _vp, _pi64,
                                          _vp, _i64, _i64, _i64, _vp, _pf,
                                          _i, _i, _i, _i, _i, _i, _i, _vp, _sz, _vp]
+    lib.ltvqkv_rotary_qk_norm_bwd_ckpt.restype = _i
+    lib.ltvqkv_rotary_qk_norm_bwd_ckpt.argtypes = [_i, _vp, _vp, _i64, _pf, _pf, _vp, _vp, _i64, ctypes.c_float,
+                                                   _vp, _pi64, _vp, _pi64, _vp, _pi64, _vp, _pi64,
+                                                   _i, _i, _i, _i, _i, _i, _i, _vp]
     lib.ltvqkv_lookback_workspace_bytes.restype = _sz
     lib.ltvqkv_lookback_workspace_bytes.argtypes = [_i, _i, _i, _i]
     lib.ltvqkv_lookback_scan_fwd.restype = _i
@@ -108,6 +114,10 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.ltvqkv_proj_scan_fwd_ckpt.restype = _i
     lib.ltvqkv_proj_scan_fwd_ckpt.argtypes = [_i, _vp, _vp, _vp, _i64, _pf, _vp, _vp, _vp, _vp, _pf,
                                               _i, _i, _i, _i, _i, _i, _i, _i, _vp, _sz, _vp]
+    lib.ltvqkv_proj_scan_fwd_ckpt_rope.restype = _i
+    lib.ltvqkv_proj_scan_fwd_ckpt_rope.argtypes = [_i, _vp, _vp, _vp, _i64, _pf, _vp, _vp, _vp, _vp, _pf,
+                                                   _vp, _vp, _i64, ctypes.c_float,
+                                                   _i, _i, _i, _i, _i, _i, _i, _i, _vp, _sz, _vp]
     lib.ltvqkv_gemm_bwd.restype = _i
     lib.ltvqkv_gemm_bwd.argtypes = [_i, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _vp, _i,
                                     _i, _i, _i, _i, _vp, _sz, _vp]

@@ -115,6 +115,64 @@ LTVQKV_DEVICE float sigmoid_f32_exact(float x) {
 }
 
 // ------------------------------------------------------------------------------------------
+// Rotary embedding + RMS norm of a head row (the reference attention's prologue on the filter's q
+// and k, nanochat/gpt.py:96-111, 224-230): y1 = x1 c + x2 s, y2 = x1 (-s) + x2 c on the element
+// pairs (j, j + D/2), then z = y r with r = (mean(y^2) + eps)^(-1/2). Shared by the standalone
+// kernels and the fused projection + scan forward / checkpoint backward, so that all of them
+// compute the same values bit for bit; every step is an explicit round-to-nearest operation.
+// ------------------------------------------------------------------------------------------
+LTVQKV_DEVICE float rq_bf16(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+// Two floats rounded to bf16 and packed (lo in the low half), as one 32-bit word.
+LTVQKV_DEVICE uint32_t pack_bf16x2(float lo, float hi) {
+  const __nv_bfloat162 p = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&p);
+}
+// The rotation of one pair with every product and sum rounded to bf16, as torch's bf16
+// elementwise ops round them (x1, x2, c, s hold bf16 values, so -s is exact).
+LTVQKV_DEVICE void rope_rotate_bf16(float x1, float x2, float c, float s, float& y1, float& y2) {
+  y1 = rq_bf16(__fadd_rn(rq_bf16(__fmul_rn(x1, c)), rq_bf16(__fmul_rn(x2, s))));
+  y2 = rq_bf16(__fadd_rn(rq_bf16(__fmul_rn(x1, -s)), rq_bf16(__fmul_rn(x2, c))));
+}
+// The same rotation for two adjacent elements at once on packed bf16 pairs (x1 = elements j, j + 1
+// of the first half, x2 = j + D/2, j + D/2 + 1): the bf16x2 multiply and add round once to bf16,
+// and since the product of two bf16 values and the sum of two bf16 values round to bf16 the same
+// whether or not they pass through an fp32 rounding first, the results equal rope_rotate_bf16's.
+LTVQKV_DEVICE void rope_rotate_bf16x2(uint32_t x1, uint32_t x2, uint32_t c, uint32_t s, uint32_t& y1,
+                                      uint32_t& y2) {
+  const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&x1);
+  const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&x2);
+  const __nv_bfloat162 cc = *reinterpret_cast<const __nv_bfloat162*>(&c);
+  const __nv_bfloat162 ss = *reinterpret_cast<const __nv_bfloat162*>(&s);
+  // the _rn forms: each product and sum rounds on its own (never contracted into a bf16 fma)
+  const __nv_bfloat162 r1 = __hadd2_rn(__hmul2_rn(a, cc), __hmul2_rn(b, ss));
+  const __nv_bfloat162 r2 = __hadd2_rn(__hmul2_rn(a, __hneg2(ss)), __hmul2_rn(b, cc));
+  y1 = *reinterpret_cast<const uint32_t*>(&r1);
+  y2 = *reinterpret_cast<const uint32_t*>(&r2);
+}
+LTVQKV_DEVICE float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
+LTVQKV_DEVICE float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+LTVQKV_DEVICE float bf16_lane(uint32_t w, int i) { return i ? bf16_hi(w) : bf16_lo(w); }
+// x / D rounded to nearest: for a power-of-two D the product with 1 / D (exact) is the same value
+LTVQKV_DEVICE float rope_div_d(float x, int D) {
+  return (D & (D - 1)) == 0 ? __fmul_rn(x, __fdiv_rn(1.0f, (float)D)) : __fdiv_rn(x, (float)D);
+}
+// r from the row's sum of squares
+LTVQKV_DEVICE float rope_inv_rms(float ss, int D, float eps) { return rsqrtf(__fadd_rn(rope_div_d(ss, D), eps)); }
+// r^3 (sum_j g_j y_j) / D, the norm backward's common term
+LTVQKV_DEVICE float rope_k3(float r, float gy, int D) {
+  return rope_div_d(__fmul_rn(__fmul_rn(__fmul_rn(r, r), r), gy), D);
+}
+// Gradient of the pair (x1, x2) from the gradient (g1, g2) of the normalised pair: through the norm,
+// dy = r g - y k3, then the transposed rotation dx1 = dy1 c - dy2 s, dx2 = dy1 s + dy2 c.
+LTVQKV_DEVICE void rope_norm_bwd(float r, float k3, float g1, float g2, float y1, float y2, float c, float s,
+                                 float& dx1, float& dx2) {
+  const float dy1 = __fmaf_rn(r, g1, -__fmul_rn(y1, k3));
+  const float dy2 = __fmaf_rn(r, g2, -__fmul_rn(y2, k3));
+  dx1 = __fmaf_rn(dy1, c, -__fmul_rn(dy2, s));
+  dx2 = __fmaf_rn(dy1, s, __fmul_rn(dy2, c));
+}
+
+// ------------------------------------------------------------------------------------------
 // Release/acquire flag helpers (gpu scope)
 // ------------------------------------------------------------------------------------------
 LTVQKV_DEVICE void st_release_u32(unsigned int* p, unsigned int v) {
@@ -126,6 +184,8 @@ LTVQKV_DEVICE unsigned int ld_acquire_u32(const unsigned int* p) {
   return v;
 }
 LTVQKV_DEVICE float ld_cg_f32(const float* p) { return __ldcg(p); }
+// Brings the line holding p into this SM's L1 (no register written, nothing waits for it).
+LTVQKV_DEVICE void prefetch_l1(const void* p) { asm volatile("prefetch.global.L1 [%0];" ::"l"(p)); }
 
 // ------------------------------------------------------------------------------------------
 // Shared-memory address helpers

@@ -281,10 +281,16 @@ extern "C" int ltvqkv_gemm_fwd(int dtype, const void* x, const void* weight, voi
 }
 
 namespace {
+struct RopeTables {  // rotary tables of the fused forward's q / k prologue (cos == nullptr: none)
+  const void* cos = nullptr;
+  const void* sin = nullptr;
+  int64_t cs = 0;
+  float eps = 0.f;
+};
 int proj_scan_fwd_impl(int dtype, const void* x, const void* weight, const void* inits, int64_t inits_bs,
                        const float* logit_bias, void* combined, void* out_q, void* out_k, void* out_v, float* ckpt,
                        int B, int T, int C, int NH, int NKVH, int Da, int r, int use_sigmoid, void* workspace,
-                       size_t workspace_bytes, void* stream);
+                       size_t workspace_bytes, void* stream, const RopeTables& rope = RopeTables());
 }  // namespace
 
 extern "C" int ltvqkv_proj_scan_fwd(int dtype, const void* x, const void* weight, const void* inits,
@@ -306,13 +312,32 @@ extern "C" int ltvqkv_proj_scan_fwd_ckpt(int dtype, const void* x, const void* w
                             C, NH, NKVH, Da, r, use_sigmoid, workspace, workspace_bytes, stream);
 }
 
+extern "C" int ltvqkv_proj_scan_fwd_ckpt_rope(int dtype, const void* x, const void* weight, const void* inits,
+                                              int64_t inits_bs, const float* logit_bias, void* combined, void* out_q,
+                                              void* out_k, void* out_v, float* ckpt, const void* rope_cos,
+                                              const void* rope_sin, int64_t rope_stride, float eps, int B, int T,
+                                              int C, int NH, int NKVH, int Da, int r, int use_sigmoid,
+                                              void* workspace, size_t workspace_bytes, void* stream) {
+  if (!ckpt || (reinterpret_cast<uintptr_t>(ckpt) & 15u) != 0) return LTVQKV_ERR_INVALID_ARG;
+  if (!rope_cos || !rope_sin) return LTVQKV_ERR_INVALID_ARG;
+  // the epilogue reads each token's table row as 32 bf16 pairs
+  if (rope_stride < Da * r / 2 || rope_stride % 2 != 0 || (reinterpret_cast<uintptr_t>(rope_cos) & 3u) != 0 ||
+      (reinterpret_cast<uintptr_t>(rope_sin) & 3u) != 0)
+    return LTVQKV_ERR_STRIDE;
+  if (inits_bs != 0 && inits_bs != (int64_t)(NH + 2 * NKVH) * Da * r) return LTVQKV_ERR_STRIDE;
+  RopeTables rope;
+  rope.cos = rope_cos; rope.sin = rope_sin; rope.cs = rope_stride; rope.eps = eps;
+  return proj_scan_fwd_impl(dtype, x, weight, inits, inits_bs, logit_bias, combined, out_q, out_k, out_v, ckpt, B, T,
+                            C, NH, NKVH, Da, r, use_sigmoid, workspace, workspace_bytes, stream, rope);
+}
+
 namespace {
 // inits_bs: elements between the sequences' initial states (0: one state for every sequence, fused
 // kernel only; < 0: contiguous [B][H][D]).
 int proj_scan_fwd_impl(int dtype, const void* x, const void* weight, const void* inits, int64_t inits_bs,
                        const float* logit_bias, void* combined, void* out_q, void* out_k, void* out_v, float* ckpt,
                        int B, int T, int C, int NH, int NKVH, int Da, int r, int use_sigmoid, void* workspace,
-                       size_t workspace_bytes, void* stream) {
+                       size_t workspace_bytes, void* stream, const RopeTables& rope) {
   if (!ltvqkv_host::valid_dtype(dtype)) return LTVQKV_ERR_DTYPE;
   if (B < 0 || T < 0 || C < 0 || NH < 0 || NKVH < 0 || Da < 1 || r < 1) return LTVQKV_ERR_SHAPE;
   const int H = NH + 2 * NKVH, D = Da * r, F = H * (D + Da);
@@ -372,6 +397,10 @@ int proj_scan_fwd_impl(int dtype, const void* x, const void* weight, const void*
   pp.out[2] = reinterpret_cast<__nv_bfloat16*>(out_v);
   pp.ckpt = ckpt;
   pp.inits_bs = inits_bs;
+  pp.rope_cos = reinterpret_cast<const __nv_bfloat16*>(rope.cos);
+  pp.rope_sin = reinterpret_cast<const __nv_bfloat16*>(rope.sin);
+  pp.rope_cs = rope.cs;
+  pp.rope_eps = rope.eps;
   pp.ws = ws;
   CUtensorMap tmW, tmXh;
   if (!make_map(&tmW, false, weight, C, F, 1, (uint64_t)C * 2, (uint64_t)C * F * 2, 64, 128) ||

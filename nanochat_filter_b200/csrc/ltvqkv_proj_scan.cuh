@@ -59,6 +59,12 @@ struct PsParams {
   const float* logit_bias;        // [H]
   __nv_bfloat16* out[3];          // [B][heads][T][128]
   float* ckpt;                    // optional [B][H][T / 32][128]: the fp32 state after every 32nd token
+  // optional rotary tables [T][64] (rows rope_cs elements apart): q and k then leave rotated and
+  // RMS-normalised (the reference attention's prologue, nanochat/gpt.py:224-230) instead of raw
+  const __nv_bfloat16* rope_cos;
+  const __nv_bfloat16* rope_sin;
+  long long rope_cs;
+  float rope_eps;
   WorkspaceHeader* ws;
 };
 
@@ -66,6 +72,16 @@ struct PsParams {
 LTVQKV_DEVICE uint4 ps_load_logits(const __nv_bfloat16* lrow, int t0, int T) {
   if (t0 >= T) return make_uint4(0, 0, 0, 0);
   return __ldg(reinterpret_cast<const uint4*>(lrow + t0));
+}
+
+// Rotary table pairs (2 lane, 2 lane + 1) of tokens t0 .. t0 + 7.
+LTVQKV_DEVICE void ps_rope_rows(const PsParams& prm, int t0, int lane, uint32_t (&c)[8], uint32_t (&s)[8]) {
+#pragma unroll
+  for (int tt = 0; tt < 8; ++tt) {
+    const long long ti = (long long)(t0 + tt) * prm.rope_cs;
+    c[tt] = __ldg(reinterpret_cast<const uint32_t*>(prm.rope_cos + ti) + lane);
+    s[tt] = __ldg(reinterpret_cast<const uint32_t*>(prm.rope_sin + ti) + lane);
+  }
 }
 
 // Head pair p -> batch and first head (the second, h0 + 1, exists when h0 + 1 < H).
@@ -247,11 +263,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPsThreads, 1)
     float2* gw = gates + ew * kPsBN;
     const uint32_t tempty_leader = mapa_shared(&tempty_bar[sl], 0);
     uint32_t acc_phase = 0;
+    // Rotary + norm: the warpgroup's four transpose buffers (8 KB, contiguous) hold a [32 token][128
+    // channel] bf16 tile of the walk's outputs between two barriers of the group (named barrier 1 +
+    // slot, 128 threads); each warp then finishes 8 of its tokens, lane l holding the channel pairs
+    // (2l, 2l + 1) and (2l + 64, 2l + 65), i.e. the rotation's pairs. The group leaves its loops
+    // together: the outcome of every bounded wait is OR-reduced over the group at a barrier, so no
+    // warp can wait at a group barrier for a warp that has left.
+    unsigned char* stg = xpose + (size_t)sl * 4 * kPsXposeBytes;
+    const int gbar = 1 + sl;
     for (int i = 0;; ++i) {
       int tk[2] = {-1, -1};
       bool got = true;
       if (lane == 0) got = sched_take(i, tk[0], tk[1], 0x6a01);
-      got = __shfl_sync(0xffffffffu, got ? 1 : 0, 0) != 0;
+      got = !named_barrier_or(gbar, 128, __shfl_sync(0xffffffffu, got ? 0 : 1, 0) != 0);
       const int tick0 = __shfl_sync(0xffffffffu, tk[0], 0);
       const int tick = __shfl_sync(0xffffffffu, sl ? tk[1] : tk[0], 0);
       if (!got) break;
@@ -265,8 +289,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPsThreads, 1)
       int which = 0, hloc = 0, nheads = 1;
       if (live) split_head(h, prm.NH, prm.NKVH, which, hloc, nheads);
       const int hh = live ? h : 0;
-      __nv_bfloat16* obase = (which == 0 ? prm.out[0] : (which == 1 ? prm.out[1] : prm.out[2])) +
-                             ((long long)b * nheads + hloc) * prm.T * kPsD + c;
+      __nv_bfloat16* orow = (which == 0 ? prm.out[0] : (which == 1 ? prm.out[1] : prm.out[2])) +
+                            ((long long)b * nheads + hloc) * prm.T * kPsD;  // the head's [T][128] output
+      __nv_bfloat16* obase = orow + c;
+      const bool rope = prm.rope_cos != nullptr && which < 2;  // the same for the warpgroup's four warps
       const long long vrow0 = (long long)b * prm.F + hh * (kPsD + 1) + q * 32;  // the warp's first value row
       const __nv_bfloat16* lrow = prm.combined + ((long long)b * prm.F + hh * (kPsD + 1) + kPsD) * prm.T;
       const float lb = prm.logit_bias[hh];
@@ -294,13 +320,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPsThreads, 1)
           __syncwarp();
         }
         const bool got2 = mbar_wait(&tfull_bar[sl], acc_phase, abort_flag, ws, 0x6a02);
-        if (__any_sync(0xffffffffu, !got2)) { ok = false; break; }
+        if (rope ? named_barrier_or(gbar, 128, !got2) : __any_sync(0xffffffffu, !got2)) { ok = false; break; }
         tc_fence_after();
         const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(sl * kPsBN);
+        uint32_t pcos[8], psin[8];  // rotary: the next block's table pairs, carried across iterations
 #pragma unroll 1
         for (int hb = 0; hb < kPsBN / 32; ++hb) {
           const int c0 = n0 + hb * 32;
           if (!live || c0 >= prm.T) break;  // uniform; T % 32 == 0, so the 32 tokens are all inside T
+          // rotary: this warp's 8 tokens' table pairs of this block (loaded one block ahead) and the next's
+          uint32_t rcos[8], rsin[8], ncos[8], nsin[8];
+          if (rope) {
+            if (hb == 0) ps_rope_rows(prm, c0 + q * 8, lane, rcos, rsin);
+            else {
+#pragma unroll
+              for (int tt = 0; tt < 8; ++tt) { rcos[tt] = pcos[tt]; rsin[tt] = psin[tt]; }
+            }
+            if (hb + 1 < kPsBN / 32 && c0 + 32 < prm.T) ps_rope_rows(prm, c0 + 32 + q * 8, lane, ncos, nsin);
+          }
           uint32_t v[32];
           tmem_ld_32x32b_x32(t_row + (uint32_t)(hb * 32), v);
           tmem_wait_ld();
@@ -324,24 +361,70 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPsThreads, 1)
             *reinterpret_cast<uint4*>(prm.combined + (vrow0 + r8) * prm.T + c0 + jj * 8) = val;
           }
           __syncwarp();  // the buffer is free for the next 32 tokens
-          // ---- the recurrence over the same 32 tokens; a warp stores 64 contiguous bytes per token ----
-          __nv_bfloat16* op = obase + (long long)c0 * kPsD;
           const int tb = hb * 32;
+          if (!rope) {
+            // ---- the recurrence over the same 32 tokens; a warp stores 64 contiguous bytes per token ----
+            __nv_bfloat16* op = obase + (long long)c0 * kPsD;
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const uint32_t w = pk[j];
-            const float u0 = __uint_as_float(w << 16), u1 = __uint_as_float(w & 0xffff0000u);
-            const float4 g = *reinterpret_cast<const float4*>(gw + tb + 2 * j);
-            E = __fmaf_rn(g.x, E, __fmul_rn(g.y, u0));
-            op[(2 * j) * kPsD] = __float2bfloat16_rn(E);
-            E = __fmaf_rn(g.z, E, __fmul_rn(g.w, u1));
-            op[(2 * j + 1) * kPsD] = __float2bfloat16_rn(E);
+            for (int j = 0; j < 16; ++j) {
+              const uint32_t w = pk[j];
+              const float u0 = __uint_as_float(w << 16), u1 = __uint_as_float(w & 0xffff0000u);
+              const float4 g = *reinterpret_cast<const float4*>(gw + tb + 2 * j);
+              E = __fmaf_rn(g.x, E, __fmul_rn(g.y, u0));
+              op[(2 * j) * kPsD] = __float2bfloat16_rn(E);
+              E = __fmaf_rn(g.z, E, __fmul_rn(g.w, u1));
+              op[(2 * j + 1) * kPsD] = __float2bfloat16_rn(E);
+            }
+          } else {
+            // ---- the recurrence into the group's [32][128] tile, then rotary + norm per token ----
+            named_barrier(gbar, 128);  // every transpose buffer of the group is read
+            __nv_bfloat16* sg = reinterpret_cast<__nv_bfloat16*>(stg) + c;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const uint32_t w = pk[j];
+              const float u0 = __uint_as_float(w << 16), u1 = __uint_as_float(w & 0xffff0000u);
+              const float4 g = *reinterpret_cast<const float4*>(gw + tb + 2 * j);
+              E = __fmaf_rn(g.x, E, __fmul_rn(g.y, u0));
+              sg[(2 * j) * kPsD] = __float2bfloat16_rn(E);
+              E = __fmaf_rn(g.z, E, __fmul_rn(g.w, u1));
+              sg[(2 * j + 1) * kPsD] = __float2bfloat16_rn(E);
+            }
+            named_barrier(gbar, 128);  // the tile is complete
+            const uint32_t* s32 = reinterpret_cast<const uint32_t*>(stg);
+            float y[8][4], ss[8];
+#pragma unroll
+            for (int tt = 0; tt < 8; ++tt) {
+              const int t = q * 8 + tt;
+              uint32_t r1, r2;
+              rope_rotate_bf16x2(s32[t * (kPsD / 2) + lane], s32[t * (kPsD / 2) + 32 + lane], rcos[tt], rsin[tt],
+                                 r1, r2);
+              y[tt][0] = bf16_lo(r1); y[tt][1] = bf16_hi(r1); y[tt][2] = bf16_lo(r2); y[tt][3] = bf16_hi(r2);
+              ss[tt] = 0.f;
+#pragma unroll
+              for (int e = 0; e < 4; ++e) ss[tt] = __fmaf_rn(y[tt][e], y[tt][e], ss[tt]);
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+              for (int tt = 0; tt < 8; ++tt) ss[tt] += __shfl_xor_sync(0xffffffffu, ss[tt], o);
+            }
+#pragma unroll
+            for (int tt = 0; tt < 8; ++tt) {
+              const float inv = rope_inv_rms(ss[tt], kPsD, prm.rope_eps);
+              uint32_t* orow32 = reinterpret_cast<uint32_t*>(orow + (long long)(c0 + q * 8 + tt) * kPsD);
+              orow32[lane] = pack_bf16x2(y[tt][0] * inv, y[tt][1] * inv);
+              orow32[32 + lane] = pack_bf16x2(y[tt][2] * inv, y[tt][3] * inv);
+            }
+            named_barrier(gbar, 128);  // the tile is read: the buffers are free again
+#pragma unroll
+            for (int tt = 0; tt < 8; ++tt) { pcos[tt] = ncos[tt]; psin[tt] = nsin[tt]; }
           }
           // the state entering the next 32 tokens: the backward replays each 32-token chunk from
           // it instead of re-reading the chunk's outputs (a warp writes 128 contiguous bytes)
           if (prm.ckpt != nullptr && c0 + 32 < prm.T)
             prm.ckpt[(((long long)b * prm.H + hh) * (prm.T / 32) + c0 / 32) * kPsD + c] = E;
         }
+        if (!ok) break;
         // all TMEM reads of this accumulator are complete (tcgen05.wait::ld above)
         tc_fence_before();
         __syncwarp();

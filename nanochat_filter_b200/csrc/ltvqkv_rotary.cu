@@ -53,11 +53,6 @@ LTVQKV_DEVICE void rst2(void* p, long long i, float x, float y) {
   if constexpr (sizeof(S) == 4) *reinterpret_cast<float2*>(reinterpret_cast<float*>(p) + i) = make_float2(x, y);
   else *reinterpret_cast<__nv_bfloat162*>(reinterpret_cast<__nv_bfloat16*>(p) + i) = __floats2bfloat162_rn(x, y);
 }
-template <typename S>
-LTVQKV_DEVICE float rq(float v) {  // rounding to the storage dtype
-  if constexpr (sizeof(S) == 4) return v;
-  else return __bfloat162float(__float2bfloat16_rn(v));
-}
 
 // CTA row y -> (tensor, b, head): q heads first. Each warp then walks tokens (one row per token),
 // so consecutive warps stream consecutive rows of the filter's head-major storage.
@@ -70,11 +65,34 @@ LTVQKV_DEVICE void rot_head(const RotArgs& a, int y, int& w, int& b, int& hh) {
   b = r / nh;
 }
 
-// The rotated row element pair (j, j + d) in the storage dtype's rounding.
+// The rotated row element pair (j, j + d) in the storage dtype's rounding (ltvqkv_common.cuh).
 template <typename S>
 LTVQKV_DEVICE void rotate(float x1, float x2, float c, float s, float& y1, float& y2) {
-  y1 = rq<S>(__fadd_rn(rq<S>(__fmul_rn(x1, c)), rq<S>(__fmul_rn(x2, s))));
-  y2 = rq<S>(__fadd_rn(rq<S>(__fmul_rn(x1, rq<S>(-s))), rq<S>(__fmul_rn(x2, c))));
+  if constexpr (sizeof(S) == 2) {
+    rope_rotate_bf16(x1, x2, c, s, y1, y2);
+  } else {
+    y1 = __fadd_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
+    y2 = __fadd_rn(__fmul_rn(x1, -s), __fmul_rn(x2, c));
+  }
+}
+
+// The rotated element pairs (j, j + 1) and (j + d, j + d + 1) of a row from adjacent-pair loads at
+// element offsets i1 (= j) and i2 (= j + d); bf16 rows rotate as packed pairs (ltvqkv_common.cuh).
+template <typename S>
+LTVQKV_DEVICE void rotate2(const void* x, long long i1, long long i2, const void* cos, const void* sin, long long ci,
+                           float& y10, float& y11, float& y20, float& y21) {
+  if constexpr (sizeof(S) == 2) {
+    const uint32_t* x32 = reinterpret_cast<const uint32_t*>(x);
+    uint32_t r1, r2;
+    rope_rotate_bf16x2(x32[i1 / 2], x32[i2 / 2], reinterpret_cast<const uint32_t*>(cos)[ci / 2],
+                       reinterpret_cast<const uint32_t*>(sin)[ci / 2], r1, r2);
+    y10 = bf16_lo(r1); y11 = bf16_hi(r1); y20 = bf16_lo(r2); y21 = bf16_hi(r2);
+  } else {
+    const float2 c = rld2<S>(cos, ci), sn = rld2<S>(sin, ci);
+    const float2 x1 = rld2<S>(x, i1), x2 = rld2<S>(x, i2);
+    rotate<S>(x1.x, x2.x, c.x, sn.x, y10, y20);
+    rotate<S>(x1.y, x2.y, c.y, sn.y, y11, y21);
+  }
 }
 
 constexpr int kRotMaxPer = 8;  // elements per lane and half (D <= 512; odd D <= 256)
@@ -100,17 +118,14 @@ __global__ void __launch_bounds__(256, 4) rotary_norm_fwd_kernel(RotArgs a) {
       const int j = 2 * (lane + 32 * n);
       y[0][n] = y[1][n] = y[2][n] = y[3][n] = 0.f;
       if (j < d) {
-        const float2 c = rld2<S>(a.cos, t * a.cs[0] + j), sn = rld2<S>(a.sin, t * a.cs[0] + j);
-        const float2 x1 = rld2<S>(a.x[w], xb + j), x2 = rld2<S>(a.x[w], xb + j + d);
-        rotate<S>(x1.x, x2.x, c.x, sn.x, y[0][n], y[2][n]);
-        rotate<S>(x1.y, x2.y, c.y, sn.y, y[1][n], y[3][n]);
+        rotate2<S>(a.x[w], xb + j, xb + j + d, a.cos, a.sin, t * a.cs[0] + j, y[0][n], y[1][n], y[2][n], y[3][n]);
 #pragma unroll
         for (int e = 0; e < 4; ++e) ss = __fmaf_rn(y[e][n], y[e][n], ss);
       }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    const float inv = rsqrtf(ss / (float)a.D + a.eps);
+    const float inv = rope_inv_rms(ss, a.D, a.eps);
 #pragma unroll
     for (int n = 0; n < kRotMaxPer / 2; ++n) {
       const int j = 2 * (lane + 32 * n);
@@ -141,7 +156,7 @@ __global__ void __launch_bounds__(256, 4) rotary_norm_fwd_kernel(RotArgs a) {
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-  const float inv = rsqrtf(ss / (float)a.D + a.eps);
+  const float inv = rope_inv_rms(ss, a.D, a.eps);
 #pragma unroll
   for (int n = 0; n < kRotMaxPer; ++n) {
     const int j = lane + 32 * n;
@@ -182,9 +197,7 @@ __global__ void __launch_bounds__(256, 3) rotary_norm_bwd_kernel(RotArgs a) {
       if (j < d) {
         const float2 c = rld2<S>(a.cos, t * a.cs[0] + j), sn = rld2<S>(a.sin, t * a.cs[0] + j);
         c2[0][n] = c.x; c2[1][n] = c.y; s2[0][n] = sn.x; s2[1][n] = sn.y;
-        const float2 x1 = rld2<S>(a.x[w], xb + j), x2 = rld2<S>(a.x[w], xb + j + d);
-        rotate<S>(x1.x, x2.x, c.x, sn.x, y[0][n], y[2][n]);
-        rotate<S>(x1.y, x2.y, c.y, sn.y, y[1][n], y[3][n]);
+        rotate2<S>(a.x[w], xb + j, xb + j + d, a.cos, a.sin, t * a.cs[0] + j, y[0][n], y[1][n], y[2][n], y[3][n]);
         const float2 ga = rld2<S>(a.g[w], gb + j), gbb = rld2<S>(a.g[w], gb + j + d);
         g[0][n] = ga.x; g[1][n] = ga.y; g[2][n] = gbb.x; g[3][n] = gbb.y;
 #pragma unroll
@@ -199,8 +212,8 @@ __global__ void __launch_bounds__(256, 3) rotary_norm_bwd_kernel(RotArgs a) {
       ss += __shfl_xor_sync(0xffffffffu, ss, o);
       gy += __shfl_xor_sync(0xffffffffu, gy, o);
     }
-    const float r = rsqrtf(ss / (float)a.D + a.eps);
-    const float k3 = r * r * r * gy / (float)a.D;
+    const float r = rope_inv_rms(ss, a.D, a.eps);
+    const float k3 = rope_k3(r, gy, a.D);
 #pragma unroll
     for (int n = 0; n < NP; ++n) {
       const int j = 2 * (lane + 32 * n);
@@ -208,9 +221,7 @@ __global__ void __launch_bounds__(256, 3) rotary_norm_bwd_kernel(RotArgs a) {
         float dx1[2], dx2[2];
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-          const float dy1 = r * g[e][n] - y[e][n] * k3, dy2 = r * g[2 + e][n] - y[2 + e][n] * k3;
-          dx1[e] = dy1 * c2[e][n] - dy2 * s2[e][n];
-          dx2[e] = dy1 * s2[e][n] + dy2 * c2[e][n];
+          rope_norm_bwd(r, k3, g[e][n], g[2 + e][n], y[e][n], y[2 + e][n], c2[e][n], s2[e][n], dx1[e], dx2[e]);
         }
         rst2<S>(a.out[w], ob + j, dx1[0], dx1[1]);
         rst2<S>(a.out[w], ob + j + d, dx2[0], dx2[1]);
@@ -244,22 +255,146 @@ __global__ void __launch_bounds__(256, 3) rotary_norm_bwd_kernel(RotArgs a) {
     ss += __shfl_xor_sync(0xffffffffu, ss, o);
     gy += __shfl_xor_sync(0xffffffffu, gy, o);
   }
-  const float r = rsqrtf(ss / (float)a.D + a.eps);
-  const float k3 = r * r * r * gy / (float)a.D;
+  const float r = rope_inv_rms(ss, a.D, a.eps);
+  const float k3 = rope_k3(r, gy, a.D);
 #pragma unroll
   for (int n = 0; n < kRotMaxPer; ++n) {
     const int j = lane + 32 * n;
     if (j < half) {
-      const float dy1 = r * g1[n] - y1[n] * k3;
       if (rot) {
-        const float dy2 = r * g2[n] - y2[n] * k3;
-        rst<S>(a.out[w], ob + j * os[3], dy1 * cs_[n] - dy2 * sn_[n]);
-        rst<S>(a.out[w], ob + (j + d) * os[3], dy1 * sn_[n] + dy2 * cs_[n]);
+        float dx1, dx2;
+        rope_norm_bwd(r, k3, g1[n], g2[n], y1[n], y2[n], cs_[n], sn_[n], dx1, dx2);
+        rst<S>(a.out[w], ob + j * os[3], dx1);
+        rst<S>(a.out[w], ob + (j + d) * os[3], dx2);
       } else {
-        rst<S>(a.out[w], ob + j * os[3], dy1);
+        rst<S>(a.out[w], ob + j * os[3], __fmaf_rn(r, g1[n], -__fmul_rn(y1[n], k3)));
       }
     }
   }
+  }
+}
+
+// ------------------------------------------------------------------------------------------
+// Backward of the prologue folded into the fused forward (ltvqkv_proj_scan_fwd_ckpt_rope): that
+// forward never stores the raw q / k, so the rotary backward replays them from the scan's
+// checkpoints. One CTA (128 threads) per (32-token chunk, batch, q or k head), chunk-major so that
+// concurrent CTAs share the chunk's table lines. Replay: thread c walks channel c of the chunk from
+// the state entering it (the checkpoint, or the initial state for the first chunk) with the
+// forward's arithmetic (E = fma(1 - a, E, a u), a = sigmoid(logit + bias), u the stored bf16
+// projection value), so the rebuilt h_t are the forward's raw outputs bit for bit; they go to
+// shared memory as a [32 token][128 channel] tile. Then each warp takes 8 tokens with the standalone
+// backward's lane layout and arithmetic (pairs (2l, 2l + 1) and (2l + 64, 2l + 65)), so dq / dk equal
+// ltvqkv_rotary_qk_norm_bwd's on the stored raw outputs bit for bit.
+// ------------------------------------------------------------------------------------------
+struct RopeCkptArgs {
+  const __nv_bfloat16* combined;  // [B][F][T]
+  const __nv_bfloat16* inits;     // [B][H][128] (sequences inits_bs elements apart; 0: shared)
+  long long inits_bs;
+  const float* logit_bias;        // [H]
+  const float* ckpt;              // [B][H][T / 32][128]
+  const __nv_bfloat16* cos;       // [T][64], rows cs elements apart
+  const __nv_bfloat16* sin;
+  long long cs;
+  const __nv_bfloat16* g[2];      // gradients of the rotated, normalised q / k
+  long long gs[2][4];
+  __nv_bfloat16* d[2];            // gradients of the raw q / k
+  long long ds[2][4];
+  int B, T, NH, NKVH, H, F, nchunks, use_sigmoid;
+  float eps;
+};
+
+constexpr int kRopeTT = 32;
+
+__global__ void __launch_bounds__(128, 8) rope_bwd_ckpt_kernel(RopeCkptArgs a) {
+  __shared__ float gate[2][kRopeTT];                 // (1 - a_t, a_t)
+  __shared__ __align__(16) uint32_t hs[kRopeTT][64];  // raw h_t, bf16 pairs
+  const int rows = a.B * (a.NH + a.NKVH);
+  const int j = blockIdx.x / rows, row = blockIdx.x % rows;
+  const int b = row / (a.NH + a.NKVH), h = row % (a.NH + a.NKVH);  // q heads, then k heads
+  const int w = h < a.NH ? 0 : 1, hloc = h < a.NH ? h : h - a.NH;
+  const int tid = threadIdx.x, lane = tid % 32, warp = tid / 32;
+  const int t0 = j * kRopeTT;
+  const long long frow = (long long)b * a.F + (long long)h * 129;
+  if (tid < kRopeTT) {
+    const float l = __bfloat162float(a.combined[(frow + 128) * a.T + t0 + tid]) + a.logit_bias[h];
+    const float al = a.use_sigmoid ? sigmoid_f32(l) : l;
+    gate[0][tid] = 1.0f - al;
+    gate[1][tid] = al;
+  }
+  float E = j == 0 ? __bfloat162float(a.inits[(long long)b * a.inits_bs + (long long)h * 128 + tid])
+                   : a.ckpt[(((long long)b * a.H + h) * a.nchunks + (j - 1)) * 128 + tid];
+  const uint4* urow = reinterpret_cast<const uint4*>(a.combined + (frow + tid) * a.T + t0);
+  uint4 u4[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) u4[k] = __ldg(urow + k);
+  __syncthreads();
+  __nv_bfloat16* hs16 = reinterpret_cast<__nv_bfloat16*>(&hs[0][0]);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const uint32_t wv[4] = {u4[k].x, u4[k].y, u4[k].z, u4[k].w};
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int t = 8 * k + e;
+      const float u = (e & 1) ? bf16_hi(wv[e / 2]) : bf16_lo(wv[e / 2]);
+      E = __fmaf_rn(gate[0][t], E, __fmul_rn(gate[1][t], u));
+      hs16[t * 128 + tid] = __float2bfloat16_rn(E);
+    }
+  }
+  __syncthreads();
+  // rotary + norm backward of this warp's 8 tokens, four at a time
+  const long long* gs = a.gs[w];
+  const long long* dsr = a.ds[w];
+#pragma unroll 1
+  for (int half = 0; half < 2; ++half) {
+    uint32_t cw[4], sw[4], gA[4], gB[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int t = t0 + warp * 8 + half * 4 + e;
+      const long long tr = (long long)t * a.cs;
+      cw[e] = __ldg(reinterpret_cast<const uint32_t*>(a.cos + tr) + lane);
+      sw[e] = __ldg(reinterpret_cast<const uint32_t*>(a.sin + tr) + lane);
+      const __nv_bfloat16* gr = a.g[w] + b * gs[0] + hloc * gs[1] + t * gs[2];
+      gA[e] = __ldg(reinterpret_cast<const uint32_t*>(gr) + lane);
+      gB[e] = __ldg(reinterpret_cast<const uint32_t*>(gr + 64) + lane);
+    }
+    float y[4][4], g[4][4], ss[4], gy[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int t = warp * 8 + half * 4 + e;
+      uint32_t r1, r2;
+      rope_rotate_bf16x2(hs[t][lane], hs[t][32 + lane], cw[e], sw[e], r1, r2);
+      y[e][0] = bf16_lo(r1); y[e][1] = bf16_hi(r1); y[e][2] = bf16_lo(r2); y[e][3] = bf16_hi(r2);
+      g[e][0] = bf16_lo(gA[e]); g[e][1] = bf16_hi(gA[e]); g[e][2] = bf16_lo(gB[e]); g[e][3] = bf16_hi(gB[e]);
+      ss[e] = 0.f;
+      gy[e] = 0.f;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        ss[e] = __fmaf_rn(y[e][q], y[e][q], ss[e]);
+        gy[e] = __fmaf_rn(g[e][q], y[e][q], gy[e]);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        ss[e] += __shfl_xor_sync(0xffffffffu, ss[e], o);
+        gy[e] += __shfl_xor_sync(0xffffffffu, gy[e], o);
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int t = t0 + warp * 8 + half * 4 + e;
+      const float r = rope_inv_rms(ss[e], 128, a.eps);
+      const float k3 = rope_k3(r, gy[e], 128);
+      float dx1[2], dx2[2];
+#pragma unroll
+      for (int q = 0; q < 2; ++q)
+        rope_norm_bwd(r, k3, g[e][q], g[e][2 + q], y[e][q], y[e][2 + q], bf16_lane(cw[e], q), bf16_lane(sw[e], q),
+                      dx1[q], dx2[q]);
+      __nv_bfloat16* dr = a.d[w] + b * dsr[0] + hloc * dsr[1] + t * dsr[2];
+      reinterpret_cast<uint32_t*>(dr)[lane] = pack_bf16x2(dx1[0], dx1[1]);
+      reinterpret_cast<uint32_t*>(dr + 64)[lane] = pack_bf16x2(dx2[0], dx2[1]);
+    }
   }
 }
 
@@ -314,6 +449,60 @@ extern "C" int ltvqkv_rotary_qk_norm_fwd(int dtype, const void* q, const int64_t
   if (B * (NH + NKVH) > 65535) return LTVQKV_ERR_SHAPE;
   if (dtype == LTVQKV_DTYPE_F32) rotary_norm_fwd_kernel<float><<<grid, 256, 0, s>>>(a);
   else rotary_norm_fwd_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(a);
+  return ltvqkv_host::check_launch();
+}
+
+extern "C" int ltvqkv_rotary_qk_norm_bwd_ckpt(int dtype, const void* combined, const void* inits, int64_t inits_bs,
+                                              const float* logit_bias, const float* ckpt, const void* rope_cos,
+                                              const void* rope_sin, int64_t rope_stride, float eps,
+                                              const void* grad_q, const int64_t* gq_strides, const void* grad_k,
+                                              const int64_t* gk_strides, void* dq, const int64_t* dq_strides,
+                                              void* dk, const int64_t* dk_strides, int B, int T, int NH, int NKVH,
+                                              int Da, int r, int use_sigmoid, void* stream) {
+  if (dtype != LTVQKV_DTYPE_BF16) return LTVQKV_ERR_DTYPE;
+  if (B < 0 || T < 0 || NH < 0 || NKVH < 0 || Da != 1 || r != 128 || T % kRopeTT != 0) return LTVQKV_ERR_SHAPE;
+  const int H = NH + 2 * NKVH;
+  if (!combined || !inits || !logit_bias || !ckpt || !rope_cos || !rope_sin) return LTVQKV_ERR_INVALID_ARG;
+  if ((NH > 0 && (!grad_q || !gq_strides || !dq || !dq_strides)) ||
+      (NKVH > 0 && (!grad_k || !gk_strides || !dk || !dk_strides)))
+    return LTVQKV_ERR_INVALID_ARG;
+  if (inits_bs != 0 && inits_bs != (int64_t)H * 128) return LTVQKV_ERR_STRIDE;
+  if (rope_stride < 64 || rope_stride % 2 != 0 || (reinterpret_cast<uintptr_t>(rope_cos) & 3u) != 0 ||
+      (reinterpret_cast<uintptr_t>(rope_sin) & 3u) != 0)
+    return LTVQKV_ERR_STRIDE;
+  // the u rows are read as 16-byte pieces: combined 16-byte aligned with T % 8 == 0 (T % 32 == 0 here);
+  // gradient rows as bf16 pairs: unit channel stride, even other strides, 4-byte aligned
+  if ((reinterpret_cast<uintptr_t>(combined) & 15u) != 0) return LTVQKV_ERR_ALIGN;
+  auto pairs_ok = [](const void* p, const int64_t* st) {
+    return p == nullptr || ((reinterpret_cast<uintptr_t>(p) & 3u) == 0 && st[3] == 1 && st[0] % 2 == 0 &&
+                            st[1] % 2 == 0 && st[2] % 2 == 0);
+  };
+  if (!pairs_ok(NH > 0 ? grad_q : nullptr, gq_strides) || !pairs_ok(NKVH > 0 ? grad_k : nullptr, gk_strides) ||
+      !pairs_ok(NH > 0 ? dq : nullptr, dq_strides) || !pairs_ok(NKVH > 0 ? dk : nullptr, dk_strides))
+    return LTVQKV_ERR_STRIDE;
+  const long long ctas = (long long)B * (NH + NKVH) * (T / kRopeTT);
+  if (ctas == 0) return LTVQKV_OK;
+  if (ctas > 0x7fffffffLL) return LTVQKV_ERR_SHAPE;
+  RopeCkptArgs a = {};
+  a.combined = reinterpret_cast<const __nv_bfloat16*>(combined);
+  a.inits = reinterpret_cast<const __nv_bfloat16*>(inits);
+  a.inits_bs = inits_bs;
+  a.logit_bias = logit_bias;
+  a.ckpt = ckpt;
+  a.cos = reinterpret_cast<const __nv_bfloat16*>(rope_cos);
+  a.sin = reinterpret_cast<const __nv_bfloat16*>(rope_sin);
+  a.cs = rope_stride;
+  a.g[0] = reinterpret_cast<const __nv_bfloat16*>(grad_q);
+  a.g[1] = reinterpret_cast<const __nv_bfloat16*>(grad_k);
+  a.d[0] = reinterpret_cast<__nv_bfloat16*>(dq);
+  a.d[1] = reinterpret_cast<__nv_bfloat16*>(dk);
+  for (int i = 0; i < 4; ++i) {
+    a.gs[0][i] = gq_strides ? gq_strides[i] : 0; a.gs[1][i] = gk_strides ? gk_strides[i] : 0;
+    a.ds[0][i] = dq_strides ? dq_strides[i] : 0; a.ds[1][i] = dk_strides ? dk_strides[i] : 0;
+  }
+  a.B = B; a.T = T; a.NH = NH; a.NKVH = NKVH; a.H = H; a.F = H * 129; a.nchunks = T / kRopeTT;
+  a.use_sigmoid = use_sigmoid; a.eps = eps;
+  rope_bwd_ckpt_kernel<<<(unsigned int)ctas, 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
   return ltvqkv_host::check_launch();
 }
 

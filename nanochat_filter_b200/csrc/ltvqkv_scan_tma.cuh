@@ -117,11 +117,6 @@ constexpr int row_bwd_min_blocks(int D, int tt, bool ckpt) {
 
 // 16-byte chunk k of row `row` in a tile of kTT bf16 per row, as TMA writes it with the 128-byte
 // (kTT = 64) or 64-byte (kTT = 32) swizzle.
-// Two floats rounded to bf16 and packed (lo in the low half), as one 32-bit shared-memory word.
-LTVQKV_DEVICE uint32_t pack_bf16x2(float lo, float hi) {
-  const __nv_bfloat162 p = __floats2bfloat162_rn(lo, hi);
-  return *reinterpret_cast<const uint32_t*>(&p);
-}
 
 template <int kTT>
 LTVQKV_DEVICE const uint4* swz_chunk(const uint8_t* tile, int row, int k) {

@@ -151,6 +151,32 @@ class LtvCudaFusedConcatHeadMajorRegisterCastBlellochScanQkvFilter(LtvCombinedHe
             hq, hk, hv = hq.to(kernel_combined.dtype), hk.to(kernel_combined.dtype), hv.to(kernel_combined.dtype)
         return hq.transpose(1, 2), hk.transpose(1, 2), hv.transpose(1, 2)
 
+    def forward_rotary_norm(self, x, previous_values: LtvInitValues, cos_sin):
+        """forward() followed by the reference attention's prologue on q and k (nanochat/gpt.py:224-230:
+        apply_rotary_emb, then norm): returns (q, k, v) [B, T, heads, D], q and k rotated and
+        RMS-normalised, v the raw filter output. bf16 sequences on the one-kernel shapes run the
+        prologue inside the filter's own kernels (the scan's epilogue forward, the checkpoint replay
+        backward), so the extra pass over q and k disappears; results equal forward() followed by the
+        fused rotary + norm operator bit for bit, which is what every other case runs."""
+        cos, sin = cos_sin
+        B, T, _ = x.size()
+        autocast_dtype = torch.get_autocast_dtype("cuda")
+        run_ltv_in_fp32 = autocast_dtype == torch.float32 if CUDA_SUPPORTS_NATIVE_BF16 else True
+        decode = (self.use_decode_kernel and T == 1 and not run_ltv_in_fp32 and x.is_cuda
+                  and not (torch.is_grad_enabled() and (x.requires_grad or self.c.weight.requires_grad)))
+        if not run_ltv_in_fp32 and not decode:
+            if previous_values.q is None:
+                inits = self.init_param
+            else:
+                inits = resolve_inits_original_dtype(B, self.init_param, previous_values).to(dtype=x.dtype).contiguous()
+            hq, hk, hv = _ops.ltv_proj_scan_rope_norm(x.contiguous(), self.c.weight, inits,
+                                                      self.logit_bias.contiguous(), cos, sin, self.n_head,
+                                                      self.n_kv_head, self.num_alpha_groups, self.r, True)
+            return hq.transpose(1, 2), hk.transpose(1, 2), hv.transpose(1, 2)
+        q, k, v = self.forward(x, previous_values)
+        q, k = _ops.rotary_qk_norm(q, k, cos, sin)
+        return q, k, v
+
     def _decode(self, x, previous_values: LtvInitValues):
         B = x.shape[0]
         pq = pk = pv = None

@@ -11,6 +11,7 @@ from typing import Optional
 
 import torch.nn as nn
 
+from . import ops as _ops
 from .filters import LtvCombinedQkvFilterBase
 from .kv_cache import KVCache
 from .util import LtvInitValues
@@ -32,6 +33,19 @@ class LtvCombinedQkvComputerModule(nn.Module):
         q, k, v = self.ltv_filter(x, previous_values)
         if kv_cache:
             kv_cache.update_last_qkv(self.layer_idx, q[:, -1, :, :], k[:, -1, :, :], v[:, -1, :, :])
+        return q, k, v
+
+    def forward_rotary_norm(self, x, kv_cache: Optional[KVCache], cos_sin):
+        """forward() followed by the attention's prologue on q and k (nanochat/gpt.py:224-230:
+        apply_rotary_emb with `cos_sin`, then norm); v as forward() returns it. Without a KV cache
+        (training) filters that have `forward_rotary_norm` fold the prologue into their kernels; with a
+        cache the raw last states go into it as forward() stores them, and the prologue runs as the
+        fused rotary + norm operator."""
+        fused = getattr(self.ltv_filter, "forward_rotary_norm", None)
+        if not kv_cache and fused is not None:
+            return fused(x, LtvInitValues(None, None, None), cos_sin)
+        q, k, v = self.forward(x, kv_cache)
+        q, k = _ops.rotary_qk_norm(q, k, cos_sin[0], cos_sin[1])
         return q, k, v
 
     def init_weights(self, alpha_mlp_bias_init: float, weight_s: float, bias_s: float, init_s: float):

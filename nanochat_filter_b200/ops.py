@@ -130,6 +130,18 @@ lib.define(
 )
 lib.define("ltv_rotary_qk_norm(Tensor q, Tensor k, Tensor cos, Tensor sin) -> (Tensor, Tensor)")
 lib.define(
+    "ltv_proj_scan_rope_norm_cuda_op("
+    "Tensor x, Tensor weight, Tensor inits, Tensor logit_bias, Tensor cos, Tensor sin, int NH, int NKVH, int da, "
+    "int r, bool use_sigmoid"
+    ") -> (Tensor, Tensor, Tensor, Tensor, Tensor)"
+)
+lib.define(
+    "ltv_rotary_qk_norm_ckpt_backward("
+    "Tensor combined, Tensor inits, Tensor logit_bias, Tensor ckpt, Tensor cos, Tensor sin, Tensor grad_q, "
+    "Tensor grad_k, int NH, int NKVH, int da, int r, bool use_sigmoid"
+    ") -> (Tensor, Tensor)"
+)
+lib.define(
     "ltv_rotary_qk_norm_backward(Tensor q, Tensor k, Tensor cos, Tensor sin, Tensor grad_q, Tensor grad_k) "
     "-> (Tensor, Tensor)"
 )
@@ -816,6 +828,198 @@ def _rot_bwd_fake(q, k, cos, sin, grad_q, grad_k):
 
 
 # ------------------------------------------------------------------------------------------
+# Projection + scan forward with the attention's q / k prologue (rotary + RMS norm) in the scan's
+# epilogue, and the matching checkpoint backward
+# ------------------------------------------------------------------------------------------
+def _rope_tables(cos, sin, x, D):
+    """The rotary tables as [T, D/2] rows of x's dtype that the kernels read as bf16 pairs (unit
+    element stride, even row stride, 4-byte aligned); the model's [1, T, 1, D/2] buffers and their
+    position slices pass as views."""
+    cos, sin = _rot_cs(cos, sin, x)
+    T = x.shape[1]
+    if tuple(cos.shape) != (T, D // 2) or tuple(sin.shape) != (T, D // 2):
+        raise RuntimeError(f"cos/sin must hold [T, D/2] = {(T, D // 2)} values, got {tuple(cos.shape)}")
+
+    def ok(t):
+        return t.stride(1) == 1 and t.stride(0) % 2 == 0 and t.data_ptr() % 4 == 0
+
+    if not (ok(cos) and ok(sin) and cos.stride() == sin.stride()):
+        cos, sin = cos.contiguous(), sin.contiguous()
+    return cos, sin
+
+
+def _proj_scan_rope_op(x, weight, inits, logit_bias, cos, sin, NH, NKVH, da, r, use_sigmoid):
+    """ltv_proj_scan_cuda_op whose q and k outputs are rotated and RMS-normalised (nanochat/gpt.py:
+    224-230, `apply_rotary_emb` then `norm`): outputs equal ltv_proj_scan_cuda_op followed by
+    ltv_rotary_qk_norm bit for bit. On the one-kernel shapes (ltv_proj_scan_cuda_op's checkpoint
+    condition) the prologue runs inside the scan's epilogue and the raw q / k are never stored;
+    elsewhere the two operators run in sequence (the fifth output is then empty)."""
+    if not x.is_contiguous() or x.dim() != 3:
+        raise RuntimeError("ltv_proj_scan_rope_norm_cuda_op requires a contiguous [B, T, C] x")
+    shape = _ckpt_shape(x, NH, NKVH, da, r)
+    if len(shape) != 4:
+        combined, q, k, v, ckpt = _proj_scan_op(x, weight, inits, logit_bias, NH, NKVH, da, r, use_sigmoid)
+        qn, kn = _rotary_qk_norm(q.transpose(1, 2), k.transpose(1, 2), cos, sin)
+        return combined, qn.transpose(1, 2), kn.transpose(1, 2), v, ckpt
+    L = _lib.load()
+    B, T, C = x.shape
+    H = NH + 2 * NKVH
+    D = da * r
+    F = H * (D + da)
+    cos, sin = _rope_tables(cos, sin, x, D)
+    if x.data_ptr() % 16:
+        x = x.clone()
+    w = (weight if weight.dtype == x.dtype else weight.to(x.dtype)).contiguous()
+    if w.data_ptr() % 16:
+        w = w.clone()
+    if tuple(w.shape) != (F, C):
+        raise RuntimeError(f"weight must be [{F}, {C}], got {tuple(w.shape)}")
+    shared = inits.dim() == 2
+    inits_k = (inits.to(x.dtype) if shared else inits).contiguous()
+    kw = dict(device=x.device, dtype=x.dtype)
+    combined = torch.empty((B, F, T), **kw)
+    _check_scan_inputs(combined.transpose(1, 2), inits_k.unsqueeze(0).expand(B, -1, -1) if shared else inits_k,
+                       logit_bias, NH, NKVH, da, r)
+    logit_bias = logit_bias.contiguous()
+    out_q = torch.empty((B, NH, T, D), **kw)
+    out_k = torch.empty((B, NKVH, T, D), **kw)
+    out_v = torch.empty((B, NKVH, T, D), **kw)
+    ckpt = torch.empty(shape, device=x.device, dtype=torch.float32)
+    nbytes = max(L.ltvqkv_scan_workspace_bytes(B, T, NH, NKVH, da, r), L.ltvqkv_gemm_workspace_bytes())
+    ws = _lib.workspace(x.device, nbytes)
+    rc = L.ltvqkv_proj_scan_fwd_ckpt_rope(
+        _lib.dtype_code(x.dtype), x.data_ptr(), w.data_ptr(), inits_k.data_ptr(), 0 if shared else H * D,
+        logit_bias.data_ptr(), combined.data_ptr(), out_q.data_ptr(), out_k.data_ptr(), out_v.data_ptr(),
+        ckpt.data_ptr(), cos.data_ptr(), sin.data_ptr(), cos.stride(0), _RMS_EPS, B, T, C, NH, NKVH, da, r,
+        int(bool(use_sigmoid)), ws.data_ptr(), ws.numel(), _lib.stream_handle(x.device))
+    _lib.check(rc, "ltvqkv_proj_scan_fwd_ckpt_rope")
+    return combined, out_q, out_k, out_v, ckpt
+
+
+def _rotary_qk_norm_ckpt_backward(combined, inits, logit_bias, ckpt, cos, sin, grad_q, grad_k, NH, NKVH, da, r,
+                                  use_sigmoid):
+    """Gradients of the raw q / k ([B, heads, T, D], head-major) from those of the rotated, normalised
+    q / k that ltv_proj_scan_rope_norm_cuda_op returned, the raw values replayed from its state
+    checkpoints: ltv_rotary_qk_norm_backward's results on the raw outputs, bit for bit."""
+    L = _lib.load()
+    B, T, _ = combined.shape
+    H, D = NH + 2 * NKVH, da * r
+    shared = inits.dim() == 2
+    _check_scan_inputs(combined, inits.unsqueeze(0).expand(B, -1, -1) if shared else inits, logit_bias, NH, NKVH,
+                       da, r)
+    comb = combined.transpose(1, 2)  # the [B, F, T] projection buffer
+    if not comb.is_contiguous():
+        raise RuntimeError("combined must be the transposed view of a contiguous [B, F, T] buffer")
+    cos, sin = _rope_tables(cos, sin, combined.new_empty((B, T, 0)), D)
+    inits = inits.contiguous()
+    logit_bias = logit_bias.contiguous()
+    if ckpt.dtype != torch.float32 or not ckpt.is_contiguous() or tuple(ckpt.shape) != (B, H, T // 32, D):
+        raise RuntimeError("ckpt must be the forward's contiguous [B, H, T / 32, D] float32 checkpoints")
+
+    def pairs(g):
+        st = g.stride()
+        ok = st[3] == 1 and all(x % 2 == 0 for x in st[:3]) and g.data_ptr() % 4 == 0
+        return g if ok and g.dtype == combined.dtype else g.to(combined.dtype).contiguous()
+
+    grad_q, grad_k = pairs(grad_q), pairs(grad_k)
+    dq = torch.empty((B, NH, T, D), device=combined.device, dtype=combined.dtype)
+    dk = torch.empty((B, NKVH, T, D), device=combined.device, dtype=combined.dtype)
+    S = _lib.strides
+    rc = L.ltvqkv_rotary_qk_norm_bwd_ckpt(
+        _lib.dtype_code(combined.dtype), comb.data_ptr(), inits.data_ptr(), 0 if shared else H * D,
+        logit_bias.data_ptr(), ckpt.data_ptr(), cos.data_ptr(), sin.data_ptr(), cos.stride(0), _RMS_EPS,
+        grad_q.data_ptr(), S(grad_q.stride()), grad_k.data_ptr(), S(grad_k.stride()), dq.data_ptr(), S(dq.stride()),
+        dk.data_ptr(), S(dk.stride()), B, T, NH, NKVH, da, r, int(bool(use_sigmoid)), _lib.stream_handle(combined.device))
+    _lib.check(rc, "ltvqkv_rotary_qk_norm_bwd_ckpt")
+    return dq, dk
+
+
+def _psr_setup(ctx, inputs, output):
+    x, weight, inits, logit_bias, cos, sin, NH, NKVH, da, r, use_sigmoid = inputs
+    combined, oq, ok, ov, ckpt = output
+    ctx.set_materialize_grads(False)
+    ctx.mark_non_differentiable(ckpt)
+    ctx.save_for_backward(x, weight, combined, inits, logit_bias, cos, sin, ckpt)
+    ctx.args = (NH, NKVH, da, r)
+    ctx.out_shapes = (oq.shape, ok.shape, ov.shape)
+    ctx.use_sigmoid = use_sigmoid
+
+
+def _psr_backward(ctx, grad_comb, grad_q, grad_k, grad_v, _grad_ckpt):
+    # the checkpoint backward with the rotary + norm backward of q / k folded in, then the
+    # projection backward (operators only: AOTAutograd traces this with fake tensors)
+    x, weight, comb, inits, logit_bias, cos, sin, ckpt = ctx.saved_tensors
+    NH, NKVH, da, r = ctx.args
+    B, T = x.shape[0], x.shape[1]
+    shared = inits.dim() == 2
+    inits_k = inits.to(x.dtype) if shared else inits
+    combined = comb.transpose(1, 2)
+    zs = [x.new_zeros(sh) for sh in ctx.out_shapes]
+    grad_q = zs[0] if grad_q is None else grad_q
+    grad_k = zs[1] if grad_k is None else grad_k
+    grad_v = zs[2] if grad_v is None else grad_v
+    grad_combined = torch.empty_like(combined)
+    if ckpt.numel():
+        # the raw q / k gradients (raw outputs replayed from the checkpoints), then the checkpoint
+        # scan backward as for ltv_proj_scan_cuda_op
+        dq, dk = torch.ops.nanochat_cuda.ltv_rotary_qk_norm_ckpt_backward(combined, inits_k, logit_bias, ckpt, cos,
+                                                                          sin, grad_q, grad_k, NH, NKVH, da, r,
+                                                                          ctx.use_sigmoid)
+        grad_inits = (torch.empty(inits_k.shape, device=x.device, dtype=torch.float32) if shared
+                      else torch.empty_like(inits_k, memory_format=torch.contiguous_format))
+        grad_logit_bias = torch.empty_like(logit_bias, memory_format=torch.contiguous_format)
+        torch.ops.nanochat_cuda.ltv_scan_ckpt_backward_kernel(combined, inits_k, logit_bias, ckpt, dq, dk, grad_v,
+                                                              grad_combined, grad_inits, grad_logit_bias, NH, NKVH,
+                                                              da, r, ctx.use_sigmoid)
+    else:
+        # the two-operator forward's raw outputs, recomputed (the same kernel, so the same values),
+        # then the rotary backward and the scan backward as their own operators
+        ib = inits_k.unsqueeze(0).expand(B, -1, -1).contiguous() if shared else inits_k
+        hq, hk, hv = (x.new_empty(sh) for sh in ctx.out_shapes)
+        torch.ops.nanochat_cuda.ltv_fused_concat_head_major_register_cast_blelloch_scan_cuda_forward_kernel(
+            combined, ib, logit_bias, hq, hk, hv, T, NH, NKVH, da, r, 8, 8, 4, ctx.use_sigmoid)
+        dq, dk = torch.ops.nanochat_cuda.ltv_rotary_qk_norm_backward(hq.transpose(1, 2), hk.transpose(1, 2), cos, sin,
+                                                                     grad_q.transpose(1, 2), grad_k.transpose(1, 2))
+        grad_inits = torch.empty_like(ib, memory_format=torch.contiguous_format)
+        grad_logit_bias = torch.zeros_like(logit_bias, memory_format=torch.contiguous_format)
+        torch.ops.nanochat_cuda.ltv_fused_concat_head_major_register_cast_blelloch_scan_cuda_backward_kernel(
+            combined, ib, logit_bias, hq, hk, hv, dq.transpose(1, 2), dk.transpose(1, 2), grad_v, grad_combined,
+            grad_inits, grad_logit_bias, NH, NKVH, da, r, 32, 2, 8, ctx.use_sigmoid)
+        if shared:
+            grad_inits = grad_inits.float().sum(0)
+    if shared:
+        grad_inits = grad_inits.to(inits.dtype)
+    grad_out = grad_combined.transpose(1, 2)
+    if grad_comb is not None:
+        grad_out = grad_out + grad_comb
+    grad_x = torch.empty_like(x, memory_format=torch.contiguous_format)
+    grad_weight = torch.empty_like(weight, memory_format=torch.contiguous_format)
+    torch.ops.nanochat_cuda.fused_linear_transpose_backward_kernel(x, weight, grad_out, grad_x, grad_weight)
+    return (grad_x, grad_weight, grad_inits, grad_logit_bias, None, None) + (None,) * 5
+
+
+torch.library.register_autograd("nanochat_cuda::ltv_proj_scan_rope_norm_cuda_op", _psr_backward,
+                                setup_context=_psr_setup)
+
+
+@torch.library.register_fake("nanochat_cuda::ltv_proj_scan_rope_norm_cuda_op")
+def _proj_scan_rope_fake(x, weight, inits, logit_bias, cos, sin, NH, NKVH, da, r, use_sigmoid):
+    B, T, _ = x.shape
+    D = da * r
+    F = (NH + 2 * NKVH) * (D + da)
+    return (x.new_empty((B, F, T)), x.new_empty((B, NH, T, D)), x.new_empty((B, NKVH, T, D)),
+            x.new_empty((B, NKVH, T, D)), x.new_empty(_ckpt_shape(x, NH, NKVH, da, r), dtype=torch.float32))
+
+
+@torch.library.register_fake("nanochat_cuda::ltv_rotary_qk_norm_ckpt_backward")
+def _rotary_qk_norm_ckpt_backward_fake(combined, inits, logit_bias, ckpt, cos, sin, grad_q, grad_k, NH, NKVH, da, r,
+                                       use_sigmoid):
+    B, T, _ = combined.shape
+    D = da * r
+    return combined.new_empty((B, NH, T, D)), combined.new_empty((B, NKVH, T, D))
+
+
+# ------------------------------------------------------------------------------------------
 # Decode step
 # ------------------------------------------------------------------------------------------
 def _decode_step(x, weight, logit_bias, prev_q, prev_k, prev_v, init_param, NH, NKVH, da, r, use_sigmoid):
@@ -912,6 +1116,8 @@ for _kind in ("blelloch", "sequential"):
 torch.library.impl("nanochat_cuda::ltv_proj_scan_forward_kernel", "CUDA", _proj_scan_forward_kernel)
 torch.library.impl("nanochat_cuda::ltv_proj_scan_cuda_op", "CUDA", _proj_scan_op)
 torch.library.impl("nanochat_cuda::ltv_scan_ckpt_backward_kernel", "CUDA", _scan_ckpt_backward_kernel)
+torch.library.impl("nanochat_cuda::ltv_proj_scan_rope_norm_cuda_op", "CUDA", _proj_scan_rope_op)
+torch.library.impl("nanochat_cuda::ltv_rotary_qk_norm_ckpt_backward", "CUDA", _rotary_qk_norm_ckpt_backward)
 
 
 
@@ -947,6 +1153,19 @@ def ltv_proj_scan(x: torch.Tensor, weight: torch.Tensor, inits: torch.Tensor, lo
     the batch (any float dtype; its gradient is summed over the batch in the kernel)."""
     return torch.ops.nanochat_cuda.ltv_proj_scan_cuda_op(x, weight, inits, logit_bias, NH, NKVH, da, r,
                                                          use_sigmoid)[:4]
+
+
+def ltv_proj_scan_rope_norm(x: torch.Tensor, weight: torch.Tensor, inits: torch.Tensor, logit_bias: torch.Tensor,
+                            cos: torch.Tensor, sin: torch.Tensor, NH: int, NKVH: int, da: int, r: int,
+                            use_sigmoid: bool = True):
+    """The filter's projection and scan followed by the attention's q / k prologue
+    (nanochat/gpt.py:224-230: apply_rotary_emb, then norm): returns (q, k, v) [B, heads, T, D] with q
+    and k rotated and RMS-normalised, v the raw filter output. The one-kernel shapes run it inside the
+    scan's epilogue (and the backward's replay), others as ltv_proj_scan then ltv_rotary_qk_norm;
+    the results are the same bit for bit. cos / sin: the model's rotary tables for these positions,
+    [T, D/2] or [1, T, 1, D/2]."""
+    return torch.ops.nanochat_cuda.ltv_proj_scan_rope_norm_cuda_op(x.contiguous(), weight, inits, logit_bias, cos,
+                                                                   sin, NH, NKVH, da, r, use_sigmoid)[1:4]
 
 
 def rotary_qk_norm(q: torch.Tensor, k: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor):

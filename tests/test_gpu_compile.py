@@ -6,7 +6,8 @@ and AOTAutograd traces their registered backward formulas. Here the filter's for
 are compiled with fullgraph=True (any graph break raises) on the one-kernel shape (projection +
 scan with state checkpoints, checkpoint backward, batch-shared initial state) and on a shape that
 takes the two-operator path, and the compiled results must equal eager's (same kernels, so equal
-to the bit).
+to the bit). The same holds for the forward with the attention's q / k prologue folded in
+(`forward_rotary_norm`, nanochat/gpt.py:224-230).
 """
 
 from __future__ import annotations
@@ -19,15 +20,16 @@ from nanochat_filter_b200 import LtvCudaFusedConcatHeadMajorRegisterCastBlelloch
 pytestmark = pytest.mark.gpu
 
 
-def _run(f, x, grads):
-    q, k, v = f(x, LtvInitValues())
+def _run(fn, f, x, grads):
+    q, k, v = fn(x)
     torch.autograd.backward([q, k, v], list(grads))
     return [t.detach().clone() for t in (q, k, v, x.grad, f.c.weight.grad, f.logit_bias.grad, f.init_param.grad)]
 
 
+@pytest.mark.parametrize("rope", [False, True])
 @pytest.mark.parametrize("backend", ["aot_eager", "inductor"])
 @pytest.mark.parametrize("B,T,C", [(32, 64, 128), (2, 96, 256)])
-def test_filter_compiles_fullgraph_and_matches_eager(cuda_device, backend, B, T, C):
+def test_filter_compiles_fullgraph_and_matches_eager(cuda_device, backend, B, T, C, rope):
     dev = cuda_device
     NH, NKVH, D, r = 6, 6, 128, 128
     torch.manual_seed(0)
@@ -39,14 +41,21 @@ def test_filter_compiles_fullgraph_and_matches_eager(cuda_device, backend, B, T,
     x0 = torch.randn(B, T, C, device=dev, generator=g).to(torch.bfloat16)
     grads = [torch.randn(B, T, n, D, device=dev, generator=g).to(torch.bfloat16) for n in (NH, NKVH, NKVH)]
 
+    inv = 1.0 / (10000 ** (torch.arange(0, D, 2, dtype=torch.float32, device=dev) / D))
+    fr = torch.outer(torch.arange(T, dtype=torch.float32, device=dev), inv)
+    cs = (fr.cos().bfloat16()[None, :, None, :], fr.sin().bfloat16()[None, :, None, :])
+
+    def fn(x):
+        return f.forward_rotary_norm(x, LtvInitValues(), cs) if rope else f(x, LtvInitValues())
+
     x = x0.clone().requires_grad_(True)
-    eager = _run(f, x, grads)
+    eager = _run(fn, f, x, grads)
     f.zero_grad(set_to_none=True)
 
     torch._dynamo.reset()
-    cf = torch.compile(f, fullgraph=True, backend=backend)
+    cfn = torch.compile(fn, fullgraph=True, backend=backend)
     xc = x0.clone().requires_grad_(True)
-    comp = _run(cf, xc, grads)
+    comp = _run(cfn, f, xc, grads)
     torch.cuda.synchronize()
     names = ("q", "k", "v", "dx", "dW", "dbias", "dinit")
     for n, a, e in zip(names, comp, eager):

@@ -132,6 +132,34 @@ def test_filter_compiles_fullgraph_on_meta(B, T, C):
     assert f.init_param.grad.shape == (NH + 2 * NKVH, D) and f.logit_bias.grad.shape == (NH + 2 * NKVH, 1)
 
 
+@pytest.mark.parametrize("B,T,C", [(32, 64, 128), (2, 96, 256)])
+def test_forward_rotary_norm_compiles_fullgraph_on_meta(B, T, C):
+    """The filter's forward with the attention's q / k prologue folded in (ltv_proj_scan_rope_norm_cuda_op:
+    one-kernel shape with checkpoints, and the two-operator shape) traces with fullgraph=True, forward
+    and backward, and gives the reference prologue's shapes ([B, T, heads, D])."""
+    NH, NKVH, D, r = 6, 6, 128, 128
+    torch._dynamo.reset()
+    with torch.device("meta"):
+        f = nf.LtvCudaFusedConcatHeadMajorRegisterCastBlellochScanQkvFilter(NH, NKVH, D, r)
+        f.c = torch.nn.Linear(C, f.c.out_features, bias=False)
+        x = torch.empty(B, T, C, dtype=torch.bfloat16).requires_grad_(True)
+        cos = torch.empty(1, T, 1, D // 2, dtype=torch.bfloat16)
+        sin = torch.empty(1, T, 1, D // 2, dtype=torch.bfloat16)
+        grads = [torch.empty(B, T, n, D, dtype=torch.bfloat16) for n in (NH, NKVH, NKVH)]
+
+    def fwd(x):
+        return f.forward_rotary_norm(x, nf.LtvInitValues(), (cos, sin))
+
+    q, k, v = torch.compile(fwd, fullgraph=True, backend="aot_eager")(x)
+    assert q.shape == (B, T, NH, D) and k.shape == (B, T, NKVH, D) and v.shape == (B, T, NKVH, D)
+    torch.autograd.backward([q, k, v], grads)
+    assert x.grad.shape == x.shape and f.c.weight.grad.shape == f.c.weight.shape
+    assert f.init_param.grad.shape == (NH + 2 * NKVH, D) and f.logit_bias.grad.shape == (NH + 2 * NKVH, 1)
+    s = str(OPS.ltv_proj_scan_rope_norm_cuda_op.default._schema)
+    assert s.startswith("nanochat_cuda::ltv_proj_scan_rope_norm_cuda_op(Tensor x, Tensor weight, Tensor inits, "
+                        "Tensor logit_bias, Tensor cos, Tensor sin, int NH, int NKVH, int da, int r, bool use_sigmoid)")
+
+
 def test_ckpt_fake_shape_mirrors_the_kernel_condition():
     """The fake kernel promises checkpoints only where the one-kernel forward runs: C % 8 != 0, a
     head dim other than 128, fp32 or T % 32 != 0 give the empty checkpoint."""
