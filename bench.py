@@ -175,6 +175,89 @@ def make_inputs(cfg, device, seed):
     return host, dev, dict(B=B, T=T, C=C, NH=NH, NKVH=NKVH, D=D, r=r, H=H, Da=Da, F=F, dt=dt)
 
 
+def _graph_us(fn, device, reps=20):
+    """Average device time (us) of `fn` replayed as one CUDA graph, timed with CUDA events."""
+    import torch
+
+    cs = torch.cuda.Stream(device)
+    cs.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(cs):
+        for _ in range(3):
+            fn()
+    torch.cuda.current_stream().wait_stream(cs)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=cs):
+        fn()
+    for _ in range(3):
+        g.replay()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(reps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / reps
+    del g
+    return us
+
+
+def prologue_timing(cfg, d, W, bias, init, s, device):
+    """The layer step followed by the reference attention's prologue on q and k (rotary embedding then
+    RMS norm, nanochat/gpt.py:224-230) and its backward, three ways on the bench's inputs: without the
+    prologue, with it as separate kernels after the filter (ltv_rotary_qk_norm and its backward), and
+    folded into the filter's kernels (ltv_proj_scan_rope_norm_cuda_op, the raw q/k replayed from the
+    checkpoints in the backward). Only on the one-kernel shapes (where the fused form exists)."""
+    import torch
+
+    import nanochat_filter_b200 as nf
+
+    ops = torch.ops.nanochat_cuda
+    B, T, NH, NKVH, D, r, H, Da, dt = (s[k] for k in ("B", "T", "NH", "NKVH", "D", "r", "H", "Da", "dt"))
+    if len(nf.ops._ckpt_shape(d["x"], NH, NKVH, Da, r)) != 4:
+        return None
+    inv = 1.0 / (10000 ** (torch.arange(0, D, 2, dtype=torch.float32, device=device) / D))
+    fr = torch.outer(torch.arange(T, dtype=torch.float32, device=device), inv)
+    cos, sin = fr.cos().to(dt)[None, :, None, :], fr.sin().to(dt)[None, :, None, :]
+    a = (NH, NKVH, Da, r)
+    Wg = torch.zeros_like(W)
+
+    def tail(comb, inits, ckpt, dq, dk):
+        combined = comb.transpose(1, 2)
+        gc = torch.empty_like(combined)
+        gi, gb = torch.empty(H, D, device=device), torch.empty_like(bias)
+        ops.ltv_scan_ckpt_backward_kernel(combined, inits, bias, ckpt, dq, dk, d["gv"], gc, gi, gb, *a, True)
+        ops.fused_linear_transpose_backward_kernel(d["x"], W.to(dt), gc.transpose(1, 2), torch.empty_like(d["x"]), Wg)
+
+    def plain():
+        inits = init.to(dt)
+        comb, q, k, v, ckpt = ops.ltv_proj_scan_cuda_op(d["x"], W.to(dt), inits, bias, *a, True)
+        tail(comb, inits, ckpt, d["gq"], d["gk"])
+
+    def separate():
+        inits = init.to(dt)
+        comb, q, k, v, ckpt = ops.ltv_proj_scan_cuda_op(d["x"], W.to(dt), inits, bias, *a, True)
+        ops.ltv_rotary_qk_norm(q.transpose(1, 2), k.transpose(1, 2), cos, sin)
+        dq, dk = ops.ltv_rotary_qk_norm_backward(q.transpose(1, 2), k.transpose(1, 2), cos, sin,
+                                                 d["gq"].transpose(1, 2), d["gk"].transpose(1, 2))
+        tail(comb, inits, ckpt, dq.transpose(1, 2), dk.transpose(1, 2))
+
+    def fused():
+        inits = init.to(dt)
+        comb, qn, kn, v, ckpt = ops.ltv_proj_scan_rope_norm_cuda_op(d["x"], W.to(dt), inits, bias, cos, sin, *a, True)
+        dq, dk = ops.ltv_rotary_qk_norm_ckpt_backward(comb.transpose(1, 2), inits, bias, ckpt, cos, sin, d["gq"],
+                                                      d["gk"], *a, True)
+        tail(comb, inits, ckpt, dq, dk)
+
+    out = {k: round(_graph_us(fn, device), 1) for k, fn in (("step_us", plain), ("separate_us", separate),
+                                                            ("fused_us", fused))}
+    out["what"] = ("layer step (fwd + bwd) followed by the attention's q/k prologue (rotary + RMS norm) and its "
+                   "backward: without it, as separate kernels after the filter, folded into the filter's kernels; "
+                   "each replayed as one CUDA graph, CUDA-event timing")
+    return out
+
+
 def run_ours(args, cfg):
     import torch
     import torch.distributed as dist
@@ -461,7 +544,7 @@ def run_ours(args, cfg):
         "vs_baseline": None,
         "dtype": cfg["dtype"],
         "data": "synthetic (seeded N(0,1) activations and upstream grads; value rows N(0,1/sqrt(C)), "
-                "decay rows N(0,0.02); random-init weights)",
+                f"decay rows N(0,{cfg.get('logit_std', 0.02)}), bias {cfg['bias']}; random-init weights)",
         "config": {
             "workload": f"{args.config}: {cfg['desc']}",
             "tokens_per_rank_per_step": B * T,
@@ -494,7 +577,9 @@ def run_ours(args, cfg):
     }
     if world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(cfg, args.cpu_seconds)
-    del graph, graph_out  # release the graph (and its memory pool) before the process group goes
+    del graph, graph_out
+    if world == 1:
+        result["prologue"] = prologue_timing(cfg, d, W, bias, init, s, device)  # release the graph (and its memory pool) before the process group goes
     if world > 1:
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()
@@ -784,6 +869,8 @@ def main():
                     help="config2 (default), config1/config3, or decode (config 4, kernel level)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--batch", type=int, default=0,
+                    help="override the config's sequences per rank (small profiling cases; not a bench line)")
     args = ap.parse_args()
     if args.config == "decode":
         if args.impl == "reference":
@@ -792,7 +879,10 @@ def main():
             return
         run_decode(args)
         return
-    cfg = CONFIGS[args.config]
+    cfg = dict(CONFIGS[args.config])
+    if args.batch:
+        cfg["B"] = args.batch
+        cfg["desc"] += f" [B overridden to {args.batch}: a profiling case, not the benchmark config]"
     if args.impl == "reference":
         run_reference(args, cfg)
     else:
