@@ -184,8 +184,11 @@ LTVQKV_DEVICE unsigned int ld_acquire_u32(const unsigned int* p) {
   return v;
 }
 LTVQKV_DEVICE float ld_cg_f32(const float* p) { return __ldcg(p); }
-// Brings the line holding p into this SM's L1 (no register written, nothing waits for it).
-LTVQKV_DEVICE void prefetch_l1(const void* p) { asm volatile("prefetch.global.L1 [%0];" ::"l"(p)); }
+// Programmatic dependent launch: let the next kernel on the stream be scheduled now; wait until the
+// previous kernel on the stream has completed and its memory is visible (returns at once when this
+// grid was not launched with programmatic stream serialisation).
+LTVQKV_DEVICE void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+LTVQKV_DEVICE void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 // ------------------------------------------------------------------------------------------
 // Shared-memory address helpers

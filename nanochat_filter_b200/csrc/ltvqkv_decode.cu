@@ -232,49 +232,58 @@ __global__ void __launch_bounds__(kDecThreads) decode_step_mma_kernel(DecodeArgs
 size_t decode_mma_smem(int Cp) { return (size_t)(kDmRows + kDmTok) * (Cp + 8) * 2 + (size_t)kDmRows * kDmTok * 4; }
 
 // bf16 path for C % 64 == 0 (the model widths): the same (head, 16-channel slice) CTAs, with
-//   * the operands staged by three bulk tensor copies issued from three warps at once: the 64-token
-//     tile of x as one 128-byte-swizzled box [C/64][64 tokens][64], the slice's value rows
-//     [C/64][16][64] and its logit rows [C/64][ngb][64] (cp.async from every thread reached about
-//     17 bytes per clock per SM, half the time of the step);
+//   * K cut into nq parts (4 when C/64 divides by 4, else 2 or 1), each part staged by bulk tensor
+//     copies issued from its own warp onto its own mbarrier: the part's k-blocks of the 64-token
+//     tile of x (one 128-byte-swizzled box [C/64/nq][64 tokens][64]), of the slice's value rows and
+//     of its logit rows; copies from several warps run side by side (one thread issues about one copy
+//     per few hundred cycles whatever its size), and the warps of a part start multiplying as soon as
+//     that part has landed;
 //   * the previous state of the thread's outputs loaded into registers while the copies land;
-//   * the K range split between two warp halves: warp w multiplies tokens 16 (w % 4) .. +15 by all
-//     24 rows (3 independent accumulator chains) over half of C, and the halves are added in fixed
-//     order (first + second), so a warp's chain is 24 k-steps instead of 48.
+//   * 16 warps: warp w < 4 nq multiplies tokens 16 (w % 4) .. +15 by all 24 rows (3 independent
+//     accumulator chains) over K part w / 4, and the parts are added in fixed order (part 0 + part 1
+//     + ...), so a warp's chain is 48 / nq k-steps and results do not depend on timing;
+//   * programmatic dependent launch: the next kernel on the stream may be scheduled while this one
+//     runs; this grid's global reads wait for the previous kernel's completion (griddepcontrol.wait).
 // The projection values and logits are rounded to bf16 exactly as the reference's projection
 // buffer stores them, then the gate and the recurrence step as in the other paths.
 constexpr int kDtTok = 64;      // tokens per tile (one box)
 constexpr int kDtRows = 24;     // 16 value rows + up to 8 logit rows (r >= 2)
 constexpr int kDtRegion = 1024; // swizzle atoms start on 1 KB boundaries
+constexpr int kDtMaxParts = 4;
 
 struct DecodeTmaLayout {
-  size_t x, wv, wl, red, bar, total;
+  size_t x, wv, wl, wl_part, red, bar, total;
 };
-__host__ __device__ inline DecodeTmaLayout decode_tma_layout(int nkb) {
+// Every box lands on a 1 KB boundary (the 128-byte swizzle's atom): x and the value rows per part
+// are whole multiples of it; the logit rows of each part get their own 1 KB-rounded slot.
+__host__ __device__ inline DecodeTmaLayout decode_tma_layout(int nkb, int nq) {
   DecodeTmaLayout L;
   size_t off = 0;
   L.x = off; off += (size_t)nkb * kDtTok * 128;
   L.wv = off; off += (size_t)nkb * 16 * 128;
-  L.wl = off; off += ((size_t)nkb * 8 * 128 + kDtRegion - 1) / kDtRegion * kDtRegion;
-  L.red = off; off += (size_t)kDtTok * kDtRows * 4;
-  L.bar = off; off += 64;
+  L.wl_part = ((size_t)(nkb / nq) * 8 * 128 + kDtRegion - 1) / kDtRegion * kDtRegion;
+  L.wl = off; off += (size_t)nq * L.wl_part;
+  L.red = off; off += (size_t)(nq > 1 ? nq - 1 : 1) * kDtTok * kDtRows * 4;
+  L.bar = off; off += 8 * kDtMaxParts;
   L.total = off + kDtRegion;  // alignment slack of the dynamic shared memory base
   return L;
 }
+inline int decode_tma_parts(int nkb) { return nkb % 4 == 0 ? 4 : (nkb % 2 == 0 ? 2 : 1); }
 
 // Byte offset of the 16-byte piece `chunk` of 128-byte row `row` in a 128B-swizzled region.
 LTVQKV_DEVICE uint32_t swz128(int row, int chunk) { return (uint32_t)(row * 128 + ((chunk ^ (row & 7)) << 4)); }
 
-__global__ void __launch_bounds__(kDecThreads, 1)
+__global__ void __launch_bounds__(32 * 4 * kDtMaxParts, 1)
     decode_step_tma_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
-                           const __grid_constant__ CUtensorMap tmWl, DecodeArgs a, int nkb, int ngb) {
+                           const __grid_constant__ CUtensorMap tmWl, DecodeArgs a, int nkb, int ngb, int nq) {
   extern __shared__ __align__(16) unsigned char dt_raw[];
   unsigned char* smem = smem_align<unsigned char>(dt_raw, kDtRegion);
-  const DecodeTmaLayout L = decode_tma_layout(nkb);
+  const DecodeTmaLayout L = decode_tma_layout(nkb, nq);
   unsigned char* sX = smem + L.x;
   unsigned char* sWv = smem + L.wv;
   unsigned char* sWl = smem + L.wl;
-  float* red = reinterpret_cast<float*>(smem + L.red);  // [kDtTok][kDtRows]
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L.bar);
+  float* red = reinterpret_cast<float*>(smem + L.red);  // [nq - 1][kDtTok][kDtRows]
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L.bar);  // [nq]
   __shared__ volatile int abort_flag;
   const int h = blockIdx.x;
   const int c0 = blockIdx.y * kDmSlice;
@@ -282,39 +291,52 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   const int g0 = c0 / a.r;
   const int head_row = h * (a.D + a.Da);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int nthr = blockDim.x;
+  const int kpq = nkb / nq;  // k-blocks per part
   int which, hloc;
   dec_split_head(h, a.NH, a.NKVH, which, hloc);
+  // Launched with programmatic stream serialisation: the next kernel on the stream may be scheduled
+  // now (its CTAs set up while this grid runs), and this grid's own global reads wait below until
+  // the previous kernel on the stream has completed and its writes are visible — every global read
+  // of this kernel (weights included: a cast kernel may have just written them) comes after that.
+  griddep_launch_dependents();
   if (threadIdx.x == 0) {
-    mbar_init(bar, 1);
+    for (int q = 0; q < nq; ++q) mbar_init(&bar[q], 1);
     abort_flag = 0;
     fence_mbar_init();
+    tma_prefetch_desc(&tmX);
+    tma_prefetch_desc(&tmW);
+    tma_prefetch_desc(&tmWl);
   }
   __syncthreads();
-  const int mt = warp % 4, kh = warp / 4;
-  const int kb_half = (nkb + 1) / 2;
-  const int kb_beg = kh * kb_half, kb_end = min(nkb, kb_beg + kb_half);
+  griddep_wait();
+  const int mt = warp % 4, kq = warp / 4;
   const uint32_t sX_u = smem_u32(sX), sWv_u = smem_u32(sWv), sWl_u = smem_u32(sWl);
   uint32_t phase = 0;
   for (int b0 = 0; b0 < a.B; b0 += kDtTok, phase ^= 1u) {
     const int nb = min(kDtTok, a.B - b0);
     const bool first = b0 == 0;
-    // the copies (x every tile; the W rows once), each issued by its own warp
-    if (threadIdx.x == 0) {
-      const uint32_t bytes = (uint32_t)nkb * 128u * (kDtTok + (first ? 16u + (uint32_t)ngb : 0u));
-      mbar_arrive_expect_tx(bar, bytes);
-      tma_load_3d(sX, &tmX, bar, 0, b0, 0);
-    } else if (first && threadIdx.x == 32) {
-      tma_load_3d(sWv, &tmW, bar, 0, head_row + c0, 0);
-    } else if (first && threadIdx.x == 64) {
-      tma_load_3d(sWl, &tmWl, bar, 0, head_row + a.D + g0, 0);
+    // part q's copies: x from lane 0 of warp q (every tile, with the part's byte count), the W rows
+    // from lane 0 of warp 4 + q (first tile only), so that eight threads issue side by side
+    if (lane == 0 && warp < nq) {
+      const int z = warp * kpq;
+      const uint32_t bytes = (uint32_t)kpq * 128u * (kDtTok + (first ? 16u + (uint32_t)ngb : 0u));
+      mbar_arrive_expect_tx(&bar[warp], bytes);
+      tma_load_3d(sX + (size_t)z * kDtTok * 128, &tmX, &bar[warp], 0, b0, z);
+    } else if (lane == 0 && first && warp >= 4 && warp < 4 + nq) {
+      const int q = warp - 4, z = q * kpq;
+      tma_load_3d(sWv + (size_t)z * 16 * 128, &tmW, &bar[q], 0, head_row + c0, z);
+      tma_load_3d(sWl + (size_t)q * L.wl_part, &tmWl, &bar[q], 0, head_row + a.D + g0, z);
     }
-    // this thread's previous states, while the copies land
-    float hp[4];
+    // this thread's previous states and logit biases, while the copies land
+    float hp[2], lbj[2];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int i = threadIdx.x + j * kDecThreads;
+    for (int j = 0; j < 2; ++j) {
+      const int i = threadIdx.x + j * nthr;
       hp[j] = 0.f;
+      lbj[j] = 0.f;
       if (i < nv * nb) {
+        lbj[j] = a.logit_bias[h * a.Da + (c0 + (i - (i / nv) * nv)) / a.r];
         const int bb = i / nv, c = c0 + (i - bb * nv), b = b0 + bb;
         if (a.prev[0] != nullptr) {
           const long long* ps = a.ps[which];
@@ -324,13 +346,16 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         }
       }
     }
-    if (!mbar_wait(bar, phase, &abort_flag, nullptr, 0x7e01)) break;
-    // tokens 16 mt .. +15 x rows 0..23 over k-blocks kb_beg .. kb_end-1
+    // tokens 16 mt .. +15 x rows 0..23 over the k-blocks of part kq, once they have landed (warps
+    // beyond 4 nq only help with the epilogue)
+    const bool got = kq < nq ? mbar_wait(&bar[kq], phase, &abort_flag, nullptr, 0x7e01) : true;
+    if (__syncthreads_or(got ? 0 : 1)) break;  // every warp leaves together
     float acc[3][4] = {};
     const int arow = 16 * mt + (lane % 16);
     const int brow = lane % 8;
     const int lrow = brow < ngb ? brow : 0;  // logit rows beyond the slice's groups: any row (unused columns)
-    for (int kb = kb_beg; kb < kb_end; ++kb) {
+    const uint32_t sWlq = sWl_u + (uint32_t)(kq * L.wl_part);
+    for (int kb = kq * kpq; kq < nq && kb < (kq + 1) * kpq; ++kb) {
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
         uint32_t af[4], b0f[2], b1f[2], blf[2];
@@ -338,44 +363,49 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         const int bc = kk * 2 + (lane / 8) % 2;
         ldsm_x2(sWv_u + (uint32_t)kb * (16 * 128) + swz128(brow, bc), b0f);
         ldsm_x2(sWv_u + (uint32_t)kb * (16 * 128) + swz128(8 + brow, bc), b1f);
-        ldsm_x2(sWl_u + swz128(kb * ngb + lrow, bc), blf);
+        ldsm_x2(sWlq + swz128((kb - kq * kpq) * ngb + lrow, bc), blf);
         mma_bf16_16816(acc[0], af, b0f);
         mma_bf16_16816(acc[1], af, b1f);
         mma_bf16_16816(acc[2], af, blf);
       }
     }
-    // the two K halves, added in fixed order: red = half 0 + half 1
+    // the parts, added in fixed order: part 0 + part 1 + ... (parts 1.. through red)
     const int tt = 16 * mt + lane / 4, rr = 2 * (lane % 4);
-    if (kh == 1) {
+    if (kq > 0 && kq < nq) {
+      float* rq = red + (size_t)(kq - 1) * kDtTok * kDtRows;
 #pragma unroll
       for (int j = 0; j < 3; ++j) {
-        *reinterpret_cast<float2*>(&red[tt * kDtRows + 8 * j + rr]) = make_float2(acc[j][0], acc[j][1]);
-        *reinterpret_cast<float2*>(&red[(tt + 8) * kDtRows + 8 * j + rr]) = make_float2(acc[j][2], acc[j][3]);
+        *reinterpret_cast<float2*>(&rq[tt * kDtRows + 8 * j + rr]) = make_float2(acc[j][0], acc[j][1]);
+        *reinterpret_cast<float2*>(&rq[(tt + 8) * kDtRows + 8 * j + rr]) = make_float2(acc[j][2], acc[j][3]);
       }
     }
     __syncthreads();
-    if (kh == 0) {
+    if (kq == 0) {
 #pragma unroll
       for (int j = 0; j < 3; ++j) {
-        float2* p0 = reinterpret_cast<float2*>(&red[tt * kDtRows + 8 * j + rr]);
-        float2* p1 = reinterpret_cast<float2*>(&red[(tt + 8) * kDtRows + 8 * j + rr]);
-        const float2 q0 = *p0, q1 = *p1;
-        *p0 = make_float2(acc[j][0] + q0.x, acc[j][1] + q0.y);
-        *p1 = make_float2(acc[j][2] + q1.x, acc[j][3] + q1.y);
+        float s0 = acc[j][0], s1 = acc[j][1], s2 = acc[j][2], s3 = acc[j][3];
+        for (int q = 1; q < nq; ++q) {
+          const float* rq = red + (size_t)(q - 1) * kDtTok * kDtRows;
+          const float2 q0 = *reinterpret_cast<const float2*>(&rq[tt * kDtRows + 8 * j + rr]);
+          const float2 q1 = *reinterpret_cast<const float2*>(&rq[(tt + 8) * kDtRows + 8 * j + rr]);
+          s0 += q0.x; s1 += q0.y; s2 += q1.x; s3 += q1.y;
+        }
+        // the sum lands in part 1's slot (or in red itself with one part)
+        *reinterpret_cast<float2*>(&red[tt * kDtRows + 8 * j + rr]) = make_float2(s0, s1);
+        *reinterpret_cast<float2*>(&red[(tt + 8) * kDtRows + 8 * j + rr]) = make_float2(s2, s3);
       }
     }
     __syncthreads();
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int i = threadIdx.x + j * kDecThreads;
+    for (int j = 0; j < 2; ++j) {
+      const int i = threadIdx.x + j * nthr;
       if (i < nv * nb) {
         const int bb = i / nv, cc = i - bb * nv;
         const int c = c0 + cc, b = b0 + bb;
         const int g = c / a.r;
         // projection values rounded to bf16, as the reference's projection buffer stores them
         const float u = __bfloat162float(__float2bfloat16_rn(red[bb * kDtRows + cc]));
-        const float l = __fadd_rn(__bfloat162float(__float2bfloat16_rn(red[bb * kDtRows + 16 + g - g0])),
-                                  a.logit_bias[h * a.Da + g]);
+        const float l = __fadd_rn(__bfloat162float(__float2bfloat16_rn(red[bb * kDtRows + 16 + g - g0])), lbj[j]);
         const float al = a.use_sigmoid ? sigmoid_f32(l) : l;
         const float hn = __fadd_rn(__fmul_rn(__fsub_rn(1.0f, al), hp[j]), __fmul_rn(al, u));
         const long long* os = a.os[which];
@@ -431,13 +461,15 @@ extern "C" int ltvqkv_decode_step(int dtype, const void* x, const void* weight, 
   const bool slice_groups = (r % kDmSlice == 0) || (kDmSlice % r == 0 && r >= 2);
   const int ngb = r >= kDmSlice ? 1 : kDmSlice / r;  // logit rows of a slice (<= 8)
   const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(weight)) & 15) == 0;
+  const int nq = decode_tma_parts(nkb > 0 ? nkb : 1);
   if (dtype == LTVQKV_DTYPE_BF16 && slice_groups && C % 64 == 0 && nkb >= 1 && nkb <= 256 && aligned &&
-      decode_tma_layout(nkb).total <= 220 * 1024) {
+      decode_tma_layout(nkb, nq).total <= 220 * 1024) {
     const int F = a.H * (a.D + Da);
     const uint64_t dx[3] = {64, (uint64_t)B, (uint64_t)nkb}, sx[2] = {(uint64_t)C * 2, 128};
     const uint64_t dw[3] = {64, (uint64_t)F, (uint64_t)nkb}, sw[2] = {(uint64_t)C * 2, 128};
-    const uint32_t bx[3] = {64, (uint32_t)kDtTok, (uint32_t)nkb}, bw[3] = {64, 16, (uint32_t)nkb},
-                   bl[3] = {64, (uint32_t)ngb, (uint32_t)nkb};
+    // boxes of one K part (nkb / nq k-blocks)
+    const uint32_t kp = (uint32_t)(nkb / nq);
+    const uint32_t bx[3] = {64, (uint32_t)kDtTok, kp}, bw[3] = {64, 16, kp}, bl[3] = {64, (uint32_t)ngb, kp};
     CUtensorMap tmX, tmW, tmWl;
     if (!ltvqkv_host::encode_tiled_map(&tmX, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, x, dx, sx, bx, CU_TENSOR_MAP_SWIZZLE_128B) ||
         !ltvqkv_host::encode_tiled_map(&tmW, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, weight, dw, sw, bw,
@@ -445,7 +477,7 @@ extern "C" int ltvqkv_decode_step(int dtype, const void* x, const void* weight, 
         !ltvqkv_host::encode_tiled_map(&tmWl, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, weight, dw, sw, bl,
                                        CU_TENSOR_MAP_SWIZZLE_128B))
       return LTVQKV_ERR_LAUNCH;
-    const size_t tsm = decode_tma_layout(nkb).total;
+    const size_t tsm = decode_tma_layout(nkb, nq).total;
     static std::mutex mu3;
     static size_t opted3[64] = {};  // dynamic shared memory this kernel is opted into, per device
     int dev = 0;
@@ -459,8 +491,23 @@ extern "C" int ltvqkv_decode_step(int dtype, const void* x, const void* weight, 
         opted3[dev] = tsm;
       }
     }
-    dim3 grid_tma(a.H, (a.D + kDmSlice - 1) / kDmSlice);
-    decode_step_tma_kernel<<<grid_tma, kDecThreads, tsm, s>>>(tmX, tmW, tmWl, a, nkb, ngb);
+    // programmatic stream serialisation (see the kernel): consecutive decode steps of a graph or a
+    // stream overlap one kernel's launch and set-up with the previous one's tail
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3(a.H, (a.D + kDmSlice - 1) / kDmSlice);
+    lc.blockDim = dim3(32 * 4 * kDtMaxParts);
+    lc.dynamicSmemBytes = tsm;
+    lc.stream = s;
+    cudaLaunchAttribute la[1];
+    la[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    la[0].val.programmaticStreamSerializationAllowed = 1;
+    lc.attrs = la;
+    lc.numAttrs = 1;
+    const cudaError_t le = cudaLaunchKernelEx(&lc, decode_step_tma_kernel, tmX, tmW, tmWl, a, nkb, ngb, nq);
+    if (le != cudaSuccess) {
+      ltvqkv_host::set_last_cuda_error(le);
+      return LTVQKV_ERR_LAUNCH;
+    }
   } else if (dtype == LTVQKV_DTYPE_BF16 && smem <= 200 * 1024 && rows_fit) {
     static std::mutex mu;
     static bool done[64] = {};

@@ -168,6 +168,111 @@ __global__ void __launch_bounds__(256, 4) rotary_norm_fwd_kernel(RotArgs a) {
   }
 }
 
+// Head dim 128, bf16, paired access (the filter's q and k): the same per-token arithmetic as the
+// paired paths above (lane l holds the element pairs (2l, 2l + 1) and (2l + 64, 2l + 65)), four
+// tokens per warp iteration with every load of the four issued before any of them is used, so that
+// a warp keeps 16 (forward) or 24 (backward) loads in flight instead of 4 or 6.
+constexpr int kRot128Tok = 4;
+
+__global__ void __launch_bounds__(256, 4) rotary_norm_fwd128_kernel(RotArgs a) {
+  const int lane = threadIdx.x % 32;
+  int w, b, hh;
+  rot_head(a, blockIdx.y, w, b, hh);
+  const long long* xs = a.xs[w];
+  const long long* os = a.os[w];
+  const int S = gridDim.x * 8;
+  for (int t0 = blockIdx.x * 8 + threadIdx.x / 32; t0 < a.T; t0 += kRot128Tok * S) {
+    uint32_t x1[kRot128Tok], x2[kRot128Tok], cw[kRot128Tok], sw[kRot128Tok];
+#pragma unroll
+    for (int u = 0; u < kRot128Tok; ++u) {
+      const int t = t0 + u * S;
+      x1[u] = x2[u] = cw[u] = sw[u] = 0u;
+      if (t < a.T) {
+        const __nv_bfloat16* xr = reinterpret_cast<const __nv_bfloat16*>(a.x[w]) + b * xs[0] + t * xs[1] + hh * xs[2];
+        x1[u] = __ldg(reinterpret_cast<const uint32_t*>(xr) + lane);
+        x2[u] = __ldg(reinterpret_cast<const uint32_t*>(xr + 64) + lane);
+        cw[u] = __ldg(reinterpret_cast<const uint32_t*>(reinterpret_cast<const __nv_bfloat16*>(a.cos) + t * a.cs[0]) + lane);
+        sw[u] = __ldg(reinterpret_cast<const uint32_t*>(reinterpret_cast<const __nv_bfloat16*>(a.sin) + t * a.cs[0]) + lane);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kRot128Tok; ++u) {
+      const int t = t0 + u * S;
+      if (t >= a.T) break;  // warp-uniform
+      uint32_t r1, r2;
+      rope_rotate_bf16x2(x1[u], x2[u], cw[u], sw[u], r1, r2);
+      const float y0 = bf16_lo(r1), y1 = bf16_hi(r1), y2 = bf16_lo(r2), y3 = bf16_hi(r2);
+      float ss = __fmaf_rn(y0, y0, 0.f);
+      ss = __fmaf_rn(y1, y1, ss);
+      ss = __fmaf_rn(y2, y2, ss);
+      ss = __fmaf_rn(y3, y3, ss);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      const float inv = rope_inv_rms(ss, 128, a.eps);
+      __nv_bfloat16* orow = reinterpret_cast<__nv_bfloat16*>(a.out[w]) + b * os[0] + t * os[1] + hh * os[2];
+      reinterpret_cast<uint32_t*>(orow)[lane] = pack_bf16x2(y0 * inv, y1 * inv);
+      reinterpret_cast<uint32_t*>(orow + 64)[lane] = pack_bf16x2(y2 * inv, y3 * inv);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256, 4) rotary_norm_bwd128_kernel(RotArgs a) {
+  const int lane = threadIdx.x % 32;
+  int w, b, hh;
+  rot_head(a, blockIdx.y, w, b, hh);
+  const long long* xs = a.xs[w];
+  const long long* gs = a.gs[w];
+  const long long* os = a.os[w];
+  const int S = gridDim.x * 8;
+  for (int t0 = blockIdx.x * 8 + threadIdx.x / 32; t0 < a.T; t0 += kRot128Tok * S) {
+    uint32_t x1[kRot128Tok], x2[kRot128Tok], cw[kRot128Tok], sw[kRot128Tok], g1[kRot128Tok], g2[kRot128Tok];
+#pragma unroll
+    for (int u = 0; u < kRot128Tok; ++u) {
+      const int t = t0 + u * S;
+      x1[u] = x2[u] = cw[u] = sw[u] = g1[u] = g2[u] = 0u;
+      if (t < a.T) {
+        const __nv_bfloat16* xr = reinterpret_cast<const __nv_bfloat16*>(a.x[w]) + b * xs[0] + t * xs[1] + hh * xs[2];
+        const __nv_bfloat16* gr = reinterpret_cast<const __nv_bfloat16*>(a.g[w]) + b * gs[0] + t * gs[1] + hh * gs[2];
+        x1[u] = __ldg(reinterpret_cast<const uint32_t*>(xr) + lane);
+        x2[u] = __ldg(reinterpret_cast<const uint32_t*>(xr + 64) + lane);
+        g1[u] = __ldg(reinterpret_cast<const uint32_t*>(gr) + lane);
+        g2[u] = __ldg(reinterpret_cast<const uint32_t*>(gr + 64) + lane);
+        cw[u] = __ldg(reinterpret_cast<const uint32_t*>(reinterpret_cast<const __nv_bfloat16*>(a.cos) + t * a.cs[0]) + lane);
+        sw[u] = __ldg(reinterpret_cast<const uint32_t*>(reinterpret_cast<const __nv_bfloat16*>(a.sin) + t * a.cs[0]) + lane);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kRot128Tok; ++u) {
+      const int t = t0 + u * S;
+      if (t >= a.T) break;  // warp-uniform
+      uint32_t r1, r2;
+      rope_rotate_bf16x2(x1[u], x2[u], cw[u], sw[u], r1, r2);
+      const float y[4] = {bf16_lo(r1), bf16_hi(r1), bf16_lo(r2), bf16_hi(r2)};
+      const float g[4] = {bf16_lo(g1[u]), bf16_hi(g1[u]), bf16_lo(g2[u]), bf16_hi(g2[u])};
+      float ss = 0.f, gy = 0.f;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        ss = __fmaf_rn(y[e], y[e], ss);
+        gy = __fmaf_rn(g[e], y[e], gy);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        gy += __shfl_xor_sync(0xffffffffu, gy, o);
+      }
+      const float r = rope_inv_rms(ss, 128, a.eps);
+      const float k3 = rope_k3(r, gy, 128);
+      float dx1[2], dx2[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e)
+        rope_norm_bwd(r, k3, g[e], g[2 + e], y[e], y[2 + e], bf16_lane(cw[u], e), bf16_lane(sw[u], e), dx1[e], dx2[e]);
+      __nv_bfloat16* orow = reinterpret_cast<__nv_bfloat16*>(a.out[w]) + b * os[0] + t * os[1] + hh * os[2];
+      reinterpret_cast<uint32_t*>(orow)[lane] = pack_bf16x2(dx1[0], dx1[1]);
+      reinterpret_cast<uint32_t*>(orow + 64)[lane] = pack_bf16x2(dx2[0], dx2[1]);
+    }
+  }
+}
+
 // Backward: z = y r, r = (mean(y^2) + eps)^(-1/2):  dy = r g - y r^3 (sum g y) / D;
 // rotation transposed: dx1 = dy1 cos - dy2 sin,  dx2 = dy1 sin + dy2 cos.
 template <typename S>
@@ -277,8 +382,9 @@ __global__ void __launch_bounds__(256, 3) rotary_norm_bwd_kernel(RotArgs a) {
 // ------------------------------------------------------------------------------------------
 // Backward of the prologue folded into the fused forward (ltvqkv_proj_scan_fwd_ckpt_rope): that
 // forward never stores the raw q / k, so the rotary backward replays them from the scan's
-// checkpoints. One CTA (128 threads) per (32-token chunk, batch, q or k head), chunk-major so that
-// concurrent CTAs share the chunk's table lines. Replay: thread c walks channel c of the chunk from
+// checkpoints. One CTA (128 threads) per (32-token chunk, batch, q or k head), consecutive CTAs on
+// consecutive chunks of one row (their value-row and gradient reads are adjacent in memory; the
+// tables are L2-resident either way). Replay: thread c walks channel c of the chunk from
 // the state entering it (the checkpoint, or the initial state for the first chunk) with the
 // forward's arithmetic (E = fma(1 - a, E, a u), a = sigmoid(logit + bias), u the stored bf16
 // projection value), so the rebuilt h_t are the forward's raw outputs bit for bit; they go to
@@ -305,11 +411,10 @@ struct RopeCkptArgs {
 
 constexpr int kRopeTT = 32;
 
-__global__ void __launch_bounds__(128, 8) rope_bwd_ckpt_kernel(RopeCkptArgs a) {
+__global__ void __launch_bounds__(128, 6) rope_bwd_ckpt_kernel(RopeCkptArgs a) {
   __shared__ float gate[2][kRopeTT];                 // (1 - a_t, a_t)
   __shared__ __align__(16) uint32_t hs[kRopeTT][64];  // raw h_t, bf16 pairs
-  const int rows = a.B * (a.NH + a.NKVH);
-  const int j = blockIdx.x / rows, row = blockIdx.x % rows;
+  const int j = blockIdx.x % a.nchunks, row = blockIdx.x / a.nchunks;
   const int b = row / (a.NH + a.NKVH), h = row % (a.NH + a.NKVH);  // q heads, then k heads
   const int w = h < a.NH ? 0 : 1, hloc = h < a.NH ? h : h - a.NH;
   const int tid = threadIdx.x, lane = tid % 32, warp = tid / 32;
@@ -327,6 +432,20 @@ __global__ void __launch_bounds__(128, 8) rope_bwd_ckpt_kernel(RopeCkptArgs a) {
   uint4 u4[4];
 #pragma unroll
   for (int k = 0; k < 4; ++k) u4[k] = __ldg(urow + k);
+  // this warp's 8 tokens: table words and output gradients, loaded with the value rows (one latency)
+  const long long* gs = a.gs[w];
+  const long long* dsr = a.ds[w];
+  uint32_t cw8[8], sw8[8], gA8[8], gB8[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const int t = t0 + warp * 8 + e;
+    const long long tr = (long long)t * a.cs;
+    cw8[e] = __ldg(reinterpret_cast<const uint32_t*>(a.cos + tr) + lane);
+    sw8[e] = __ldg(reinterpret_cast<const uint32_t*>(a.sin + tr) + lane);
+    const __nv_bfloat16* gr = a.g[w] + b * gs[0] + hloc * gs[1] + t * gs[2];
+    gA8[e] = __ldg(reinterpret_cast<const uint32_t*>(gr) + lane);
+    gB8[e] = __ldg(reinterpret_cast<const uint32_t*>(gr + 64) + lane);
+  }
   __syncthreads();
   __nv_bfloat16* hs16 = reinterpret_cast<__nv_bfloat16*>(&hs[0][0]);
 #pragma unroll
@@ -342,20 +461,13 @@ __global__ void __launch_bounds__(128, 8) rope_bwd_ckpt_kernel(RopeCkptArgs a) {
   }
   __syncthreads();
   // rotary + norm backward of this warp's 8 tokens, four at a time
-  const long long* gs = a.gs[w];
-  const long long* dsr = a.ds[w];
-#pragma unroll 1
+#pragma unroll
   for (int half = 0; half < 2; ++half) {
     uint32_t cw[4], sw[4], gA[4], gB[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      const int t = t0 + warp * 8 + half * 4 + e;
-      const long long tr = (long long)t * a.cs;
-      cw[e] = __ldg(reinterpret_cast<const uint32_t*>(a.cos + tr) + lane);
-      sw[e] = __ldg(reinterpret_cast<const uint32_t*>(a.sin + tr) + lane);
-      const __nv_bfloat16* gr = a.g[w] + b * gs[0] + hloc * gs[1] + t * gs[2];
-      gA[e] = __ldg(reinterpret_cast<const uint32_t*>(gr) + lane);
-      gB[e] = __ldg(reinterpret_cast<const uint32_t*>(gr + 64) + lane);
+      cw[e] = cw8[4 * half + e]; sw[e] = sw8[4 * half + e];
+      gA[e] = gA8[4 * half + e]; gB[e] = gB8[4 * half + e];
     }
     float y[4][4], g[4][4], ss[4], gy[4];
 #pragma unroll
@@ -448,6 +560,7 @@ extern "C" int ltvqkv_rotary_qk_norm_fwd(int dtype, const void* q, const int64_t
   const dim3 grid((unsigned int)std::min(64, (T + 63) / 64), (unsigned int)(B * (NH + NKVH)));
   if (B * (NH + NKVH) > 65535) return LTVQKV_ERR_SHAPE;
   if (dtype == LTVQKV_DTYPE_F32) rotary_norm_fwd_kernel<float><<<grid, 256, 0, s>>>(a);
+  else if (a.vec && D == 128) rotary_norm_fwd128_kernel<<<grid, 256, 0, s>>>(a);
   else rotary_norm_fwd_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(a);
   return ltvqkv_host::check_launch();
 }
@@ -534,6 +647,7 @@ extern "C" int ltvqkv_rotary_qk_norm_bwd(int dtype, const void* q, const int64_t
   const dim3 grid((unsigned int)std::min(64, (T + 63) / 64), (unsigned int)(B * (NH + NKVH)));
   if (B * (NH + NKVH) > 65535) return LTVQKV_ERR_SHAPE;
   if (dtype == LTVQKV_DTYPE_F32) rotary_norm_bwd_kernel<float><<<grid, 256, 0, s>>>(a);
+  else if (a.vec && D == 128) rotary_norm_bwd128_kernel<<<grid, 256, 0, s>>>(a);
   else rotary_norm_bwd_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(a);
   return ltvqkv_host::check_launch();
 }
