@@ -859,14 +859,72 @@ def run_decode(args):
     del graph
 
 
+def run_lookback(args):
+    """The look-back (chunk-restarting) scan, forward + backward, kernel level (f1): config 2's
+    shape (B=32, T=1024, 6+6+6 heads x 128, r=128, bf16) with the reference's chunking
+    (P, Q, K) = (128, 112, 17) — the first 128 tokens as one chunk, then 112-token chunks each
+    restarted 16 tokens back. The scan's input `combined` is the projection buffer's [B, T, F]
+    view, as the look-back filter passes it. Replayed as one CUDA graph per step."""
+    import torch
+
+    from nanochat_filter_b200 import _lib
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    _lib.load()
+    B, T, NH, NKVH, D, r, P, Q, K = 32, 1024, 6, 6, 128, 128, 128, 112, 17
+    H, Da = NH + 2 * NKVH, D // r
+    F = H * (D + Da)
+    g = torch.Generator(device="cpu").manual_seed(5)
+    comb = torch.randn(B, F, T, generator=g).to(device, torch.bfloat16)
+    combined = comb.transpose(1, 2)
+    inits = torch.zeros(B, H, D, device=device, dtype=torch.bfloat16)
+    bias = torch.zeros(H, Da, device=device)
+    grads = [torch.randn(B, n, T, D, generator=g).to(device, torch.bfloat16) for n in (NH, NKVH, NKVH)]
+    outs = [torch.empty(B, n, T, D, device=device, dtype=torch.bfloat16) for n in (NH, NKVH, NKVH)]
+    gc = torch.empty_like(combined)
+    gi = torch.empty_like(inits)
+    gb = torch.empty_like(bias)
+    name = "ltv_look_back_fused_concat_head_major_register_cast_blelloch_scan_cuda_{}"
+    fwd = getattr(torch.ops.nanochat_cuda, name.format("forward_kernel"))
+    bwd = getattr(torch.ops.nanochat_cuda, name.format("backward_kernel"))
+
+    def step():
+        fwd(combined, inits, bias, *outs, B, T, NH, NKVH, Da, r, P, Q, K, 8, 8, 4, True)
+        gb.zero_()
+        bwd(combined, inits, bias, *outs, *grads, gc, gi, gb, NH, NKVH, Da, r, P, Q, K, 32, 2, 8, True)
+
+    steps = max(1, args.steps)
+    us = _graph_us(step, device, reps=steps)
+    nch = 1 + (T - P + Q - 1) // Q
+    # bytes per step: forward reads combined and writes q/k/v; backward reads combined, the outputs
+    # and their gradients, and writes grad_combined (the warm-up prefixes re-read combined from L2)
+    step_bytes = 2 * (B * T * F) * 2 + 3 * (B * T * H * D) * 2 + B * T * F * 2
+    peaks, src = load_peaks()
+    achieved = step_bytes / (us * 1e-6) / 1e9
+    print(json.dumps({
+        "metric": "look-back scan fwd+bwd tokens/s", "value": round(B * T / (us * 1e-6), 1), "unit": "tokens/s",
+        "n_gpus": 1, "steps": steps, "warmup": 3, "ms_per_step": round(us / 1e3, 4), "higher_is_better": True,
+        "dtype": "bf16", "data": "synthetic (N(0,1) projection buffer and upstream gradients)",
+        "config": {"workload": f"look-back scan (kernel level): B={B}, T={T}, 6+6+6 heads x 128, r=128, "
+                               f"(P, Q, K) = ({P}, {Q}, {K}): {nch} chunks per row",
+                   "launch": "one CUDA graph per step (forward kernel, bias-gradient zero fill, backward kernel)"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(achieved / peaks["hbm_gbs"], 4), "bytes_per_step": step_bytes,
+                     "peak_source": src},
+        "gpu_launches": 2 * steps,
+    }))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=sorted(CONFIGS) + ["decode"], default="config2",
-                    help="config2 (default), config1/config3, or decode (config 4, kernel level)")
+    ap.add_argument("--config", choices=sorted(CONFIGS) + ["decode", "lookback"], default="config2",
+                    help="config2 (default), config1/config3, decode (config 4, kernel level) or lookback "
+                         "(the look-back scan at config 2's shape, kernel level)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--batch", type=int, default=0,
@@ -878,6 +936,13 @@ def main():
                               "(the reference's decode runs inside its GPT model, which is outside the path)"}))
             return
         run_decode(args)
+        return
+    if args.config == "lookback":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the look-back scan is measured at kernel level only "
+                              "(the reference's CPU code for it is the same token loop as the main path's)"}))
+            return
+        run_lookback(args)
         return
     cfg = dict(CONFIGS[args.config])
     if args.batch:

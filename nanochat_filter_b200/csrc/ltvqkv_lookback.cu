@@ -14,9 +14,12 @@
 // then the warm-up prefix, whose states are replayed in 32-token blocks from checkpoints kept in
 // shared memory. Contributions of overlapping prefixes to one element of grad_combined are added
 // in the reference autograd graph's order — later chunks first, each rounded to the storage dtype
-// and summed in it — and the per-token group sums of dalpha are sequential in the channel index,
-// so fp32 results follow the reference oracle's operation order (separately rounded multiplies
-// and adds, no FMA contraction). Every grad_combined element is written by exactly one thread.
+// and summed in it — and in fp32 the per-token group sums of dalpha are sequential in the channel
+// index, so fp32 results follow the reference oracle's operation order (separately rounded
+// multiplies and adds, no FMA contraction); bf16 sums each warp's 32 channels by a shuffle tree.
+// Every grad_combined element is written by exactly one thread. The bf16 forward of the
+// production layout (T contiguous per channel row) reads 16-byte pieces of its row instead of one
+// element per token (lookback_fwd_rows_kernel, same arithmetic).
 #include "ltvqkv_common.cuh"
 
 namespace ltvqkv {
@@ -108,6 +111,63 @@ __global__ void __launch_bounds__(1024) lookback_fwd_kernel(LbArgs a) {
   }
 }
 
+// Forward for the production layout — the projection buffer's transposed view (T contiguous per
+// channel row, element strides sc_t = 1, sc_e = T), bf16: thread c reads its channel row 32 tokens
+// at a time as four 16-byte loads, the next 32 tokens' loads in flight while the current ones are
+// walked, and the decays come from a table of the row's T gates per decay group built once in
+// shared memory (one sigmoid per (group, token) instead of one per thread). Same arithmetic as
+// lookback_fwd_kernel token for token, so the outputs are identical.
+constexpr int kLbGroup = 32;
+
+LTVQKV_DEVICE void lb_load_group(const __nv_bfloat16* urow, int tb, int T, uint4 (&u)[4]) {
+#pragma unroll
+  for (int k = 0; k < 4; ++k)
+    u[k] = tb + 8 * k < T ? __ldg(reinterpret_cast<const uint4*>(urow + tb + 8 * k)) : make_uint4(0, 0, 0, 0);
+}
+
+__global__ void __launch_bounds__(1024) lookback_fwd_rows_kernel(LbArgs a) {
+  extern __shared__ float lb_gate[];  // [Da][T]
+  const int b = blockIdx.x / a.H, h = blockIdx.x % a.H;
+  const int c = threadIdx.x;
+  const long long cb = (long long)b * a.sc_b;
+  const int col = h * (a.D + a.Da);
+  for (int i = threadIdx.x; i < a.Da * a.T; i += blockDim.x)
+    lb_gate[i] = lb_alpha<__nv_bfloat16>(a, cb, i % a.T, col, h, i / a.T);
+  __syncthreads();
+  if (c >= a.D) return;
+  int which, hloc, nheads;
+  split_head(h, a.NH, a.NKVH, which, hloc, nheads);
+  const float* gr = lb_gate + (c / a.r) * a.T;
+  const float init = ld<__nv_bfloat16>(a.inits, ((long long)b * a.H + h) * a.D + c);
+  const __nv_bfloat16* urow = reinterpret_cast<const __nv_bfloat16*>(a.combined) + cb + (long long)(col + c) * a.T;
+  __nv_bfloat16* orow = reinterpret_cast<__nv_bfloat16*>(a.out[which]) + ((long long)b * nheads + hloc) * a.T * a.D + c;
+  for (int ci = 0; ci < a.nchunks; ++ci) {
+    int t_start, t_end, t_pref;
+    chunk_bounds(a, ci, t_start, t_end, t_pref);
+    float s = init;
+    int tb = t_pref & ~(kLbGroup - 1);
+    uint4 cur[4], nxt[4];
+    lb_load_group(urow, tb, a.T, cur);
+    for (; tb < t_end; tb += kLbGroup) {
+      if (tb + kLbGroup < t_end) lb_load_group(urow, tb + kLbGroup, a.T, nxt);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const uint32_t wv[4] = {cur[k].x, cur[k].y, cur[k].z, cur[k].w};
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int t = tb + 8 * k + e;
+          if (t >= t_pref && t < t_end) {
+            s = lb_step(s, gr[t], (e & 1) ? bf16_hi(wv[e / 2]) : bf16_lo(wv[e / 2]));
+            if (t >= t_start) orow[(long long)t * a.D] = __float2bfloat16_rn(s);
+          }
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) cur[k] = nxt[k];
+    }
+  }
+}
+
 // One token of the reverse sweep: du and dlogit contributions of this chunk (rounded to the
 // storage dtype and added to what later chunks left, or stored when no later chunk reached the
 // token), the group sums of dalpha, and the adjoint carry. All threads of the CTA call it.
@@ -123,10 +183,25 @@ LTVQKV_DEVICE void lb_bwd_token(const LbArgs& a, float* red, long long cb, long 
     st<S>(a.grad_combined, gi, first ? du : __fadd_rn(ld<S>(a.grad_combined, gi), du));
     red[c] = __fmul_rn(gacc, __fsub_rn(u, sprev));
   }
+  // bf16 with groups of whole warps: each warp's 32 terms summed by a shuffle tree, the warps of a
+  // group in order (fp32 keeps the oracle's sequential channel order)
+  constexpr bool kTree = sizeof(S) == 2;
+  const bool tree = kTree && a.r % 32 == 0;
+  if (tree) {
+    float v = active ? red[c] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    __syncthreads();  // every red[c] has been read
+    if ((c & 31) == 0) red[c / 32] = v;
+  }
   __syncthreads();
   if (c < a.Da) {
     float ga = 0.f;
-    for (int k = 0; k < a.r; ++k) ga = __fadd_rn(ga, red[c * a.r + k]);
+    if (tree) {
+      for (int k = 0; k < a.r / 32; ++k) ga = __fadd_rn(ga, red[c * (a.r / 32) + k]);
+    } else {
+      for (int k = 0; k < a.r; ++k) ga = __fadd_rn(ga, red[c * a.r + k]);
+    }
     const float ag = lb_alpha<S>(a, cb, t, col, h, c);
     const float graw = a.use_sigmoid ? __fmul_rn(__fmul_rn(ga, __fsub_rn(1.0f, ag)), ag) : ga;
     const long long gi = gcb + (long long)t * a.gc_t + (long long)(col + a.D + c) * a.gc_e;
@@ -267,7 +342,11 @@ extern "C" int ltvqkv_lookback_scan_fwd(int dtype, const void* combined, int64_t
   a.nchunks = lb_chunks(T, P, Q);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const int threads = lb_threads(a.D);
-  if (dtype == LTVQKV_DTYPE_F32)
+  const size_t gate_bytes = sizeof(float) * (size_t)Da * T;
+  if (dtype == LTVQKV_DTYPE_BF16 && sc_t == 1 && sc_e == T && T % 8 == 0 && sc_b % 8 == 0 &&
+      (reinterpret_cast<uintptr_t>(combined) & 15) == 0 && gate_bytes <= 48 * 1024)
+    lookback_fwd_rows_kernel<<<(unsigned int)(B * H), threads, gate_bytes, s>>>(a);
+  else if (dtype == LTVQKV_DTYPE_F32)
     lookback_fwd_kernel<float><<<(unsigned int)(B * H), threads, 0, s>>>(a);
   else
     lookback_fwd_kernel<__nv_bfloat16><<<(unsigned int)(B * H), threads, 0, s>>>(a);
