@@ -894,8 +894,12 @@ def run_lookback(args):
         gb.zero_()
         bwd(combined, inits, bias, *outs, *grads, gc, gi, gb, NH, NKVH, Da, r, P, Q, K, 32, 2, 8, True)
 
+    def fwd_only():
+        fwd(combined, inits, bias, *outs, B, T, NH, NKVH, Da, r, P, Q, K, 8, 8, 4, True)
+
     steps = max(1, args.steps)
     us = _graph_us(step, device, reps=steps)
+    fwd_us = _graph_us(fwd_only, device, reps=steps)
     nch = 1 + (T - P + Q - 1) // Q
     # bytes per step: forward reads combined and writes q/k/v; backward reads combined, the outputs
     # and their gradients, and writes grad_combined (the warm-up prefixes re-read combined from L2)
@@ -908,11 +912,13 @@ def run_lookback(args):
         "dtype": "bf16", "data": "synthetic (N(0,1) projection buffer and upstream gradients)",
         "config": {"workload": f"look-back scan (kernel level): B={B}, T={T}, 6+6+6 heads x 128, r=128, "
                                f"(P, Q, K) = ({P}, {Q}, {K}): {nch} chunks per row",
-                   "launch": "one CUDA graph per step (forward kernel, bias-gradient zero fill, backward kernel)"},
+                   "launch": "one CUDA graph per step: forward kernel, bias-gradient zero fill, chunk-parallel "
+                             "backward kernel, overlap fix-up kernel, logit-bias reduction"},
+        "forward_us": round(fwd_us, 1), "backward_us": round(us - fwd_us, 1),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(achieved / peaks["hbm_gbs"], 4), "bytes_per_step": step_bytes,
                      "peak_source": src},
-        "gpu_launches": 2 * steps,
+        "gpu_launches": 4 * steps,
     }))
 
 

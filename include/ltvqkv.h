@@ -180,6 +180,18 @@ LTVQKV_API int ltvqkv_scan_bwd_ckpt(int dtype,
  * oracle's operation order (separately rounded products and sums, later chunks' contributions
  * first). A warm-up prefix longer than about 13k tokens (D = 128) returns LTVQKV_ERR_TOO_LARGE. */
 LTVQKV_API size_t ltvqkv_lookback_workspace_bytes(int B, int NH, int NKVH, int Da);
+
+/* Workspace for ltvqkv_lookback_scan_bwd that also lets bf16 problems whose warm-up prefix is no
+ * longer than any chunk (K - 1 <= min(P, Q), K - 1 <= 64, more than one chunk, D + Da <= 256,
+ * r % 32 == 0) in the projection buffer's transposed layout (sc_t = gc_t = 1, T, the row and batch
+ * strides multiples of 8, both buffers 16-byte aligned) take the chunk-parallel backward: one CTA per (row, chunk) — the chunks restart from the initial state, so
+ * their backward passes are independent — and a fix-up pass that adds the two contributions of every
+ * token reached by two chunks in the sequential order (later chunk first, each rounded to bf16) and
+ * sums the initial-state gradients over the chunks in descending order. Same grad_combined and
+ * grad_inits as the sequential form; the logit-bias sum over tokens is associated per chunk. A
+ * workspace of ltvqkv_lookback_workspace_bytes() keeps the sequential form. Zero-filled once. */
+LTVQKV_API size_t ltvqkv_lookback_bwd_workspace_bytes(int B, int T, int NH, int NKVH, int Da, int r,
+                    int64_t P, int64_t Q, int64_t K);
 LTVQKV_API int ltvqkv_lookback_scan_fwd(int dtype,
                     const void* combined, int64_t sc_b, int64_t sc_t, int64_t sc_e,
                     const void* inits, const float* logit_bias,

@@ -42,6 +42,7 @@ EXPORTED_SYMBOLS = (
     "ltvqkv_proj_scan_fwd_ckpt",
     "ltvqkv_proj_scan_fwd_ckpt_rope",
     "ltvqkv_lookback_workspace_bytes",
+    "ltvqkv_lookback_bwd_workspace_bytes",
     "ltvqkv_lookback_scan_fwd",
     "ltvqkv_lookback_scan_bwd",
     "ltvqkv_rotary_qk_norm_fwd",
@@ -89,6 +90,8 @@ def _declare(lib: ctypes.CDLL) -> None:
                                                    _i, _i, _i, _i, _i, _i, _i, _vp]
     lib.ltvqkv_lookback_workspace_bytes.restype = _sz
     lib.ltvqkv_lookback_workspace_bytes.argtypes = [_i, _i, _i, _i]
+    lib.ltvqkv_lookback_bwd_workspace_bytes.restype = _sz
+    lib.ltvqkv_lookback_bwd_workspace_bytes.argtypes = [_i, _i, _i, _i, _i, _i, _i64, _i64, _i64]
     lib.ltvqkv_lookback_scan_fwd.restype = _i
     lib.ltvqkv_lookback_scan_fwd.argtypes = [_i, _vp, _i64, _i64, _i64, _vp, _pf, _vp, _vp, _vp,
                                              _i, _i, _i, _i, _i, _i, _i64, _i64, _i64, _i, _vp]

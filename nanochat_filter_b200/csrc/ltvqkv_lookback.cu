@@ -82,6 +82,19 @@ LTVQKV_DEVICE float lb_alpha(const LbArgs& a, long long cb, int t, int col, int 
   else return sigmoid_f32(raw);
 }
 
+// lb_alpha in two steps, so that the load can be issued tokens ahead of the arithmetic
+template <typename S>
+LTVQKV_DEVICE float lb_logit_ld(const LbArgs& a, long long cb, int t, int col, int g) {
+  return ld<S>(a.combined, cb + (long long)t * a.sc_t + (long long)(col + a.D + g) * a.sc_e);
+}
+template <typename S>
+LTVQKV_DEVICE float lb_gate(const LbArgs& a, float logit, int h, int g) {
+  const float raw = __fadd_rn(logit, a.logit_bias[h * a.Da + g]);
+  if (!a.use_sigmoid) return raw;
+  if constexpr (sizeof(S) == 4) return sigmoid_f32_exact(raw);
+  else return sigmoid_f32(raw);
+}
+
 // s' = (1 - a) s + a u, each product and the sum rounded once
 LTVQKV_DEVICE float lb_step(float s, float al, float u) {
   return __fadd_rn(__fmul_rn(__fsub_rn(1.0f, al), s), __fmul_rn(al, u));
@@ -283,6 +296,245 @@ __global__ void __launch_bounds__(1024) lookback_bwd_kernel(LbArgs a) {
   if (c < a.Da) a.bias_part[((long long)b * a.H + h) * a.Da + c] = bias_acc;
 }
 
+// ------------------------------------------------------------------------------------------
+// Chunk-parallel backward (bf16, warm-up prefix no longer than any chunk: K - 1 <= min(P, Q)).
+// Every chunk restarts from the initial state, so the chunks' backward passes are independent:
+// one CTA per (row, chunk) runs lookback_bwd_kernel's per-chunk body (prefix replay from
+// checkpoints, own tokens with h_{t-1} from the saved outputs, then the prefix), reading the value and
+// logit rows in aligned 8-token pieces (16 bytes) and writing grad_combined the same way where a
+// piece is the chunk's alone. Tokens reached by two chunks — a chunk's last K - 1 own
+// tokens are the next chunk's warm-up prefix — have both contributions, each rounded to bf16, kept
+// in workspace slots; lookback_bwd_fixup_kernel then adds them in the sequential kernel's order
+// (later chunk first) and sums the chunks' initial-state gradients in descending chunk order, as
+// the sequential kernel does. The per-row logit-bias sum adds per-chunk partials (a different
+// association than the sequential walk; bf16 only).
+struct LbParWs {  // workspace slots of the chunk-parallel backward
+  __nv_bfloat16* own;  // [rows][nchunks][K - 1][D + Da]: a chunk's contributions to its last K - 1 tokens
+  __nv_bfloat16* pre;  // [rows][nchunks][K - 1][D + Da]: a chunk's contributions to its warm-up prefix
+  float* gi;           // [rows][nchunks][D]: each chunk's initial-state gradient
+  float* bp;           // [rows][nchunks][Da]: each chunk's logit-bias partial
+};
+
+__host__ __device__ inline size_t lb_par_ws_bytes(int B, int H, int D, int Da, int nchunks, long long K) {
+  const size_t rows = (size_t)B * H, slots = rows * (size_t)nchunks;
+  const size_t kk = (size_t)(K > 1 ? K - 1 : 0);
+  const size_t bf = slots * kk * (size_t)(D + Da) * 2;
+  return 2 * ((bf + 255) / 256 * 256) + slots * (size_t)D * 4 + ((slots * (size_t)Da * 4 + 255) / 256 * 256);
+}
+
+// Eight tokens (8-aligned group starting at t0) of a channel / logit row in the production layout.
+LTVQKV_DEVICE uint4 lb_row8(const LbArgs& a, long long cb, int rowidx, int t0) {
+  return __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.combined) + cb +
+                                               (long long)rowidx * a.sc_e + t0));
+}
+LTVQKV_DEVICE float lb_pick(const uint4& w8, int e) {
+  const uint32_t wv = e < 2 ? w8.x : (e < 4 ? w8.y : (e < 6 ? w8.z : w8.w));
+  return (e & 1) ? bf16_hi(wv) : bf16_lo(wv);
+}
+
+__global__ void __launch_bounds__(256) lookback_bwd_par_kernel(LbArgs a, LbParWs w) {
+  extern __shared__ float sm[];
+  const int nwarps = blockDim.x / 32;
+  float* wsum = sm;                       // [2][nwarps]: per-warp dalpha sums, by token parity
+  float* pst = wsum + 2 * nwarps;         // [K - 1][D]: the warm-up prefix's states (before each token)
+  const int row = blockIdx.x / a.nchunks, ci = blockIdx.x % a.nchunks;
+  const int b = row / a.H, h = row % a.H;
+  const int c = threadIdx.x, warp = c / 32, lane = c % 32;
+  const bool active = c < a.D;
+  const int cc = active ? c : 0;
+  using S = __nv_bfloat16;
+  int which, hloc, nheads;
+  split_head(h, a.NH, a.NKVH, which, hloc, nheads);
+  const long long cb = (long long)b * a.sc_b, gcb = (long long)b * a.gc_b;
+  const int col = h * (a.D + a.Da);
+  const int g = cc / a.r;
+  const long long* hs = a.hs[which];
+  const long long* gs = a.gs[which];
+  const long long hb = (long long)b * hs[0] + (long long)hloc * hs[1] + (long long)cc * hs[3];
+  const long long gb = (long long)b * gs[0] + (long long)hloc * gs[1] + (long long)cc * gs[3];
+  const float init = active ? ld<S>(a.inits, ((long long)b * a.H + h) * a.D + cc) : 0.f;
+  const float bias_g = a.logit_bias[h * a.Da + g];
+  const float bias_c = c < a.Da ? a.logit_bias[h * a.Da + c] : 0.f;
+  const int kk = (int)(a.K - 1), DW = a.D + a.Da;
+  const long long slot = (long long)row * a.nchunks + ci;
+  __nv_bfloat16* gc = reinterpret_cast<__nv_bfloat16*>(a.grad_combined);
+  int t_start, t_end, t_pref;
+  chunk_bounds(a, ci, t_start, t_end, t_pref);
+  // first token reached by the next chunk's warm-up prefix (T: none)
+  int np = a.T;
+  if (ci + 1 < a.nchunks) {
+    int s2, e2, p2;
+    chunk_bounds(a, ci + 1, s2, e2, p2);
+    np = p2;
+  }
+  auto gate = [&](float lg, float bias) {
+    const float raw = __fadd_rn(lg, bias);
+    return a.use_sigmoid ? sigmoid_f32(raw) : raw;
+  };
+  const int npre = t_start - t_pref;  // <= K - 1
+  // warm-up prefix states, one aligned 8-token group of reads at a time
+  float s = init;
+  for (int ga = t_pref & ~7; ga < t_start; ga += 8) {
+    uint4 u8 = make_uint4(0, 0, 0, 0), l8 = make_uint4(0, 0, 0, 0);
+    if (active) {
+      u8 = lb_row8(a, cb, col + c, ga);
+      l8 = lb_row8(a, cb, col + a.D + g, ga);
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int t = ga + e;
+      if (active && t >= t_pref && t < t_start) {
+        pst[(long long)(t - t_pref) * a.D + c] = s;
+        s = lb_step(s, gate(lb_pick(l8, e), bias_g), lb_pick(u8, e));
+      }
+    }
+  }
+  const float s_pre = qz<S>(s);
+  float gacc = 0.f, bias_acc = 0.f;
+  int par = 0;
+  // One token: du and dlogit (returned for grad_combined, or into this chunk's own / prefix slot),
+  // the group sum of dalpha (shuffle trees, then the group's warps in order), the adjoint carry.
+  // One barrier per token: the per-warp sums alternate between two buffers.
+  auto token = [&](int t, float sprev, float lg, float u, float lgc, float& du_out, float& dl_out) {
+    const int dst = t < t_start ? 2 : (t >= np ? 1 : 0);
+    __nv_bfloat16* sl = dst == 2 ? w.pre + (slot * kk + (t - t_pref)) * DW
+                                 : (dst == 1 ? w.own + (slot * kk + (t - np)) * DW : nullptr);
+    float al = 0.f, v = 0.f;
+    if (active) {
+      al = gate(lg, bias_g);
+      const float du = qz<S>(__fmul_rn(gacc, al));
+      if (dst == 0) du_out = du;
+      else sl[c] = __float2bfloat16_rn(du);
+      v = __fmul_rn(gacc, __fsub_rn(u, sprev));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) wsum[par * nwarps + warp] = v;
+    __syncthreads();
+    if (c < a.Da) {
+      float ga = 0.f;
+      for (int q = 0; q < a.r / 32; ++q) ga = __fadd_rn(ga, wsum[par * nwarps + c * (a.r / 32) + q]);
+      const float ag = gate(lgc, bias_c);
+      const float graw = a.use_sigmoid ? __fmul_rn(__fmul_rn(ga, __fsub_rn(1.0f, ag)), ag) : ga;
+      const float dl = qz<S>(graw);
+      if (dst == 0) dl_out = dl;
+      else sl[a.D + c] = __float2bfloat16_rn(dl);
+      bias_acc = __fadd_rn(bias_acc, graw);
+    }
+    par ^= 1;
+    if (active) gacc = __fmul_rn(gacc, __fsub_rn(1.0f, al));
+  };
+  // own tokens, one aligned 8-token group at a time from the last: the group's reads first (its
+  // value and logit rows as 16-byte pieces), its grad_combined entries written as 16-byte pieces when
+  // the whole group is this chunk's alone
+  for (int ga = (t_end - 1) & ~7; ga + 8 > t_start; ga -= 8) {
+    const int lo = max(ga, t_start), hi = min(ga + 8, t_end);
+    uint4 u8 = make_uint4(0, 0, 0, 0), l8 = make_uint4(0, 0, 0, 0), lc8 = make_uint4(0, 0, 0, 0);
+    float ghv[8], hv[8];
+    if (active) {
+      u8 = lb_row8(a, cb, col + c, ga);
+      l8 = lb_row8(a, cb, col + a.D + g, ga);
+    }
+    if (c < a.Da) lc8 = lb_row8(a, cb, col + a.D + c, ga);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int t = ga + e;
+      ghv[e] = hv[e] = 0.f;
+      if (active && t >= lo && t < hi) {
+        ghv[e] = ld<S>(a.gh[which], gb + (long long)t * gs[2]);
+        hv[e] = t > t_start ? ld<S>(a.h[which], hb + (long long)(t - 1) * hs[2]) : s_pre;
+      }
+    }
+    float duv[8], dlv[8];
+#pragma unroll
+    for (int e = 7; e >= 0; --e) {
+      const int t = ga + e;
+      duv[e] = dlv[e] = 0.f;
+      if (t >= lo && t < hi) {  // uniform
+        if (active) gacc = __fadd_rn(gacc, ghv[e]);
+        token(t, active ? hv[e] : 0.f, lb_pick(l8, e), lb_pick(u8, e), lb_pick(lc8, e), duv[e], dlv[e]);
+      }
+    }
+    // this chunk's direct entries: tokens lo .. min(hi, np) - 1
+    const int dhi = min(hi, np);
+    const bool whole = lo == ga && dhi == ga + 8;
+    if (active) {
+      __nv_bfloat16* gr = gc + gcb + (long long)(col + c) * a.gc_e;
+      if (whole) {
+        *reinterpret_cast<uint4*>(gr + ga) = make_uint4(pack_bf16x2(duv[0], duv[1]), pack_bf16x2(duv[2], duv[3]),
+                                                       pack_bf16x2(duv[4], duv[5]), pack_bf16x2(duv[6], duv[7]));
+      } else {
+        for (int t = lo; t < dhi; ++t) gr[t] = __float2bfloat16_rn(duv[t - ga]);
+      }
+    }
+    if (c < a.Da) {
+      __nv_bfloat16* gr = gc + gcb + (long long)(col + a.D + c) * a.gc_e;
+      if (whole) {
+        *reinterpret_cast<uint4*>(gr + ga) = make_uint4(pack_bf16x2(dlv[0], dlv[1]), pack_bf16x2(dlv[2], dlv[3]),
+                                                       pack_bf16x2(dlv[4], dlv[5]), pack_bf16x2(dlv[6], dlv[7]));
+      } else {
+        for (int t = lo; t < dhi; ++t) gr[t] = __float2bfloat16_rn(dlv[t - ga]);
+      }
+    }
+  }
+  // the warm-up prefix, from its stored states (every entry goes to the prefix slot)
+  for (int ga = (t_start - 1) & ~7; npre > 0 && ga + 8 > t_pref; ga -= 8) {
+    const int lo = max(ga, t_pref), hi = min(ga + 8, t_start);
+    uint4 u8 = make_uint4(0, 0, 0, 0), l8 = make_uint4(0, 0, 0, 0), lc8 = make_uint4(0, 0, 0, 0);
+    if (active) {
+      u8 = lb_row8(a, cb, col + c, ga);
+      l8 = lb_row8(a, cb, col + a.D + g, ga);
+    }
+    if (c < a.Da) lc8 = lb_row8(a, cb, col + a.D + c, ga);
+#pragma unroll
+    for (int e = 7; e >= 0; --e) {
+      const int t = ga + e;
+      if (t >= lo && t < hi) {  // uniform
+        float du_unused = 0.f, dl_unused = 0.f;
+        token(t, active ? qz<S>(pst[(long long)(t - t_pref) * a.D + c]) : 0.f, lb_pick(l8, e), lb_pick(u8, e),
+              lb_pick(lc8, e), du_unused, dl_unused);
+      }
+    }
+  }
+  if (active) w.gi[slot * a.D + c] = gacc;
+  if (c < a.Da) w.bp[slot * a.Da + c] = bias_acc;
+}
+
+// Per row: the two contributions of every token reached by two chunks (later chunk first, then
+// the earlier one, in bf16), the initial-state gradient (chunks in descending order) and the
+// logit-bias partial (chunks in descending order).
+__global__ void __launch_bounds__(256) lookback_bwd_fixup_kernel(LbArgs a, LbParWs w) {
+  using S = __nv_bfloat16;
+  const int row = blockIdx.x;
+  const int b = row / a.H, h = row % a.H;
+  const long long gcb = (long long)b * a.gc_b;
+  const int col = h * (a.D + a.Da);
+  const int kk = (int)(a.K - 1), DW = a.D + a.Da;
+  for (int ci = 0; ci + 1 < a.nchunks; ++ci) {
+    int s1, e1, p1, s2, e2, p2;
+    chunk_bounds(a, ci, s1, e1, p1);
+    chunk_bounds(a, ci + 1, s2, e2, p2);
+    const long long so = (long long)row * a.nchunks + ci, sp = so + 1;
+    const int n = e1 - p2;  // tokens p2 .. e1 - 1 (the next chunk's prefix)
+    for (int idx = threadIdx.x; idx < n * DW; idx += blockDim.x) {
+      const int i = idx / DW, e = idx % DW, t = p2 + i;
+      const float later = __bfloat162float(w.pre[(sp * kk + i) * DW + e]);
+      const float earlier = __bfloat162float(w.own[(so * kk + i) * DW + e]);
+      st<S>(a.grad_combined, gcb + (long long)t * a.gc_t + (long long)(col + e) * a.gc_e, __fadd_rn(later, earlier));
+    }
+  }
+  for (int c = threadIdx.x; c < a.D; c += blockDim.x) {
+    float gi = 0.f;
+    for (int ci = a.nchunks - 1; ci >= 0; --ci) gi = __fadd_rn(gi, w.gi[((long long)row * a.nchunks + ci) * a.D + c]);
+    st<S>(a.grad_inits, (long long)row * a.D + c, gi);
+  }
+  for (int g = threadIdx.x; g < a.Da; g += blockDim.x) {
+    float bs = 0.f;
+    for (int ci = a.nchunks - 1; ci >= 0; --ci) bs = __fadd_rn(bs, w.bp[((long long)row * a.nchunks + ci) * a.Da + g]);
+    a.bias_part[(long long)row * a.Da + g] = bs;
+  }
+}
+
 // grad_logit_bias[h, g] += sum over b (descending, the oracle's order) of per-(b, h) partials.
 __global__ void lookback_bias_reduce_kernel(const float* part, float* grad_bias, int B, int H, int Da) {
   const int idx = blockIdx.x * blockDim.x + threadIdx.x;
@@ -320,6 +572,24 @@ using namespace ltvqkv;
 extern "C" size_t ltvqkv_lookback_workspace_bytes(int B, int NH, int NKVH, int Da) {
   if (B < 0 || NH < 0 || NKVH < 0 || Da < 1) return 0;
   return 256 + sizeof(float) * (size_t)B * (NH + 2 * NKVH) * Da;
+}
+
+// Whether the chunk-parallel backward takes these sizes, and the workspace it needs beyond the
+// sequential kernel's.
+bool lb_par_ok(int dtype, int T, int D, int Da, int r, long long P, long long Q, long long K) {
+  (void)r;
+  const int nch = lb_chunks(T, P, Q);
+  return dtype == LTVQKV_DTYPE_BF16 && D + Da <= 256 && r % 32 == 0 && nch > 1 && K - 1 <= P && K - 1 <= Q &&
+         K - 1 <= 64 && T > 0;
+}
+
+extern "C" size_t ltvqkv_lookback_bwd_workspace_bytes(int B, int T, int NH, int NKVH, int Da, int r, int64_t P,
+                                                      int64_t Q, int64_t K) {
+  const size_t base = ltvqkv_lookback_workspace_bytes(B, NH, NKVH, Da);
+  if (base == 0 || T < 0 || r < 1 || P < 1 || Q < 1 || K < 1) return base;
+  const int H = NH + 2 * NKVH, D = Da * r;
+  if (!lb_par_ok(LTVQKV_DTYPE_BF16, T, D, Da, r, P, Q, K)) return base;
+  return (base + 255) / 256 * 256 + lb_par_ws_bytes(B, H, D, Da, lb_chunks(T, P, Q), K);
 }
 
 extern "C" int ltvqkv_lookback_scan_fwd(int dtype, const void* combined, int64_t sc_b, int64_t sc_t, int64_t sc_e,
@@ -407,6 +677,37 @@ extern "C" int ltvqkv_lookback_scan_bwd(int dtype, const void* combined, int64_t
   const size_t smem = lb_bwd_smem(D, T, K, a.ncp);
   if (smem > 220 * 1024) return LTVQKV_ERR_TOO_LARGE;  // warm-up prefix too long for the checkpoints
   const int threads = lb_threads(D);
+  const size_t base = (ltvqkv_lookback_workspace_bytes(B, NH, NKVH, Da) + 255) / 256 * 256;
+  // the chunk-parallel form reads and writes 8-token pieces of the production layout (the projection
+  // buffer's transposed view: tokens contiguous per row, 16-byte aligned rows)
+  const bool prod = T % 8 == 0 && sc_t == 1 && gc_t == 1 && sc_e % 8 == 0 && gc_e % 8 == 0 &&
+                    sc_b % 8 == 0 && gc_b % 8 == 0 && (reinterpret_cast<uintptr_t>(combined) & 15) == 0 &&
+                    (reinterpret_cast<uintptr_t>(grad_combined) & 15) == 0;
+  if (prod && lb_par_ok(dtype, T, D, Da, r, P, Q, K) &&
+      workspace_bytes >= base + lb_par_ws_bytes(B, H, D, Da, a.nchunks, K)) {
+    // chunk-parallel form (the caller's workspace holds its slots)
+    char* wp = reinterpret_cast<char*>(workspace) + base;
+    const size_t rows = (size_t)B * H, slots = rows * (size_t)a.nchunks, kk = (size_t)(K - 1);
+    const size_t bf = (slots * kk * (size_t)(D + Da) * 2 + 255) / 256 * 256;
+    LbParWs w;
+    w.own = reinterpret_cast<__nv_bfloat16*>(wp);
+    w.pre = reinterpret_cast<__nv_bfloat16*>(wp + bf);
+    w.gi = reinterpret_cast<float*>(wp + 2 * bf);
+    w.bp = reinterpret_cast<float*>(wp + 2 * bf + slots * (size_t)D * 4);
+    const size_t psm = sizeof(float) * (2 * (size_t)(threads / 32) + (size_t)(K - 1) * D);
+    if (slots > 0x7fffffffULL) return LTVQKV_ERR_SHAPE;
+    if (psm > 48 * 1024 && cudaFuncSetAttribute(lookback_bwd_par_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                (int)psm) != cudaSuccess)
+      return ltvqkv_host::check_launch();
+    lookback_bwd_par_kernel<<<(unsigned int)slots, threads, psm, s>>>(a, w);
+    rc = ltvqkv_host::check_launch();
+    if (rc != LTVQKV_OK) return rc;
+    lookback_bwd_fixup_kernel<<<(unsigned int)rows, 256, 0, s>>>(a, w);
+    rc = ltvqkv_host::check_launch();
+    if (rc != LTVQKV_OK) return rc;
+    lookback_bias_reduce_kernel<<<(H * Da + 127) / 128, 128, 0, s>>>(a.bias_part, grad_logit_bias, B, H, Da);
+    return ltvqkv_host::check_launch();
+  }
   auto kern = dtype == LTVQKV_DTYPE_F32 ? lookback_bwd_kernel<float> : lookback_bwd_kernel<__nv_bfloat16>;
   if (smem > 48 * 1024 &&
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)

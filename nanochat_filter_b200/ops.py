@@ -445,7 +445,8 @@ def _lb_backward_kernel(combined, inits, logit_bias, hq, hk, hv, grad_hq, grad_h
     B, T, _ = combined.shape
     inits = inits.contiguous()
     logit_bias = logit_bias.contiguous()
-    ws = _lib.workspace(combined.device, L.ltvqkv_lookback_workspace_bytes(B, NH, NKVH, da))
+    ws = _lib.workspace(combined.device, L.ltvqkv_lookback_bwd_workspace_bytes(B, T, NH, NKVH, da, r, P, Q, K),
+                        kind="lookback_bwd")
     sc, gc = combined.stride(), grad_combined.stride()
     S = _lib.strides
     rc = L.ltvqkv_lookback_scan_bwd(
