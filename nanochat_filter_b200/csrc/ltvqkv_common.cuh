@@ -195,6 +195,16 @@ LTVQKV_DEVICE void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "mem
 // ------------------------------------------------------------------------------------------
 LTVQKV_DEVICE uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
+// 16-byte global -> shared copy that bypasses registers (cp.async, L2 only); commit of this thread's
+// copies issued since the last commit as one group; waits for all / all but the newest N groups.
+LTVQKV_DEVICE void cp_async16(void* smem_dst, const void* gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
+}
+LTVQKV_DEVICE void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+LTVQKV_DEVICE void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+template <int N>
+LTVQKV_DEVICE void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
 // ------------------------------------------------------------------------------------------
 // mbarrier
 // ------------------------------------------------------------------------------------------

@@ -114,13 +114,6 @@ constexpr int kDmSlice = 16;
 constexpr int kDmRows = 32;
 constexpr int kDmNt = kDmRows / 8 / 2;  // n-tiles (8 rows) per warp
 
-// 16-byte global -> shared copy that bypasses registers (cp.async, L2 only), and the wait for all
-// of this thread's copies.
-LTVQKV_DEVICE void cp_async16(void* smem_dst, const void* gsrc) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
-}
-LTVQKV_DEVICE void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
-
 LTVQKV_DEVICE void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])

@@ -125,10 +125,11 @@ __global__ void __launch_bounds__(1024) lookback_fwd_kernel(LbArgs a) {
 }
 
 // Forward for the production layout — the projection buffer's transposed view (T contiguous per
-// channel row, element strides sc_t = 1, sc_e = T), bf16: thread c reads its channel row 32 tokens
-// at a time as four 16-byte loads, the next 32 tokens' loads in flight while the current ones are
-// walked, and the decays come from a table of the row's T gates per decay group built once in
-// shared memory (one sigmoid per (group, token) instead of one per thread). Same arithmetic as
+// channel row, element strides sc_t = 1, sc_e = T), bf16: one CTA per (row, chunk) — every chunk
+// restarts from the initial state, so the chunks are independent — thread c reads its channel row
+// 32 tokens at a time as four 16-byte loads, the next 32 tokens' loads in flight while the current
+// ones are walked, and the decays come from a table of the chunk's gates per decay group built once
+// in shared memory (one sigmoid per (group, token) instead of one per thread). Same arithmetic as
 // lookback_fwd_kernel token for token, so the outputs are identical.
 constexpr int kLbGroup = 32;
 
@@ -138,46 +139,56 @@ LTVQKV_DEVICE void lb_load_group(const __nv_bfloat16* urow, int tb, int T, uint4
     u[k] = tb + 8 * k < T ? __ldg(reinterpret_cast<const uint4*>(urow + tb + 8 * k)) : make_uint4(0, 0, 0, 0);
 }
 
+// Gate-table length of one chunk (its warm-up prefix and own tokens; the longest chunk is
+// max(P, Q) tokens).
+__host__ __device__ inline int lb_chunk_gate_len(int T, long long P, long long Q, long long K) {
+  const long long n = (P > Q ? P : Q) + K - 1;
+  return (int)(n < T ? n : T);
+}
+
 __global__ void __launch_bounds__(1024) lookback_fwd_rows_kernel(LbArgs a) {
-  extern __shared__ float lb_gate[];  // [Da][T]
-  const int b = blockIdx.x / a.H, h = blockIdx.x % a.H;
+  extern __shared__ float lb_gate[];  // [Da][gstride]: gates of tokens t_pref ..
+  const int row = blockIdx.x / a.nchunks, ci = blockIdx.x % a.nchunks;
+  const int b = row / a.H, h = row % a.H;
   const int c = threadIdx.x;
   const long long cb = (long long)b * a.sc_b;
   const int col = h * (a.D + a.Da);
-  for (int i = threadIdx.x; i < a.Da * a.T; i += blockDim.x)
-    lb_gate[i] = lb_alpha<__nv_bfloat16>(a, cb, i % a.T, col, h, i / a.T);
+  const int gstride = lb_chunk_gate_len(a.T, a.P, a.Q, a.K);
+  int t_start, t_end, t_pref;
+  chunk_bounds(a, ci, t_start, t_end, t_pref);
+  const int ntok = t_end - t_pref;
+  for (int i = threadIdx.x; i < a.Da * ntok; i += blockDim.x) {
+    const int g = i / ntok, j = i - g * ntok;
+    lb_gate[g * gstride + j] = lb_alpha<__nv_bfloat16>(a, cb, t_pref + j, col, h, g);
+  }
   __syncthreads();
   if (c >= a.D) return;
   int which, hloc, nheads;
   split_head(h, a.NH, a.NKVH, which, hloc, nheads);
-  const float* gr = lb_gate + (c / a.r) * a.T;
+  const float* gr = lb_gate + (c / a.r) * gstride - t_pref;  // indexed by token
   const float init = ld<__nv_bfloat16>(a.inits, ((long long)b * a.H + h) * a.D + c);
   const __nv_bfloat16* urow = reinterpret_cast<const __nv_bfloat16*>(a.combined) + cb + (long long)(col + c) * a.T;
   __nv_bfloat16* orow = reinterpret_cast<__nv_bfloat16*>(a.out[which]) + ((long long)b * nheads + hloc) * a.T * a.D + c;
-  for (int ci = 0; ci < a.nchunks; ++ci) {
-    int t_start, t_end, t_pref;
-    chunk_bounds(a, ci, t_start, t_end, t_pref);
-    float s = init;
-    int tb = t_pref & ~(kLbGroup - 1);
-    uint4 cur[4], nxt[4];
-    lb_load_group(urow, tb, a.T, cur);
-    for (; tb < t_end; tb += kLbGroup) {
-      if (tb + kLbGroup < t_end) lb_load_group(urow, tb + kLbGroup, a.T, nxt);
+  float s = init;
+  int tb = t_pref & ~7;
+  uint4 cur[4], nxt[4];
+  lb_load_group(urow, tb, a.T, cur);
+  for (; tb < t_end; tb += kLbGroup) {
+    if (tb + kLbGroup < t_end) lb_load_group(urow, tb + kLbGroup, a.T, nxt);
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const uint32_t wv[4] = {cur[k].x, cur[k].y, cur[k].z, cur[k].w};
+    for (int k = 0; k < 4; ++k) {
+      const uint32_t wv[4] = {cur[k].x, cur[k].y, cur[k].z, cur[k].w};
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const int t = tb + 8 * k + e;
-          if (t >= t_pref && t < t_end) {
-            s = lb_step(s, gr[t], (e & 1) ? bf16_hi(wv[e / 2]) : bf16_lo(wv[e / 2]));
-            if (t >= t_start) orow[(long long)t * a.D] = __float2bfloat16_rn(s);
-          }
+      for (int e = 0; e < 8; ++e) {
+        const int t = tb + 8 * k + e;
+        if (t >= t_pref && t < t_end) {
+          s = lb_step(s, gr[t], (e & 1) ? bf16_hi(wv[e / 2]) : bf16_lo(wv[e / 2]));
+          if (t >= t_start) orow[(long long)t * a.D] = __float2bfloat16_rn(s);
         }
       }
-#pragma unroll
-      for (int k = 0; k < 4; ++k) cur[k] = nxt[k];
     }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) cur[k] = nxt[k];
   }
 }
 
@@ -299,10 +310,10 @@ __global__ void __launch_bounds__(1024) lookback_bwd_kernel(LbArgs a) {
 // ------------------------------------------------------------------------------------------
 // Chunk-parallel backward (bf16, warm-up prefix no longer than any chunk: K - 1 <= min(P, Q)).
 // Every chunk restarts from the initial state, so the chunks' backward passes are independent:
-// one CTA per (row, chunk) runs lookback_bwd_kernel's per-chunk body (prefix replay from
-// checkpoints, own tokens with h_{t-1} from the saved outputs, then the prefix), reading the value and
-// logit rows in aligned 8-token pieces (16 bytes) and writing grad_combined the same way where a
-// piece is the chunk's alone. Tokens reached by two chunks — a chunk's last K - 1 own
+// one CTA per (row, chunk) runs lookback_bwd_kernel's per-chunk body (prefix states replayed into
+// shared memory, own tokens with h_{t-1} from the saved outputs, then the prefix), reading the value
+// rows in aligned 8-token pieces (16 bytes) and writing grad_combined the same way where a piece is
+// the chunk's alone. Tokens reached by two chunks — a chunk's last K - 1 own
 // tokens are the next chunk's warm-up prefix — have both contributions, each rounded to bf16, kept
 // in workspace slots; lookback_bwd_fixup_kernel then adds them in the sequential kernel's order
 // (later chunk first) and sums the chunks' initial-state gradients in descending chunk order, as
@@ -332,11 +343,50 @@ LTVQKV_DEVICE float lb_pick(const uint4& w8, int e) {
   return (e & 1) ? bf16_hi(wv) : bf16_lo(wv);
 }
 
-__global__ void __launch_bounds__(256) lookback_bwd_par_kernel(LbArgs a, LbParWs w) {
-  extern __shared__ float sm[];
+// Sums eight values over the warp's 32 lanes, each by the tree of a 16-8-4-2-1 xor butterfly (the
+// same pairs of partial sums, so the same result bit for bit), in 9 shuffles instead of 40: every
+// level keeps half of the lane's values and sends the other half. Lane l ends with the sum of
+// value (l >> 2) & 7.
+LTVQKV_DEVICE float lb_warp_sum8(const float (&v)[8], int lane) {
+  const bool h4 = lane & 16, h3 = lane & 8, h2 = lane & 4;
+  float r1[4], r2[2];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float keep = h4 ? v[k + 4] : v[k], send = h4 ? v[k] : v[k + 4];
+    r1[k] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const float keep = h3 ? r1[j + 2] : r1[j], send = h3 ? r1[j] : r1[j + 2];
+    r2[j] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+  }
+  float r3 = (h2 ? r2[1] : r2[0]) + __shfl_xor_sync(0xffffffffu, h2 ? r2[0] : r2[1], 4);
+  r3 += __shfl_xor_sync(0xffffffffu, r3, 2);
+  r3 += __shfl_xor_sync(0xffffffffu, r3, 1);
+  return r3;
+}
+
+constexpr int kLbStages = 3;  // 8-token groups of copies in flight (the current one and two ahead)
+__host__ __device__ inline size_t lb_par_stage_bytes(int D) { return (size_t)48 * D; }
+
+// One CTA per (row, chunk), thread = channel. Shared memory: three stages of 8-token group tiles
+// (upstream-gradient rows, saved-output rows one token back, the value rows' 16-byte pieces) copied
+// by cp.async two groups ahead of their use, the chunk's gates (every token's gate computed once,
+// not by each thread), the warm-up prefix's states, and per group the warps' dalpha sums and the
+// group's logit gradients. The group's eight tokens walk the adjoint carry; their dalpha terms are
+// summed over each warp by one reduce-scatter tree and over the gate group's warps after one
+// barrier per group, by 8 * Da threads (token, gate group) at once.
+__global__ void __launch_bounds__(256, 4) lookback_bwd_par_kernel(LbArgs a, LbParWs w) {
+  extern __shared__ __align__(16) float sm[];
   const int nwarps = blockDim.x / 32;
-  float* wsum = sm;                       // [2][nwarps]: per-warp dalpha sums, by token parity
-  float* pst = wsum + 2 * nwarps;         // [K - 1][D]: the warm-up prefix's states (before each token)
+  const int gstride = lb_chunk_gate_len(a.T, a.P, a.Q, a.K);
+  const size_t stage_bytes = lb_par_stage_bytes(a.D);
+  char* stages = reinterpret_cast<char*>(sm);
+  float* wsum = reinterpret_cast<float*>(stages + kLbStages * stage_bytes);  // [2][8][nwarps]: per-warp
+                                                                               // dalpha sums, by group parity
+  float* grs = wsum + 16 * nwarps;    // [2][Da][8]: the group's logit-bias terms, by group parity
+  float* gt = grs + 16 * a.Da;        // [Da][gstride]: gates of tokens t_pref ..
+  float* pst = gt + a.Da * gstride;   // [K - 1][D]: the warm-up prefix's states (before each token)
   const int row = blockIdx.x / a.nchunks, ci = blockIdx.x % a.nchunks;
   const int b = row / a.H, h = row % a.H;
   const int c = threadIdx.x, warp = c / 32, lane = c % 32;
@@ -347,14 +397,13 @@ __global__ void __launch_bounds__(256) lookback_bwd_par_kernel(LbArgs a, LbParWs
   split_head(h, a.NH, a.NKVH, which, hloc, nheads);
   const long long cb = (long long)b * a.sc_b, gcb = (long long)b * a.gc_b;
   const int col = h * (a.D + a.Da);
-  const int g = cc / a.r;
+  const int g = cc / a.r, rw = a.r / 32;
   const long long* hs = a.hs[which];
   const long long* gs = a.gs[which];
-  const long long hb = (long long)b * hs[0] + (long long)hloc * hs[1] + (long long)cc * hs[3];
-  const long long gb = (long long)b * gs[0] + (long long)hloc * gs[1] + (long long)cc * gs[3];
+  // channel 0 of this row's saved outputs and upstream gradients (channels contiguous)
+  const S* h0 = reinterpret_cast<const S*>(a.h[which]) + (long long)b * hs[0] + (long long)hloc * hs[1];
+  const S* gh0 = reinterpret_cast<const S*>(a.gh[which]) + (long long)b * gs[0] + (long long)hloc * gs[1];
   const float init = active ? ld<S>(a.inits, ((long long)b * a.H + h) * a.D + cc) : 0.f;
-  const float bias_g = a.logit_bias[h * a.Da + g];
-  const float bias_c = c < a.Da ? a.logit_bias[h * a.Da + c] : 0.f;
   const int kk = (int)(a.K - 1), DW = a.D + a.Da;
   const long long slot = (long long)row * a.nchunks + ci;
   __nv_bfloat16* gc = reinterpret_cast<__nv_bfloat16*>(a.grad_combined);
@@ -367,171 +416,187 @@ __global__ void __launch_bounds__(256) lookback_bwd_par_kernel(LbArgs a, LbParWs
     chunk_bounds(a, ci + 1, s2, e2, p2);
     np = p2;
   }
-  auto gate = [&](float lg, float bias) {
-    const float raw = __fadd_rn(lg, bias);
-    return a.use_sigmoid ? sigmoid_f32(raw) : raw;
+  // Group n (tokens ga_n = ga_0 - 8 n .. + 7) goes to stage n % 3: its upstream-gradient rows
+  // ga_n .. ga_n + 7 and saved-output rows ga_n - 1 .. ga_n + 6 as [8][D] tiles (one 16-byte piece
+  // each per thread: D / 8 pieces per row), and this thread's value piece (tokens ga_n .. + 7).
+  // Every commit is one group (empty past the last), so waiting for all but the newest one leaves
+  // the next group landed.
+  const int ga0 = (t_end - 1) & ~7;
+  const int ngroups = (ga0 - (t_pref & ~7)) / 8 + 1;
+  auto issue = [&](int n) {
+    if (active && n < ngroups) {
+      const int ga = ga0 - 8 * n;
+      char* base = stages + (size_t)(n % kLbStages) * stage_bytes;
+      S* ghs = reinterpret_cast<S*>(base);
+      S* hts = ghs + 8 * a.D;
+      const int pr = a.D / 8, e = c / pr, p8 = (c - e * pr) * 8, t = ga + e;
+      cp_async16(ghs + e * a.D + p8, gh0 + (long long)t * gs[2] + p8);
+      if (t >= 1) cp_async16(hts + e * a.D + p8, h0 + (long long)(t - 1) * hs[2] + p8);
+      cp_async16(reinterpret_cast<uint4*>(hts + 8 * a.D) + c,
+                 reinterpret_cast<const S*>(a.combined) + cb + (long long)(col + c) * a.sc_e + ga);
+    }
+    cp_async_commit();
   };
-  const int npre = t_start - t_pref;  // <= K - 1
-  // warm-up prefix states, one aligned 8-token group of reads at a time
+  issue(0);
+  issue(1);
+  // the chunk's gates, tokens t_pref .. t_end - 1 (same arithmetic as the sequential kernels)
+  const int ntok = t_end - t_pref;
+  for (int i = c; i < a.Da * ntok; i += blockDim.x) {
+    const int gg = i / ntok, j = i - gg * ntok;
+    gt[gg * gstride + j] = lb_gate<S>(a, lb_logit_ld<S>(a, cb, t_pref + j, col, gg), h, gg);
+  }
+  __syncthreads();
+  const float* gtc = gt + g * gstride - t_pref;  // this thread's gate row, indexed by token
+  // warm-up prefix states, one aligned 8-token group of value reads at a time
   float s = init;
   for (int ga = t_pref & ~7; ga < t_start; ga += 8) {
-    uint4 u8 = make_uint4(0, 0, 0, 0), l8 = make_uint4(0, 0, 0, 0);
-    if (active) {
-      u8 = lb_row8(a, cb, col + c, ga);
-      l8 = lb_row8(a, cb, col + a.D + g, ga);
-    }
+    const uint4 u8 = active ? lb_row8(a, cb, col + c, ga) : make_uint4(0, 0, 0, 0);
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
       const int t = ga + e;
       if (active && t >= t_pref && t < t_start) {
         pst[(long long)(t - t_pref) * a.D + c] = s;
-        s = lb_step(s, gate(lb_pick(l8, e), bias_g), lb_pick(u8, e));
+        s = lb_step(s, gtc[t], lb_pick(u8, e));
       }
     }
   }
   const float s_pre = qz<S>(s);
   float gacc = 0.f, bias_acc = 0.f;
-  int par = 0;
-  // One token: du and dlogit (returned for grad_combined, or into this chunk's own / prefix slot),
-  // the group sum of dalpha (shuffle trees, then the group's warps in order), the adjoint carry.
-  // One barrier per token: the per-warp sums alternate between two buffers.
-  auto token = [&](int t, float sprev, float lg, float u, float lgc, float& du_out, float& dl_out) {
-    const int dst = t < t_start ? 2 : (t >= np ? 1 : 0);
-    __nv_bfloat16* sl = dst == 2 ? w.pre + (slot * kk + (t - t_pref)) * DW
-                                 : (dst == 1 ? w.own + (slot * kk + (t - np)) * DW : nullptr);
-    float al = 0.f, v = 0.f;
-    if (active) {
-      al = gate(lg, bias_g);
-      const float du = qz<S>(__fmul_rn(gacc, al));
-      if (dst == 0) du_out = du;
-      else sl[c] = __float2bfloat16_rn(du);
-      v = __fmul_rn(gacc, __fsub_rn(u, sprev));
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    if (lane == 0) wsum[par * nwarps + warp] = v;
-    __syncthreads();
-    if (c < a.Da) {
-      float ga = 0.f;
-      for (int q = 0; q < a.r / 32; ++q) ga = __fadd_rn(ga, wsum[par * nwarps + c * (a.r / 32) + q]);
-      const float ag = gate(lgc, bias_c);
-      const float graw = a.use_sigmoid ? __fmul_rn(__fmul_rn(ga, __fsub_rn(1.0f, ag)), ag) : ga;
-      const float dl = qz<S>(graw);
-      if (dst == 0) dl_out = dl;
-      else sl[a.D + c] = __float2bfloat16_rn(dl);
-      bias_acc = __fadd_rn(bias_acc, graw);
-    }
-    par ^= 1;
-    if (active) gacc = __fmul_rn(gacc, __fsub_rn(1.0f, al));
-  };
-  // own tokens, one aligned 8-token group at a time from the last: the group's reads first (its
-  // value and logit rows as 16-byte pieces), its grad_combined entries written as 16-byte pieces when
-  // the whole group is this chunk's alone
-  for (int ga = (t_end - 1) & ~7; ga + 8 > t_start; ga -= 8) {
-    const int lo = max(ga, t_start), hi = min(ga + 8, t_end);
-    uint4 u8 = make_uint4(0, 0, 0, 0), l8 = make_uint4(0, 0, 0, 0), lc8 = make_uint4(0, 0, 0, 0);
+  int buf = 0, plo = 0, phi = 0, pga = 0;  // the previous group's tokens (bias terms not yet added)
+  cp_async_wait<1>();
+  __syncthreads();
+  // Aligned 8-token groups from the last: own tokens (upstream gradient added, h_{t-1} from the saved
+  // outputs, the first one from the prefix replay), then the warm-up prefix (stored states). Each
+  // entry goes to grad_combined, or, for a token that another chunk also reaches, to this chunk's
+  // own (t >= np) or prefix (t < t_start) slot.
+  for (int n = 0; n < ngroups; ++n) {
+    const int ga = ga0 - 8 * n;
+    issue(n + 2);
+    const int lo = max(ga, t_pref), hi = min(ga + 8, t_end);
+    const S* ghs = reinterpret_cast<const S*>(stages + (size_t)(n % kLbStages) * stage_bytes);
+    const S* hts = ghs + 8 * a.D;
+    const uint4 u8 = active ? reinterpret_cast<const uint4*>(hts + 8 * a.D)[c] : make_uint4(0, 0, 0, 0);
     float ghv[8], hv[8];
-    if (active) {
-      u8 = lb_row8(a, cb, col + c, ga);
-      l8 = lb_row8(a, cb, col + a.D + g, ga);
-    }
-    if (c < a.Da) lc8 = lb_row8(a, cb, col + a.D + c, ga);
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
       const int t = ga + e;
       ghv[e] = hv[e] = 0.f;
-      if (active && t >= lo && t < hi) {
-        ghv[e] = ld<S>(a.gh[which], gb + (long long)t * gs[2]);
-        hv[e] = t > t_start ? ld<S>(a.h[which], hb + (long long)(t - 1) * hs[2]) : s_pre;
+      if (active && t >= max(lo, t_start) && t < hi) {
+        ghv[e] = __bfloat162float(ghs[e * a.D + c]);
+        hv[e] = t > t_start ? __bfloat162float(hts[e * a.D + c]) : s_pre;
       }
+      if (active && t >= lo && t < t_start) hv[e] = qz<S>(pst[(long long)(t - t_pref) * a.D + c]);
     }
-    float duv[8], dlv[8];
+    float duv[8], v[8];
 #pragma unroll
     for (int e = 7; e >= 0; --e) {
       const int t = ga + e;
-      duv[e] = dlv[e] = 0.f;
-      if (t >= lo && t < hi) {  // uniform
-        if (active) gacc = __fadd_rn(gacc, ghv[e]);
-        token(t, active ? hv[e] : 0.f, lb_pick(l8, e), lb_pick(u8, e), lb_pick(lc8, e), duv[e], dlv[e]);
+      duv[e] = v[e] = 0.f;
+      if (active && t >= lo && t < hi) {
+        gacc = __fadd_rn(gacc, ghv[e]);  // zero for prefix tokens
+        const float al = gtc[t];
+        const float du = qz<S>(__fmul_rn(gacc, al));
+        if (t < t_start) w.pre[(slot * kk + (t - t_pref)) * DW + c] = __float2bfloat16_rn(du);
+        else if (t >= np) w.own[(slot * kk + (t - np)) * DW + c] = __float2bfloat16_rn(du);
+        else duv[e] = du;
+        v[e] = __fmul_rn(gacc, __fsub_rn(lb_pick(u8, e), hv[e]));
+        gacc = __fmul_rn(gacc, __fsub_rn(1.0f, al));
       }
     }
-    // this chunk's direct entries: tokens lo .. min(hi, np) - 1
-    const int dhi = min(hi, np);
-    const bool whole = lo == ga && dhi == ga + 8;
-    if (active) {
+    const float vs = lb_warp_sum8(v, lane);
+    if ((lane & 3) == 0) wsum[(buf * 8 + (lane >> 2)) * nwarps + warp] = vs;
+    cp_async_wait<1>();  // group n + 1's copies (this thread's) landed; the barrier publishes them
+    __syncthreads();
+    if (c < a.Da) {  // the previous group's logit-bias terms, tokens in descending order
+      for (int t = phi - 1; t >= plo; --t) bias_acc = __fadd_rn(bias_acc, grs[((buf ^ 1) * a.Da + c) * 8 + t - pga]);
+    }
+    if (c < 8 * a.Da) {  // thread (token ga + (c & 7), gate group c >> 3)
+      const int e = c & 7, gg = c >> 3, t = ga + e;
+      if (t >= lo && t < hi) {
+        float gsum = 0.f;
+        for (int q = 0; q < rw; ++q) gsum = __fadd_rn(gsum, wsum[(buf * 8 + e) * nwarps + gg * rw + q]);
+        const float ag = gt[gg * gstride + t - t_pref];
+        const float graw = a.use_sigmoid ? __fmul_rn(__fmul_rn(gsum, __fsub_rn(1.0f, ag)), ag) : gsum;
+        const __nv_bfloat16 dl = __float2bfloat16_rn(graw);
+        if (t < t_start) w.pre[(slot * kk + (t - t_pref)) * DW + a.D + gg] = dl;
+        else if (t >= np) w.own[(slot * kk + (t - np)) * DW + a.D + gg] = dl;
+        else gc[gcb + (long long)(col + a.D + gg) * a.gc_e + t] = dl;
+        grs[(buf * a.Da + gg) * 8 + e] = graw;
+      }
+    }
+    plo = lo; phi = hi; pga = ga;
+    buf ^= 1;
+    // this chunk's direct value entries: tokens max(lo, t_start) .. min(hi, np) - 1
+    const int dlo = max(lo, t_start), dhi = min(hi, np);
+    if (active && dlo < dhi) {
       __nv_bfloat16* gr = gc + gcb + (long long)(col + c) * a.gc_e;
-      if (whole) {
+      if (dlo == ga && dhi == ga + 8) {
         *reinterpret_cast<uint4*>(gr + ga) = make_uint4(pack_bf16x2(duv[0], duv[1]), pack_bf16x2(duv[2], duv[3]),
                                                        pack_bf16x2(duv[4], duv[5]), pack_bf16x2(duv[6], duv[7]));
       } else {
-        for (int t = lo; t < dhi; ++t) gr[t] = __float2bfloat16_rn(duv[t - ga]);
-      }
-    }
-    if (c < a.Da) {
-      __nv_bfloat16* gr = gc + gcb + (long long)(col + a.D + c) * a.gc_e;
-      if (whole) {
-        *reinterpret_cast<uint4*>(gr + ga) = make_uint4(pack_bf16x2(dlv[0], dlv[1]), pack_bf16x2(dlv[2], dlv[3]),
-                                                       pack_bf16x2(dlv[4], dlv[5]), pack_bf16x2(dlv[6], dlv[7]));
-      } else {
-        for (int t = lo; t < dhi; ++t) gr[t] = __float2bfloat16_rn(dlv[t - ga]);
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          if (ga + e >= dlo && ga + e < dhi) gr[ga + e] = __float2bfloat16_rn(duv[e]);
       }
     }
   }
-  // the warm-up prefix, from its stored states (every entry goes to the prefix slot)
-  for (int ga = (t_start - 1) & ~7; npre > 0 && ga + 8 > t_pref; ga -= 8) {
-    const int lo = max(ga, t_pref), hi = min(ga + 8, t_start);
-    uint4 u8 = make_uint4(0, 0, 0, 0), l8 = make_uint4(0, 0, 0, 0), lc8 = make_uint4(0, 0, 0, 0);
-    if (active) {
-      u8 = lb_row8(a, cb, col + c, ga);
-      l8 = lb_row8(a, cb, col + a.D + g, ga);
-    }
-    if (c < a.Da) lc8 = lb_row8(a, cb, col + a.D + c, ga);
-#pragma unroll
-    for (int e = 7; e >= 0; --e) {
-      const int t = ga + e;
-      if (t >= lo && t < hi) {  // uniform
-        float du_unused = 0.f, dl_unused = 0.f;
-        token(t, active ? qz<S>(pst[(long long)(t - t_pref) * a.D + c]) : 0.f, lb_pick(l8, e), lb_pick(u8, e),
-              lb_pick(lc8, e), du_unused, dl_unused);
-      }
-    }
+  __syncthreads();
+  if (c < a.Da) {
+    for (int t = phi - 1; t >= plo; --t) bias_acc = __fadd_rn(bias_acc, grs[((buf ^ 1) * a.Da + c) * 8 + t - pga]);
   }
   if (active) w.gi[slot * a.D + c] = gacc;
   if (c < a.Da) w.bp[slot * a.Da + c] = bias_acc;
 }
 
-// Per row: the two contributions of every token reached by two chunks (later chunk first, then
-// the earlier one, in bf16), the initial-state gradient (chunks in descending order) and the
-// logit-bias partial (chunks in descending order).
+// One CTA per (row, pair of consecutive chunks ci, ci + 1): every token reached by both (the later
+// chunk's warm-up prefix) gets the later chunk's contribution plus the earlier one's, in bf16, staged
+// through shared memory so that the slots are read and grad_combined written along their contiguous
+// axes. The CTAs of ci = 0 also sum the row's initial-state gradient and logit-bias partials over the
+// chunks in descending order.
+constexpr int kLbFixTok = 16;
 __global__ void __launch_bounds__(256) lookback_bwd_fixup_kernel(LbArgs a, LbParWs w) {
   using S = __nv_bfloat16;
-  const int row = blockIdx.x;
+  __shared__ float st_sum[256 * (kLbFixTok + 1)];  // [D + Da][kLbFixTok], rows padded by one
+  const int row = blockIdx.x / (a.nchunks - 1), ci = blockIdx.x % (a.nchunks - 1);
   const int b = row / a.H, h = row % a.H;
   const long long gcb = (long long)b * a.gc_b;
   const int col = h * (a.D + a.Da);
   const int kk = (int)(a.K - 1), DW = a.D + a.Da;
-  for (int ci = 0; ci + 1 < a.nchunks; ++ci) {
-    int s1, e1, p1, s2, e2, p2;
-    chunk_bounds(a, ci, s1, e1, p1);
-    chunk_bounds(a, ci + 1, s2, e2, p2);
-    const long long so = (long long)row * a.nchunks + ci, sp = so + 1;
-    const int n = e1 - p2;  // tokens p2 .. e1 - 1 (the next chunk's prefix)
-    for (int idx = threadIdx.x; idx < n * DW; idx += blockDim.x) {
-      const int i = idx / DW, e = idx % DW, t = p2 + i;
-      const float later = __bfloat162float(w.pre[(sp * kk + i) * DW + e]);
-      const float earlier = __bfloat162float(w.own[(so * kk + i) * DW + e]);
-      st<S>(a.grad_combined, gcb + (long long)t * a.gc_t + (long long)(col + e) * a.gc_e, __fadd_rn(later, earlier));
+  int s1, e1, p1, s2, e2, p2;
+  chunk_bounds(a, ci, s1, e1, p1);
+  chunk_bounds(a, ci + 1, s2, e2, p2);
+  const long long so = (long long)row * a.nchunks + ci, sp = so + 1;
+  const int n = e1 - p2;  // tokens p2 .. e1 - 1
+  for (int i0 = 0; i0 < n; i0 += kLbFixTok) {
+    const int m = min(kLbFixTok, n - i0);
+    for (int e = threadIdx.x; e < DW; e += blockDim.x) {  // slot rows: D + Da contiguous entries
+      const __nv_bfloat16* later = w.pre + (sp * kk + i0) * DW + e;
+      const __nv_bfloat16* earlier = w.own + (so * kk + i0) * DW + e;
+#pragma unroll 4
+      for (int i = 0; i < m; ++i)
+        st_sum[e * (kLbFixTok + 1) + i] =
+            __fadd_rn(__bfloat162float(later[(long long)i * DW]), __bfloat162float(earlier[(long long)i * DW]));
     }
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < DW * kLbFixTok; idx += blockDim.x) {  // grad_combined rows: tokens
+      const int e = idx / kLbFixTok, i = idx % kLbFixTok;                   // contiguous
+      if (i < m)
+        st<S>(a.grad_combined, gcb + (long long)(p2 + i0 + i) * a.gc_t + (long long)(col + e) * a.gc_e,
+              st_sum[e * (kLbFixTok + 1) + i]);
+    }
+    __syncthreads();
   }
+  if (ci != 0) return;
   for (int c = threadIdx.x; c < a.D; c += blockDim.x) {
     float gi = 0.f;
-    for (int ci = a.nchunks - 1; ci >= 0; --ci) gi = __fadd_rn(gi, w.gi[((long long)row * a.nchunks + ci) * a.D + c]);
+    for (int cj = a.nchunks - 1; cj >= 0; --cj) gi = __fadd_rn(gi, w.gi[((long long)row * a.nchunks + cj) * a.D + c]);
     st<S>(a.grad_inits, (long long)row * a.D + c, gi);
   }
-  for (int g = threadIdx.x; g < a.Da; g += blockDim.x) {
+  for (int gg = threadIdx.x; gg < a.Da; gg += blockDim.x) {
     float bs = 0.f;
-    for (int ci = a.nchunks - 1; ci >= 0; --ci) bs = __fadd_rn(bs, w.bp[((long long)row * a.nchunks + ci) * a.Da + g]);
-    a.bias_part[(long long)row * a.Da + g] = bs;
+    for (int cj = a.nchunks - 1; cj >= 0; --cj)
+      bs = __fadd_rn(bs, w.bp[((long long)row * a.nchunks + cj) * a.Da + gg]);
+    a.bias_part[(long long)row * a.Da + gg] = bs;
   }
 }
 
@@ -580,7 +645,7 @@ bool lb_par_ok(int dtype, int T, int D, int Da, int r, long long P, long long Q,
   (void)r;
   const int nch = lb_chunks(T, P, Q);
   return dtype == LTVQKV_DTYPE_BF16 && D + Da <= 256 && r % 32 == 0 && nch > 1 && K - 1 <= P && K - 1 <= Q &&
-         K - 1 <= 64 && T > 0;
+         K - 1 <= 64 && T > 0 && (long long)Da * lb_chunk_gate_len(T, P, Q, K) * 4 <= 32 * 1024;
 }
 
 extern "C" size_t ltvqkv_lookback_bwd_workspace_bytes(int B, int T, int NH, int NKVH, int Da, int r, int64_t P,
@@ -612,10 +677,11 @@ extern "C" int ltvqkv_lookback_scan_fwd(int dtype, const void* combined, int64_t
   a.nchunks = lb_chunks(T, P, Q);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const int threads = lb_threads(a.D);
-  const size_t gate_bytes = sizeof(float) * (size_t)Da * T;
+  const size_t gate_bytes = sizeof(float) * (size_t)Da * lb_chunk_gate_len(T, P, Q, K);
+  const size_t ctas = (size_t)B * H * a.nchunks;
   if (dtype == LTVQKV_DTYPE_BF16 && sc_t == 1 && sc_e == T && T % 8 == 0 && sc_b % 8 == 0 &&
-      (reinterpret_cast<uintptr_t>(combined) & 15) == 0 && gate_bytes <= 48 * 1024)
-    lookback_fwd_rows_kernel<<<(unsigned int)(B * H), threads, gate_bytes, s>>>(a);
+      (reinterpret_cast<uintptr_t>(combined) & 15) == 0 && gate_bytes <= 48 * 1024 && ctas <= 0x7fffffffULL)
+    lookback_fwd_rows_kernel<<<(unsigned int)ctas, threads, gate_bytes, s>>>(a);
   else if (dtype == LTVQKV_DTYPE_F32)
     lookback_fwd_kernel<float><<<(unsigned int)(B * H), threads, 0, s>>>(a);
   else
@@ -680,9 +746,16 @@ extern "C" int ltvqkv_lookback_scan_bwd(int dtype, const void* combined, int64_t
   const size_t base = (ltvqkv_lookback_workspace_bytes(B, NH, NKVH, Da) + 255) / 256 * 256;
   // the chunk-parallel form reads and writes 8-token pieces of the production layout (the projection
   // buffer's transposed view: tokens contiguous per row, 16-byte aligned rows)
-  const bool prod = T % 8 == 0 && sc_t == 1 && gc_t == 1 && sc_e % 8 == 0 && gc_e % 8 == 0 &&
-                    sc_b % 8 == 0 && gc_b % 8 == 0 && (reinterpret_cast<uintptr_t>(combined) & 15) == 0 &&
-                    (reinterpret_cast<uintptr_t>(grad_combined) & 15) == 0;
+  bool prod = T % 8 == 0 && sc_t == 1 && gc_t == 1 && sc_e % 8 == 0 && gc_e % 8 == 0 && sc_b % 8 == 0 &&
+              gc_b % 8 == 0 && (reinterpret_cast<uintptr_t>(combined) & 15) == 0 &&
+              (reinterpret_cast<uintptr_t>(grad_combined) & 15) == 0;
+  // and the saved outputs and their gradients copied as 16-byte pieces of channel-contiguous rows
+  for (int w = 0; w < 3; ++w) {
+    if ((w == 0 ? NH : NKVH) == 0) continue;
+    for (const int64_t* st : {hst[w], gst[w]})
+      prod = prod && st && st[3] == 1 && st[0] % 8 == 0 && st[1] % 8 == 0 && st[2] % 8 == 0;
+    prod = prod && (reinterpret_cast<uintptr_t>(hp[w]) & 15) == 0 && (reinterpret_cast<uintptr_t>(gp[w]) & 15) == 0;
+  }
   if (prod && lb_par_ok(dtype, T, D, Da, r, P, Q, K) &&
       workspace_bytes >= base + lb_par_ws_bytes(B, H, D, Da, a.nchunks, K)) {
     // chunk-parallel form (the caller's workspace holds its slots)
@@ -694,7 +767,9 @@ extern "C" int ltvqkv_lookback_scan_bwd(int dtype, const void* combined, int64_t
     w.pre = reinterpret_cast<__nv_bfloat16*>(wp + bf);
     w.gi = reinterpret_cast<float*>(wp + 2 * bf);
     w.bp = reinterpret_cast<float*>(wp + 2 * bf + slots * (size_t)D * 4);
-    const size_t psm = sizeof(float) * (2 * (size_t)(threads / 32) + (size_t)(K - 1) * D);
+    const size_t psm = kLbStages * lb_par_stage_bytes(D) +
+                       sizeof(float) * (16 * (size_t)(threads / 32) + 16 * (size_t)Da +
+                                        (size_t)Da * lb_chunk_gate_len(T, P, Q, K) + (size_t)(K - 1) * D);
     if (slots > 0x7fffffffULL) return LTVQKV_ERR_SHAPE;
     if (psm > 48 * 1024 && cudaFuncSetAttribute(lookback_bwd_par_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                 (int)psm) != cudaSuccess)
@@ -702,7 +777,7 @@ extern "C" int ltvqkv_lookback_scan_bwd(int dtype, const void* combined, int64_t
     lookback_bwd_par_kernel<<<(unsigned int)slots, threads, psm, s>>>(a, w);
     rc = ltvqkv_host::check_launch();
     if (rc != LTVQKV_OK) return rc;
-    lookback_bwd_fixup_kernel<<<(unsigned int)rows, 256, 0, s>>>(a, w);
+    lookback_bwd_fixup_kernel<<<(unsigned int)(rows * (size_t)(a.nchunks - 1)), 256, 0, s>>>(a, w);
     rc = ltvqkv_host::check_launch();
     if (rc != LTVQKV_OK) return rc;
     lookback_bias_reduce_kernel<<<(H * Da + 127) / 128, 128, 0, s>>>(a.bias_part, grad_logit_bias, B, H, Da);

@@ -185,3 +185,58 @@ def test_lookback_filter_decode_equals_batch(cuda_device, variant, dtype):
             # the 40 steps: norm-wise bound, as for the whole bf16 layer
             d, e = _np(dec), _np(batch[i])
             assert np.abs(d - e).max() <= 2e-2 * np.abs(e).max()
+
+
+def _bwd_abi(comb, inits, bias, outs, grads, NH, NKVH, Da, r, P, Q, K, ws_bytes):
+    """ltvqkv_lookback_scan_bwd through the C-ABI with a workspace of ws_bytes (fresh, zeroed)."""
+    L = _lib.load()
+    B, T, _ = comb.shape
+    gc = torch.zeros(comb.shape[0], comb.shape[2], comb.shape[1], dtype=comb.dtype,
+                     device=comb.device).transpose(1, 2)  # the production (transposed) layout
+    gi = torch.empty_like(inits)
+    gb = torch.zeros_like(bias)
+    ws = torch.zeros(max(ws_bytes, 4096), dtype=torch.uint8, device=comb.device)
+    S = _lib.strides
+    sc, gs = comb.stride(), gc.stride()
+    rc = L.ltvqkv_lookback_scan_bwd(
+        _lib.dtype_code(comb.dtype), comb.data_ptr(), sc[0], sc[1], sc[2], inits.data_ptr(), bias.data_ptr(),
+        *[x for o in outs for x in (o.data_ptr(), S(o.stride()))],
+        *[x for o in grads for x in (o.data_ptr(), S(o.stride()))],
+        gc.data_ptr(), gs[0], gs[1], gs[2], gi.data_ptr(), gb.data_ptr(),
+        B, T, NH, NKVH, Da, r, P, Q, K, 1, ws.data_ptr(), ws.numel(), _lib.stream_handle(comb.device))
+    _lib.check(rc, "ltvqkv_lookback_scan_bwd")
+    torch.cuda.synchronize()
+    return gc, gi, gb
+
+
+@pytest.mark.parametrize("B,T,NH,NKVH,Da,r,P,Q,K", [
+    (2, 304, 1, 1, 1, 128, 64, 60, 5),        # chunk edges off the 8-token grid
+    (2, 512, 2, 1, 1, 128, 128, 112, 17),     # the reference's production chunking
+    (1, 256, 1, 1, 2, 64, 32, 16, 17),        # prefix as long as a chunk, two gate groups
+    (2, 200, 1, 1, 4, 32, 24, 24, 9),         # four gate groups per head
+    (3, 136, 1, 0, 1, 128, 32, 32, 1),        # restarts without a prefix
+])
+def test_lookback_chunk_parallel_backward(cuda_device, B, T, NH, NKVH, Da, r, P, Q, K):
+    """The chunk-parallel backward (bf16, production layout, T % 8 == 0, taken when the workspace holds
+    its slots) against the one-CTA-per-row form (the minimal workspace) and the oracle: grad_combined
+    and grad_inits bit for bit, the logit-bias gradient within fp32 reassociation (per-chunk partials)."""
+    comb, inits, bias, gq, gk, gv = _random(B * 1000 + T, B, T, NH, NKVH, Da, r)
+    comb, inits, gq, gk, gv = (O.round_bf16(a) for a in (comb, inits, gq, gk, gv))
+    dev, bf = cuda_device, torch.bfloat16
+    tc = torch.from_numpy(comb).to(dev, bf).transpose(1, 2).contiguous().transpose(1, 2)
+    ti, tb = torch.from_numpy(inits).to(dev, bf), torch.from_numpy(bias).to(dev)
+    grads = [torch.from_numpy(a).to(dev, bf) for a in (gq, gk, gv)]
+    outs = getattr(OPS, LB.format("blelloch"))(tc, ti, tb, NH, NKVH, Da, r, P, Q, K, 8, 8, 4, 32, 2, 8, True)
+    L = _lib.load()
+    small = L.ltvqkv_lookback_workspace_bytes(B, NH, NKVH, Da)
+    full = L.ltvqkv_lookback_bwd_workspace_bytes(B, T, NH, NKVH, Da, r, P, Q, K)
+    assert full > small  # eligible shape: the query asks for the chunk slots
+    seq = _bwd_abi(tc, ti, tb, outs, grads, NH, NKVH, Da, r, P, Q, K, small)
+    par = _bwd_abi(tc, ti, tb, outs, grads, NH, NKVH, Da, r, P, Q, K, full)
+    assert torch.equal(par[0], seq[0]), "grad_combined"
+    assert torch.equal(par[1], seq[1]), "grad_inits"
+    assert max_rel_err(_np(par[2]), _np(seq[2]), FLOOR) <= 1e-5, "grad_logit_bias"
+    egc, egi, egb = O.scan_bwd(comb, inits, bias, gq, gk, gv, NH, NKVH, Da, r, True, True, (P, Q, K))
+    for a, e, n in zip(par, (egc, egi, egb), ("grad_combined", "grad_inits", "grad_logit_bias")):
+        if e.size:
+            assert max_rel_err(_np(a), e, FLOOR) <= 2e-2, n
