@@ -423,13 +423,14 @@ __global__ void __launch_bounds__(256, 4) lookback_bwd_par_kernel(LbArgs a, LbPa
   // the next group landed.
   const int ga0 = (t_end - 1) & ~7;
   const int ngroups = (ga0 - (t_pref & ~7)) / 8 + 1;
+  const int pe = cc / (a.D / 8), p8 = (cc - pe * (a.D / 8)) * 8;  // this thread's tile piece: row, channel
   auto issue = [&](int n) {
     if (active && n < ngroups) {
       const int ga = ga0 - 8 * n;
       char* base = stages + (size_t)(n % kLbStages) * stage_bytes;
       S* ghs = reinterpret_cast<S*>(base);
       S* hts = ghs + 8 * a.D;
-      const int pr = a.D / 8, e = c / pr, p8 = (c - e * pr) * 8, t = ga + e;
+      const int e = pe, t = ga + e;
       cp_async16(ghs + e * a.D + p8, gh0 + (long long)t * gs[2] + p8);
       if (t >= 1) cp_async16(hts + e * a.D + p8, h0 + (long long)(t - 1) * hs[2] + p8);
       cp_async16(reinterpret_cast<uint4*>(hts + 8 * a.D) + c,
@@ -495,7 +496,7 @@ __global__ void __launch_bounds__(256, 4) lookback_bwd_par_kernel(LbArgs a, LbPa
       if (active && t >= lo && t < hi) {
         gacc = __fadd_rn(gacc, ghv[e]);  // zero for prefix tokens
         const float al = gtc[t];
-        const float du = qz<S>(__fmul_rn(gacc, al));
+        const float du = __fmul_rn(gacc, al);  // rounded to bf16 once, where it is stored
         if (t < t_start) w.pre[(slot * kk + (t - t_pref)) * DW + c] = __float2bfloat16_rn(du);
         else if (t >= np) w.own[(slot * kk + (t - np)) * DW + c] = __float2bfloat16_rn(du);
         else duv[e] = du;
