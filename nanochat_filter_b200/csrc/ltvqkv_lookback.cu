@@ -477,31 +477,43 @@ __global__ void __launch_bounds__(256, 4) lookback_bwd_par_kernel(LbArgs a, LbPa
     const S* ghs = reinterpret_cast<const S*>(stages + (size_t)(n % kLbStages) * stage_bytes);
     const S* hts = ghs + 8 * a.D;
     const uint4 u8 = active ? reinterpret_cast<const uint4*>(hts + 8 * a.D)[c] : make_uint4(0, 0, 0, 0);
-    float ghv[8], hv[8];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const int t = ga + e;
-      ghv[e] = hv[e] = 0.f;
-      if (active && t >= max(lo, t_start) && t < hi) {
-        ghv[e] = __bfloat162float(ghs[e * a.D + c]);
-        hv[e] = t > t_start ? __bfloat162float(hts[e * a.D + c]) : s_pre;
-      }
-      if (active && t >= lo && t < t_start) hv[e] = qz<S>(pst[(long long)(t - t_pref) * a.D + c]);
-    }
     float duv[8], v[8];
+    if (active && ga > t_start && ga + 8 <= min(t_end, np)) {
+      // interior group: eight own tokens, all entries direct, h_{t-1} all from the saved outputs
 #pragma unroll
-    for (int e = 7; e >= 0; --e) {
-      const int t = ga + e;
-      duv[e] = v[e] = 0.f;
-      if (active && t >= lo && t < hi) {
-        gacc = __fadd_rn(gacc, ghv[e]);  // zero for prefix tokens
-        const float al = gtc[t];
-        const float du = __fmul_rn(gacc, al);  // rounded to bf16 once, where it is stored
-        if (t < t_start) w.pre[(slot * kk + (t - t_pref)) * DW + c] = __float2bfloat16_rn(du);
-        else if (t >= np) w.own[(slot * kk + (t - np)) * DW + c] = __float2bfloat16_rn(du);
-        else duv[e] = du;
-        v[e] = __fmul_rn(gacc, __fsub_rn(lb_pick(u8, e), hv[e]));
+      for (int e = 7; e >= 0; --e) {
+        gacc = __fadd_rn(gacc, __bfloat162float(ghs[e * a.D + c]));
+        const float al = gtc[ga + e];
+        duv[e] = __fmul_rn(gacc, al);  // rounded to bf16 once, where it is stored
+        v[e] = __fmul_rn(gacc, __fsub_rn(lb_pick(u8, e), __bfloat162float(hts[e * a.D + c])));
         gacc = __fmul_rn(gacc, __fsub_rn(1.0f, al));
+      }
+    } else {
+      float ghv[8], hv[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int t = ga + e;
+        ghv[e] = hv[e] = 0.f;
+        if (active && t >= max(lo, t_start) && t < hi) {
+          ghv[e] = __bfloat162float(ghs[e * a.D + c]);
+          hv[e] = t > t_start ? __bfloat162float(hts[e * a.D + c]) : s_pre;
+        }
+        if (active && t >= lo && t < t_start) hv[e] = qz<S>(pst[(long long)(t - t_pref) * a.D + c]);
+      }
+#pragma unroll
+      for (int e = 7; e >= 0; --e) {
+        const int t = ga + e;
+        duv[e] = v[e] = 0.f;
+        if (active && t >= lo && t < hi) {
+          gacc = __fadd_rn(gacc, ghv[e]);  // zero for prefix tokens
+          const float al = gtc[t];
+          const float du = __fmul_rn(gacc, al);  // rounded to bf16 once, where it is stored
+          if (t < t_start) w.pre[(slot * kk + (t - t_pref)) * DW + c] = __float2bfloat16_rn(du);
+          else if (t >= np) w.own[(slot * kk + (t - np)) * DW + c] = __float2bfloat16_rn(du);
+          else duv[e] = du;
+          v[e] = __fmul_rn(gacc, __fsub_rn(lb_pick(u8, e), hv[e]));
+          gacc = __fmul_rn(gacc, __fsub_rn(1.0f, al));
+        }
       }
     }
     const float vs = lb_warp_sum8(v, lane);
