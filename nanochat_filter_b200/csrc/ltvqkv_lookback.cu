@@ -376,11 +376,13 @@ __host__ __device__ inline size_t lb_par_stage_bytes(int D) { return (size_t)48 
 // group's logit gradients. The group's eight tokens walk the adjoint carry; their dalpha terms are
 // summed over each warp by one reduce-scatter tree and over the gate group's warps after one
 // barrier per group, by 8 * Da threads (token, gate group) at once.
+template <int kD>  // head dim when known at compile time (0: a.D)
 __global__ void __launch_bounds__(256, 4) lookback_bwd_par_kernel(LbArgs a, LbParWs w) {
+  const int D = kD ? kD : a.D;
   extern __shared__ __align__(16) float sm[];
   const int nwarps = blockDim.x / 32;
   const int gstride = lb_chunk_gate_len(a.T, a.P, a.Q, a.K);
-  const size_t stage_bytes = lb_par_stage_bytes(a.D);
+  const size_t stage_bytes = lb_par_stage_bytes(D);
   char* stages = reinterpret_cast<char*>(sm);
   float* wsum = reinterpret_cast<float*>(stages + kLbStages * stage_bytes);  // [2][8][nwarps]: per-warp
                                                                                // dalpha sums, by group parity
@@ -390,21 +392,21 @@ __global__ void __launch_bounds__(256, 4) lookback_bwd_par_kernel(LbArgs a, LbPa
   const int row = blockIdx.x / a.nchunks, ci = blockIdx.x % a.nchunks;
   const int b = row / a.H, h = row % a.H;
   const int c = threadIdx.x, warp = c / 32, lane = c % 32;
-  const bool active = c < a.D;
+  const bool active = c < D;
   const int cc = active ? c : 0;
   using S = __nv_bfloat16;
   int which, hloc, nheads;
   split_head(h, a.NH, a.NKVH, which, hloc, nheads);
   const long long cb = (long long)b * a.sc_b, gcb = (long long)b * a.gc_b;
-  const int col = h * (a.D + a.Da);
+  const int col = h * (D + a.Da);
   const int g = cc / a.r, rw = a.r / 32;
   const long long* hs = a.hs[which];
   const long long* gs = a.gs[which];
   // channel 0 of this row's saved outputs and upstream gradients (channels contiguous)
   const S* h0 = reinterpret_cast<const S*>(a.h[which]) + (long long)b * hs[0] + (long long)hloc * hs[1];
   const S* gh0 = reinterpret_cast<const S*>(a.gh[which]) + (long long)b * gs[0] + (long long)hloc * gs[1];
-  const float init = active ? ld<S>(a.inits, ((long long)b * a.H + h) * a.D + cc) : 0.f;
-  const int kk = (int)(a.K - 1), DW = a.D + a.Da;
+  const float init = active ? ld<S>(a.inits, ((long long)b * a.H + h) * D + cc) : 0.f;
+  const int kk = (int)(a.K - 1), DW = D + a.Da;
   const long long slot = (long long)row * a.nchunks + ci;
   __nv_bfloat16* gc = reinterpret_cast<__nv_bfloat16*>(a.grad_combined);
   int t_start, t_end, t_pref;
@@ -423,17 +425,17 @@ __global__ void __launch_bounds__(256, 4) lookback_bwd_par_kernel(LbArgs a, LbPa
   // the next group landed.
   const int ga0 = (t_end - 1) & ~7;
   const int ngroups = (ga0 - (t_pref & ~7)) / 8 + 1;
-  const int pe = cc / (a.D / 8), p8 = (cc - pe * (a.D / 8)) * 8;  // this thread's tile piece: row, channel
+  const int pe = cc / (D / 8), p8 = (cc - pe * (D / 8)) * 8;  // this thread's tile piece: row, channel
   auto issue = [&](int n) {
     if (active && n < ngroups) {
       const int ga = ga0 - 8 * n;
       char* base = stages + (size_t)(n % kLbStages) * stage_bytes;
       S* ghs = reinterpret_cast<S*>(base);
-      S* hts = ghs + 8 * a.D;
+      S* hts = ghs + 8 * D;
       const int e = pe, t = ga + e;
-      cp_async16(ghs + e * a.D + p8, gh0 + (long long)t * gs[2] + p8);
-      if (t >= 1) cp_async16(hts + e * a.D + p8, h0 + (long long)(t - 1) * hs[2] + p8);
-      cp_async16(reinterpret_cast<uint4*>(hts + 8 * a.D) + c,
+      cp_async16(ghs + e * D + p8, gh0 + (long long)t * gs[2] + p8);
+      if (t >= 1) cp_async16(hts + e * D + p8, h0 + (long long)(t - 1) * hs[2] + p8);
+      cp_async16(reinterpret_cast<uint4*>(hts + 8 * D) + c,
                  reinterpret_cast<const S*>(a.combined) + cb + (long long)(col + c) * a.sc_e + ga);
     }
     cp_async_commit();
@@ -456,7 +458,7 @@ __global__ void __launch_bounds__(256, 4) lookback_bwd_par_kernel(LbArgs a, LbPa
     for (int e = 0; e < 8; ++e) {
       const int t = ga + e;
       if (active && t >= t_pref && t < t_start) {
-        pst[(long long)(t - t_pref) * a.D + c] = s;
+        pst[(long long)(t - t_pref) * D + c] = s;
         s = lb_step(s, gtc[t], lb_pick(u8, e));
       }
     }
@@ -475,17 +477,17 @@ __global__ void __launch_bounds__(256, 4) lookback_bwd_par_kernel(LbArgs a, LbPa
     issue(n + 2);
     const int lo = max(ga, t_pref), hi = min(ga + 8, t_end);
     const S* ghs = reinterpret_cast<const S*>(stages + (size_t)(n % kLbStages) * stage_bytes);
-    const S* hts = ghs + 8 * a.D;
-    const uint4 u8 = active ? reinterpret_cast<const uint4*>(hts + 8 * a.D)[c] : make_uint4(0, 0, 0, 0);
+    const S* hts = ghs + 8 * D;
+    const uint4 u8 = active ? reinterpret_cast<const uint4*>(hts + 8 * D)[c] : make_uint4(0, 0, 0, 0);
     float duv[8], v[8];
     if (active && ga > t_start && ga + 8 <= min(t_end, np)) {
       // interior group: eight own tokens, all entries direct, h_{t-1} all from the saved outputs
 #pragma unroll
       for (int e = 7; e >= 0; --e) {
-        gacc = __fadd_rn(gacc, __bfloat162float(ghs[e * a.D + c]));
+        gacc = __fadd_rn(gacc, __bfloat162float(ghs[e * D + c]));
         const float al = gtc[ga + e];
         duv[e] = __fmul_rn(gacc, al);  // rounded to bf16 once, where it is stored
-        v[e] = __fmul_rn(gacc, __fsub_rn(lb_pick(u8, e), __bfloat162float(hts[e * a.D + c])));
+        v[e] = __fmul_rn(gacc, __fsub_rn(lb_pick(u8, e), __bfloat162float(hts[e * D + c])));
         gacc = __fmul_rn(gacc, __fsub_rn(1.0f, al));
       }
     } else {
@@ -495,10 +497,10 @@ __global__ void __launch_bounds__(256, 4) lookback_bwd_par_kernel(LbArgs a, LbPa
         const int t = ga + e;
         ghv[e] = hv[e] = 0.f;
         if (active && t >= max(lo, t_start) && t < hi) {
-          ghv[e] = __bfloat162float(ghs[e * a.D + c]);
-          hv[e] = t > t_start ? __bfloat162float(hts[e * a.D + c]) : s_pre;
+          ghv[e] = __bfloat162float(ghs[e * D + c]);
+          hv[e] = t > t_start ? __bfloat162float(hts[e * D + c]) : s_pre;
         }
-        if (active && t >= lo && t < t_start) hv[e] = qz<S>(pst[(long long)(t - t_pref) * a.D + c]);
+        if (active && t >= lo && t < t_start) hv[e] = qz<S>(pst[(long long)(t - t_pref) * D + c]);
       }
 #pragma unroll
       for (int e = 7; e >= 0; --e) {
@@ -531,9 +533,9 @@ __global__ void __launch_bounds__(256, 4) lookback_bwd_par_kernel(LbArgs a, LbPa
         const float ag = gt[gg * gstride + t - t_pref];
         const float graw = a.use_sigmoid ? __fmul_rn(__fmul_rn(gsum, __fsub_rn(1.0f, ag)), ag) : gsum;
         const __nv_bfloat16 dl = __float2bfloat16_rn(graw);
-        if (t < t_start) w.pre[(slot * kk + (t - t_pref)) * DW + a.D + gg] = dl;
-        else if (t >= np) w.own[(slot * kk + (t - np)) * DW + a.D + gg] = dl;
-        else gc[gcb + (long long)(col + a.D + gg) * a.gc_e + t] = dl;
+        if (t < t_start) w.pre[(slot * kk + (t - t_pref)) * DW + D + gg] = dl;
+        else if (t >= np) w.own[(slot * kk + (t - np)) * DW + D + gg] = dl;
+        else gc[gcb + (long long)(col + D + gg) * a.gc_e + t] = dl;
         grs[(buf * a.Da + gg) * 8 + e] = graw;
       }
     }
@@ -557,7 +559,7 @@ __global__ void __launch_bounds__(256, 4) lookback_bwd_par_kernel(LbArgs a, LbPa
   if (c < a.Da) {
     for (int t = phi - 1; t >= plo; --t) bias_acc = __fadd_rn(bias_acc, grs[((buf ^ 1) * a.Da + c) * 8 + t - pga]);
   }
-  if (active) w.gi[slot * a.D + c] = gacc;
+  if (active) w.gi[slot * D + c] = gacc;
   if (c < a.Da) w.bp[slot * a.Da + c] = bias_acc;
 }
 
@@ -784,10 +786,11 @@ extern "C" int ltvqkv_lookback_scan_bwd(int dtype, const void* combined, int64_t
                        sizeof(float) * (16 * (size_t)(threads / 32) + 16 * (size_t)Da +
                                         (size_t)Da * lb_chunk_gate_len(T, P, Q, K) + (size_t)(K - 1) * D);
     if (slots > 0x7fffffffULL) return LTVQKV_ERR_SHAPE;
-    if (psm > 48 * 1024 && cudaFuncSetAttribute(lookback_bwd_par_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                (int)psm) != cudaSuccess)
+    auto par = D == 128 ? lookback_bwd_par_kernel<128> : lookback_bwd_par_kernel<0>;
+    if (psm > 48 * 1024 &&
+        cudaFuncSetAttribute(par, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)psm) != cudaSuccess)
       return ltvqkv_host::check_launch();
-    lookback_bwd_par_kernel<<<(unsigned int)slots, threads, psm, s>>>(a, w);
+    par<<<(unsigned int)slots, threads, psm, s>>>(a, w);
     rc = ltvqkv_host::check_launch();
     if (rc != LTVQKV_OK) return rc;
     lookback_bwd_fixup_kernel<<<(unsigned int)(rows * (size_t)(a.nchunks - 1)), 256, 0, s>>>(a, w);

@@ -215,6 +215,8 @@ def _bwd_abi(comb, inits, bias, outs, grads, NH, NKVH, Da, r, P, Q, K, ws_bytes)
     (1, 256, 1, 1, 2, 64, 32, 16, 17),        # prefix as long as a chunk, two gate groups
     (2, 200, 1, 1, 4, 32, 24, 24, 9),         # four gate groups per head
     (3, 136, 1, 0, 1, 128, 32, 32, 1),        # restarts without a prefix
+    (2, 256, 1, 1, 2, 32, 32, 28, 5),         # head dim 64 (the kernel's runtime head-dim form)
+    (1, 128, 1, 0, 3, 32, 16, 16, 9),         # head dim 96, three gate groups
 ])
 def test_lookback_chunk_parallel_backward(cuda_device, B, T, NH, NKVH, Da, r, P, Q, K):
     """The chunk-parallel backward (bf16, production layout, T % 8 == 0, taken when the workspace holds
