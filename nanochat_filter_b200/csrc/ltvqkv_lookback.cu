@@ -320,16 +320,19 @@ __global__ void __launch_bounds__(1024) lookback_bwd_kernel(LbArgs a) {
 // the sequential kernel does. The per-row logit-bias sum adds per-chunk partials (a different
 // association than the sequential walk; bf16 only).
 struct LbParWs {  // workspace slots of the chunk-parallel backward
-  __nv_bfloat16* own;  // [rows][nchunks][K - 1][D + Da]: a chunk's contributions to its last K - 1 tokens
-  __nv_bfloat16* pre;  // [rows][nchunks][K - 1][D + Da]: a chunk's contributions to its warm-up prefix
+  __nv_bfloat16* own;  // [rows][nchunks][K - 1][lb_slot_row]: a chunk's contributions to its last K - 1 tokens
+  __nv_bfloat16* pre;  // [rows][nchunks][K - 1][lb_slot_row]: a chunk's contributions to its warm-up prefix
   float* gi;           // [rows][nchunks][D]: each chunk's initial-state gradient
   float* bp;           // [rows][nchunks][Da]: each chunk's logit-bias partial
 };
 
+// A slot's token row: D + Da entries padded to a multiple of 8 (16-byte rows).
+__host__ __device__ inline int lb_slot_row(int D, int Da) { return (D + Da + 7) & ~7; }
+
 __host__ __device__ inline size_t lb_par_ws_bytes(int B, int H, int D, int Da, int nchunks, long long K) {
   const size_t rows = (size_t)B * H, slots = rows * (size_t)nchunks;
   const size_t kk = (size_t)(K > 1 ? K - 1 : 0);
-  const size_t bf = slots * kk * (size_t)(D + Da) * 2;
+  const size_t bf = slots * kk * (size_t)lb_slot_row(D, Da) * 2;
   return 2 * ((bf + 255) / 256 * 256) + slots * (size_t)D * 4 + ((slots * (size_t)Da * 4 + 255) / 256 * 256);
 }
 
@@ -406,7 +409,7 @@ __global__ void __launch_bounds__(256, 4) lookback_bwd_par_kernel(LbArgs a, LbPa
   const S* h0 = reinterpret_cast<const S*>(a.h[which]) + (long long)b * hs[0] + (long long)hloc * hs[1];
   const S* gh0 = reinterpret_cast<const S*>(a.gh[which]) + (long long)b * gs[0] + (long long)hloc * gs[1];
   const float init = active ? ld<S>(a.inits, ((long long)b * a.H + h) * D + cc) : 0.f;
-  const int kk = (int)(a.K - 1), DW = D + a.Da;
+  const int kk = (int)(a.K - 1), DW = lb_slot_row(D, a.Da);  // slot row
   const long long slot = (long long)row * a.nchunks + ci;
   __nv_bfloat16* gc = reinterpret_cast<__nv_bfloat16*>(a.grad_combined);
   int t_start, t_end, t_pref;
@@ -576,7 +579,7 @@ __global__ void __launch_bounds__(256) lookback_bwd_fixup_kernel(LbArgs a, LbPar
   const int b = row / a.H, h = row % a.H;
   const long long gcb = (long long)b * a.gc_b;
   const int col = h * (a.D + a.Da);
-  const int kk = (int)(a.K - 1), DW = a.D + a.Da;
+  const int kk = (int)(a.K - 1), DW = a.D + a.Da, DWp = lb_slot_row(a.D, a.Da), pr = DWp / 8;
   int s1, e1, p1, s2, e2, p2;
   chunk_bounds(a, ci, s1, e1, p1);
   chunk_bounds(a, ci + 1, s2, e2, p2);
@@ -584,13 +587,19 @@ __global__ void __launch_bounds__(256) lookback_bwd_fixup_kernel(LbArgs a, LbPar
   const int n = e1 - p2;  // tokens p2 .. e1 - 1
   for (int i0 = 0; i0 < n; i0 += kLbFixTok) {
     const int m = min(kLbFixTok, n - i0);
-    for (int e = threadIdx.x; e < DW; e += blockDim.x) {  // slot rows: D + Da contiguous entries
-      const __nv_bfloat16* later = w.pre + (sp * kk + i0) * DW + e;
-      const __nv_bfloat16* earlier = w.own + (so * kk + i0) * DW + e;
-#pragma unroll 4
-      for (int i = 0; i < m; ++i)
-        st_sum[e * (kLbFixTok + 1) + i] =
-            __fadd_rn(__bfloat162float(later[(long long)i * DW]), __bfloat162float(earlier[(long long)i * DW]));
+    for (int idx = threadIdx.x; idx < m * pr; idx += blockDim.x) {  // slot rows as 16-byte pieces
+      const int i = idx / pr, e0 = (idx - i * pr) * 8;
+      const uint4 lv = *reinterpret_cast<const uint4*>(w.pre + (sp * kk + i0 + i) * DWp + e0);
+      const uint4 ev = *reinterpret_cast<const uint4*>(w.own + (so * kk + i0 + i) * DWp + e0);
+      const uint32_t lw[4] = {lv.x, lv.y, lv.z, lv.w}, ew[4] = {ev.x, ev.y, ev.z, ev.w};
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        if (e0 + k < DW) {
+          const float later = (k & 1) ? bf16_hi(lw[k / 2]) : bf16_lo(lw[k / 2]);
+          const float earlier = (k & 1) ? bf16_hi(ew[k / 2]) : bf16_lo(ew[k / 2]);
+          st_sum[(e0 + k) * (kLbFixTok + 1) + i] = __fadd_rn(later, earlier);
+        }
+      }
     }
     __syncthreads();
     for (int idx = threadIdx.x; idx < DW * kLbFixTok; idx += blockDim.x) {  // grad_combined rows: tokens
@@ -776,7 +785,7 @@ extern "C" int ltvqkv_lookback_scan_bwd(int dtype, const void* combined, int64_t
     // chunk-parallel form (the caller's workspace holds its slots)
     char* wp = reinterpret_cast<char*>(workspace) + base;
     const size_t rows = (size_t)B * H, slots = rows * (size_t)a.nchunks, kk = (size_t)(K - 1);
-    const size_t bf = (slots * kk * (size_t)(D + Da) * 2 + 255) / 256 * 256;
+    const size_t bf = (slots * kk * (size_t)lb_slot_row(D, Da) * 2 + 255) / 256 * 256;
     LbParWs w;
     w.own = reinterpret_cast<__nv_bfloat16*>(wp);
     w.pre = reinterpret_cast<__nv_bfloat16*>(wp + bf);
