@@ -276,10 +276,13 @@ def run_ours(args, cfg):
         # The filter-grad all-reduce (7 MB) runs concurrently with the next step's persistent
         # kernels; capping NCCL at 4 channels (4 CTAs) leaves them more SMs and still finishes the
         # reduction well inside one step (2 GPUs: 124.1M -> 128.3M tokens/s). On NVSwitch NCCL picks
-        # NVLS for this size, whose channel count the first cap does not bound (24 CTAs here), so it
-        # is capped too (8 GPUs: 494.5M -> 518.3M tokens/s; NVLS off, ring: 356.8M). Overridable.
+        # NVLS for this size, whose channel count the first cap does not bound (24 CTAs at 8 GPUs),
+        # so from 4 GPUs up it is capped too (8 GPUs: 494.5M -> 518.3M tokens/s; NVLS off, ring:
+        # 356.8M); 2 GPUs measured no better with it (130.8M against 141.9M without, other boxes).
+        # Overridable.
         os.environ.setdefault("NCCL_MAX_NCHANNELS", "4")
-        os.environ.setdefault("NCCL_NVLS_NCHANNELS", "4")
+        if world >= 4:
+            os.environ.setdefault("NCCL_NVLS_NCHANNELS", "4")
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
