@@ -51,6 +51,27 @@ def test_workspace_sizes():
     assert lib.ltvqkv_gemm_workspace_bytes() >= 256
 
 
+def test_lookback_bwd_workspace_sizes():
+    """The look-back backward's workspace query asks for the chunk-parallel slots exactly when that
+    form applies (bf16, K - 1 <= min(P, Q) and <= 64, more than one chunk, D + Da <= 256, r % 32 == 0);
+    otherwise it returns the one-CTA-per-row form's size."""
+    lib = _lib.load()
+    r256 = lambda n: (n + 255) // 256 * 256
+    base = lib.ltvqkv_lookback_workspace_bytes(32, 6, 6, 1)
+    full = lib.ltvqkv_lookback_bwd_workspace_bytes(32, 1024, 6, 6, 1, 128, 128, 112, 17)
+    # 576 rows x 9 chunks; two slot arrays of 16 token rows of 136 entries (129 padded to 16 bytes),
+    # the chunks' fp32 initial-state gradients and logit-bias partials
+    slots = 32 * 18 * 9
+    assert full == r256(base) + 2 * r256(slots * 16 * 136 * 2) + slots * 128 * 4 + r256(slots * 4)
+    for args in ((2, 300, 1, 1, 1, 128, 224, 100, 125),   # warm-up prefix longer than a chunk
+                 (2, 100, 1, 1, 1, 128, 1024, 1024, 1),   # one chunk
+                 (2, 256, 1, 1, 2, 2, 32, 32, 5),          # r not a multiple of 32
+                 (2, 256, 1, 1, 2, 128, 32, 32, 5),        # D + Da > 256
+                 (2, 1024, 1, 1, 1, 128, 128, 112, 66)):   # prefix beyond 64 tokens
+        B, T, NH, NKVH, Da = args[:5]
+        assert lib.ltvqkv_lookback_bwd_workspace_bytes(*args) == lib.ltvqkv_lookback_workspace_bytes(B, NH, NKVH, Da), args
+
+
 def test_argument_validation_without_device():
     lib = _lib.load()
     # bad dtype code
