@@ -78,7 +78,7 @@ def _worker(rank, world, port, out_q):
 
 def test_two_gpu_hook_reduced_gradients_equal_full_batch_oracle():
     if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs (run under gpurun --gpus 2)")
+        pytest.skip("needs two GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
